@@ -1,0 +1,232 @@
+// ref_driver.cpp -- builds the REFERENCE's own game-logic headers on the host.
+//
+// TEST INFRASTRUCTURE ONLY.  This file contains no reference code: it
+// #includes the reference's headers from the reference tree at build time
+// (oracle/Makefile passes -I <reference>/hive_gpu/csrc) and wraps their
+// __device__ functions in batched extern "C" loops, the way the reference's
+// own host build hive_gpu/csrc/cpu_native.cpp:14-46 does.  The resulting
+// oracle/_ref/libhive_ref.so is used (a) to validate the C restatement in
+// oracle/hive_oracle.c and (b) as the timed CPU baseline ("kind":
+// "reference") in bench.py.  It is never part of the product.
+//
+// Kernel loops mirror the reference kernels in hive_gpu/csrc/game_logic.cu:
+//   generate_legal_moves_and_fnn_features_kernel  game_logic.cu:76-91
+//   fnn_successor_features_kernel                 game_logic.cu:182-229
+//   apply_moves_kernel                            game_logic.cu:233-244
+//   legal_moves_to_actions_kernel                 game_logic.cu:811-835
+
+#include <cstdint>
+#include <cstring>
+#include <cmath>
+#include <omp.h>
+
+#define HIVE_CPU_NATIVE 1
+#define __CUDACC__ 1
+#define __device__
+#define __host__
+#define __forceinline__ inline
+#define __global__
+#define __managed__
+#define __constant__
+#define max(a, b) (((a) > (b)) ? (a) : (b))
+#define min(a, b) (((a) < (b)) ? (a) : (b))
+
+static inline int __ffsll(unsigned long long x) { return x ? __builtin_ctzll(x) + 1 : 0; }
+template <typename T>
+static inline T atomicAdd(T* p, T v) { T o = *p; *p += v; return o; }
+static inline int atomicCAS(int* p, int cmp, int v) { int o = *p; if (o == cmp) *p = v; return o; }
+static inline void __threadfence() {}
+struct hv_dim3 { unsigned x, y, z; };
+static thread_local hv_dim3 threadIdx = {0, 0, 0}, blockIdx = {0, 0, 0};
+static const hv_dim3 blockDim = {1, 1, 1};
+
+#include "hex_grid.cuh"
+#include "hive_state.cuh"
+#include "articulation.cuh"
+#include "move_gen.cuh"
+#include "fnn_features.cuh"
+#include "state_encoder.cuh"
+#include "mcts_tree.cuh"
+
+#undef max
+#undef min
+
+using namespace hive_gpu;
+
+static_assert(sizeof(HiveState) == 3424, "HiveState layout");
+static_assert(sizeof(GPUMove) == 6, "GPUMove layout");
+
+static void tables_once() {
+    static bool done = false;
+    if (done) return;
+#pragma omp critical(ref_tables)
+    {
+        if (!done) {
+            init_hex_tables();
+            std::memcpy(NEIGHBORS, HOST_NEIGHBOR_TABLE, sizeof(HOST_NEIGHBOR_TABLE));
+            std::memcpy(SLIDE_FLANKS, HOST_SLIDE_TABLE, sizeof(HOST_SLIDE_TABLE));
+            done = true;
+        }
+    }
+}
+
+static inline int nthreads(int t) { return t > 0 ? t : omp_get_max_threads(); }
+
+extern "C" {
+
+int ref_sizeof_state() { return (int)sizeof(HiveState); }
+
+void ref_init_states(uint8_t* out, int64_t count, int mask) {
+    tables_once();
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memset(&s, 0, sizeof(s));
+        init_state(s, (uint8_t)mask);
+        std::memcpy(out + i * sizeof(HiveState), &s, sizeof(s));
+    }
+}
+
+void ref_legal_moves_features_batch(const uint8_t* states, int64_t count, uint8_t* moves,
+                                    int32_t* num_legal, float* feats, int threads) {
+    tables_once();
+#pragma omp parallel for schedule(dynamic, 64) num_threads(nthreads(threads))
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        GPUMove mv[MAX_LEGAL_MOVES];
+        std::memset(mv, 0, sizeof(mv));
+        int n = generate_legal_moves(s, mv);
+        num_legal[i] = n;
+        if (moves) std::memcpy(moves + i * sizeof(mv), mv, sizeof(mv));
+        if (feats) extract_fnn_features_device(s, mv, n, feats + i * FNN_FEAT_DIM);
+    }
+}
+
+void ref_features_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                        int64_t count, float* feats, int threads) {
+    tables_once();
+#pragma omp parallel for schedule(dynamic, 64) num_threads(nthreads(threads))
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        extract_fnn_features_device(
+            s, reinterpret_cast<const GPUMove*>(moves + i * MAX_LEGAL_MOVES * sizeof(GPUMove)),
+            num_legal[i], feats + i * FNN_FEAT_DIM);
+    }
+}
+
+void ref_compact_moves_batch(const uint8_t* states, int64_t count, uint8_t* moves,
+                             int32_t* num_legal, int threads) {
+    tables_once();
+#pragma omp parallel for schedule(dynamic, 64) num_threads(nthreads(threads))
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        GPUMove mv[MAX_LEGAL_MOVES];
+        std::memset(mv, 0, sizeof(mv));
+        num_legal[i] = generate_fnn_feature_moves(s, mv);
+        std::memcpy(moves + i * sizeof(mv), mv, sizeof(mv));
+    }
+}
+
+void ref_successor_features_batch(const uint8_t* states, const uint8_t* moves,
+                                  const int64_t* action_to_root, const int64_t* move_indices,
+                                  int64_t count, float* feats, int threads) {
+    tables_once();
+#pragma omp parallel for schedule(dynamic, 64) num_threads(nthreads(threads))
+    for (int64_t i = 0; i < count; i++) {
+        int64_t root = action_to_root[i];
+        HiveState child;
+        std::memcpy(&child, states + root * sizeof(HiveState), sizeof(child));
+        GPUMove mv;
+        std::memcpy(&mv, moves + (root * MAX_LEGAL_MOVES + move_indices[i]) * sizeof(GPUMove),
+                    sizeof(mv));
+        apply_move(child, mv);
+        GPUMove cm[MAX_LEGAL_MOVES];
+        int n = generate_fnn_feature_moves(child, cm);
+        extract_fnn_features_device(child, cm, n, feats + i * FNN_FEAT_DIM);
+    }
+}
+
+void ref_apply_moves_batch(uint8_t* states, const uint8_t* moves, int64_t count) {
+    tables_once();
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        GPUMove mv;
+        std::memcpy(&mv, moves + i * sizeof(GPUMove), sizeof(mv));
+        apply_move(s, mv);
+        std::memcpy(states + i * sizeof(HiveState), &s, sizeof(s));
+    }
+}
+
+void ref_articulation_batch(const uint8_t* states, int64_t count, uint64_t* ap, int threads) {
+    tables_once();
+#pragma omp parallel for schedule(dynamic, 64) num_threads(nthreads(threads))
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        Bitboard b = find_articulation_points(s);
+        std::memcpy(ap + i * BB_WORDS, b.w, sizeof(b.w));
+    }
+}
+
+void ref_actions_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                       int64_t count, int32_t* actions, int32_t* centroids) {
+    tables_once();
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        int cq, cr;
+        compute_centroid(s, cq, cr);
+        if (centroids) { centroids[2 * i] = cq; centroids[2 * i + 1] = cr; }
+        const GPUMove* mv =
+            reinterpret_cast<const GPUMove*>(moves + i * MAX_LEGAL_MOVES * sizeof(GPUMove));
+        for (int m = 0; m < MAX_LEGAL_MOVES; m++) actions[i * MAX_LEGAL_MOVES + m] = -1;
+        for (int m = 0; m < num_legal[i]; m++)
+            actions[i * MAX_LEGAL_MOVES + m] = gpu_move_to_action(mv[m], cq, cr);
+    }
+}
+
+// Seeded playout generator with the same counter RNG as oracle/hive_oracle.c
+// (orc_rng / orc_playout), driven by the reference's own move generator.
+static inline uint64_t rmix(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+static inline uint64_t rrng(uint64_t seed, uint64_t game, uint64_t ply) {
+    return rmix(rmix(seed ^ rmix(game)) + ply);
+}
+
+void ref_generate_positions(uint64_t seed, int64_t first_game, int64_t count, int max_ply,
+                            int mask, uint8_t* out, int threads) {
+    tables_once();
+#pragma omp parallel for schedule(dynamic, 16) num_threads(nthreads(threads))
+    for (int64_t i = 0; i < count; i++) {
+        uint64_t g = (uint64_t)(first_game + i);
+        HiveState s;
+        std::memset(&s, 0, sizeof(s));
+        init_state(s, (uint8_t)mask);
+        int stop = (int)(rrng(seed, g, 0) % (uint64_t)(max_ply + 1));
+        GPUMove mv[MAX_LEGAL_MOVES];
+        for (int p = 1; p <= stop; p++) {
+            if (s.result != IN_PROGRESS) break;
+            int n = generate_legal_moves(s, mv);
+            apply_move(s, mv[rrng(seed, g, (uint64_t)p) % (uint64_t)n]);
+        }
+        std::memcpy(out + i * sizeof(HiveState), &s, sizeof(s));
+    }
+}
+
+void ref_queen_escape_batch(const uint8_t* states, int64_t count, uint8_t* flags) {
+    tables_once();
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        flags[i] = has_queen_escape_move(s) ? 1 : 0;
+    }
+}
+
+}  // extern "C"
