@@ -1,0 +1,96 @@
+"""Loader for the C-ABI library ``libhive_b200.so`` (declared in include/hive_b200.h).
+
+The library is built in-tree by :func:`build` (nvcc, sm_100a only).  Loading
+fails loudly when it is missing: there is no CPU or Python fallback on the
+product path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+LIB_PATH = os.path.join(PKG_DIR, "libhive_b200.so")
+CSRC = os.path.join(PKG_DIR, "csrc")
+SOURCES = ["hv_kernels.cu"]
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
+]
+
+HV_OK = 0
+
+
+class HiveB200Error(RuntimeError):
+    """A C-ABI entry point returned a non-zero hv_status."""
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
+        if cand and (os.path.sep not in cand or os.path.exists(cand)):
+            return cand
+    return "nvcc"
+
+
+def build(verbose: bool = False) -> str:
+    """Compile every CUDA source of the package into libhive_b200.so."""
+    srcs = [os.path.join(CSRC, s) for s in SOURCES]
+    cmd = [_nvcc(), *NVCC_FLAGS, "-o", LIB_PATH, *srcs]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True, cwd=PKG_DIR)
+    return LIB_PATH
+
+
+_vp = C.c_void_p
+_i64 = C.c_int64
+_int = C.c_int
+
+_SIGNATURES = {
+    "hv_version": ([], _int),
+    "hv_status_string": ([_int], C.c_char_p),
+    "hv_get_error": ([_vp, _int], _int),
+    "hv_create_initial_states": ([_vp, _i64, _int, _vp], _int),
+    "hv_generate_legal_moves": ([_vp, _i64, _vp, _vp, _vp], _int),
+    "hv_generate_legal_moves_and_fnn_features": ([_vp, _i64, _vp, _vp, _vp, _vp], _int),
+    "hv_extract_fnn_features": ([_vp, _vp, _vp, _i64, _vp, _vp], _int),
+    "hv_fnn_successor_features": ([_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp], _int),
+    "hv_apply_moves": ([_vp, _vp, _i64, _vp], _int),
+    "hv_check_results": ([_vp, _i64, _vp, _vp], _int),
+    "hv_compute_centroids": ([_vp, _i64, _vp, _vp], _int),
+    "hv_legal_moves_to_actions": ([_vp, _vp, _vp, _i64, _vp, _vp], _int),
+    "hv_generate_positions": ([C.c_uint64, _i64, _i64, _int, _int, _vp, _vp], _int),
+}
+
+_lib = None
+
+
+def exported_symbols() -> list[str]:
+    return sorted(_SIGNATURES)
+
+
+def load() -> C.CDLL:
+    """Load libhive_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+            "(nvcc, sm_100a). There is no CPU fallback.")
+    lib = C.CDLL(LIB_PATH)
+    for name, (args, res) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != HV_OK:
+        msg = load().hv_status_string(status).decode()
+        raise HiveB200Error(f"{what} failed: hv_status={status} ({msg})")

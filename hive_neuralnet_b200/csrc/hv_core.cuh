@@ -1,0 +1,336 @@
+// hv_core.cuh -- warp-per-position Hive game logic for sm_100a.
+//
+// One warp owns one position.  The 3424-byte HiveState (the boundary format
+// of the reference, hive_gpu/csrc/hive_state.cuh:239-269) is staged in the
+// warp's shared-memory slot; everything else is derived from it:
+//
+//   * row bitboards: lane r (r < 23) holds the 23-bit occupancy mask of grid
+//     row r, so a hex-direction shift of a whole 529-cell board is one
+//     shuffle plus one shift (hv_shift_* below);
+//   * piece lanes: lane i (i < N <= 28) owns the i-th occupied cell in
+//     ascending cell order (the reference's iteration order);
+//   * slide masks sl[d]: the set of cells that can slide one step in
+//     direction d (destination empty, exactly one flank occupied), built for
+//     the whole board with row-bitboard algebra, so each freedom-to-move test
+//     of the reference (move_gen.cuh:82-131) becomes one shared-memory bit
+//     test.
+//
+// Move generators are warp-cooperative: one lane per direction (queen,
+// grasshopper, beetle, throws), one lane per (queue item, direction) for the
+// ant breadth-first search, and one lane per (path, direction) for the
+// three-step spider/ladybug walks, with __match_any_sync/__ballot_sync
+// reproducing the reference's first-seen emission order exactly.
+#pragma once
+
+#include <cstdint>
+
+namespace hv {
+
+constexpr int kBoard = 23;
+constexpr int kCells = 529;
+constexpr int kMaxMoves = 256;
+constexpr int kFeat = 122;
+constexpr int kStateBytes = 3424;
+constexpr int kMoveBytes = 6;
+constexpr int kOffHeight = 2645;
+constexpr int kOffOcc = 3176;
+constexpr int kOffWTop = 3248;
+constexpr int kOffBTop = 3320;
+constexpr int kOffQCell = 3392;
+constexpr int kOffHands = 3396;
+constexpr int kOffTurn = 3412;
+constexpr int kOffQPlaced = 3414;
+constexpr int kOffResult = 3415;
+constexpr int kOffStun = 3416;
+constexpr uint32_t kFull = 0xffffffffu;
+constexpr uint32_t kRowBits = 0x7fffffu;
+
+// Error bits reported through the per-launch status word.
+constexpr uint32_t kErrBuffer = 1u;  // a generator list exceeded its buffer
+constexpr uint32_t kErrIndex = 2u;   // a root / move index was out of range
+
+struct __align__(16) WarpSmem {
+    uint8_t st[kStateBytes];     // staged HiveState
+    uint16_t mv[kMaxMoves * 3];  // move list: (type | pt << 8, from, to) per move
+    uint32_t occ[24];            // occupied row masks
+    uint32_t sl[6][24];          // slide masks of the position
+    uint32_t slx[6][24];         // slide masks with the current mover lifted
+    uint32_t seen[18];           // 529-bit scratch set
+    uint32_t prow[24];           // placement row masks
+    uint32_t adj[32];            // piece adjacency (piece-index space)
+    uint16_t pcell[32];          // cell of piece i
+    uint32_t own[24];            // side-to-move top-piece row masks
+    uint16_t pref[24];           // piece index of the first occupied cell of row r
+    uint16_t ppref[24];          // placement index of the first placement cell of row r
+    uint8_t pflag[32];           // bit0: pinned
+    uint16_t dst[128];           // destination list of the running generator
+    uint16_t tmp[128];           // sub-generator list (mosquito)
+    uint16_t l2a[40];            // three-step walks: level-2 (p1)
+    uint16_t l2b[40];            //                   level-2 (p2)
+    int acc[112];                // feature accumulators
+    uint32_t bm[16 * 17 + 18];   // per (type, owner) source-cell sets + placement set
+};
+
+// ---------------------------------------------------------------------------
+// small helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+    uint32_t m;
+    asm volatile("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// direction order E, NE, NW, W, SW, SE (hex_grid.cuh:41-49); packed (d+1) in 2 bits
+__device__ __forceinline__ int dcol(int d) { return ((1050 >> (2 * d)) & 3) - 1; }
+__device__ __forceinline__ int drow(int d) { return ((2625 >> (2 * d)) & 3) - 1; }
+__device__ __forceinline__ int cw_dir(int d) { return d == 0 ? 5 : d - 1; }
+__device__ __forceinline__ int ccw_dir(int d) { return d == 5 ? 0 : d + 1; }
+__device__ __forceinline__ int opp_dir(int d) { return d < 3 ? d + 3 : d - 3; }
+
+__device__ __forceinline__ int nbr(int c, int d) {
+    int r = c / kBoard, q = c - r * kBoard;
+    int r2 = r + drow(d), q2 = q + dcol(d);
+    return ((unsigned)r2 < (unsigned)kBoard && (unsigned)q2 < (unsigned)kBoard) ? r2 * kBoard + q2
+                                                                                : -1;
+}
+
+__device__ __forceinline__ int rowbit(const uint32_t* rows, int c) {
+    int r = c / kBoard;
+    return (int)((rows[r] >> (c - r * kBoard)) & 1u);
+}
+
+__device__ __forceinline__ int hex_distance(int a, int b) {
+    int ra = a / kBoard, qa = a - ra * kBoard;
+    int rb = b / kBoard, qb = b - rb * kBoard;
+    int dq = qb - qa, dr = rb - ra, ds = -(dq + dr);
+    dq = dq < 0 ? -dq : dq;
+    dr = dr < 0 ? -dr : dr;
+    ds = ds < 0 ? -ds : ds;
+    int m = dq > dr ? dq : dr;
+    return m > ds ? m : ds;
+}
+
+// ---------------------------------------------------------------------------
+// state field access (boundary byte layout)
+// ---------------------------------------------------------------------------
+
+struct Pos {
+    WarpSmem* w;
+    __device__ __forceinline__ int height(int c) const { return c >= 0 ? w->st[kOffHeight + c] : 0; }
+    // top piece byte; a corrupt height above the stack limit reads level 5
+    __device__ __forceinline__ int top(int c) const {
+        int h = height(c);
+        h = h > 5 ? 5 : h;
+        return h ? w->st[(h - 1) * kCells + c] : 0;
+    }
+    __device__ __forceinline__ bool occupied(int c) const { return c >= 0 && rowbit(w->occ, c); }
+    __device__ __forceinline__ int turn() const {
+        return w->st[kOffTurn] | (w->st[kOffTurn + 1] << 8);
+    }
+    __device__ __forceinline__ int stunned() const {
+        return w->st[kOffStun] | (w->st[kOffStun + 1] << 8);
+    }
+    __device__ __forceinline__ int queen_cell(int c) const {
+        return w->st[kOffQCell + 2 * c] | (w->st[kOffQCell + 2 * c + 1] << 8);
+    }
+    __device__ __forceinline__ int hand(int color, int t) const {
+        return w->st[kOffHands + color * 8 + t];
+    }
+    __device__ __forceinline__ int result() const { return w->st[kOffResult]; }
+    __device__ __forceinline__ int queen_placed() const { return w->st[kOffQPlaced]; }
+    __device__ __forceinline__ bool is_stunned(int c) const {
+        int s = stunned();
+        return s != 0xFFFF && s == c;
+    }
+    // piece index of an occupied cell
+    __device__ __forceinline__ int pidx(int c) const {
+        int r = c / kBoard, q = c - r * kBoard;
+        return w->pref[r] + __popc(w->occ[r] & ((1u << q) - 1u));
+    }
+    // elevated gate (move_gen.cuh:659-667): both flanks strictly higher than h
+    __device__ __forceinline__ bool gate_blocked(int c, int d, int h) const {
+        return height(nbr(c, cw_dir(d))) > h && height(nbr(c, ccw_dir(d))) > h;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// row bitboards (lane r = grid row r; lanes >= 23 hold zero)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t row_valid_mask() { return lane_id() < kBoard ? kRowBits : 0u; }
+
+// X[r-1] and X[r+1] for the calling lane
+__device__ __forceinline__ uint32_t from_row_above(uint32_t x) {
+    uint32_t v = __shfl_up_sync(kFull, x, 1);
+    return lane_id() == 0 ? 0u : v;
+}
+__device__ __forceinline__ uint32_t from_row_below(uint32_t x) { return __shfl_down_sync(kFull, x, 1); }
+
+// N_d(X): cells whose neighbour in direction d lies in X, all six directions.
+__device__ __forceinline__ void neighbour_sets(uint32_t x, uint32_t* out) {
+    uint32_t up = from_row_above(x), dn = from_row_below(x), m = row_valid_mask();
+    out[0] = (x >> 1) & m;   // E : (r, q+1)
+    out[1] = (up >> 1) & m;  // NE: (r-1, q+1)
+    out[2] = up & m;         // NW: (r-1, q)
+    out[3] = (x << 1) & m;   // W : (r, q-1)
+    out[4] = (dn << 1) & m;  // SW: (r+1, q-1)
+    out[5] = dn & m;         // SE: (r+1, q)
+}
+
+__device__ __forceinline__ uint32_t dilate(uint32_t x) {
+    uint32_t n[6];
+    neighbour_sets(x, n);
+    return n[0] | n[1] | n[2] | n[3] | n[4] | n[5];
+}
+
+// Slide masks for occupancy x (freedom to move, move_gen.cuh:82-118):
+// sl[d] = {c : nb(c,d) on grid and empty, occ(nb(c,cw d)) xor occ(nb(c,ccw d))}
+__device__ __forceinline__ void build_slide_masks(uint32_t x, uint32_t (*sl)[24]) {
+    uint32_t nx[6], ne[6];
+    uint32_t m = row_valid_mask();
+    neighbour_sets(x, nx);
+    neighbour_sets(~x & m, ne);
+    int l = lane_id();
+    if (l < 24) {
+#pragma unroll
+        for (int d = 0; d < 6; d++) sl[d][l] = ne[d] & (nx[(d + 5) % 6] ^ nx[(d + 1) % 6]);
+    }
+}
+
+// exclusive prefix sum over lanes
+__device__ __forceinline__ int warp_excl_scan(int v) {
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(kFull, x, o);
+        if (lane_id() >= o) x += y;
+    }
+    return x - v;
+}
+
+// k-th set cell (k < total) of a row-bitboard stored in smem with row prefix
+__device__ __forceinline__ int kth_cell(const uint32_t* rows, const uint16_t* pre, int k) {
+    int lo = 0, hi = kBoard - 1;  // largest r with pre[r] <= k
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= k) lo = mid;
+        else hi = mid - 1;
+    }
+    int q = __fns(rows[lo], 0, k - pre[lo] + 1);
+    return lo * kBoard + q;
+}
+
+// ---------------------------------------------------------------------------
+// per-position setup
+// ---------------------------------------------------------------------------
+
+struct Setup {
+    int n;          // occupied cells (<= 28 used, as the reference's MAX_PIECES)
+    int color;      // side to move
+    int my_cell;    // piece lane: cell (or -1)
+    int my_h;       // piece lane: stack height
+    int my_top;     // piece lane: top byte
+    bool my_ap;     // piece lane: articulation point
+    uint32_t own;   // row lane: own top pieces
+    uint32_t opp;   // row lane: opponent top pieces
+    uint32_t occ;   // row lane: occupancy
+};
+
+__device__ __forceinline__ uint32_t load_row(const uint8_t* st, int off, int lane) {
+    if (lane >= kBoard) return 0u;
+    const uint32_t* w32 = reinterpret_cast<const uint32_t*>(st + off);
+    int b = lane * kBoard;
+    uint32_t lo = w32[b >> 5], hi = w32[(b >> 5) + 1];
+    return __funnelshift_r(lo, hi, b & 31) & kRowBits;
+}
+
+// Bitboards, piece list, slide masks, articulation points.
+__device__ __forceinline__ Setup setup_position(WarpSmem* w) {
+    Setup S;
+    Pos P{w};
+    int l = lane_id();
+    S.occ = load_row(w->st, kOffOcc, l);
+    uint32_t wt = load_row(w->st, kOffWTop, l), bt = load_row(w->st, kOffBTop, l);
+    S.color = P.turn() & 1;
+    S.own = S.color ? bt : wt;
+    S.opp = S.color ? wt : bt;
+    if (l < 24) {
+        w->occ[l] = S.occ;
+        w->own[l] = S.own;
+    }
+    int cnt = __popc(S.occ);
+    int pre = warp_excl_scan(cnt);
+    if (l < 24) w->pref[l] = (uint16_t)pre;
+    S.n = __shfl_sync(kFull, pre + cnt, 31);
+    if (S.n > 28) S.n = 28;
+    // cells of this row into the piece list (ascending order)
+    {
+        uint32_t bits = S.occ;
+        int k = pre;
+        while (bits) {
+            int q = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (k < 32) w->pcell[k] = (uint16_t)(l * kBoard + q);
+            k++;
+        }
+    }
+    build_slide_masks(S.occ, w->sl);
+    __syncwarp();
+    S.my_cell = l < S.n ? (int)w->pcell[l] : -1;
+    S.my_h = P.height(S.my_cell);
+    S.my_top = P.top(S.my_cell);
+
+    // adjacency in piece-index space
+    uint32_t adj = 0;
+    if (S.my_cell >= 0) {
+#pragma unroll
+        for (int d = 0; d < 6; d++) {
+            int nb = nbr(S.my_cell, d);
+            if (nb >= 0 && rowbit(w->occ, nb)) {
+                int j = P.pidx(nb);
+                if (j < S.n) adj |= 1u << j;
+            }
+        }
+    }
+    w->adj[l] = adj;
+    __syncwarp();
+    // One-Hive rule (articulation.cuh:34-168): the reference runs Tarjan from
+    // the lowest occupied cell, i.e. it reports the articulation points of
+    // that cell's component.  Lane x < n removes vertex x and floods from a
+    // vertex of that component; lane 31 floods the component itself.
+    uint32_t all = S.n >= 32 ? kFull : ((1u << S.n) - 1u);
+    uint32_t adj0 = w->adj[0];
+    uint32_t allowed = all;
+    int start = 0;
+    bool active = S.n > 2 && (l < S.n || l == 31);
+    if (l < S.n) {
+        allowed = all & ~(1u << l);
+        if (l == 0) start = adj0 ? __ffs(adj0) - 1 : -1;
+    }
+    uint32_t seen = 0;
+    if (active && start >= 0) {
+        seen = 1u << start;
+        uint32_t fr = seen;
+        while (fr) {
+            int v = __ffs(fr) - 1;
+            fr &= fr - 1;
+            uint32_t nw = w->adj[v] & allowed & ~seen;
+            seen |= nw;
+            fr |= nw;
+        }
+    }
+    uint32_t comp = __shfl_sync(kFull, seen, 31);
+    S.my_ap = false;
+    if (S.n > 2 && l < S.n && ((comp >> l) & 1u)) {
+        uint32_t rest = comp & ~(1u << l);
+        S.my_ap = (l == 0) ? (adj0 != 0 && seen != rest) : (seen != rest);
+    }
+    if (l < 32) w->pflag[l] = (S.my_ap && S.my_h == 1) ? 1 : 0;
+    __syncwarp();
+    return S;
+}
+
+}  // namespace hv

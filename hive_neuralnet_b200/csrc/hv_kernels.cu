@@ -1,0 +1,441 @@
+// hv_kernels.cu -- sm_100a kernels of the Hive self-play hot path and the
+// C-ABI entry points declared in include/hive_b200.h.
+//
+// Every kernel is a persistent grid of warps (one warp per position, a
+// grid of SMs x resident blocks) that strides over the batch.  Inputs are
+// staged into the warp's shared-memory slot with 16-byte vector loads; the
+// move list is assembled in shared memory and written back as 16-byte
+// vector stores including its zero padding, so the [B, 256, 6] output needs
+// no separate memset pass.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "hv_core.cuh"
+#include "hv_movegen.cuh"
+#include "hv_state.cuh"
+#include "../../include/hive_b200.h"
+
+namespace hv {
+
+constexpr int kWarpsPerBlock = 8;
+constexpr int kThreads = kWarpsPerBlock * 32;
+
+// device error word (sticky until read and cleared by hv_get_error)
+__device__ uint32_t g_error;
+
+__device__ __forceinline__ WarpSmem* warp_slot() {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    return reinterpret_cast<WarpSmem*>(smem_raw) + (threadIdx.x >> 5);
+}
+
+__device__ __forceinline__ void stage_state(WarpSmem* w, const uint8_t* src) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(w->st);
+    for (int i = lane_id(); i < kStateBytes / 16; i += 32) d4[i] = __ldg(s4 + i);
+    __syncwarp();
+}
+
+__device__ __forceinline__ void zero_moves(WarpSmem* w) {
+    uint4* m4 = reinterpret_cast<uint4*>(w->mv);
+    for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+}
+
+__device__ __forceinline__ void store_moves(const WarpSmem* w, uint8_t* dst) {
+    const uint4* m4 = reinterpret_cast<const uint4*>(w->mv);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) d4[i] = m4[i];
+}
+
+// ---------------------------------------------------------------------------
+// root positions: legal moves (+ features), or features of a given list
+// (game_logic.cu:63-91 generate_legal_moves[_and_fnn_features]_kernel,
+//  fnn_features.cuh:334-350 extract_fnn_features_kernel)
+// ---------------------------------------------------------------------------
+template <bool GEN, bool WRITE_MOVES, bool FEATS>
+__global__ void __launch_bounds__(kThreads) k_root(const uint8_t* __restrict__ states,
+                                                   const uint8_t* __restrict__ moves_in,
+                                                   const int32_t* __restrict__ nl_in, int64_t batch,
+                                                   uint8_t* __restrict__ moves_out,
+                                                   int32_t* __restrict__ nl_out,
+                                                   float* __restrict__ feats_out) {
+    WarpSmem* w = warp_slot();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        stage_state(w, states + p * kStateBytes);
+        int n;
+        if (GEN) {
+            zero_moves(w);
+            Setup S = setup_position(w);
+            n = gen_legal(w, S, &g_error);
+            if (WRITE_MOVES) {
+                store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes));
+                if (lane_id() == 0) nl_out[p] = n;
+            }
+            if (FEATS) features(w, S, n, feats_out + p * kFeat);
+        } else {
+            const uint4* s4 = reinterpret_cast<const uint4*>(moves_in + p * (kMaxMoves * kMoveBytes));
+            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
+            for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
+            n = nl_in[p];
+            n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
+            __syncwarp();
+            Setup S = setup_position(w);
+            features(w, S, n, feats_out + p * kFeat);
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// successor features: apply one root move, compact list, features
+// (game_logic.cu:182-229 fnn_successor_features_kernel)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) k_successor_features(
+    const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
+    const int64_t* __restrict__ action_to_root, const int64_t* __restrict__ move_indices,
+    int64_t num_actions, float* __restrict__ feats_out) {
+    WarpSmem* w = warp_slot();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t a = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); a < num_actions;
+         a += nwarps) {
+        int64_t root = action_to_root[a];
+        int64_t mi = move_indices[a];
+        if (root < 0 || root >= num_states || mi < 0 || mi >= kMaxMoves) {
+            // out-of-range request: zero row, flag it, touch nothing else
+            for (int k = lane_id(); k < kFeat; k += 32) feats_out[a * kFeat + k] = 0.0f;
+            if (lane_id() == 0) atomicOr(&g_error, kErrIndex);
+            __syncwarp();
+            continue;
+        }
+        stage_state(w, states + root * kStateBytes);
+        if (lane_id() == 0) {
+            const uint8_t* m = legal_moves + (root * kMaxMoves + mi) * kMoveBytes;
+            st_apply(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+        }
+        __syncwarp();
+        Setup S = setup_position(w);
+        int n = gen_compact(w, S, &g_error);
+        features(w, S, n, feats_out + a * kFeat);
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// state operations
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) k_init_states(uint8_t* __restrict__ states,
+                                                          int64_t batch, int mask) {
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        uint8_t* st = states + p * kStateBytes;
+        uint4* d4 = reinterpret_cast<uint4*>(st);
+        for (int i = lane_id(); i < kStateBytes / 16; i += 32) d4[i] = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+        if (lane_id() == 0) st_init_fields(st, mask);
+        __syncwarp();
+    }
+}
+
+__global__ void k_apply_moves(uint8_t* __restrict__ states, const uint8_t* __restrict__ moves,
+                              int64_t batch) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch) return;
+    const uint8_t* m = moves + i * kMoveBytes;
+    st_apply(states + i * kStateBytes, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+}
+
+__global__ void k_check_results(const uint8_t* __restrict__ states, int64_t batch,
+                                int32_t* __restrict__ results) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < batch) results[i] = states[i * kStateBytes + kOffResult];
+}
+
+// seeded uniform random legal playouts (benchmark / test inputs)
+__global__ void __launch_bounds__(kThreads) k_playouts(uint64_t seed, int64_t first_game,
+                                                       int64_t count, int max_ply, int mask,
+                                                       uint8_t* __restrict__ out) {
+    WarpSmem* w = warp_slot();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t i = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); i < count;
+         i += nwarps) {
+        uint64_t g = (uint64_t)(first_game + i);
+        uint4* d4 = reinterpret_cast<uint4*>(w->st);
+        for (int k = lane_id(); k < kStateBytes / 16; k += 32) d4[k] = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+        if (lane_id() == 0) st_init_fields(w->st, mask);
+        __syncwarp();
+        int stop = (int)(game_rng(seed, g, 0) % (uint64_t)(max_ply + 1));
+        for (int p = 1; p <= stop; p++) {
+            if (w->st[kOffResult] != 0) break;
+            Setup S = setup_position(w);
+            int n = gen_legal(w, S, &g_error);
+            int k = (int)(game_rng(seed, g, (uint64_t)p) % (uint64_t)n);
+            if (lane_id() == 0) {
+                const uint16_t* m = w->mv + 3 * k;
+                st_apply(w->st, m[0] & 255, m[0] >> 8, m[1], m[2]);
+            }
+            __syncwarp();
+        }
+        uint4* o4 = reinterpret_cast<uint4*>(out + i * kStateBytes);
+        for (int k = lane_id(); k < kStateBytes / 16; k += 32) o4[k] = d4[k];
+        __syncwarp();
+    }
+}
+
+// round-half-to-even of sum / n (state_encoder.cuh:55-79)
+__device__ __forceinline__ int round_half_even(int sum, int n) {
+    int q = sum / n, r = sum - q * n;
+    int twice = 2 * (r < 0 ? -r : r);
+    if (twice < n) return q;
+    int away = sum > 0 ? q + 1 : q - 1;
+    if (twice > n) return away;
+    return (q & 1) == 0 ? q : away;
+}
+
+// centroid (state_encoder.cuh:889-906) and move -> action index
+// (mcts_tree.cuh:146-179, game_logic.cu:811-835); one warp per state
+__global__ void __launch_bounds__(kThreads) k_actions(const uint8_t* __restrict__ states,
+                                                      const uint8_t* __restrict__ moves,
+                                                      const int32_t* __restrict__ num_legal,
+                                                      int64_t batch, int32_t* __restrict__ actions,
+                                                      int32_t* __restrict__ centroids) {
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    const int l = lane_id();
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        const uint8_t* h = states + p * kStateBytes + kOffHeight;
+        int sq = 0, sr = 0, n = 0;
+        for (int c = l; c < kCells; c += 32) {
+            if (h[c]) {
+                int r = c / kBoard;
+                sq += c - r * kBoard - 11;
+                sr += r - 11;
+                n++;
+            }
+        }
+        sq = __reduce_add_sync(kFull, sq);
+        sr = __reduce_add_sync(kFull, sr);
+        n = __reduce_add_sync(kFull, n);
+        int cq = n ? round_half_even(sq, n) : 0, cr = n ? round_half_even(sr, n) : 0;
+        if (centroids && l == 0) {
+            centroids[2 * p] = cq;
+            centroids[2 * p + 1] = cr;
+        }
+        if (actions) {
+            int nl = num_legal[p];
+            const uint8_t* mv = moves + p * (kMaxMoves * kMoveBytes);
+            for (int m = l; m < kMaxMoves; m += 32) {
+                int a = -1;
+                if (m < nl) {
+                    const uint8_t* x = mv + m * kMoveBytes;
+                    int type = x[0], pt = x[1], from = x[2] | (x[3] << 8), to = x[4] | (x[5] << 8);
+                    if (type == 2) a = 85833;
+                    else if (type == 0) {
+                        int ec = (to % kBoard - 11) - cq + 8, er = (to / kBoard - 11) - cr + 8;
+                        if (ec >= 0 && ec < 17 && er >= 0 && er < 17) a = (pt - 1) * 289 + er * 17 + ec;
+                    } else {
+                        int sc = (from % kBoard - 11) - cq + 8, srr = (from / kBoard - 11) - cr + 8;
+                        int dc = (to % kBoard - 11) - cq + 8, dr = (to / kBoard - 11) - cr + 8;
+                        if (sc >= 0 && sc < 17 && srr >= 0 && srr < 17 && dc >= 0 && dc < 17 &&
+                            dr >= 0 && dr < 17)
+                            a = 2312 + (srr * 17 + sc) * 289 + dr * 17 + dc;
+                    }
+                }
+                actions[p * kMaxMoves + m] = a;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// launch helpers
+// ---------------------------------------------------------------------------
+struct DeviceInfo {
+    int sms = 0;
+    int blocks_per_sm = 0;
+};
+static DeviceInfo g_dev[64];
+
+template <typename K>
+static int grid_for(K kernel, int64_t units, size_t smem, int* out_grid) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HV_ECUDA;
+    DeviceInfo& d = g_dev[dev];
+    if (d.sms == 0) {
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return HV_ECUDA;
+    }
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return HV_ECUDA;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) !=
+        cudaSuccess)
+        return HV_ECUDA;
+    if (per_sm < 1) per_sm = 1;
+    int64_t want = (units + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    int64_t cap = (int64_t)d.sms * per_sm;
+    *out_grid = (int)(want < cap ? want : cap);
+    if (*out_grid < 1) *out_grid = 1;
+    return HV_OK;
+}
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static inline int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? HV_OK : HV_ECUDA;
+}
+
+template <bool GEN, bool WM, bool FE>
+static int launch_root(const uint8_t* states, const uint8_t* mi, const int32_t* nli, int64_t batch,
+                       uint8_t* mo, int32_t* nlo, float* fo, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!states || !aligned16(states)) return HV_EINVAL;
+    if (WM && (!mo || !nlo || !aligned16(mo))) return HV_EINVAL;
+    if (FE && !fo) return HV_EINVAL;
+    if (!GEN && (!mi || !nli || !aligned16(mi))) return HV_EINVAL;
+    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_root<GEN, WM, FE>, batch, smem, &grid);
+    if (rc) return rc;
+    k_root<GEN, WM, FE><<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, mi, nli, batch, mo,
+                                                                        nlo, fo);
+    return launch_status();
+}
+
+}  // namespace hv
+
+using namespace hv;
+
+extern "C" {
+
+int hv_version(void) { return HV_ABI_VERSION; }
+
+const char* hv_status_string(int status) {
+    switch (status) {
+        case HV_OK: return "ok";
+        case HV_EINVAL: return "invalid argument (null, misaligned or negative size)";
+        case HV_ECUDA: return "CUDA launch or runtime error";
+        case HV_ENOMEM_TREE: return "tree node pool exhausted";
+        case HV_ETIMEOUT: return "bounded device wait gave up";
+        case HV_EDEVICE: return "device error word set (a generator buffer overflowed)";
+        default: return "unknown status";
+    }
+}
+
+int hv_get_error(uint32_t* out, int clear) {
+    uint32_t v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_error, sizeof(v)) != cudaSuccess) return HV_ECUDA;
+    if (out) *out = v;
+    if (clear && v) {
+        uint32_t z = 0;
+        if (cudaMemcpyToSymbol(g_error, &z, sizeof(z)) != cudaSuccess) return HV_ECUDA;
+    }
+    return HV_OK;
+}
+
+int hv_create_initial_states(uint8_t* states, int64_t batch, int expansion_mask, void* stream) {
+    if (batch < 0 || (batch && (!states || !aligned16(states)))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    int grid = 0;
+    int rc = grid_for(k_init_states, batch, 0, &grid);
+    if (rc) return rc;
+    k_init_states<<<grid, kThreads, 0, (cudaStream_t)stream>>>(states, batch, expansion_mask & 7);
+    return launch_status();
+}
+
+int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves,
+                            int32_t* num_legal, void* stream) {
+    return launch_root<true, true, false>(states, nullptr, nullptr, batch, moves, num_legal,
+                                          nullptr, stream);
+}
+
+int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
+                                             int32_t* num_legal, float* features, void* stream) {
+    return launch_root<true, true, true>(states, nullptr, nullptr, batch, moves, num_legal,
+                                         features, stream);
+}
+
+int hv_extract_fnn_features(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                            int64_t batch, float* features, void* stream) {
+    return launch_root<false, false, true>(states, moves, num_legal, batch, nullptr, nullptr,
+                                           features, stream);
+}
+
+int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const uint8_t* legal_moves,
+                              const int64_t* action_to_root, const int64_t* move_indices,
+                              int64_t num_actions, float* features, void* stream) {
+    if (num_actions < 0 || num_states < 0) return HV_EINVAL;
+    if (num_actions == 0) return HV_OK;
+    if (!states || !legal_moves || !action_to_root || !move_indices || !features ||
+        !aligned16(states))
+        return HV_EINVAL;
+    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_successor_features, num_actions, smem, &grid);
+    if (rc) return rc;
+    k_successor_features<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+        states, num_states, legal_moves, action_to_root, move_indices, num_actions, features);
+    return launch_status();
+}
+
+int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream) {
+    if (batch < 0 || (batch && (!states || !moves || !aligned16(states)))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    int blocks = (int)((batch + 255) / 256);
+    k_apply_moves<<<blocks, 256, 0, (cudaStream_t)stream>>>(states, moves, batch);
+    return launch_status();
+}
+
+int hv_check_results(const uint8_t* states, int64_t batch, int32_t* results, void* stream) {
+    if (batch < 0 || (batch && (!states || !results))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    int blocks = (int)((batch + 255) / 256);
+    k_check_results<<<blocks, 256, 0, (cudaStream_t)stream>>>(states, batch, results);
+    return launch_status();
+}
+
+int hv_compute_centroids(const uint8_t* states, int64_t batch, int32_t* centroids, void* stream) {
+    if (batch < 0 || (batch && (!states || !centroids))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    int grid = 0;
+    int rc = grid_for(k_actions, batch, 0, &grid);
+    if (rc) return rc;
+    k_actions<<<grid, kThreads, 0, (cudaStream_t)stream>>>(states, nullptr, nullptr, batch, nullptr,
+                                                            centroids);
+    return launch_status();
+}
+
+int hv_legal_moves_to_actions(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                              int64_t batch, int32_t* actions, void* stream) {
+    if (batch < 0 || (batch && (!states || !moves || !num_legal || !actions))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    int grid = 0;
+    int rc = grid_for(k_actions, batch, 0, &grid);
+    if (rc) return rc;
+    k_actions<<<grid, kThreads, 0, (cudaStream_t)stream>>>(states, moves, num_legal, batch, actions,
+                                                            nullptr);
+    return launch_status();
+}
+
+int hv_generate_positions(uint64_t seed, int64_t first_game, int64_t count, int max_ply,
+                          int expansion_mask, uint8_t* states, void* stream) {
+    if (count < 0 || max_ply < 0 || (count && (!states || !aligned16(states)))) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_playouts, count, smem, &grid);
+    if (rc) return rc;
+    k_playouts<<<grid, kThreads, smem, (cudaStream_t)stream>>>(seed, first_game, count, max_ply,
+                                                                expansion_mask & 7, states);
+    return launch_status();
+}
+
+}  // extern "C"

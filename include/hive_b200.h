@@ -1,0 +1,107 @@
+/*
+ * hive_b200.h -- C ABI of the B200-native Hive self-play hot path.
+ *
+ * Plain pointers and sizes only.  Every pointer argument named states /
+ * moves / features / ... is DEVICE memory on the current CUDA device; the
+ * library never allocates behind the caller's back.  `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Every entry
+ * point returns an hv_status; kernels are launched asynchronously on
+ * `stream`, and device-side conditions are accumulated in a sticky error
+ * word read by hv_get_error().
+ *
+ * Byte formats at the boundary are the reference's (chrismejias/hive_neuralnet):
+ *   state  3424-byte HiveState   hive_gpu/csrc/hive_state.cuh:239-269
+ *   move   6-byte GPUMove        hive_gpu/csrc/hive_state.cuh:228-233
+ *   moves  [B, 256, 6] uint8, zero padded after num_legal[b]
+ *   features [B, 122] float32    hive_gpu/csrc/fnn_features.cuh:21-38
+ *
+ * Each entry point below names the reference operator it replaces
+ * (hive_gpu/csrc/bindings.cpp and the host wrapper in
+ * hive_gpu/csrc/game_logic.cu).  Buffers for states and move lists must be
+ * 16-byte aligned (torch allocations are).
+ */
+#ifndef HIVE_B200_H
+#define HIVE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HV_ABI_VERSION 1
+
+enum hv_status {
+    HV_OK = 0,
+    HV_EINVAL = 1,      /* null / misaligned pointer, negative size */
+    HV_ECUDA = 2,       /* CUDA runtime or launch error */
+    HV_ENOMEM_TREE = 3, /* MCTS node pool exhausted */
+    HV_ETIMEOUT = 4,    /* a bounded device wait gave up */
+    HV_EDEVICE = 5      /* device error word set */
+};
+
+int hv_version(void);
+const char* hv_status_string(int status);
+
+/* Read (and optionally clear) the sticky device error word of the current
+ * device.  Synchronous: call it between steps, not inside a hot loop. */
+int hv_get_error(uint32_t* out, int clear);
+
+/* create_initial_states(batch_size, expansion_mask)
+ * replaces bindings.cpp:264-266 / game_logic.cu:413-428.
+ * states: [batch, 3424] uint8 (written). */
+int hv_create_initial_states(uint8_t* states, int64_t batch, int expansion_mask, void* stream);
+
+/* generate_legal_moves_batch(states, batch_size)
+ * replaces bindings.cpp:268-270 / game_logic.cu:436-459. */
+int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves,
+                            int32_t* num_legal, void* stream);
+
+/* generate_legal_moves_and_fnn_features_batch(states, batch_size)
+ * replaces bindings.cpp:335-338 / game_logic.cu:1440-1464. */
+int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
+                                             int32_t* num_legal, float* features, void* stream);
+
+/* extract_fnn_features_batch(states, legal_moves, num_legal, batch_size)
+ * replaces bindings.cpp:330-333 / game_logic.cu:1409-1431. */
+int hv_extract_fnn_features(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                            int64_t batch, float* features, void* stream);
+
+/* fnn_successor_features_batch(states, legal_moves, action_to_root,
+ * move_indices, num_actions) replaces bindings.cpp:371-376 /
+ * game_logic.cu:1648-1671.  features: [num_actions, 122] float32.
+ * num_states bounds action_to_root; an out-of-range (root, move) pair gets a
+ * zero row and sets the device error word instead of reading out of bounds. */
+int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const uint8_t* legal_moves,
+                              const int64_t* action_to_root, const int64_t* move_indices,
+                              int64_t num_actions, float* features, void* stream);
+
+/* apply_moves_batch(states, moves, batch_size)
+ * replaces bindings.cpp:272-274 / game_logic.cu:465-477.  moves: [batch, 6]. */
+int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream);
+
+/* check_results_batch(states, batch_size)
+ * replaces bindings.cpp:276-278 / game_logic.cu:483-497. */
+int hv_check_results(const uint8_t* states, int64_t batch, int32_t* results, void* stream);
+
+/* compute_centroids_batch(states, batch_size)
+ * replaces bindings.cpp:302-304 / game_logic.cu:910-926.  centroids: [batch, 2]. */
+int hv_compute_centroids(const uint8_t* states, int64_t batch, int32_t* centroids, void* stream);
+
+/* legal_moves_to_actions_batch(states, legal_moves, num_legal, batch_size)
+ * replaces bindings.cpp:306-309 / game_logic.cu:837-857.  actions: [batch, 256]. */
+int hv_legal_moves_to_actions(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                              int64_t batch, int32_t* actions, void* stream);
+
+/* Seeded uniform random legal playouts: game g of the batch is game
+ * first_game + g; stop ply U[0, max_ply]; at each ply the move index is a
+ * counter-based splitmix64 draw modulo num_legal.  Benchmark/test inputs in
+ * the spirit of hive_gpu/endgame_generator.py:284-289 (random playouts). */
+int hv_generate_positions(uint64_t seed, int64_t first_game, int64_t count, int max_ply,
+                          int expansion_mask, uint8_t* states, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HIVE_B200_H */
