@@ -1,0 +1,370 @@
+"""Benchmark: batched legal move generation + FNN feature encoding on B200.
+
+Workload: 262,144 positions per GPU from the seeded
+random-playout generator with all expansions (mosquito, ladybug, pillbug)
+and stop ply U[0, 120]; one step = one pass of
+``generate_legal_moves_and_fnn_features_batch`` over the whole batch
+(moves [P,256,6] u8, num_legal [P] i32, features [P,122] f32).  Inputs
+(898 MB per GPU) are larger than L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs one process per GPU under torch.distributed (weak scaling: every
+rank owns its own 262,144 games, no data-path collective); timing is the
+max over ranks of CUDA-event time.  ``--impl reference`` times the
+reference's own CPU implementation (its hive_gpu/csrc headers compiled on
+the host, oracle/_ref) on all host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "movegen+encode positions/sec"
+UNIT = "positions/s"
+POSITIONS = 262144
+MAX_PLY = 120
+EXPANSIONS = 7
+SEED = 20260101
+STATE_BYTES = 3424
+MOVE_BYTES = 6
+MAX_MOVES = 256
+FEAT = 122
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "config2: movegen+FNN-encode, 262144 positions/GPU, all expansions, ply U[0,120]",
+        "positions_per_gpu": POSITIONS,
+        "global_positions": POSITIONS * n_gpus,
+        "expansion_mask": EXPANSIONS,
+        "max_ply": MAX_PLY,
+        "seed": SEED,
+        "parallelism": f"games sharded dp{n_gpus}" if n_gpus > 1 else "single GPU",
+        "l2": "inputs (898 MB/GPU) larger than the 126 MB L2; no flush",
+    }
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# --------------------------------------------------------------------------
+# CPU legs (reference build of the reference headers, or the C oracle)
+# --------------------------------------------------------------------------
+def _cpu_lib():
+    from oracle import oracle as O
+    if not O.ref_available() and os.path.isdir("/root/reference/hive_gpu/csrc"):
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref"], check=False)
+    if O.ref_available():
+        return O.ref(), "reference"
+    if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "liboracle.so"], check=True)
+    return O.oracle(), "port"
+
+
+def cpu_rate(states_np, threads: int, target_s: float = 12.0):
+    """positions/s of the CPU implementation over a bounded sample."""
+    lib, kind = _cpu_lib()
+    probe = states_np[:2048]
+    t0 = time.perf_counter()
+    lib.legal_moves_features(probe, threads)
+    dt = max(time.perf_counter() - t0, 1e-6)
+    est = len(probe) / dt
+    n = int(min(len(states_np), max(4096, est * target_s)))
+    sample = states_np[:n]
+    t0 = time.perf_counter()
+    lib.legal_moves_features(sample, threads)
+    dt = time.perf_counter() - t0
+    return n / dt, kind, n, dt
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+
+        def mhz(s):
+            try:
+                return float(s.split()[0])
+            except Exception:
+                return None
+
+        sm = [mhz(r[1]) for r in rows if mhz(r[1]) is not None]
+        mx = [mhz(r[2]) for r in rows if mhz(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# roofline helpers
+# --------------------------------------------------------------------------
+def measured_peak_gbs():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic_per_position():
+    """DRAM bytes per position of the movegen kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "movegen_features_config2.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_position:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except Exception:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------------
+# reference arm
+# --------------------------------------------------------------------------
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lib, kind = _cpu_lib()
+    cores = host_cores()
+    # the same generator recipe, run by the CPU implementation itself
+    sample_n = 16384
+    states = lib.generate_positions(SEED, 0, sample_n, MAX_PLY, EXPANSIONS, cores)
+    rates = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        lib.legal_moves_features(states, cores)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            rates.append((sample_n, dt))
+    total_n = sum(n for n, _ in rates)
+    total_t = sum(t for _, t in rates)
+    value = total_n / total_t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_t / len(rates),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic", "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"{sample_n} positions of the workload per step, {cpu_model()}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# B200 arm
+# --------------------------------------------------------------------------
+def run_gpu(args) -> None:
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from hive_neuralnet_b200.hive_gpu import load_extension
+    ext = load_extension()
+    P = POSITIONS
+    states = ext.generate_positions(SEED, rank * P, P, MAX_PLY, EXPANSIONS, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+
+    # ---- device-resident throughput ----
+    for _ in range(args.warmup):
+        out = ext.generate_legal_moves_and_fnn_features_batch(states, P)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = ext.generate_legal_moves_and_fnn_features_batch(states, P)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * P * args.steps / (ms_max / 1e3)
+    mean_legal = float(out[1].float().mean().item())
+
+    # ---- end to end through the public API with host buffers ----
+    host_states = torch.empty((P, STATE_BYTES), dtype=torch.uint8, pin_memory=True)
+    host_states.copy_(states)
+    h_moves = torch.empty((P, MAX_MOVES, MOVE_BYTES), dtype=torch.uint8, pin_memory=True)
+    h_nl = torch.empty((P,), dtype=torch.int32, pin_memory=True)
+    h_feat = torch.empty((P, FEAT), dtype=torch.float32, pin_memory=True)
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        d_states = host_states.to(dev, non_blocking=True)
+        m, nl, f = ext.generate_legal_moves_and_fnn_features_batch(d_states, P)
+        h_moves.copy_(m, non_blocking=True)
+        h_nl.copy_(nl, non_blocking=True)
+        h_feat.copy_(f, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t2 = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = world * P * e2e_steps / (float(t2.item()) / 1e3)
+    h2d = P * STATE_BYTES
+    d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
+
+    # ---- roofline: algorithmic bytes per launch / average launch time ----
+    peak, peak_kind = measured_peak_gbs()
+    launch_s = (ms / args.steps) / 1e3
+    alg_bytes = P * (STATE_BYTES + 4 + FEAT * 4 + MOVE_BYTES * mean_legal)
+    achieved = alg_bytes / launch_s / 1e9
+    tpp = profiled_traffic_per_position()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": peak_kind,
+                "traffic": (tpp * P) if tpp else None,
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "kernel": "k_root<gen,moves,features> (movegen+FNN features)"}
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            sample = states[:65536].cpu().numpy()
+            cores = host_cores()
+            rate, kind, n, dt = cpu_rate(sample, cores)
+            cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": kind,
+                   "sample": f"first {n} positions of the workload ({dt:.1f} s), {cpu_model()}"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": workload_config(world),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": args.steps,
+            "mean_legal_moves": mean_legal,
+        }
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    global POSITIONS
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--positions", type=int, default=POSITIONS,
+                    help="positions per GPU (profiling runs use a smaller case)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    POSITIONS = args.positions
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

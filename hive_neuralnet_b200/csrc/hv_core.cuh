@@ -2,24 +2,24 @@
 //
 // One warp owns one position.  The 3424-byte HiveState (the boundary format
 // of the reference, hive_gpu/csrc/hive_state.cuh:239-269) is staged in the
-// warp's shared-memory slot; everything else is derived from it:
+// warp's shared-memory slot; everything else is derived from it.
 //
-//   * row bitboards: lane r (r < 23) holds the 23-bit occupancy mask of grid
-//     row r, so a hex-direction shift of a whole 529-cell board is one
-//     shuffle plus one shift (hv_shift_* below);
+// Internal cell index.  Inside the kernels a cell is p = row * 32 + col
+// (rows and columns 0..22 of the reference's 23x23 grid): one grid row is one
+// 32-bit word, so a neighbour is p + step, a bit test is a shift, and a
+// 529-cell set is 23 words.  The reference's index c = row * 23 + col is used
+// only where bytes cross the boundary (state arrays, move lists):
+// c = p - 9 * (p >> 5).
+//
+//   * row bitboards: lane r (r < 23) holds the occupancy word of grid row r,
+//     so a hex-direction shift of the whole board is one shuffle plus one
+//     shift;
 //   * piece lanes: lane i (i < N <= 28) owns the i-th occupied cell in
 //     ascending cell order (the reference's iteration order);
-//   * slide masks sl[d]: the set of cells that can slide one step in
-//     direction d (destination empty, exactly one flank occupied), built for
-//     the whole board with row-bitboard algebra, so each freedom-to-move test
-//     of the reference (move_gen.cuh:82-131) becomes one shared-memory bit
-//     test.
-//
-// Move generators are warp-cooperative: one lane per direction (queen,
-// grasshopper, beetle, throws), one lane per (queue item, direction) for the
-// ant breadth-first search, and one lane per (path, direction) for the
-// three-step spider/ladybug walks, with __match_any_sync/__ballot_sync
-// reproducing the reference's first-seen emission order exactly.
+//   * slide masks sl[d]: the cells that can slide one step in direction d
+//     (destination empty, exactly one flank occupied), built for the whole
+//     board with row-bitboard algebra, so each freedom-to-move test of the
+//     reference (move_gen.cuh:82-131) becomes one shared-memory bit test.
 #pragma once
 
 #include <cstdint>
@@ -28,6 +28,7 @@ namespace hv {
 
 constexpr int kBoard = 23;
 constexpr int kCells = 529;
+constexpr int kPCells = kBoard * 32;  // padded index space
 constexpr int kMaxMoves = 256;
 constexpr int kFeat = 122;
 constexpr int kStateBytes = 3424;
@@ -45,30 +46,37 @@ constexpr int kOffStun = 3416;
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint32_t kRowBits = 0x7fffffu;
 
-// Error bits reported through the per-launch status word.
+// The move generators are called from several places (full list, compact
+// list, mosquito union); keeping one out-of-line copy of each keeps the
+// kernel's instruction footprint small.
+#ifndef HV_GEN_INLINE
+#define HV_GEN_INLINE __noinline__
+#endif
+
+// Error bits reported through the device error word.
 constexpr uint32_t kErrBuffer = 1u;  // a generator list exceeded its buffer
 constexpr uint32_t kErrIndex = 2u;   // a root / move index was out of range
 
 struct __align__(16) WarpSmem {
     uint8_t st[kStateBytes];     // staged HiveState
     uint16_t mv[kMaxMoves * 3];  // move list: (type | pt << 8, from, to) per move
-    uint32_t occ[24];            // occupied row masks
+    uint32_t occ[24];            // occupied row words
+    uint32_t own[24];            // side-to-move top-piece row words
     uint32_t sl[6][24];          // slide masks of the position
     uint32_t slx[6][24];         // slide masks with the current mover lifted
-    uint32_t seen[18];           // 529-bit scratch set
-    uint32_t prow[24];           // placement row masks
+    uint32_t seen[24];           // scratch cell set
+    uint32_t prow[24];           // placement row words
     uint32_t adj[32];            // piece adjacency (piece-index space)
     uint16_t pcell[32];          // cell of piece i
-    uint32_t own[24];            // side-to-move top-piece row masks
     uint16_t pref[24];           // piece index of the first occupied cell of row r
     uint16_t ppref[24];          // placement index of the first placement cell of row r
     uint8_t pflag[32];           // bit0: pinned
     uint16_t dst[128];           // destination list of the running generator
     uint16_t tmp[128];           // sub-generator list (mosquito)
-    uint16_t l2a[40];            // three-step walks: level-2 (p1)
-    uint16_t l2b[40];            //                   level-2 (p2)
+    uint16_t qcell[48];          // walk queue (spider / ladybug paths): cell
+    uint16_t qanc[48];           //                                      previous cell
     int acc[112];                // feature accumulators
-    uint32_t bm[16 * 17 + 18];   // per (type, owner) source-cell sets + placement set
+    uint32_t bm[16 * 17 + 24];   // per (type, owner) source-cell sets + placement set
 };
 
 // ---------------------------------------------------------------------------
@@ -83,29 +91,31 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
     return m;
 }
 
-// direction order E, NE, NW, W, SW, SE (hex_grid.cuh:41-49); packed (d+1) in 2 bits
-__device__ __forceinline__ int dcol(int d) { return ((1050 >> (2 * d)) & 3) - 1; }
-__device__ __forceinline__ int drow(int d) { return ((2625 >> (2 * d)) & 3) - 1; }
+__device__ __forceinline__ int p_to_c(int p) { return p - 9 * (p >> 5); }
+__device__ __forceinline__ int c_to_p(int c) { return c + 9 * (c / kBoard); }
+
+// direction order E, NE, NW, W, SW, SE (hex_grid.cuh:41-49) as p-steps
+// +1, -31, -32, -1, +31, +32, packed (step + 32) in 7 bits each
+constexpr unsigned long long kDirPack =
+    33ull | (1ull << 7) | (0ull << 14) | (31ull << 21) | (63ull << 28) | (64ull << 35);
+__device__ __forceinline__ int dstep(int d) { return (int)((kDirPack >> (7 * d)) & 127ull) - 32; }
 __device__ __forceinline__ int cw_dir(int d) { return d == 0 ? 5 : d - 1; }
 __device__ __forceinline__ int ccw_dir(int d) { return d == 5 ? 0 : d + 1; }
 __device__ __forceinline__ int opp_dir(int d) { return d < 3 ? d + 3 : d - 3; }
 
-__device__ __forceinline__ int nbr(int c, int d) {
-    int r = c / kBoard, q = c - r * kBoard;
-    int r2 = r + drow(d), q2 = q + dcol(d);
-    return ((unsigned)r2 < (unsigned)kBoard && (unsigned)q2 < (unsigned)kBoard) ? r2 * kBoard + q2
-                                                                                : -1;
+// neighbour of p in direction d, -1 off the grid
+__device__ __forceinline__ int nbr(int p, int d) {
+    int q = p + dstep(d);
+    return ((unsigned)q < (unsigned)kPCells && (q & 31) < kBoard) ? q : -1;
 }
 
-__device__ __forceinline__ int rowbit(const uint32_t* rows, int c) {
-    int r = c / kBoard;
-    return (int)((rows[r] >> (c - r * kBoard)) & 1u);
+__device__ __forceinline__ int rowbit(const uint32_t* rows, int p) {
+    return (int)((rows[p >> 5] >> (p & 31)) & 1u);
 }
 
+// hex distance (fnn_features.cuh:45-60) on (row, col) of p-space indices
 __device__ __forceinline__ int hex_distance(int a, int b) {
-    int ra = a / kBoard, qa = a - ra * kBoard;
-    int rb = b / kBoard, qb = b - rb * kBoard;
-    int dq = qb - qa, dr = rb - ra, ds = -(dq + dr);
+    int dq = (b & 31) - (a & 31), dr = (b >> 5) - (a >> 5), ds = -(dq + dr);
     dq = dq < 0 ? -dq : dq;
     dr = dr < 0 ? -dr : dr;
     ds = ds < 0 ? -ds : ds;
@@ -119,40 +129,37 @@ __device__ __forceinline__ int hex_distance(int a, int b) {
 
 struct Pos {
     WarpSmem* w;
-    __device__ __forceinline__ int height(int c) const { return c >= 0 ? w->st[kOffHeight + c] : 0; }
+    __device__ __forceinline__ int height(int p) const { return p >= 0 ? w->st[kOffHeight + p_to_c(p)] : 0; }
     // top piece byte; a corrupt height above the stack limit reads level 5
-    __device__ __forceinline__ int top(int c) const {
-        int h = height(c);
+    __device__ __forceinline__ int top(int p) const {
+        int h = height(p);
         h = h > 5 ? 5 : h;
-        return h ? w->st[(h - 1) * kCells + c] : 0;
+        return h ? w->st[(h - 1) * kCells + p_to_c(p)] : 0;
     }
-    __device__ __forceinline__ bool occupied(int c) const { return c >= 0 && rowbit(w->occ, c); }
+    __device__ __forceinline__ bool occupied(int p) const { return p >= 0 && rowbit(w->occ, p); }
     __device__ __forceinline__ int turn() const {
         return w->st[kOffTurn] | (w->st[kOffTurn + 1] << 8);
     }
-    __device__ __forceinline__ int stunned() const {
-        return w->st[kOffStun] | (w->st[kOffStun + 1] << 8);
+    // reference-index field -> p-space (-1 for the 0xFFFF "none" marker)
+    __device__ __forceinline__ int cell_field(int off) const {
+        int c = w->st[off] | (w->st[off + 1] << 8);
+        return c == 0xFFFF ? -1 : c_to_p(c);
     }
-    __device__ __forceinline__ int queen_cell(int c) const {
-        return w->st[kOffQCell + 2 * c] | (w->st[kOffQCell + 2 * c + 1] << 8);
-    }
+    __device__ __forceinline__ int stunned() const { return cell_field(kOffStun); }
+    __device__ __forceinline__ int queen_cell(int color) const { return cell_field(kOffQCell + 2 * color); }
     __device__ __forceinline__ int hand(int color, int t) const {
         return w->st[kOffHands + color * 8 + t];
     }
     __device__ __forceinline__ int result() const { return w->st[kOffResult]; }
     __device__ __forceinline__ int queen_placed() const { return w->st[kOffQPlaced]; }
-    __device__ __forceinline__ bool is_stunned(int c) const {
-        int s = stunned();
-        return s != 0xFFFF && s == c;
-    }
     // piece index of an occupied cell
-    __device__ __forceinline__ int pidx(int c) const {
-        int r = c / kBoard, q = c - r * kBoard;
-        return w->pref[r] + __popc(w->occ[r] & ((1u << q) - 1u));
+    __device__ __forceinline__ int pidx(int p) const {
+        int r = p >> 5;
+        return w->pref[r] + __popc(w->occ[r] & ((1u << (p & 31)) - 1u));
     }
     // elevated gate (move_gen.cuh:659-667): both flanks strictly higher than h
-    __device__ __forceinline__ bool gate_blocked(int c, int d, int h) const {
-        return height(nbr(c, cw_dir(d))) > h && height(nbr(c, ccw_dir(d))) > h;
+    __device__ __forceinline__ bool gate_blocked(int p, int d, int h) const {
+        return height(nbr(p, cw_dir(d))) > h && height(nbr(p, ccw_dir(d))) > h;
     }
 };
 
@@ -187,7 +194,7 @@ __device__ __forceinline__ uint32_t dilate(uint32_t x) {
 }
 
 // Slide masks for occupancy x (freedom to move, move_gen.cuh:82-118):
-// sl[d] = {c : nb(c,d) on grid and empty, occ(nb(c,cw d)) xor occ(nb(c,ccw d))}
+// sl[d] = {p : nb(p,d) on grid and empty, occ(nb(p,cw d)) xor occ(nb(p,ccw d))}
 __device__ __forceinline__ void build_slide_masks(uint32_t x, uint32_t (*sl)[24]) {
     uint32_t nx[6], ne[6];
     uint32_t m = row_valid_mask();
@@ -214,13 +221,13 @@ __device__ __forceinline__ int warp_excl_scan(int v) {
 // k-th set cell (k < total) of a row-bitboard stored in smem with row prefix
 __device__ __forceinline__ int kth_cell(const uint32_t* rows, const uint16_t* pre, int k) {
     int lo = 0, hi = kBoard - 1;  // largest r with pre[r] <= k
+#pragma unroll 1
     while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
         if (pre[mid] <= k) lo = mid;
         else hi = mid - 1;
     }
-    int q = __fns(rows[lo], 0, k - pre[lo] + 1);
-    return lo * kBoard + q;
+    return (lo << 5) + __fns(rows[lo], 0, k - pre[lo] + 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -230,7 +237,7 @@ __device__ __forceinline__ int kth_cell(const uint32_t* rows, const uint16_t* pr
 struct Setup {
     int n;          // occupied cells (<= 28 used, as the reference's MAX_PIECES)
     int color;      // side to move
-    int my_cell;    // piece lane: cell (or -1)
+    int my_cell;    // piece lane: cell p (or -1)
     int my_h;       // piece lane: stack height
     int my_top;     // piece lane: top byte
     bool my_ap;     // piece lane: articulation point
@@ -239,6 +246,7 @@ struct Setup {
     uint32_t occ;   // row lane: occupancy
 };
 
+// row r of a reference bitboard (bits c = 23r .. 23r+22) as a 23-bit word
 __device__ __forceinline__ uint32_t load_row(const uint8_t* st, int off, int lane) {
     if (lane >= kBoard) return 0u;
     const uint32_t* w32 = reinterpret_cast<const uint32_t*>(st + off);
@@ -270,10 +278,11 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
     {
         uint32_t bits = S.occ;
         int k = pre;
+#pragma unroll 1
         while (bits) {
             int q = __ffs(bits) - 1;
             bits &= bits - 1;
-            if (k < 32) w->pcell[k] = (uint16_t)(l * kBoard + q);
+            if (k < 32) w->pcell[k] = (uint16_t)((l << 5) + q);
             k++;
         }
     }
@@ -286,7 +295,7 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
     // adjacency in piece-index space
     uint32_t adj = 0;
     if (S.my_cell >= 0) {
-#pragma unroll
+#pragma unroll 1
         for (int d = 0; d < 6; d++) {
             int nb = nbr(S.my_cell, d);
             if (nb >= 0 && rowbit(w->occ, nb)) {
@@ -314,6 +323,7 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
     if (active && start >= 0) {
         seen = 1u << start;
         uint32_t fr = seen;
+#pragma unroll 1
         while (fr) {
             int v = __ffs(fr) - 1;
             fr &= fr - 1;
@@ -328,7 +338,7 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
         uint32_t rest = comp & ~(1u << l);
         S.my_ap = (l == 0) ? (adj0 != 0 && seen != rest) : (seen != rest);
     }
-    if (l < 32) w->pflag[l] = (S.my_ap && S.my_h == 1) ? 1 : 0;
+    w->pflag[l] = (S.my_ap && S.my_h == 1) ? 1 : 0;
     __syncwarp();
     return S;
 }

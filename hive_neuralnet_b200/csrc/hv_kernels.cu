@@ -19,6 +19,9 @@
 
 namespace hv {
 
+#ifndef HV_MIN_BLOCKS
+#define HV_MIN_BLOCKS 3  // resident blocks per SM the register budget is sized for
+#endif
 constexpr int kWarpsPerBlock = 8;
 constexpr int kThreads = kWarpsPerBlock * 32;
 
@@ -55,7 +58,7 @@ __device__ __forceinline__ void store_moves(const WarpSmem* w, uint8_t* dst) {
 //  fnn_features.cuh:334-350 extract_fnn_features_kernel)
 // ---------------------------------------------------------------------------
 template <bool GEN, bool WRITE_MOVES, bool FEATS>
-__global__ void __launch_bounds__(kThreads) k_root(const uint8_t* __restrict__ states,
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t* __restrict__ states,
                                                    const uint8_t* __restrict__ moves_in,
                                                    const int32_t* __restrict__ nl_in, int64_t batch,
                                                    uint8_t* __restrict__ moves_out,
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) k_root(const uint8_t* __restrict__ s
 // successor features: apply one root move, compact list, features
 // (game_logic.cu:182-229 fnn_successor_features_kernel)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads) k_successor_features(
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
     const int64_t* __restrict__ action_to_root, const int64_t* __restrict__ move_indices,
     int64_t num_actions, float* __restrict__ feats_out) {

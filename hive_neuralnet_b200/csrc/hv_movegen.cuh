@@ -7,228 +7,172 @@
 //   features       hive_gpu/csrc/fnn_features.cuh:68-331
 // including its emission order, duplicates (throws vs. ordinary moves),
 // truncation at 256 moves, 32-destination caps for spider/ladybug and the
-// 128-destination cap of a mosquito's union.
+// 128-destination cap of a mosquito's union.  Cells are p-space (see
+// hv_core.cuh) internally; move lists hold the reference's cell index.
+//
+// All piece movements run through one warp-cooperative walk engine (walk()),
+// so the kernel carries a single copy of the generator loop: its instruction
+// footprint is what bounds this code on the SM, not arithmetic.
 #pragma once
 
 #include "hv_core.cuh"
 
 namespace hv {
 
-__device__ __forceinline__ void put_move(WarpSmem* w, int m, int type, int pt, int from, int to) {
+// move list entry in reference cell indices
+__device__ __forceinline__ void put_move(WarpSmem* w, int m, int type, int pt, int from_c, int to_c) {
     w->mv[3 * m] = (uint16_t)(type | (pt << 8));
-    w->mv[3 * m + 1] = (uint16_t)from;
-    w->mv[3 * m + 2] = (uint16_t)to;
+    w->mv[3 * m + 1] = (uint16_t)from_c;
+    w->mv[3 * m + 2] = (uint16_t)to_c;
 }
 
-__device__ __forceinline__ bool set_has(const uint32_t* s, int c) { return (s[c >> 5] >> (c & 31)) & 1u; }
-__device__ __forceinline__ void set_add(uint32_t* s, int c) { atomicOr(&s[c >> 5], 1u << (c & 31)); }
+__device__ __forceinline__ bool set_has(const uint32_t* s, int p) { return (s[p >> 5] >> (p & 31)) & 1u; }
+__device__ __forceinline__ void set_add(uint32_t* s, int p) { atomicOr(&s[p >> 5], 1u << (p & 31)); }
 __device__ __forceinline__ void set_clear(uint32_t* s) {
-    if (lane_id() < 18) s[lane_id()] = 0u;
+    if (lane_id() < 24) s[lane_id()] = 0u;
     __syncwarp();
 }
 
 // occupancy minus one cell -> slx (the mover is lifted off the board)
 __device__ __forceinline__ void lift_mover(WarpSmem* w, uint32_t occ_row, int cell) {
-    int l = lane_id();
-    int r = cell / kBoard;
     uint32_t x = occ_row;
-    if (l == r) x &= ~(1u << (cell - r * kBoard));
+    if (lane_id() == (cell >> 5)) x &= ~(1u << (cell & 31));
     build_slide_masks(x, w->slx);
     __syncwarp();
 }
 
-// one-step slide in the six directions (queen / pillbug), move_gen.cuh:202-212
-__device__ __forceinline__ int gen_step1(WarpSmem* w, int cell, uint16_t* out, bool first_only) {
-    int l = lane_id();
-    bool ok = l < 6 && rowbit(w->sl[l], cell);
-    uint32_t b = __ballot_sync(kFull, ok);
-    if (first_only) return b ? 1 : 0;
-    if (ok) out[__popc(b & lanemask_lt())] = (uint16_t)nbr(cell, l);
-    __syncwarp();
-    return __popc(b);
-}
+// ---------------------------------------------------------------------------
+// walk engine
+// ---------------------------------------------------------------------------
+enum WalkMode : int {
+    WM_STEP = 0,    // queen / pillbug one-step slide      move_gen.cuh:202-219, 644-651
+    WM_BEETLE = 1,  // beetle: elevated gate or slide       move_gen.cuh:468-524
+    WM_HOP = 2,     // grasshopper jump                     move_gen.cuh:228-257
+    WM_ANT = 3,     // ant breadth-first search             move_gen.cuh:267-388
+    WM_SPIDER = 4,  // exactly three slides, no revisits    move_gen.cuh:397-454
+    WM_LADY = 5,    // up, across, down                     move_gen.cuh:538-637
+};
 
-// grasshopper jumps, move_gen.cuh:228-257
-__device__ __forceinline__ int gen_hopper(WarpSmem* w, int cell, uint16_t* out, bool first_only) {
+// Destinations of the piece at `cell` moving as `mode`, in the reference's
+// emission order, into out (at most cap).  Lanes take (queue item, direction)
+// pairs, five items per round: the queue holds the ant's reached cells (the
+// output list itself, as in the reference) or the spider/ladybug partial
+// paths (level-1 then level-2 cells, i.e. lexicographic (d1, d2) order).  A
+// destination reached by several lanes in one round is kept by the lowest
+// lane, which reproduces the reference's sequential first-seen order.
+// first_only: return 1 as soon as one destination exists (has_*_move).
+// Ant and spider need slx built for this cell.
+__device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out, int cap,
+                                 bool first_only) {
     Pos P{w};
-    int l = lane_id();
-    bool ok = false;
-    int p = -1;
-    if (l < 6) {
-        p = nbr(cell, l);
-        if (p >= 0 && P.occupied(p)) {
-            while (p >= 0 && P.occupied(p)) p = nbr(p, l);
-            ok = p >= 0;
-        }
-    }
-    uint32_t b = __ballot_sync(kFull, ok);
-    if (first_only) return b ? 1 : 0;
-    if (ok) out[__popc(b & lanemask_lt())] = (uint16_t)p;
-    __syncwarp();
-    return __popc(b);
-}
-
-// beetle: elevated gate or ground slide, move_gen.cuh:468-524
-__device__ __forceinline__ int gen_beetle(WarpSmem* w, int cell, uint16_t* out, bool first_only) {
-    Pos P{w};
-    int l = lane_id();
-    bool ok = false;
-    int dest = -1;
-    if (l < 6) {
-        dest = nbr(cell, l);
-        if (dest >= 0) {
-            int below = P.height(cell) - 1;
-            int hd = P.height(dest);
-            int mh = hd > below ? hd : below;
-            ok = mh > 0 ? !P.gate_blocked(cell, l, mh) : (bool)rowbit(w->sl[l], cell);
-        }
-    }
-    uint32_t b = __ballot_sync(kFull, ok);
-    if (first_only) return b ? 1 : 0;
-    if (ok) out[__popc(b & lanemask_lt())] = (uint16_t)dest;
-    __syncwarp();
-    return __popc(b);
-}
-
-// Ant breadth-first search over slide steps with the ant lifted (slx).
-// Lanes take (queue item, direction) pairs, five items per round; the
-// lowest lane wins a shared destination, which is exactly the reference's
-// sequential first-seen order (move_gen.cuh:267-313, 348-388).
-// out doubles as the queue; at most cap (<= 128) entries.
-__device__ __forceinline__ int gen_ant(WarpSmem* w, int cell, uint16_t* out, int cap,
-                                       bool first_only) {
-    int l = lane_id();
-    if (first_only) {
-        bool ok = l < 6 && rowbit(w->slx[l], cell);
-        return __ballot_sync(kFull, ok) ? 1 : 0;
-    }
-    if (cap <= 0) return 0;
+    const int l = lane_id();
+    const uint32_t lt = lanemask_lt();
+    const int k = l / 6, d = l - 6 * (l / 6);  // lanes 30, 31 idle (k == 5)
+    uint16_t* Q = mode == WM_ANT ? out : w->qcell;
+    const int hcell = P.height(cell);
     set_clear(w->seen);
-    if (l == 0) set_add(w->seen, cell);
+    if (mode == WM_ANT && l == 0) set_add(w->seen, cell);
     __syncwarp();
-    int rd = 0, wr = 0;
+    int rd = 0, wr = 0, cnt = 0, l2start = 0;
     bool seed = true;
-    const uint32_t lt = lanemask_lt();
-    const int k = l / 6, d = l - (l / 6) * 6;
-    while (seed || (rd < wr && wr < cap)) {
-        int items = seed ? 1 : min(5, wr - rd);
-        bool ok = false;
-        int dest = -1;
+#pragma unroll 1
+    while (true) {
+        int items = 1;
+        if (!seed) {
+            if (rd >= wr || (mode == WM_ANT && wr >= cap)) break;
+            items = min(5, wr - rd);
+        }
+        int dest = -1, cur = cell;
+        bool fin = false, app = false;
         if (k < items) {
-            int cur = seed ? cell : (int)out[rd + k];
-            if (rowbit(w->slx[d], cur)) {
-                dest = nbr(cur, d);
-                ok = !set_has(w->seen, dest);
+            int lev = 0, anc = cell;
+            if (!seed) {
+                cur = Q[rd + k];
+                lev = (mode == WM_ANT || rd + k < l2start) ? 1 : 2;
+                if (lev == 2) anc = w->qanc[rd + k];
             }
-        }
-        uint32_t mm = __match_any_sync(kFull, ok ? dest : -1 - l);
-        bool keep = ok && ((mm & lt) == 0u);
-        uint32_t b = __ballot_sync(kFull, keep);
-        int pos = wr + __popc(b & lt);
-        if (keep && pos < cap) {
-            out[pos] = (uint16_t)dest;
-            set_add(w->seen, dest);
-        }
-        wr = min(cap, wr + __popc(b));
-        if (!seed) rd += items;
-        seed = false;
-        __syncwarp();
-    }
-    return wr;
-}
-
-// Three-step walks: spider (three slides, no revisits, move_gen.cuh:397-454)
-// and ladybug (up, across, down, move_gen.cuh:538-637).  Candidates are
-// enumerated level by level in (d1, d2, d3) lexicographic order, 32 per
-// round; duplicates keep their first occurrence; at most 32 destinations.
-template <bool LADY>
-__device__ __noinline__ int gen_walk3(WarpSmem* w, int cell, uint16_t* out, bool first_only) {
-    Pos P{w};
-    int l = lane_id();
-    const uint32_t lt = lanemask_lt();
-    bool v1 = false;
-    int p1 = -1;
-    if (l < 6) {
-        if (!LADY) {
-            v1 = rowbit(w->slx[l], cell);
-            p1 = v1 ? nbr(cell, l) : -1;
-        } else {
-            p1 = nbr(cell, l);
-            if (p1 >= 0 && P.occupied(p1)) {
-                int a = P.height(cell) - 1, b = P.height(p1);
-                v1 = !P.gate_blocked(cell, l, a > b ? a : b);
+            const int nb = nbr(cur, d);
+            switch (mode) {
+                case WM_STEP:
+                    fin = rowbit(w->sl[d], cur);
+                    dest = nb;
+                    break;
+                case WM_BEETLE:
+                    if (nb >= 0) {
+                        int hd = P.height(nb), mh = hd > hcell - 1 ? hd : hcell - 1;
+                        fin = mh > 0 ? !P.gate_blocked(cur, d, mh) : (bool)rowbit(w->sl[d], cur);
+                        dest = nb;
+                    }
+                    break;
+                case WM_HOP:
+                    if (nb >= 0 && P.occupied(nb)) {
+                        int p = nb;
+#pragma unroll 1
+                        while (p >= 0 && P.occupied(p)) p = nbr(p, d);
+                        fin = p >= 0;
+                        dest = p;
+                    }
+                    break;
+                case WM_ANT:
+                    if (rowbit(w->slx[d], cur)) {
+                        dest = nb;
+                        fin = !set_has(w->seen, nb);
+                    }
+                    break;
+                case WM_SPIDER:
+                    if (rowbit(w->slx[d], cur)) {
+                        dest = nb;
+                        if (lev == 0) app = true;
+                        else if (nb != cell && (lev == 1 || nb != anc)) {
+                            app = lev == 1;
+                            fin = lev == 2;
+                        }
+                    }
+                    break;
+                default:  // WM_LADY
+                    if (nb >= 0) {
+                        dest = nb;
+                        int hn = P.height(nb);
+                        bool on = P.occupied(nb);
+                        if (lev == 0) {
+                            app = on && !P.gate_blocked(cur, d, hn > hcell - 1 ? hn : hcell - 1);
+                        } else if (lev == 1) {
+                            int hc = P.height(cur);
+                            app = nb != cell && on && !P.gate_blocked(cur, d, hn > hc ? hn : hc);
+                        } else {
+                            fin = nb != cell && nb != anc && !on &&
+                                  !P.gate_blocked(cur, d, P.height(cur));
+                        }
+                    }
+                    break;
             }
-        }
-    }
-    uint32_t b1 = __ballot_sync(kFull, v1);
-    int c1 = 6 * __popc(b1);
-    int n2 = 0;
-    for (int base = 0; base < c1; base += 32) {
-        int c = base + l;
-        bool in = c < c1;
-        int k1 = c / 6, d2 = c - (c / 6) * 6;
-        int src = in ? __fns(b1, 0, k1 + 1) : 0;
-        int a = __shfl_sync(kFull, p1, src & 31);
-        bool v2 = false;
-        int bcell = -1;
-        if (in) {
-            if (!LADY) {
-                if (rowbit(w->slx[d2], a)) {
-                    bcell = nbr(a, d2);
-                    v2 = bcell != cell && bcell != a;
-                }
-            } else {
-                bcell = nbr(a, d2);
-                if (bcell >= 0 && bcell != cell && P.occupied(bcell)) {
-                    int ha = P.height(a), hb = P.height(bcell);
-                    v2 = !P.gate_blocked(a, d2, ha > hb ? ha : hb);
-                }
-            }
-        }
-        uint32_t b2 = __ballot_sync(kFull, v2);
-        if (v2) {
-            int pos = n2 + __popc(b2 & lt);
-            w->l2a[pos] = (uint16_t)a;
-            w->l2b[pos] = (uint16_t)bcell;
-        }
-        n2 += __popc(b2);
-    }
-    __syncwarp();
-    if (!first_only) set_clear(w->seen);
-    int c3 = 6 * n2, cnt = 0;
-    for (int base = 0; base < c3; base += 32) {
-        int c = base + l;
-        bool v3 = false;
-        int p3 = -1;
-        if (c < c3) {
-            int k2 = c / 6, d3 = c - (c / 6) * 6;
-            int a = w->l2a[k2], bcell = w->l2b[k2];
-            if (!LADY) {
-                if (rowbit(w->slx[d3], bcell)) {
-                    p3 = nbr(bcell, d3);
-                    v3 = p3 != cell && p3 != a && p3 != bcell;
-                }
-            } else {
-                p3 = nbr(bcell, d3);
-                v3 = p3 >= 0 && p3 != cell && p3 != a && !P.occupied(p3) &&
-                     !P.gate_blocked(bcell, d3, P.height(bcell));
-            }
+            if (fin && mode >= WM_SPIDER) fin = !set_has(w->seen, dest);
         }
         if (first_only) {
-            if (__ballot_sync(kFull, v3)) return 1;
-            continue;
+            if (__ballot_sync(kFull, fin)) return 1;
+        } else {
+            uint32_t mm = __match_any_sync(kFull, fin ? dest : -1 - l);
+            bool keep = fin && ((mm & lt) == 0u);
+            uint32_t b = __ballot_sync(kFull, keep);
+            int pos = cnt + __popc(b & lt);
+            if (keep && pos < cap) {
+                out[pos] = (uint16_t)dest;
+                set_add(w->seen, dest);
+            }
+            cnt = min(cap, cnt + __popc(b));
         }
-        bool fresh = v3 && !set_has(w->seen, p3);
-        uint32_t mm = __match_any_sync(kFull, fresh ? p3 : -1 - l);
-        bool keep = fresh && ((mm & lt) == 0u);
-        uint32_t b = __ballot_sync(kFull, keep);
-        int pos = cnt + __popc(b & lt);
-        if (keep && pos < 32) {
-            out[pos] = (uint16_t)p3;
-            set_add(w->seen, p3);
+        uint32_t ba = __ballot_sync(kFull, app);
+        if (app) {
+            int pos = wr + __popc(ba & lt);
+            Q[pos] = (uint16_t)dest;
+            w->qanc[pos] = (uint16_t)cur;
         }
-        cnt = min(32, cnt + __popc(b));
+        wr = mode == WM_ANT ? cnt : wr + __popc(ba);
+        if (seed) l2start = wr;
+        else rd += items;
+        seed = false;
         __syncwarp();
+        if (!first_only && cnt >= cap) break;
     }
     return first_only ? 0 : cnt;
 }
@@ -248,42 +192,39 @@ __device__ __forceinline__ uint32_t neighbour_types(WarpSmem* w, int cell) {
     return __reduce_or_sync(kFull, t);
 }
 
+// walk mode of a piece type (1..8), pillbug moves like the queen
+__device__ __forceinline__ int mode_of(int pt) {
+    // Q A G S B M L P -> STEP ANT HOP SPIDER BEETLE (mosquito) LADY STEP
+    return (int)((0x05014230u >> (4 * (pt - 1))) & 15u);
+}
+
 // Mosquito: beetle when stacked, otherwise the union of the neighbours'
 // movements in Q/P, A, G, S, B, L order, first occurrence kept, capped at
-// 128 (move_gen.cuh:907-1049).  Needs slx built for this cell.
+// 128 (move_gen.cuh:907-1049).  Needs slx built for this cell.  The list goes
+// to w->tmp.
 __device__ __noinline__ int gen_mosquito(WarpSmem* w, int cell, bool first_only, uint32_t* err) {
     Pos P{w};
-    if (P.height(cell) > 1) return gen_beetle(w, cell, w->tmp, first_only);
-    uint32_t t = neighbour_types(w, cell);
-    if (first_only) {
-        if ((t & 0x102u) && gen_step1(w, cell, w->dst, true)) return 1;
-        if ((t & 0x4u) && gen_ant(w, cell, w->dst, 128, true)) return 1;
-        if ((t & 0x8u) && gen_hopper(w, cell, w->dst, true)) return 1;
-        if ((t & 0x10u) && gen_walk3<false>(w, cell, w->dst, true)) return 1;
-        if ((t & 0x20u) && gen_beetle(w, cell, w->dst, true)) return 1;
-        if ((t & 0x80u) && gen_walk3<true>(w, cell, w->dst, true)) return 1;
-        return 0;
-    }
-    int l = lane_id();
+    if (P.height(cell) > 1) return walk(w, cell, WM_BEETLE, w->tmp, 6, first_only);
+    const uint32_t t = neighbour_types(w, cell);
+    const int l = lane_id();
     const uint32_t lt = lanemask_lt();
-    uint32_t* uni = w->bm + 16 * 17;  // 529-bit union set (free during generation)
-    set_clear(uni);
+    uint32_t* uni = w->bm + 16 * 17;  // union set (free during generation)
+    if (!first_only) set_clear(uni);
     int cnt = 0;
+    // part order Q/P, A, G, S, B, L: walk modes 0 3 2 4 1 5, and the
+    // neighbour type bits each part needs
+#pragma unroll 1
     for (int part = 0; part < 6; part++) {
-        int k = 0;
-        switch (part) {
-            case 0: if (t & 0x102u) k = gen_step1(w, cell, w->dst, false); break;
-            case 1:
-                if (t & 0x4u) {
-                    k = gen_ant(w, cell, w->dst, 128, false);
-                    if (k >= 128 && l == 0) atomicOr(err, kErrBuffer);
-                }
-                break;
-            case 2: if (t & 0x8u) k = gen_hopper(w, cell, w->dst, false); break;
-            case 3: if (t & 0x10u) k = gen_walk3<false>(w, cell, w->dst, false); break;
-            case 4: if (t & 0x20u) k = gen_beetle(w, cell, w->dst, false); break;
-            case 5: if (t & 0x80u) k = gen_walk3<true>(w, cell, w->dst, false); break;
+        const uint32_t need = part == 0 ? 0x102u : (part == 5 ? 0x80u : (1u << (part + 1)));
+        if (!(t & need)) continue;
+        const int mode = (int)((0x514230u >> (4 * part)) & 15u);
+        int k = walk(w, cell, mode, w->dst, mode == WM_ANT ? 128 : 32, first_only);
+        if (first_only) {
+            if (k) return 1;
+            continue;
         }
+        if (mode == WM_ANT && k >= 128 && l == 0) atomicOr(err, kErrBuffer);
+#pragma unroll 1
         for (int base = 0; base < k; base += 32) {
             int i = base + l;
             int v = i < k ? (int)w->dst[i] : -1;
@@ -301,9 +242,25 @@ __device__ __noinline__ int gen_mosquito(WarpSmem* w, int cell, bool first_only,
     return cnt;
 }
 
-// Is the top piece at cell a mosquito-or-pillbug thrower (move_gen.cuh:1316-1345)?
+// Destinations of one own piece; returns the list (w->dst or w->tmp) and count.
+__device__ __forceinline__ int piece_moves(WarpSmem* w, uint32_t occ_row, int cell, int pt, int cap,
+                                           bool first_only, uint32_t* err, const uint16_t** list) {
+    *list = w->dst;
+    if (pt == 2 || pt == 4 || pt == 6) lift_mover(w, occ_row, cell);
+    if (pt == 6) {
+        *list = w->tmp;
+        return gen_mosquito(w, cell, first_only, err);
+    }
+    if (pt < 1 || pt > 8) return 0;
+    int mode = mode_of(pt);
+    int c = mode == WM_ANT ? cap : (mode >= WM_SPIDER ? 32 : 6);
+    return walk(w, cell, mode, w->dst, c, first_only);
+}
+
+// Is any neighbour topped by a pillbug (move_gen.cuh:1326-1336)?
 __device__ __forceinline__ bool next_to_pillbug(WarpSmem* w, int cell) {
     Pos P{w};
+#pragma unroll 1
     for (int d = 0; d < 6; d++) {
         int nb = nbr(cell, d);
         if (nb >= 0 && P.occupied(nb) && (P.top(nb) & 15) == 8) return true;
@@ -313,14 +270,15 @@ __device__ __forceinline__ bool next_to_pillbug(WarpSmem* w, int cell) {
 
 // Pillbug throws from thrower pb: valid targets x valid drop cells, in
 // (target direction, drop direction) order (move_gen.cuh:691-769).
-__device__ __forceinline__ void throw_sets(WarpSmem* w, int pb, uint32_t& tmask, uint32_t& dmask) {
+__device__ __noinline__ void throw_sets(WarpSmem* w, int pb, uint32_t& tmask, uint32_t& dmask) {
     Pos P{w};
     int l = lane_id();
     int pbh = P.height(pb);
+    int stun = P.stunned();
     bool okt = false, okd = false;
     if (l < 6) {
         int t = nbr(pb, l);
-        if (t >= 0 && P.occupied(t) && P.height(t) == 1 && !P.is_stunned(t)) {
+        if (t >= 0 && P.occupied(t) && P.height(t) == 1 && stun != t) {
             int j = P.pidx(t);
             bool pinned = j < 32 && (w->pflag[j] & 1);
             if (!pinned) {
@@ -328,8 +286,7 @@ __device__ __forceinline__ void throw_sets(WarpSmem* w, int pb, uint32_t& tmask,
                 okt = !P.gate_blocked(t, opp_dir(l), ht > pbh ? ht : pbh);
             }
         }
-        int dcell = nbr(pb, l);
-        okd = dcell >= 0 && !P.occupied(dcell) && !P.gate_blocked(pb, l, pbh);
+        okd = t >= 0 && !P.occupied(t) && !P.gate_blocked(pb, l, pbh);
     }
     tmask = __ballot_sync(kFull, okt);
     dmask = __ballot_sync(kFull, okd);
@@ -338,12 +295,13 @@ __device__ __forceinline__ void throw_sets(WarpSmem* w, int pb, uint32_t& tmask,
 // ---------------------------------------------------------------------------
 // placement cells (move_gen.cuh:1064-1140) into w->prow / w->ppref
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int placement_cells(WarpSmem* w, const Setup& S, int turn) {
+__device__ __noinline__ int placement_cells(WarpSmem* w, uint32_t occ, uint32_t own, uint32_t opp,
+                                            int turn) {
     int l = lane_id();
     uint32_t p;
     if (turn == 0) p = (l == 11) ? (1u << 11) : 0u;
-    else if (turn == 1) p = dilate(S.occ) & ~S.occ;
-    else p = dilate(S.own) & ~S.occ & ~dilate(S.opp);
+    else if (turn == 1) p = dilate(occ) & ~occ;
+    else p = dilate(own) & ~occ & ~dilate(opp);
     p &= row_valid_mask();
     int c = __popc(p);
     int pre = warp_excl_scan(c);
@@ -355,6 +313,15 @@ __device__ __forceinline__ int placement_cells(WarpSmem* w, const Setup& S, int 
     return __shfl_sync(kFull, pre + c, 31);
 }
 
+// placeable piece-type mask of the side to move (move_gen.cuh:1161-1174)
+__device__ __forceinline__ uint32_t placeable_types(const Pos& P, int color, bool forced) {
+    uint32_t m = 0;
+#pragma unroll 1
+    for (int t = 0; t < 8; t++)
+        if (P.hand(color, t) > 0) m |= 1u << t;
+    return forced ? (m & 1u) : m;
+}
+
 // ---------------------------------------------------------------------------
 // full legal move list -> w->mv, returns the count
 // ---------------------------------------------------------------------------
@@ -364,23 +331,19 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err
     if (P.result() != 0) return 0;
     const int color = S.color, turn = P.turn(), ptn = turn >> 1;
     const bool queen_down = (P.queen_placed() >> color) & 1;
-    const bool forced = ptn == 3 && !queen_down;
-    uint32_t placeable = 0;
-    for (int t = 0; t < 8; t++) {
-        bool ok = forced ? (t == 0 && P.hand(color, 0) > 0) : (P.hand(color, t) > 0);
-        if (ok) placeable |= 1u << t;
-    }
+    const uint32_t placeable = placeable_types(P, color, ptn == 3 && !queen_down);
     int count = 0;
     if (placeable) {
-        int np = placement_cells(w, S, turn);
+        int np = placement_cells(w, S.occ, S.own, S.opp, turn);
         uint32_t types = placeable & ~(ptn == 0 ? 1u : 0u);
         int nt = __popc(types);
         int total = np * nt;
         if (total > kMaxMoves) total = kMaxMoves;
+#pragma unroll 1
         for (int m = l; m < total; m += 32) {
             int k = m / nt, j = m - (m / nt) * nt;
             int cell = kth_cell(w->prow, w->ppref, k);
-            put_move(w, m, 0, __fns(types, 0, j + 1) + 1, 0, cell);
+            put_move(w, m, 0, __fns(types, 0, j + 1) + 1, 0, p_to_c(cell));
         }
         count = total;
     }
@@ -389,42 +352,22 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err
         // own top pieces according to the side's top bitboard
         bool mine = S.my_cell >= 0 && rowbit(w->own, S.my_cell);
         // movers: own, not stunned, not pinned (move_gen.cuh:1221-1234)
-        bool mov = mine && !(stun != 0xFFFF && stun == S.my_cell) && !(w->pflag[l] & 1);
+        bool mov = mine && stun != S.my_cell && !(w->pflag[l] & 1);
         uint32_t movers = __ballot_sync(kFull, mov);
+#pragma unroll 1
         while (movers) {
             int i = __ffs(movers) - 1;
             movers &= movers - 1;
             int cell = w->pcell[i];
             int pt = P.top(cell) & 15;
-            int k = 0;
-            const uint16_t* list = w->dst;
-            switch (pt) {
-                case 1:
-                case 8: k = gen_step1(w, cell, w->dst, false); break;
-                case 2: {
-                    lift_mover(w, S.occ, cell);
-                    int room = kMaxMoves - count;
-                    int cap = room < 128 ? room : 128;
-                    k = gen_ant(w, cell, w->dst, cap, false);
-                    if (k >= 128 && room > 128 && l == 0) atomicOr(err, kErrBuffer);
-                    break;
-                }
-                case 3: k = gen_hopper(w, cell, w->dst, false); break;
-                case 4:
-                    lift_mover(w, S.occ, cell);
-                    k = gen_walk3<false>(w, cell, w->dst, false);
-                    break;
-                case 5: k = gen_beetle(w, cell, w->dst, false); break;
-                case 6:
-                    lift_mover(w, S.occ, cell);
-                    k = gen_mosquito(w, cell, false, err);
-                    list = w->tmp;
-                    break;
-                case 7: k = gen_walk3<true>(w, cell, w->dst, false); break;
-                default: break;
-            }
+            int room = kMaxMoves - count;
+            const uint16_t* list;
+            int k = piece_moves(w, S.occ, cell, pt, room < 128 ? room : 128, false, err, &list);
+            if (pt == 2 && k >= 128 && room > 128 && l == 0) atomicOr(err, kErrBuffer);
+            const int from_c = p_to_c(cell);
+#pragma unroll 1
             for (int m = l; m < k; m += 32)
-                if (count + m < kMaxMoves) put_move(w, count + m, 1, pt, cell, list[m]);
+                if (count + m < kMaxMoves) put_move(w, count + m, 1, pt, from_c, p_to_c(list[m]));
             count = min(kMaxMoves, count + k);
             __syncwarp();
         }
@@ -432,6 +375,7 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err
         int mt = S.my_top & 15;
         bool thr = mine && (mt == 8 || (mt == 6 && S.my_h == 1 && next_to_pillbug(w, S.my_cell)));
         uint32_t throwers = __ballot_sync(kFull, thr);
+#pragma unroll 1
         while (throwers) {
             int i = __ffs(throwers) - 1;
             throwers &= throwers - 1;
@@ -439,11 +383,13 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err
             uint32_t tm, dm;
             throw_sets(w, pb, tm, dm);
             int nt = __popc(tm), nd = __popc(dm), total = nt * nd;
+#pragma unroll 1
             for (int m = l; m < total; m += 32) {
                 int kt = m / nd, kd = m - (m / nd) * nd;
                 int target = nbr(pb, __fns(tm, 0, kt + 1));
                 int dest = nbr(pb, __fns(dm, 0, kd + 1));
-                if (count + m < kMaxMoves) put_move(w, count + m, 1, P.top(target) & 15, target, dest);
+                if (count + m < kMaxMoves)
+                    put_move(w, count + m, 1, P.top(target) & 15, p_to_c(target), p_to_c(dest));
             }
             count = min(kMaxMoves, count + total);
             __syncwarp();
@@ -466,18 +412,14 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
     if (P.result() != 0) return 0;
     const int color = S.color, turn = P.turn(), ptn = turn >> 1;
     const bool queen_down = (P.queen_placed() >> color) & 1;
-    const bool forced = ptn == 3 && !queen_down;
-    bool any = false;
-    for (int t = 0; t < 8; t++) {
-        bool ok = forced ? (t == 0 && P.hand(color, 0) > 0) : (P.hand(color, t) > 0);
-        if (ptn == 0 && t == 0) ok = false;
-        any |= ok;
-    }
+    const uint32_t any = placeable_types(P, color, ptn == 3 && !queen_down) & ~(ptn == 0 ? 1u : 0u);
     int count = 0;
     if (any) {
-        int np = placement_cells(w, S, turn);
+        int np = placement_cells(w, S.occ, S.own, S.opp, turn);
         int total = np < kMaxMoves ? np : kMaxMoves;
-        for (int m = l; m < total; m += 32) put_move(w, m, 0, 0, 0, kth_cell(w->prow, w->ppref, m));
+#pragma unroll 1
+        for (int m = l; m < total; m += 32)
+            put_move(w, m, 0, 0, 0, p_to_c(kth_cell(w->prow, w->ppref, m)));
         count = total;
     }
     if (!queen_down || count >= kMaxMoves) {
@@ -490,9 +432,10 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
     }
     const int stun = P.stunned();
     bool mine = S.my_cell >= 0 && rowbit(w->own, S.my_cell);
-    bool mov = mine && !(stun != 0xFFFF && stun == S.my_cell) && !(w->pflag[l] & 1);
+    bool mov = mine && stun != S.my_cell && !(w->pflag[l] & 1);
     uint32_t movers = __ballot_sync(kFull, mov);
     uint32_t seen = 0;  // (type, owner) flags, emit_fnn_move_flag move_gen.cuh:1362-1377
+#pragma unroll 1
     while (movers && count < kMaxMoves) {
         int i = __ffs(movers) - 1;
         movers &= movers - 1;
@@ -500,30 +443,10 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
         int pt = P.top(cell) & 15;
         uint32_t bit = 1u << ((pt - 1) * 2 + color);
         if (seen & bit) continue;
-        int has = 0;
-        switch (pt) {
-            case 1:
-            case 8: has = gen_step1(w, cell, w->dst, true); break;
-            case 2:
-                lift_mover(w, S.occ, cell);
-                has = gen_ant(w, cell, w->dst, 128, true);
-                break;
-            case 3: has = gen_hopper(w, cell, w->dst, true); break;
-            case 4:
-                lift_mover(w, S.occ, cell);
-                has = gen_walk3<false>(w, cell, w->dst, true);
-                break;
-            case 5: has = gen_beetle(w, cell, w->dst, true); break;
-            case 6:
-                lift_mover(w, S.occ, cell);
-                has = gen_mosquito(w, cell, true, err);
-                break;
-            case 7: has = gen_walk3<true>(w, cell, w->dst, true); break;
-            default: break;
-        }
-        if (has) {
+        const uint16_t* list;
+        if (piece_moves(w, S.occ, cell, pt, 128, true, err, &list)) {
             seen |= bit;
-            if (l == 0) put_move(w, count, 1, pt, cell, 0);
+            if (l == 0) put_move(w, count, 1, pt, p_to_c(cell), 0);
             count++;
         }
         __syncwarp();
@@ -531,6 +454,7 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
     int mt = S.my_top & 15;
     bool thr = mine && (mt == 8 || (mt == 6 && S.my_h == 1 && next_to_pillbug(w, S.my_cell)));
     uint32_t throwers = __ballot_sync(kFull, thr);
+#pragma unroll 1
     while (throwers && count < kMaxMoves) {
         int i = __ffs(throwers) - 1;
         throwers &= throwers - 1;
@@ -538,17 +462,16 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
         uint32_t tm, dm;
         throw_sets(w, pb, tm, dm);
         if (dm == 0u) continue;
+#pragma unroll 1
         while (tm) {  // summarize_pillbug_throws_for_fnn, move_gen.cuh:1379-1410
             int dt = __ffs(tm) - 1;
             tm &= tm - 1;
             int target = nbr(pb, dt);
-            int h = P.height(target);
             int tt = P.top(target);
-            int owner = (tt >> 4) & 1;
-            uint32_t bit = 1u << (((tt & 15) - 1) * 2 + owner);
-            if (h > 0 && !(seen & bit) && count < kMaxMoves) {
+            uint32_t bit = 1u << (((tt & 15) - 1) * 2 + ((tt >> 4) & 1));
+            if (P.height(target) > 0 && !(seen & bit) && count < kMaxMoves) {
                 seen |= bit;
-                if (l == 0) put_move(w, count, 1, tt & 15, target, 0);
+                if (l == 0) put_move(w, count, 1, tt & 15, p_to_c(target), 0);
                 count++;
             }
         }
@@ -571,11 +494,20 @@ enum : int {
     A_PLACE = 106, A_SURR = 107, A_N = 110
 };
 
+// top byte of a reference-index cell c (< 529)
+__device__ __forceinline__ int top_c(const WarpSmem* w, int c) {
+    int h = w->st[kOffHeight + c];
+    h = h > 5 ? 5 : h;
+    return h ? w->st[(h - 1) * kCells + c] : 0;
+}
+
 __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, float* out) {
     Pos P{w};
     int l = lane_id();
+#pragma unroll 1
     for (int i = l; i < A_N; i += 32) w->acc[i] = 0;
-    for (int i = l; i < 16 * 17 + 18; i += 32) w->bm[i] = 0u;
+#pragma unroll 1
+    for (int i = l; i < 16 * 17 + 17; i += 32) w->bm[i] = 0u;
     __syncwarp();
     const int turn = P.turn(), cur = turn & 1, stun = P.stunned();
     const int q0 = P.queen_cell(0), q1 = P.queen_cell(1);
@@ -586,25 +518,30 @@ __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, f
     if (cell >= 0 && pt >= 1 && pt <= 8) {
         atomicAdd(&w->acc[A_CNT + tc], 1);
         int occn = 0;
+#pragma unroll 1
         for (int d = 0; d < 6; d++) occn += P.height(nbr(cell, d)) > 0;
         if (occn == 0) atomicAdd(&w->acc[A_SINGLE + col], 1);
         int oq = col ? q0 : q1;
-        if (oq != 0xFFFF) {
-            if (oq < kCells && hex_distance(cell, oq) == 1) atomicAdd(&w->acc[A_QADJ + tc], 1);
-            atomicAdd(&w->acc[A_DSUM + tc], hex_distance(cell, oq));
+        if (oq >= 0) {
+            int dist = hex_distance(cell, oq);
+            if (oq < kPCells && dist == 1) atomicAdd(&w->acc[A_QADJ + tc], 1);
+            atomicAdd(&w->acc[A_DSUM + tc], dist);
             atomicAdd(&w->acc[A_DCNT + tc], 1);
         }
-        adjq0 = q0 != 0xFFFF && q0 < kCells && hex_distance(cell, q0) == 1;
-        adjq1 = q1 != 0xFFFF && q1 < kCells && hex_distance(cell, q1) == 1;
+        adjq0 = q0 >= 0 && q0 < kPCells && hex_distance(cell, q0) == 1;
+        adjq1 = q1 >= 0 && q1 < kPCells && hex_distance(cell, q1) == 1;
         if (h == 1 && S.my_ap) atomicAdd(&w->acc[A_AP + tc], 1);
         if (pt != 1) {
+            const int c = p_to_c(cell);
+#pragma unroll 1
             for (int lv = 0; lv < h - 1 && lv < 4; lv++) {
-                int b = w->st[lv * kCells + cell];
+                int b = w->st[lv * kCells + c];
                 if ((b & 15) == 1) w->acc[A_COVER + ((b >> 4) & 1)] = 1;
             }
         }
         capable = stun != cell && pt == 8;
         if (!capable && stun != cell && pt == 6 && h == 1) {
+#pragma unroll 1
             for (int d = 0; d < 6; d++) {
                 int nb = nbr(cell, d);
                 if (nb < 0 || P.height(nb) == 0 || stun == nb) continue;
@@ -621,21 +558,22 @@ __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, f
     uint32_t cap0 = __ballot_sync(kFull, capable && col == 0);
     uint32_t cap1 = __ballot_sync(kFull, capable && col == 1);
     if (capable && __popc((col ? cap1 : cap0) & lanemask_lt()) < 8) {
+#pragma unroll 1
         for (int d = 0; d < 6; d++) {
             int nb = nbr(cell, d);
             if (nb < 0 || P.height(nb) == 0 || stun == nb) continue;
             int nc = (P.top(nb) >> 4) & 1;
-            if (nc == col) atomicAdd(&w->acc[A_TOWN + col], 1);
-            else atomicAdd(&w->acc[A_TOPP + nc], 1);
+            atomicAdd(&w->acc[nc == col ? A_TOWN + col : A_TOPP + nc], 1);
         }
     }
     // source cells per (type, owner) and placement cells from the list
+#pragma unroll 1
     for (int m = l; m < nmoves; m += 32) {
         int tp = w->mv[3 * m], from = w->mv[3 * m + 1], to = w->mv[3 * m + 2];
         int type = tp & 255, mpt = tp >> 8;
         if (type == 1) {
             if (mpt >= 1 && mpt <= 8 && from < kCells) {
-                int owner = P.height(from) > 0 ? ((P.top(from) >> 4) & 1) : cur;
+                int owner = w->st[kOffHeight + from] > 0 ? ((top_c(w, from) >> 4) & 1) : cur;
                 atomicOr(&w->bm[((mpt - 1) * 2 + owner) * 17 + (from >> 5)], 1u << (from & 31));
             }
         } else if (type == 0 && to < kCells) {
@@ -643,6 +581,7 @@ __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, f
         }
     }
     __syncwarp();
+#pragma unroll 1
     for (int i = l; i < 16 * 17 + 17; i += 32) {
         int c = __popc(w->bm[i]);
         if (c) atomicAdd(&w->acc[i < 16 * 17 ? A_SRC + i / 17 : A_PLACE], c);
@@ -652,37 +591,50 @@ __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, f
         w->acc[A_SURR + 1] = __popc(s1);
     }
     __syncwarp();
-    for (int k = l; k < kFeat; k += 32) {
-        float v = 0.0f;
-        if (k < 16) v = (float)w->acc[A_CNT + k];
-        else if (k < 32) {
-            int t = (k - 16) >> 1, c = (k - 16) & 1;
-            const float per = (t == 1 || t == 2) ? 3.0f : ((t == 3 || t == 4) ? 2.0f : 1.0f);
-            v = (float)P.hand(c, t) / per;
-        } else if (k < 48) v = (float)w->acc[A_QADJ + k - 32];
-        else if (k < 64) {
-            int n = w->acc[A_DCNT + k - 48];
-            if (n > 0) v = (float)w->acc[A_DSUM + k - 48] / (float)n / 10.0f;
-        } else if (k < 80) v = (float)w->acc[A_SRC + k - 64];
-        else if (k < 96) v = (float)w->acc[A_AP + k - 80];
-        else if (k < 98) v = (float)w->acc[A_SINGLE + k - 96];
-        else if (k < 100) v = (float)w->acc[A_COVER + k - 98];
-        else if (k < 102) v = (k - 100 == cur) ? (float)w->acc[A_PLACE] / 10.0f : 0.0f;
-        else if (k == 102) {
-            int left = 200 - turn;
-            v = (float)(left < 0 ? 0 : left) / 200.0f;
-        } else if (k == 103) {
-            float t = (float)turn / 100.0f;
-            v = t < 1.0f ? t : 1.0f;
-        } else if (k < 106) v = (float)w->acc[A_CAP + k - 104];
-        else if (k < 108) v = (float)w->acc[A_TOWN + k - 106];
-        else if (k < 110) v = (float)w->acc[A_TOPP + k - 108];
-        else {
-            int qc = (k - 110) / 6, b = (k - 110) - qc * 6;
-            int s = w->acc[A_SURR + qc];
-            v = (s == b + 1) ? 1.0f : 0.0f;
+    // write-out in three uniform lane groups (no per-lane formula switch)
+    if (l < 16) {
+        out[l] = (float)w->acc[A_CNT + l];
+        out[32 + l] = (float)w->acc[A_QADJ + l];
+        out[64 + l] = (float)w->acc[A_SRC + l];
+        out[80 + l] = (float)w->acc[A_AP + l];
+        const int t = l >> 1;
+        const float per = (t == 1 || t == 2) ? 3.0f : ((t == 3 || t == 4) ? 2.0f : 1.0f);
+        out[16 + l] = (float)P.hand(l & 1, t) / per;
+        const int n = w->acc[A_DCNT + l];
+        out[48 + l] = n > 0 ? (float)w->acc[A_DSUM + l] / (float)n / 10.0f : 0.0f;
+    } else if (l < 28) {
+        const int j = l - 16, qc = j >= 6, b = j - 6 * qc;
+        out[110 + j] = w->acc[A_SURR + qc] == b + 1 ? 1.0f : 0.0f;
+    } else {
+        // lanes 28..31: features 96..109, up to four each
+        const int j = l - 28;
+        const int left = 200 - turn;
+        const float tt = (float)turn / 100.0f;
+        float v[4];
+        if (j == 0) {  // 96..99
+            v[0] = (float)w->acc[A_SINGLE];
+            v[1] = (float)w->acc[A_SINGLE + 1];
+            v[2] = (float)w->acc[A_COVER];
+            v[3] = (float)w->acc[A_COVER + 1];
+        } else if (j == 1) {  // 100..103
+            const float pl = (float)w->acc[A_PLACE] / 10.0f;
+            v[0] = cur == 0 ? pl : 0.0f;
+            v[1] = cur == 1 ? pl : 0.0f;
+            v[2] = (float)(left < 0 ? 0 : left) / 200.0f;
+            v[3] = tt < 1.0f ? tt : 1.0f;
+        } else if (j == 2) {  // 104..107
+            v[0] = (float)w->acc[A_CAP];
+            v[1] = (float)w->acc[A_CAP + 1];
+            v[2] = (float)w->acc[A_TOWN];
+            v[3] = (float)w->acc[A_TOWN + 1];
+        } else {  // 108..109
+            v[0] = (float)w->acc[A_TOPP];
+            v[1] = (float)w->acc[A_TOPP + 1];
         }
-        out[k] = v;
+        const int base = 96 + 4 * j, cntv = j == 3 ? 2 : 4;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            if (i < cntv) out[base + i] = v[i];
     }
     __syncwarp();
 }

@@ -36,10 +36,10 @@ __device__ __forceinline__ bool st_queen_surrounded(const uint8_t* st, int color
     if (!((st[kOffQPlaced] >> color) & 1)) return false;
     int q = st_u16(st, kOffQCell + 2 * color);
     if (q >= kCells) return false;
-    int n = 0;
+    int p = c_to_p(q), n = 0;
     for (int d = 0; d < 6; d++) {
-        int nb = nbr(q, d);
-        if (nb >= 0 && st_bb_get(st, kOffOcc, nb)) n++;
+        int nb = nbr(p, d);
+        if (nb >= 0 && st_bb_get(st, kOffOcc, p_to_c(nb))) n++;
     }
     return n == 6;
 }
