@@ -15,6 +15,7 @@
 #include "hv_core.cuh"
 #include "hv_movegen.cuh"
 #include "hv_state.cuh"
+#include "hv_fnn.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -123,6 +124,100 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
         Setup S = setup_position(w);
         int n = gen_compact(w, S, &g_error);
         features(w, S, n, feats_out + a * kFeat);
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// fused leaf evaluation: successors + FNN + softmax
+// (fnn_mcts_orchestrator.py:243-316 _eval_states with fnn_network.py encode /
+//  value_head / score_actions)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ FnnSmem* fnn_slot() {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    return reinterpret_cast<FnnSmem*>(smem_raw + sizeof(WarpSmem) * kWarpsPerBlock) +
+           (threadIdx.x >> 5);
+}
+
+__global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
+    const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal_moves,
+    const int32_t* __restrict__ num_legal, const float* __restrict__ root_feats, int64_t count,
+    const float* __restrict__ wts, FnnDims dims, float* __restrict__ priors,
+    float* __restrict__ values, float* __restrict__ child_q, float* __restrict__ logits_out) {
+    WarpSmem* w = warp_slot();
+    FnnSmem* f = fnn_slot();
+    const FnnOffsets off = fnn_offsets(dims);
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < count;
+         p += nwarps) {
+        int n = num_legal[p];
+        n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
+        const uint8_t* st_g = states + p * kStateBytes;
+        const uint8_t* mv_g = legal_moves + p * (kMaxMoves * kMoveBytes);
+        if (root_feats) {
+            for (int k = l; k < kFeat; k += 32) f->xs[0][k] = root_feats[p * kFeat + k];
+            __syncwarp();
+        } else {
+            stage_state(w, st_g);
+            const uint4* s4 = reinterpret_cast<const uint4*>(mv_g);
+            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
+            for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
+            __syncwarp();
+            Setup S = setup_position(w);
+            features(w, S, n, f->xs[0]);
+        }
+        float val[kFnnChunk], lg[kFnnChunk];
+        fnn_encode_chunk(wts, dims, off, f, 1, val);
+        const float root_value = val[0];
+        fnn_root_pre(wts, dims, off, f);
+        float* cq = child_q + p * kMaxMoves;
+#pragma unroll 1
+        for (int base = 0; base < n; base += kFnnChunk) {
+            const int ns = min(kFnnChunk, n - base);
+#pragma unroll 1
+            for (int s = 0; s < ns; s++) {
+                stage_state(w, st_g);
+                if (l == 0) {
+                    const uint8_t* m = mv_g + (base + s) * kMoveBytes;
+                    st_apply(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+                }
+                __syncwarp();
+                Setup S = setup_position(w);
+                int cn = gen_compact(w, S, &g_error);
+                features(w, S, cn, f->xs[s]);
+            }
+            fnn_encode_chunk(wts, dims, off, f, ns, val);
+            fnn_score_chunk(wts, dims, off, f, ns, lg);
+            if (l < ns) {
+                // lane s stores successor s (values are warp-uniform)
+                float lv = lg[0], vv = val[0];
+#pragma unroll
+                for (int s = 1; s < kFnnChunk; s++)
+                    if (l == s) {
+                        lv = lg[s];
+                        vv = val[s];
+                    }
+                f->logit[base + l] = lv;
+                cq[base + l] = -vv;
+            }
+            __syncwarp();
+        }
+        // softmax over the legal slots (-1e30 padding, then zeroed)
+        float mx = -INFINITY;
+        for (int i = l; i < n; i += 32) mx = fmaxf(mx, f->logit[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        float sum = 0.0f;
+        for (int i = l; i < n; i += 32) sum += expf(f->logit[i] - mx);
+        sum = warp_sum(sum);
+        float* pr = priors + p * kMaxMoves;
+        for (int i = l; i < kMaxMoves; i += 32) {
+            pr[i] = i < n ? expf(f->logit[i] - mx) / sum : 0.0f;
+            if (i >= n) cq[i] = 0.0f;
+            if (logits_out) logits_out[p * kMaxMoves + i] = i < n ? f->logit[i] : 0.0f;
+        }
+        if (l == 0) values[p] = root_value;
         __syncwarp();
     }
 }
@@ -387,6 +482,33 @@ int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const u
     k_successor_features<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
         states, num_states, legal_moves, action_to_root, move_indices, num_actions, features);
     return launch_status();
+}
+
+int hv_fnn_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                       const float* root_features, int64_t count, const float* weights, int hidden,
+                       int embed, int action_hidden, float* priors, float* values, float* child_q,
+                       float* logits, void* stream) {
+    if (count < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!states || !legal_moves || !num_legal || !weights || !priors || !values || !child_q ||
+        !aligned16(states) || !aligned16(legal_moves))
+        return HV_EINVAL;
+    if (hidden < 1 || hidden > kFnnMaxDim || embed < 1 || embed > kFnnMaxDim || action_hidden < 1 ||
+        action_hidden > kFnnMaxDim)
+        return HV_EINVAL;
+    size_t smem = (sizeof(WarpSmem) + sizeof(FnnSmem)) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_fnn_eval, count, smem, &grid);
+    if (rc) return rc;
+    FnnDims d{hidden, embed, action_hidden};
+    k_fnn_eval<<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, legal_moves, num_legal,
+                                                                root_features, count, weights, d,
+                                                                priors, values, child_q, logits);
+    return launch_status();
+}
+
+int hv_fnn_weights_size(int hidden, int embed, int action_hidden) {
+    return fnn_offsets(FnnDims{hidden, embed, action_hidden}).total;
 }
 
 int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream) {

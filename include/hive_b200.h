@@ -76,6 +76,25 @@ int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const u
                               const int64_t* action_to_root, const int64_t* move_indices,
                               int64_t num_actions, float* features, void* stream);
 
+/* FNN leaf evaluation fused with successor generation: the body of
+ * FNNMCTSOrchestrator._eval_states (hive_fnn/fnn_mcts_orchestrator.py:243-316)
+ * with HiveFNN.encode / value_head / score_actions
+ * (hive_fnn/fnn_network.py:98-143), which the reference runs as
+ * fnn_successor_features_batch + torch GEMMs + softmax/scatter.
+ * Per leaf p (count leaves): priors[p, 0..255] = softmax of the successor
+ * logits over the num_legal[p] slots (zero elsewhere); values[p] = root value;
+ * child_q[p, i] = -value(successor i) (zero past num_legal).  root_features
+ * [count, 122] may be NULL (computed from states + legal_moves); logits
+ * [count, 256] may be NULL.  weights: packed fp32 (layout in
+ * hive_neuralnet_b200/fnn.py pack_weights); dims 1..64. */
+int hv_fnn_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                       const float* root_features, int64_t count, const float* weights, int hidden,
+                       int embed, int action_hidden, float* priors, float* values, float* child_q,
+                       float* logits, void* stream);
+
+/* number of floats hv_fnn_eval_leaves expects in `weights` */
+int hv_fnn_weights_size(int hidden, int embed, int action_hidden);
+
 /* apply_moves_batch(states, moves, batch_size)
  * replaces bindings.cpp:272-274 / game_logic.cu:465-477.  moves: [batch, 6]. */
 int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream);
