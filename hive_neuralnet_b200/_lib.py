@@ -49,7 +49,26 @@ _vp = C.c_void_p
 _i64 = C.c_int64
 _int = C.c_int
 
+class HvTree(C.Structure):
+    """hv_tree of include/hive_b200.h: the 12 tree arrays + max_nodes."""
+    _fields_ = [(n, C.c_void_p) for n in (
+        "visit_count", "total_value", "prior", "parent_idx", "virtual_q_penalty", "move_bytes",
+        "action_idx", "first_child", "num_children", "is_terminal", "terminal_value", "node_count")] + [
+        ("max_nodes", C.c_int32)]
+
+
+_tp = C.POINTER(HvTree)
+_f = C.c_float
+
 _SIGNATURES = {
+    "hv_mcts_select": ([_tp, _int, _vp, _vp, _vp, _vp, _vp, _int, _int, _f, _int, _int, _int, _f, _f,
+                        _vp, _vp, _vp, _vp, _vp, _vp], _int),
+    "hv_mcts_replay": ([_vp, _vp, _vp, _vp, _vp, _int, _int, _vp], _int),
+    "hv_mcts_expand": ([_tp, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f,
+                        _int, _int, _vp], _int),
+    "hv_mcts_backprop": ([_tp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp], _int),
+    "hv_mcts_root_noise": ([_tp, _vp, _vp, _int, _f, _f, _int, _vp], _int),
+    "hv_mcts_extract_policy": ([_tp, _vp, _vp, _vp, _f, _int, _f, _int, _vp], _int),
     "hv_version": ([], _int),
     "hv_status_string": ([_int], C.c_char_p),
     "hv_get_error": ([_vp, _int], _int),

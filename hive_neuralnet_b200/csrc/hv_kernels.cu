@@ -16,6 +16,7 @@
 #include "hv_movegen.cuh"
 #include "hv_state.cuh"
 #include "hv_fnn.cuh"
+#include "hv_mcts.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -219,6 +220,137 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
         }
         if (l == 0) values[p] = root_value;
         __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// MCTS tree kernels: one warp per game (hv_mcts.cuh)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) k_mcts_select(TreeDev t, SelectArgs a) {
+    const int nwarps = gridDim.x * kWarpsPerBlock;
+    for (int g = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); g < a.B; g += nwarps)
+        select_game(t, a, g);
+}
+
+__global__ void __launch_bounds__(kThreads) k_mcts_expand(TreeDev t, ExpandArgs a) {
+    const int nwarps = gridDim.x * kWarpsPerBlock;
+    for (int g = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); g < a.B; g += nwarps)
+        expand_game(t, a, g);
+}
+
+__global__ void __launch_bounds__(kThreads) k_mcts_backprop(TreeDev t, const int32_t* leaf,
+                                                            const float* values, const int32_t* vlp,
+                                                            const int32_t* vll, const int8_t* was,
+                                                            int B, int total) {
+    const int nwarps = gridDim.x * kWarpsPerBlock;
+    for (int g = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); g < B; g += nwarps)
+        backprop_game(t, leaf, values, vlp, vll, was, B, total, g);
+}
+
+// leaf state = root state + path moves (mcts_tree.cuh:298-320); one warp per simulation
+__global__ void __launch_bounds__(kThreads) k_mcts_replay(const uint8_t* __restrict__ roots,
+                                                          uint8_t* __restrict__ leaves,
+                                                          const uint8_t* __restrict__ paths,
+                                                          const int32_t* __restrict__ plen,
+                                                          const int32_t* __restrict__ leaf, int B,
+                                                          int total) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint8_t* st = smem_raw + (threadIdx.x >> 5) * kStateBytes;
+    const int nwarps = gridDim.x * kWarpsPerBlock;
+    for (int s = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); s < total; s += nwarps) {
+        if (leaf[s] < 0) continue;
+        const uint4* s4 = reinterpret_cast<const uint4*>(roots + (int64_t)(s % B) * kStateBytes);
+        uint4* d4 = reinterpret_cast<uint4*>(st);
+        for (int i = lane_id(); i < kStateBytes / 16; i += 32) d4[i] = __ldg(s4 + i);
+        __syncwarp();
+        if (lane_id() == 0) {
+            int n = plen[s];
+            n = n < 0 ? 0 : (n > kTreeDepth ? kTreeDepth : n);
+            for (int k = 0; k < n; k++) {
+                const uint8_t* m = paths + ((int64_t)s * kTreeDepth + k) * 6;
+                st_apply(st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+            }
+        }
+        __syncwarp();
+        uint4* o4 = reinterpret_cast<uint4*>(leaves + (int64_t)s * kStateBytes);
+        for (int i = lane_id(); i < kStateBytes / 16; i += 32) o4[i] = d4[i];
+        __syncwarp();
+    }
+}
+
+// root prior temperature + Dirichlet mix (mcts_tree.cuh:1192-1234); one thread per game
+__global__ void k_mcts_root_noise(TreeDev t, const float* noise, const int32_t* roots, int pad,
+                                  float eps, float temp, int B) {
+    int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= B) return;
+    int64_t ri = tix(t, g, roots[g]);
+    int fc = t.fc[ri], nc = t.nc[ri];
+    if (fc < 0 || nc == 0) return;
+    if (temp > 1.0f) {
+        float inv = __fdiv_rn(1.0f, temp), sum = 0.0f;
+        for (int c = 0; c < nc; c++) {
+            int64_t ci = tix(t, g, fc + c);
+            float p = powf(t.pr[ci], inv);
+            t.pr[ci] = p;
+            sum = __fadd_rn(sum, p);
+        }
+        if (sum > 0.0f)
+            for (int c = 0; c < nc; c++) {
+                int64_t ci = tix(t, g, fc + c);
+                t.pr[ci] = __fdiv_rn(t.pr[ci], sum);
+            }
+    }
+    if (eps > 0.0f)
+        for (int c = 0; c < nc; c++) {
+            int64_t ci = tix(t, g, fc + c);
+            float x = __fmul_rn(__fsub_rn(1.0f, eps), t.pr[ci]);
+            float y = __fmul_rn(eps, noise[(int64_t)g * pad + c]);
+            t.pr[ci] = __fadd_rn(x, y);
+        }
+}
+
+// visit-count policy over the action space (mcts_tree.cuh:607-684); one thread per game
+__global__ void k_mcts_extract_policy(TreeDev t, float* pol, const int32_t* move_numbers,
+                                      const int32_t* roots, float temperature, int drop, float prune,
+                                      int B) {
+    int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= B) return;
+    float* p = pol + (int64_t)g * 85834;
+    int64_t ri = tix(t, g, roots[g]);
+    int fc = t.fc[ri], nc = t.nc[ri];
+    if (fc < 0 || nc == 0) return;
+    float temp = move_numbers[g] >= drop ? 0.0f : temperature;
+    if (temp <= 0.0f) {
+        int ba = -1, bv = -1;
+        for (int c = 0; c < nc; c++) {
+            int64_t ci = tix(t, g, fc + c);
+            if (t.vc[ci] > bv) {
+                bv = t.vc[ci];
+                ba = t.ai[ci];
+            }
+        }
+        if (ba >= 0 && ba < 85834) p[ba] = 1.0f;
+        return;
+    }
+    float mx = 0.0f, sum = 0.0f;
+    for (int c = 0; c < nc; c++) {
+        float v = (float)t.vc[tix(t, g, fc + c)];
+        if (v > mx) mx = v;
+    }
+    for (int c = 0; c < nc; c++) {
+        int64_t ci = tix(t, g, fc + c);
+        float v = (float)t.vc[ci];
+        if (prune > 0.0f && mx > 0.0f && v < __fmul_rn(mx, prune)) v = 0.0f;
+        if (temp != 1.0f) v = powf(v, __fdiv_rn(1.0f, temp));
+        int act = t.ai[ci];
+        if (act >= 0 && act < 85834) {
+            p[act] = v;
+            sum = __fadd_rn(sum, v);
+        }
+    }
+    for (int c = 0; c < nc; c++) {
+        int act = t.ai[tix(t, g, fc + c)];
+        if (act >= 0 && act < 85834) p[act] = sum > 0.0f ? __fdiv_rn(p[act], sum) : __fdiv_rn(1.0f, (float)nc);
     }
 }
 
@@ -509,6 +641,107 @@ int hv_fnn_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const 
 
 int hv_fnn_weights_size(int hidden, int embed, int action_hidden) {
     return fnn_offsets(FnnDims{hidden, embed, action_hidden}).total;
+}
+
+static bool tree_ok(const hv_tree* t) {
+    return t && t->visit_count && t->total_value && t->prior && t->parent_idx && t->virtual_q_penalty &&
+           t->move_bytes && t->action_idx && t->first_child && t->num_children && t->is_terminal &&
+           t->terminal_value && t->node_count && t->max_nodes > 0;
+}
+
+static TreeDev tree_dev(const hv_tree* t) {
+    return TreeDev{t->visit_count, t->total_value, t->prior, t->parent_idx, t->virtual_q_penalty,
+                   t->move_bytes, t->action_idx, t->first_child, t->num_children, t->is_terminal,
+                   t->terminal_value, t->node_count, t->max_nodes};
+}
+
+static int game_grid(int B) { return (B + kWarpsPerBlock - 1) / kWarpsPerBlock; }
+
+int hv_mcts_select(const hv_tree* tree, int mode, const float* child_init_q, const int8_t* game_active,
+                   const int32_t* root_nodes, const int8_t* alive_mask, const int32_t* root_slots,
+                   int num_candidates, int max_root_children, float c_puct, int B, int W,
+                   int deterministic_non_root, float non_root_sigma, float q_penalty, int32_t* leaf,
+                   uint8_t* move_paths, int32_t* path_len, int32_t* vl_paths, int32_t* vl_len,
+                   void* stream) {
+    if (!tree_ok(tree) || mode < 0 || mode > 2 || B < 0 || W < 0) return HV_EINVAL;
+    if (mode == 2 && num_candidates < 1) return HV_EINVAL;
+    const int total = mode == 2 ? W * num_candidates * B : W * B;
+    if (total == 0) return HV_OK;
+    if (!game_active || !root_nodes || !leaf || !move_paths || !path_len || !vl_paths || !vl_len)
+        return HV_EINVAL;
+    if ((mode == 1 && !alive_mask) || (mode == 2 && !root_slots)) return HV_EINVAL;
+    if (deterministic_non_root && mode != 0 && !child_init_q) return HV_EINVAL;
+    SelectArgs a{mode, child_init_q, game_active, root_nodes, alive_mask, root_slots, num_candidates,
+                 max_root_children, c_puct, B, total, deterministic_non_root, non_root_sigma,
+                 q_penalty, leaf, move_paths, path_len, vl_paths, vl_len};
+    k_mcts_select<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+    return launch_status();
+}
+
+int hv_mcts_replay(const uint8_t* root_states, uint8_t* leaf_states, const uint8_t* move_paths,
+                   const int32_t* path_len, const int32_t* leaf, int B, int total, void* stream) {
+    if (B <= 0 || total < 0) return total == 0 ? HV_OK : HV_EINVAL;
+    if (total == 0) return HV_OK;
+    if (!root_states || !leaf_states || !move_paths || !path_len || !leaf || !aligned16(root_states) ||
+        !aligned16(leaf_states))
+        return HV_EINVAL;
+    size_t smem = (size_t)kStateBytes * kWarpsPerBlock;
+    int grid = (total + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    k_mcts_replay<<<grid, kThreads, smem, (cudaStream_t)stream>>>(root_states, leaf_states, move_paths,
+                                                                  path_len, leaf, B, total);
+    return launch_status();
+}
+
+int hv_mcts_expand(const hv_tree* tree, int dense, int backprop, float* child_init_q,
+                   const float* child_q, const int32_t* leaf, const uint8_t* leaf_states,
+                   const uint8_t* legal_moves, const int32_t* num_legal, const float* priors,
+                   const int32_t* results, const float* values, const int32_t* vl_paths,
+                   const int32_t* vl_len, int8_t* was_expanded, float q_penalty, int B, int total,
+                   void* stream) {
+    if (!tree_ok(tree) || B < 0 || total < 0) return HV_EINVAL;
+    if (total == 0 || B == 0) return HV_OK;
+    if (!leaf || !leaf_states || !legal_moves || !num_legal || !priors || !results) return HV_EINVAL;
+    if (dense && (!child_init_q || !child_q)) return HV_EINVAL;
+    if (backprop && (!values || !vl_paths || !vl_len)) return HV_EINVAL;
+    ExpandArgs a{dense, backprop, child_init_q, child_q, leaf, leaf_states, legal_moves, num_legal,
+                 priors, results, values, vl_paths, vl_len, was_expanded, q_penalty, B, total};
+    k_mcts_expand<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+    return launch_status();
+}
+
+int hv_mcts_backprop(const hv_tree* tree, const int32_t* leaf, const float* values,
+                     const int32_t* vl_paths, const int32_t* vl_len, const int8_t* was_expanded, int B,
+                     int total, void* stream) {
+    if (!tree_ok(tree) || B < 0 || total < 0) return HV_EINVAL;
+    if (total == 0 || B == 0) return HV_OK;
+    if (!leaf || !values || !vl_paths || !vl_len || !was_expanded) return HV_EINVAL;
+    k_mcts_backprop<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), leaf, values,
+                                                                         vl_paths, vl_len,
+                                                                         was_expanded, B, total);
+    return launch_status();
+}
+
+int hv_mcts_root_noise(const hv_tree* tree, const float* noise, const int32_t* root_nodes,
+                       int max_children_pad, float dir_eps, float root_policy_temp, int B,
+                       void* stream) {
+    if (!tree_ok(tree) || B < 0) return HV_EINVAL;
+    if (B == 0) return HV_OK;
+    if (!root_nodes || (dir_eps > 0.0f && !noise)) return HV_EINVAL;
+    k_mcts_root_noise<<<(B + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
+        tree_dev(tree), noise, root_nodes, max_children_pad, dir_eps, root_policy_temp, B);
+    return launch_status();
+}
+
+int hv_mcts_extract_policy(const hv_tree* tree, float* policies, const int32_t* move_numbers,
+                           const int32_t* root_nodes, float temperature, int temp_drop_move,
+                           float pruning_threshold, int B, void* stream) {
+    if (!tree_ok(tree) || B < 0) return HV_EINVAL;
+    if (B == 0) return HV_OK;
+    if (!policies || !move_numbers || !root_nodes) return HV_EINVAL;
+    k_mcts_extract_policy<<<(B + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
+        tree_dev(tree), policies, move_numbers, root_nodes, temperature, temp_drop_move,
+        pruning_threshold, B);
+    return launch_status();
 }
 
 int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream) {

@@ -208,6 +208,210 @@ class HiveGPUExtension:
                        "legal_moves_to_actions_batch")
         return out
 
+    # -- MCTS tree (bindings.cpp:110-226) ------------------------------------
+    # Tree tensors in binding order: (vc i32, tv f32, pr f32, pa i32, vq f32,
+    # mb u8[...,6], ai i32, fc i32, nc i32, it i8, tv2 f32, cnt i32[B]).
+    _TREE_DTYPES = (torch.int32, torch.float32, torch.float32, torch.int32, torch.float32, torch.uint8,
+                    torch.int32, torch.int32, torch.int32, torch.int8, torch.float32, torch.int32)
+
+    def _tree(self, tensors, max_nodes: int, B: int) -> "_lib.HvTree":
+        if len(tensors) != 12:
+            raise ValueError(f"expected 12 tree tensors, got {len(tensors)}")
+        for i, (t, dt) in enumerate(zip(tensors, self._TREE_DTYPES)):
+            if not isinstance(t, torch.Tensor) or t.dtype != dt or not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"tree tensor {i}: expected contiguous CUDA {dt}")
+            need = B if i == 11 else B * max_nodes * (6 if i == 5 else 1)
+            if t.numel() < need:
+                raise ValueError(f"tree tensor {i}: {t.numel()} elements < {need} for B={B}, max_nodes={max_nodes}")
+        return _lib.HvTree(*[t.data_ptr() for t in tensors], int(max_nodes))
+
+    def _select(self, tree, mode, child_init_q, game_active, root_nodes, alive_mask, root_slots,
+                num_candidates, max_root_children, c_puct, B, W, max_nodes, det, sigma, q_penalty):
+        import ctypes
+        dev = tree[0].device
+        total = W * num_candidates * B if mode == 2 else W * B
+        leaf = torch.zeros((total,), dtype=torch.int32, device=dev)
+        paths = torch.zeros((total, MAX_TREE_DEPTH, SIZEOF_GPU_MOVE), dtype=torch.uint8, device=dev)
+        plen = torch.zeros((total,), dtype=torch.int32, device=dev)
+        vlp = torch.zeros((total, MAX_TREE_DEPTH), dtype=torch.int32, device=dev)
+        vll = torch.zeros((total,), dtype=torch.int32, device=dev)
+        ts = self._tree(tree, max_nodes, B)
+        game_active = _need(game_active, "game_active", torch.int8, B)
+        root_nodes = _need(root_nodes, "root_nodes", torch.int32, B)
+        if alive_mask is not None:
+            alive_mask = _need(alive_mask, "alive_mask", torch.int8, B)
+        if root_slots is not None:
+            root_slots = _need(root_slots, "root_slots", torch.int32, B)
+        if child_init_q is not None:
+            child_init_q = _need(child_init_q, "child_init_q", torch.float32, B)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_select(
+                ctypes.byref(ts), mode, _ptr(child_init_q), _ptr(game_active), _ptr(root_nodes),
+                _ptr(alive_mask), _ptr(root_slots), num_candidates, max_root_children, float(c_puct), B, W,
+                int(bool(det)), float(sigma), float(q_penalty), _ptr(leaf), _ptr(paths), _ptr(plen),
+                _ptr(vlp), _ptr(vll), _stream(dev)), "mcts_select")
+        return leaf, paths, plen, vlp, vll
+
+    def mcts_select_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, game_active, root_nodes,
+                          c_puct, B, W, max_nodes):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        return self._select(tree, 0, None, game_active, root_nodes, None, None, 1, MAX_LEGAL_MOVES, c_puct,
+                            B, W, max_nodes, False, 4.0, 0.0)
+
+    def mcts_select_with_root_mask_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt,
+                                         child_init_q, game_active, root_nodes, alive_mask, max_root_children,
+                                         c_puct, B, W, max_nodes, deterministic_non_root=False,
+                                         non_root_sigma=4.0, q_penalty=0.0):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        return self._select(tree, 1, child_init_q, game_active, root_nodes, alive_mask, None, 1,
+                            max_root_children, c_puct, B, W, max_nodes, deterministic_non_root,
+                            non_root_sigma, q_penalty)
+
+    def mcts_select_with_root_slots_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt,
+                                          child_init_q, game_active, root_nodes, root_slots, num_candidates,
+                                          max_root_children, c_puct, B, W, max_nodes,
+                                          deterministic_non_root=False, non_root_sigma=4.0, q_penalty=0.0):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        return self._select(tree, 2, child_init_q, game_active, root_nodes, None, root_slots, num_candidates,
+                            max_root_children, c_puct, B, W, max_nodes, deterministic_non_root,
+                            non_root_sigma, q_penalty)
+
+    def mcts_replay_batch(self, root_states, leaf_states, move_paths, path_lengths, leaf_indices, B, total):
+        root_states = _need(root_states, "root_states", torch.uint8, B, (SIZEOF_HIVE_STATE,))
+        if not leaf_states.is_contiguous() or leaf_states.dtype != torch.uint8 or leaf_states.shape[0] < total:
+            raise ValueError("leaf_states: expected contiguous uint8 [total, 3424] (written in place)")
+        move_paths = _need(move_paths, "move_paths", torch.uint8, total)
+        path_lengths = _need(path_lengths, "path_lengths", torch.int32, total)
+        leaf_indices = _need(leaf_indices, "leaf_indices", torch.int32, total)
+        dev = root_states.device
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_replay(_ptr(root_states), _ptr(leaf_states), _ptr(move_paths),
+                                                _ptr(path_lengths), _ptr(leaf_indices), B, total, _stream(dev)),
+                       "mcts_replay")
+
+    def _expand(self, tree, dense, backprop, child_init_q, child_q, leaf_indices, leaf_states, legal_moves,
+                num_legal, priors, results, values, vl_paths, vl_lengths, B, total, max_nodes, q_penalty,
+                want_was):
+        import ctypes
+        dev = tree[0].device
+        ts = self._tree(tree, max_nodes, B)
+        leaf_indices = _need(leaf_indices, "leaf_indices", torch.int32, total)
+        leaf_states = _need(leaf_states, "leaf_states", torch.uint8, total, (SIZEOF_HIVE_STATE,))
+        legal_moves = _need(legal_moves, "legal_moves", torch.uint8, total, (MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE))
+        num_legal = _need(num_legal, "num_legal", torch.int32, total)
+        priors = _need(priors, "priors", torch.float32, total,
+                       (MAX_LEGAL_MOVES,) if dense else (ACTION_SPACE_SIZE,))
+        results = _need(results, "results", torch.int32, total)
+        if dense:
+            child_q = _need(child_q, "child_q_values", torch.float32, total, (MAX_LEGAL_MOVES,))
+            child_init_q = _need(child_init_q, "child_init_q", torch.float32, B)
+        if backprop:
+            values = _need(values.reshape(-1), "nn_values", torch.float32, total)
+            vl_paths = _need(vl_paths, "vl_paths", torch.int32, total)
+            vl_lengths = _need(vl_lengths, "vl_lengths", torch.int32, total)
+        was = torch.zeros((total,), dtype=torch.int8, device=dev) if want_was else None
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_expand(
+                ctypes.byref(ts), int(dense), int(backprop), _ptr(child_init_q), _ptr(child_q),
+                _ptr(leaf_indices), _ptr(leaf_states), _ptr(legal_moves), _ptr(num_legal), _ptr(priors),
+                _ptr(results), _ptr(values), _ptr(vl_paths), _ptr(vl_lengths), _ptr(was), float(q_penalty),
+                B, total, _stream(dev)), "mcts_expand")
+        return was
+
+    def mcts_expand_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, leaf_indices, leaf_states,
+                          legal_moves, num_legal, action_probs, results, B, total, max_nodes):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        return self._expand(tree, False, False, None, None, leaf_indices, leaf_states, legal_moves, num_legal,
+                            action_probs, results, None, None, None, B, total, max_nodes, 0.0, True)
+
+    def mcts_expand_and_backprop_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, leaf_indices,
+                                       leaf_states, legal_moves, num_legal, action_probs, results, nn_values,
+                                       vl_paths, vl_lengths, B, total, max_nodes):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        self._expand(tree, False, True, None, None, leaf_indices, leaf_states, legal_moves, num_legal,
+                     action_probs, results, nn_values, vl_paths, vl_lengths, B, total, max_nodes, 0.0, False)
+
+    def mcts_expand_dense_priors_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, child_init_q,
+                                       child_q_values, leaf_indices, leaf_states, legal_moves, num_legal,
+                                       priors_per_legal, results, B, total, max_nodes):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        return self._expand(tree, True, False, child_init_q, child_q_values, leaf_indices, leaf_states,
+                            legal_moves, num_legal, priors_per_legal, results, None, None, None, B, total,
+                            max_nodes, 0.0, True)
+
+    def mcts_expand_and_backprop_dense_priors_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt,
+                                                    child_init_q, child_q_values, leaf_indices, leaf_states,
+                                                    legal_moves, num_legal, priors_per_legal, results,
+                                                    nn_values, vl_paths, vl_lengths, B, total, max_nodes,
+                                                    q_penalty=0.0):
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        self._expand(tree, True, True, child_init_q, child_q_values, leaf_indices, leaf_states, legal_moves,
+                     num_legal, priors_per_legal, results, nn_values, vl_paths, vl_lengths, B, total, max_nodes,
+                     q_penalty, False)
+
+    def mcts_backprop_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, leaf_indices, nn_values,
+                            vl_paths, vl_lengths, was_expanded, B, total, max_nodes):
+        import ctypes
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        ts = self._tree(tree, max_nodes, B)
+        dev = vc.device
+        leaf_indices = _need(leaf_indices, "leaf_indices", torch.int32, total)
+        nn_values = _need(nn_values.reshape(-1), "nn_values", torch.float32, total)
+        vl_paths = _need(vl_paths, "vl_paths", torch.int32, total)
+        vl_lengths = _need(vl_lengths, "vl_lengths", torch.int32, total)
+        was_expanded = _need(was_expanded, "was_expanded", torch.int8, total)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_backprop(ctypes.byref(ts), _ptr(leaf_indices), _ptr(nn_values),
+                                                  _ptr(vl_paths), _ptr(vl_lengths), _ptr(was_expanded), B, total,
+                                                  _stream(dev)), "mcts_backprop")
+
+    def mcts_extract_policy_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, move_numbers,
+                                  root_nodes, temperature, temp_drop_move, pruning_threshold, B, max_nodes):
+        import ctypes
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        ts = self._tree(tree, max_nodes, B)
+        dev = vc.device
+        move_numbers = _need(move_numbers.to(torch.int32), "move_numbers", torch.int32, B)
+        root_nodes = _need(root_nodes, "root_nodes", torch.int32, B)
+        pol = torch.zeros((B, ACTION_SPACE_SIZE), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_extract_policy(ctypes.byref(ts), _ptr(pol), _ptr(move_numbers),
+                                                        _ptr(root_nodes), float(temperature), int(temp_drop_move),
+                                                        float(pruning_threshold), B, _stream(dev)),
+                       "mcts_extract_policy")
+        return pol
+
+    def mcts_apply_root_noise(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, noise, root_nodes,
+                              max_children_pad, dir_eps, root_policy_temp, B, max_nodes):
+        import ctypes
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        ts = self._tree(tree, max_nodes, B)
+        dev = vc.device
+        noise = _need(noise, "noise", torch.float32, B)
+        root_nodes = _need(root_nodes, "root_nodes", torch.int32, B)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_root_noise(ctypes.byref(ts), _ptr(noise), _ptr(root_nodes),
+                                                    int(max_children_pad), float(dir_eps), float(root_policy_temp),
+                                                    B, _stream(dev)), "mcts_apply_root_noise")
+
+    def mcts_select_replay_legal_fnn_root_slots_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt,
+                                                      child_init_q, root_states, game_active, root_nodes,
+                                                      root_slots, num_candidates, max_root_children, c_puct, B, W,
+                                                      max_nodes, deterministic_non_root=False, non_root_sigma=4.0,
+                                                      q_penalty=0.0):
+        """Fused prefix of one Gumbel wave (game_logic.cu:1184-1254): root-slot
+        select, replay, result check, legal moves + FNN features of the leaves."""
+        leaf, paths, plen, vlp, vll = self.mcts_select_with_root_slots_batch(
+            vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, child_init_q, game_active, root_nodes, root_slots,
+            num_candidates, max_root_children, c_puct, B, W, max_nodes, deterministic_non_root, non_root_sigma,
+            q_penalty)
+        total = leaf.shape[0]
+        leaf_states = torch.zeros((total, SIZEOF_HIVE_STATE), dtype=torch.uint8, device=leaf.device)
+        self.mcts_replay_batch(root_states, leaf_states, paths, plen, leaf, B, total)
+        results = self.check_results_batch(leaf_states, total)
+        legal, num_legal, feats = self.generate_legal_moves_and_fnn_features_batch(leaf_states, total)
+        return leaf, leaf_states, legal, num_legal, feats, results, vlp, vll
+
     # -- inputs for benchmarks and tests --------------------------------------
     def generate_positions(self, seed: int, first_game: int, count: int, max_ply: int,
                            expansion_mask: int = 0, device: str | torch.device = "cuda") -> torch.Tensor:

@@ -95,6 +95,80 @@ int hv_fnn_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const 
 /* number of floats hv_fnn_eval_leaves expects in `weights` */
 int hv_fnn_weights_size(int hidden, int embed, int action_hidden);
 
+/* ---------------------------------------------------------------------------
+ * MCTS tree: the reference's SoA tree (hive_gpu/csrc/mcts_tree.cuh:31-45),
+ * per-game arrays [B, max_nodes] in the binding order of bindings.cpp:130-135.
+ * Every tree entry point processes the simulations of one game in
+ * simulation-index order (sim = j * B + game), which is the reference's
+ * kernel semantics with its concurrent simulations serialised: results are
+ * deterministic and equal to the reference kernels run one simulation at a
+ * time in index order.
+ * ------------------------------------------------------------------------- */
+typedef struct hv_tree {
+    int32_t* visit_count;      /* [B, max_nodes] */
+    float* total_value;        /* [B, max_nodes] */
+    float* prior;              /* [B, max_nodes] */
+    int32_t* parent_idx;       /* [B, max_nodes], -1 = none */
+    float* virtual_q_penalty;  /* [B, max_nodes] */
+    uint8_t* move_bytes;       /* [B, max_nodes, 6] */
+    int32_t* action_idx;       /* [B, max_nodes], -1 = none */
+    int32_t* first_child;      /* [B, max_nodes], -1 = unexpanded */
+    int32_t* num_children;     /* [B, max_nodes] */
+    int8_t* is_terminal;       /* [B, max_nodes] */
+    float* terminal_value;     /* [B, max_nodes] */
+    int32_t* node_count;       /* [B] */
+    int32_t max_nodes;
+} hv_tree;
+
+/* Selection with virtual loss.  mode 0: mcts_select_batch (bindings.cpp:
+ * 112-116, mcts_tree.cuh:205-291), W * B simulations; mode 1:
+ * mcts_select_with_root_mask_batch (:166-175, :689-800) with alive_mask
+ * [B, max_root_children]; mode 2: mcts_select_with_root_slots_batch
+ * (:177-186, :811-955) with root_slots [B, num_candidates], W * C * B
+ * simulations.  Outputs leaf [T], move_paths [T,128,6], path_len [T],
+ * vl_paths [T,128], vl_len [T]. */
+int hv_mcts_select(const hv_tree* tree, int mode, const float* child_init_q, const int8_t* game_active,
+                   const int32_t* root_nodes, const int8_t* alive_mask, const int32_t* root_slots,
+                   int num_candidates, int max_root_children, float c_puct, int B, int W,
+                   int deterministic_non_root, float non_root_sigma, float q_penalty, int32_t* leaf,
+                   uint8_t* move_paths, int32_t* path_len, int32_t* vl_paths, int32_t* vl_len,
+                   void* stream);
+
+/* mcts_replay_batch (bindings.cpp:118-121, mcts_tree.cuh:298-320):
+ * leaf_states[s] = root_states[s % B] + move path s. */
+int hv_mcts_replay(const uint8_t* root_states, uint8_t* leaf_states, const uint8_t* move_paths,
+                   const int32_t* path_len, const int32_t* leaf, int B, int total, void* stream);
+
+/* Expansion, optionally fused with the backup.
+ * dense=1: per-legal priors [T,256] + child_q -> child_init_q
+ *   (mcts_expand_dense_priors_batch / ..._and_backprop_dense_priors_batch,
+ *    bindings.cpp:200-219, mcts_tree.cuh:971-1187);
+ * dense=0: action-space priors [T,85834] (mcts_expand_batch /
+ *   mcts_expand_and_backprop_batch, bindings.cpp:123-147, :330-549).
+ * was_expanded [T] is written when backprop=0 (may be NULL). */
+int hv_mcts_expand(const hv_tree* tree, int dense, int backprop, float* child_init_q,
+                   const float* child_q, const int32_t* leaf, const uint8_t* leaf_states,
+                   const uint8_t* legal_moves, const int32_t* num_legal, const float* priors,
+                   const int32_t* results, const float* values, const int32_t* vl_paths,
+                   const int32_t* vl_len, int8_t* was_expanded, float q_penalty, int B, int total,
+                   void* stream);
+
+/* mcts_backprop_batch (bindings.cpp:131-136, mcts_tree.cuh:555-605). */
+int hv_mcts_backprop(const hv_tree* tree, const int32_t* leaf, const float* values,
+                     const int32_t* vl_paths, const int32_t* vl_len, const int8_t* was_expanded, int B,
+                     int total, void* stream);
+
+/* mcts_apply_root_noise (bindings.cpp:221-226, mcts_tree.cuh:1192-1234). */
+int hv_mcts_root_noise(const hv_tree* tree, const float* noise, const int32_t* root_nodes,
+                       int max_children_pad, float dir_eps, float root_policy_temp, int B,
+                       void* stream);
+
+/* mcts_extract_policy_batch (bindings.cpp:149-155, mcts_tree.cuh:607-684):
+ * policies [B, 85834] must be zeroed by the caller. */
+int hv_mcts_extract_policy(const hv_tree* tree, float* policies, const int32_t* move_numbers,
+                           const int32_t* root_nodes, float temperature, int temp_drop_move,
+                           float pruning_threshold, int B, void* stream);
+
 /* apply_moves_batch(states, moves, batch_size)
  * replaces bindings.cpp:272-274 / game_logic.cu:465-477.  moves: [batch, 6]. */
 int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream);

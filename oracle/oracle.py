@@ -162,3 +162,150 @@ def ref() -> _Lib:
             return None
         _ref = _Lib(os.path.join(HERE, "_ref", "libhive_ref.so"), "ref_")
     return _ref
+
+
+# ---------------------------------------------------------------------------
+# MCTS tree arrays and the sequential tree operations (orc_mcts_* / ref_mcts_*)
+# ---------------------------------------------------------------------------
+class _TreePtrs(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("vc", "tv", "pr", "pa", "vq", "mb", "ai", "fc", "nc", "it",
+                                          "tval", "cnt")] + [("max_nodes", C.c_int32)]
+
+
+TREE_FIELDS = (("visit_count", np.int32, 0), ("total_value", np.float32, 0), ("prior", np.float32, 0),
+               ("parent_idx", np.int32, -1), ("virtual_q_penalty", np.float32, 0),
+               ("move_bytes", np.uint8, 0), ("action_idx", np.int32, -1), ("first_child", np.int32, -1),
+               ("num_children", np.int32, 0), ("is_terminal", np.int8, 0), ("terminal_value", np.float32, 0),
+               ("node_count", np.int32, 1))
+
+
+class TreeArrays:
+    """numpy copy of the reference's SoA tree (binding order of bindings.cpp:130-135)."""
+
+    def __init__(self, B: int, max_nodes: int):
+        self.B, self.max_nodes = B, max_nodes
+        for name, dt, fill in TREE_FIELDS:
+            shape = (B,) if name == "node_count" else ((B, max_nodes, 6) if name == "move_bytes" else (B, max_nodes))
+            setattr(self, name, np.full(shape, fill, dtype=dt))
+        self.child_init_q = np.zeros((B, max_nodes), np.float32)
+
+    def copy(self) -> "TreeArrays":
+        t = TreeArrays.__new__(TreeArrays)
+        t.B, t.max_nodes = self.B, self.max_nodes
+        for name, _, _ in TREE_FIELDS:
+            setattr(t, name, getattr(self, name).copy())
+        t.child_init_q = self.child_init_q.copy()
+        return t
+
+    def arrays(self):
+        return [getattr(self, n) for n, _, _ in TREE_FIELDS]
+
+    def ptrs(self) -> _TreePtrs:
+        a = self.arrays()
+        return _TreePtrs(*[x.ctypes.data for x in a], self.max_nodes)
+
+    def equal(self, other: "TreeArrays") -> list[str]:
+        bad = []
+        for name, _, _ in TREE_FIELDS + (("child_init_q", None, None),):
+            x, y = getattr(self, name), getattr(other, name)
+            if x.dtype == np.float32:
+                x, y = x.view(np.uint32), y.view(np.uint32)
+            if not np.array_equal(x, y):
+                bad.append(name)
+        return bad
+
+
+def _p(a):
+    return None if a is None else np.ascontiguousarray(a).ctypes.data
+
+
+def mcts_select(lib_name: str, tree: TreeArrays, mode: int, game_active, root_nodes, alive_mask=None,
+                root_slots=None, num_candidates=1, max_root_children=256, c_puct=1.25, W=1, det=False,
+                sigma=4.0, q_penalty=0.0):
+    lib = (oracle() if lib_name == "orc" else ref()).lib
+    fn = getattr(lib, f"{lib_name}_mcts_select")
+    B = tree.B
+    total = W * num_candidates * B if mode == 2 else W * B
+    leaf = np.zeros(total, np.int32)
+    paths = np.zeros((total, 128, 6), np.uint8)
+    plen = np.zeros(total, np.int32)
+    vlp = np.zeros((total, 128), np.int32)
+    vll = np.zeros(total, np.int32)
+    ptrs = tree.ptrs()
+    fn(C.byref(ptrs), C.c_int(mode), C.c_void_p(tree.child_init_q.ctypes.data),
+       C.c_void_p(_p(game_active)), C.c_void_p(_p(root_nodes)), C.c_void_p(_p(alive_mask)),
+       C.c_void_p(_p(root_slots)), C.c_int(num_candidates), C.c_int(max_root_children),
+       C.c_float(c_puct), C.c_int(B), C.c_int(W), C.c_int(int(det)), C.c_float(sigma), C.c_float(q_penalty),
+       C.c_void_p(leaf.ctypes.data), C.c_void_p(paths.ctypes.data), C.c_void_p(plen.ctypes.data),
+       C.c_void_p(vlp.ctypes.data), C.c_void_p(vll.ctypes.data))
+    return leaf, paths, plen, vlp, vll
+
+
+def mcts_replay(lib_name: str, root_states, paths, plen, leaf, B):
+    lib = (oracle() if lib_name == "orc" else ref()).lib
+    total = len(leaf)
+    out = np.zeros((total, STATE_BYTES), np.uint8)
+    rs = np.ascontiguousarray(root_states)
+    getattr(lib, f"{lib_name}_mcts_replay")(C.c_void_p(rs.ctypes.data), C.c_void_p(out.ctypes.data),
+                                            C.c_void_p(paths.ctypes.data), C.c_void_p(plen.ctypes.data),
+                                            C.c_void_p(leaf.ctypes.data), C.c_int(B), C.c_int(total))
+    return out
+
+
+def mcts_expand_dense(lib_name: str, tree: TreeArrays, child_q, leaf, leaf_states, legal, num_legal,
+                      priors, results, values=None, vl_paths=None, vl_len=None, q_penalty=0.0,
+                      with_backprop=True):
+    lib = (oracle() if lib_name == "orc" else ref()).lib
+    total = len(leaf)
+    was = np.zeros(total, np.int8)
+    keep = [np.ascontiguousarray(x) for x in (child_q, leaf, leaf_states, legal, num_legal, priors, results)]
+    vals = np.ascontiguousarray(values if values is not None else np.zeros(total, np.float32))
+    vlp = np.ascontiguousarray(vl_paths if vl_paths is not None else np.zeros((total, 128), np.int32))
+    vll = np.ascontiguousarray(vl_len if vl_len is not None else np.zeros(total, np.int32))
+    ptrs = tree.ptrs()
+    getattr(lib, f"{lib_name}_mcts_expand_dense")(
+        C.byref(ptrs), C.c_void_p(tree.child_init_q.ctypes.data), *[C.c_void_p(k.ctypes.data) for k in keep],
+        C.c_void_p(vals.ctypes.data), C.c_void_p(vlp.ctypes.data), C.c_void_p(vll.ctypes.data),
+        C.c_int(tree.B), C.c_int(total), C.c_float(q_penalty), C.c_int(int(with_backprop)),
+        C.c_void_p(was.ctypes.data))
+    return was
+
+
+def mcts_expand_action(lib_name: str, tree: TreeArrays, mode: int, leaf, leaf_states, legal, num_legal,
+                       probs, results, values=None, vl_paths=None, vl_len=None, was_expanded=None):
+    lib = (oracle() if lib_name == "orc" else ref()).lib
+    total = len(leaf)
+    was = np.ascontiguousarray(was_expanded if was_expanded is not None else np.zeros(total, np.int8))
+    keep = [np.ascontiguousarray(x) for x in (leaf, leaf_states, legal, num_legal, probs, results)]
+    vals = np.ascontiguousarray(values if values is not None else np.zeros(total, np.float32))
+    vlp = np.ascontiguousarray(vl_paths if vl_paths is not None else np.zeros((total, 128), np.int32))
+    vll = np.ascontiguousarray(vl_len if vl_len is not None else np.zeros(total, np.int32))
+    ptrs = tree.ptrs()
+    getattr(lib, f"{lib_name}_mcts_expand_action")(
+        C.byref(ptrs), *[C.c_void_p(k.ctypes.data) for k in keep], C.c_void_p(vals.ctypes.data),
+        C.c_void_p(vlp.ctypes.data), C.c_void_p(vll.ctypes.data), C.c_int(tree.B), C.c_int(total),
+        C.c_int(mode), C.c_void_p(was.ctypes.data))
+    return was
+
+
+def mcts_extract_policy(lib_name: str, tree: TreeArrays, move_numbers, root_nodes, temperature,
+                        temp_drop_move, pruning_threshold):
+    lib = (oracle() if lib_name == "orc" else ref()).lib
+    pol = np.zeros((tree.B, 85834), np.float32)
+    mn = np.ascontiguousarray(move_numbers, np.int32)
+    rn = np.ascontiguousarray(root_nodes, np.int32)
+    ptrs = tree.ptrs()
+    getattr(lib, f"{lib_name}_mcts_extract_policy")(
+        C.byref(ptrs), C.c_void_p(pol.ctypes.data), C.c_void_p(mn.ctypes.data), C.c_void_p(rn.ctypes.data),
+        C.c_float(temperature), C.c_int(temp_drop_move), C.c_float(pruning_threshold), C.c_int(tree.B))
+    return pol
+
+
+def mcts_root_noise(lib_name: str, tree: TreeArrays, noise, root_nodes, dir_eps, root_policy_temp):
+    lib = (oracle() if lib_name == "orc" else ref()).lib
+    nz = np.ascontiguousarray(noise, np.float32)
+    rn = np.ascontiguousarray(root_nodes, np.int32)
+    ptrs = tree.ptrs()
+    getattr(lib, f"{lib_name}_mcts_root_noise")(
+        C.byref(ptrs), C.c_void_p(nz.ctypes.data), C.c_void_p(rn.ctypes.data), C.c_int(nz.shape[1]),
+        C.c_float(dir_eps), C.c_float(root_policy_temp), C.c_int(tree.B))

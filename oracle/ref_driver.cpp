@@ -230,3 +230,160 @@ void ref_queen_escape_batch(const uint8_t* states, int64_t count, uint8_t* flags
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// MCTS: the reference's tree kernels (mcts_tree.cuh) executed sequentially in
+// simulation-index order on the host.  This is the defined order the B200
+// kernels reproduce (the reference's own GPU launch races when several
+// simulations of one game share a wave).
+// ---------------------------------------------------------------------------
+struct ref_tree_ptrs {
+    int32_t* visit_count;
+    float* total_value;
+    float* prior;
+    int32_t* parent_idx;
+    float* virtual_q_penalty;
+    uint8_t* move_bytes;
+    int32_t* action_idx;
+    int32_t* first_child;
+    int32_t* num_children;
+    int8_t* is_terminal;
+    float* terminal_value;
+    int32_t* node_count;
+    int32_t max_nodes;
+};
+
+static MCTSTree to_tree(const ref_tree_ptrs* p) {
+    MCTSTree t;
+    t.visit_count = p->visit_count;
+    t.total_value = p->total_value;
+    t.prior = p->prior;
+    t.virtual_q_penalty = p->virtual_q_penalty;
+    t.parent_idx = p->parent_idx;
+    t.move_bytes = p->move_bytes;
+    t.action_idx = p->action_idx;
+    t.first_child = p->first_child;
+    t.num_children = p->num_children;
+    t.is_terminal = p->is_terminal;
+    t.terminal_value = p->terminal_value;
+    t.node_count = p->node_count;
+    t.max_nodes = p->max_nodes;
+    return t;
+}
+
+static inline void as_thread(int sim) {
+    blockIdx.x = (unsigned)sim;
+    threadIdx.x = 0;
+}
+
+extern "C" {
+
+void ref_mcts_select(const ref_tree_ptrs* tp, int mode, const float* child_init_q,
+                     const int8_t* game_active, const int32_t* root_nodes, const int8_t* alive_mask,
+                     const int32_t* root_slots, int num_candidates, int max_root_children,
+                     float c_puct, int B, int W, int deterministic_non_root, float non_root_sigma,
+                     float q_penalty, int32_t* leaf, uint8_t* move_paths, int32_t* path_len,
+                     int32_t* vl_paths, int32_t* vl_len) {
+    tables_once();
+    MCTSTree t = to_tree(tp);
+    int total = mode == 2 ? W * num_candidates * B : W * B;
+    for (int s = 0; s < total; s++) {
+        as_thread(s);
+        if (mode == 0)
+            mcts_select_kernel(t, leaf, move_paths, path_len, vl_paths, vl_len, game_active,
+                               root_nodes, c_puct, B, total);
+        else if (mode == 1)
+            mcts_select_with_root_mask_kernel(t, leaf, move_paths, path_len, vl_paths, vl_len,
+                                              game_active, root_nodes, alive_mask,
+                                              max_root_children, c_puct,
+                                              deterministic_non_root != 0, non_root_sigma,
+                                              q_penalty, child_init_q, B, total);
+        else
+            mcts_select_with_root_slots_kernel(t, leaf, move_paths, path_len, vl_paths, vl_len,
+                                               game_active, root_nodes, root_slots, num_candidates,
+                                               max_root_children, c_puct,
+                                               deterministic_non_root != 0, non_root_sigma,
+                                               q_penalty, child_init_q, B, total);
+    }
+}
+
+void ref_mcts_replay(const uint8_t* root_states, uint8_t* leaf_states, const uint8_t* move_paths,
+                     const int32_t* path_len, const int32_t* leaf, int B, int total) {
+    tables_once();
+    for (int s = 0; s < total; s++) {
+        as_thread(s);
+        mcts_replay_kernel(reinterpret_cast<const HiveState*>(root_states),
+                           reinterpret_cast<HiveState*>(leaf_states), move_paths, path_len, leaf, B,
+                           total);
+    }
+}
+
+// dense-prior expansion, optionally fused with the backup
+void ref_mcts_expand_dense(const ref_tree_ptrs* tp, float* child_init_q, const float* child_q,
+                           const int32_t* leaf, const uint8_t* leaf_states, const uint8_t* legal,
+                           const int32_t* num_legal, const float* priors, const int32_t* results,
+                           const float* values, const int32_t* vl_paths, const int32_t* vl_len,
+                           int B, int total, float q_penalty, int with_backprop,
+                           int8_t* was_expanded) {
+    tables_once();
+    MCTSTree t = to_tree(tp);
+    for (int s = 0; s < total; s++) {
+        as_thread(s);
+        if (with_backprop)
+            mcts_expand_and_backprop_dense_priors_kernel(
+                t, leaf, reinterpret_cast<const HiveState*>(leaf_states),
+                reinterpret_cast<const GPUMove*>(legal), num_legal, priors, child_q, child_init_q,
+                results, values, vl_paths, vl_len, q_penalty, B, total);
+        else
+            mcts_expand_dense_priors_kernel(t, leaf, reinterpret_cast<const HiveState*>(leaf_states),
+                                            reinterpret_cast<const GPUMove*>(legal), num_legal,
+                                            priors, child_q, child_init_q, results, was_expanded, B,
+                                            total);
+    }
+}
+
+// action-space expansion / backup (legacy path)
+void ref_mcts_expand_action(const ref_tree_ptrs* tp, const int32_t* leaf, const uint8_t* leaf_states,
+                            const uint8_t* legal, const int32_t* num_legal, const float* probs,
+                            const int32_t* results, const float* values, const int32_t* vl_paths,
+                            const int32_t* vl_len, int B, int total, int mode, int8_t* was_expanded) {
+    tables_once();
+    MCTSTree t = to_tree(tp);
+    for (int s = 0; s < total; s++) {
+        as_thread(s);
+        if (mode == 0)
+            mcts_expand_kernel(t, leaf, reinterpret_cast<const HiveState*>(leaf_states),
+                               reinterpret_cast<const GPUMove*>(legal), num_legal, probs, results,
+                               was_expanded, B, total);
+        else if (mode == 1)
+            mcts_expand_and_backprop_kernel(t, leaf, reinterpret_cast<const HiveState*>(leaf_states),
+                                            reinterpret_cast<const GPUMove*>(legal), num_legal, probs,
+                                            results, values, vl_paths, vl_len, B, total);
+        else
+            mcts_backprop_kernel(t, leaf, values, vl_paths, vl_len, was_expanded, B, total);
+    }
+}
+
+void ref_mcts_extract_policy(const ref_tree_ptrs* tp, float* policies, const int32_t* move_numbers,
+                             const int32_t* root_nodes, float temperature, int temp_drop_move,
+                             float pruning_threshold, int B) {
+    tables_once();
+    MCTSTree t = to_tree(tp);
+    for (int g = 0; g < B; g++) {
+        as_thread(g);
+        mcts_extract_policy_kernel(t, policies, move_numbers, root_nodes, temperature,
+                                   temp_drop_move, pruning_threshold, B);
+    }
+}
+
+void ref_mcts_root_noise(const ref_tree_ptrs* tp, const float* noise, const int32_t* root_nodes,
+                         int max_children_pad, float dir_eps, float root_policy_temp, int B) {
+    tables_once();
+    MCTSTree t = to_tree(tp);
+    for (int g = 0; g < B; g++) {
+        as_thread(g);
+        mcts_root_noise_kernel(t, noise, root_nodes, max_children_pad, dir_eps, root_policy_temp, B);
+    }
+}
+
+}  // extern "C"
