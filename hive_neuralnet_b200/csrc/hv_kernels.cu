@@ -224,6 +224,107 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
 }
 
 // ---------------------------------------------------------------------------
+// queen escape flags (game_logic.cu:133-142, move_gen.cuh:771-821): can the
+// side to move's queen slide away, or be thrown by an own pillbug / a ground
+// mosquito next to a pillbug?
+// ---------------------------------------------------------------------------
+// queen escape of the staged state (move_gen.cuh:771-821); warp-uniform result
+__device__ __noinline__ bool queen_escape_staged(WarpSmem* w) {
+    Pos P{w};
+    const int color = P.turn() & 1;
+    const int q = P.queen_cell(color);
+    if (!((P.queen_placed() >> color) & 1) || q < 0 || q >= kPCells || (q & 31) >= kBoard) return false;
+    Setup S = setup_position(w);
+    if (!P.occupied(q)) return false;
+    const int top = P.top(q);
+    const int qi = P.pidx(q);
+    const bool pinned = qi < 32 && (w->pflag[qi] & 1);
+    if ((top & 15) == 1 && ((top >> 4) & 1) == color && !pinned && walk(w, q, WM_STEP, w->dst, 6, true))
+        return true;
+    int mt = S.my_top & 15;
+    bool mine = S.my_cell >= 0 && rowbit(w->own, S.my_cell);
+    bool adj = S.my_cell >= 0 && hex_distance(S.my_cell, q) == 1;
+    bool thr = mine && adj && (mt == 8 || (mt == 6 && S.my_h == 1 && next_to_pillbug(w, S.my_cell)));
+    uint32_t throwers = __ballot_sync(kFull, thr);
+    while (throwers) {
+        int i = __ffs(throwers) - 1;
+        throwers &= throwers - 1;
+        int pb = w->pcell[i];
+        uint32_t tm, dm;
+        throw_sets(w, pb, tm, dm);
+        int dq = -1;
+        for (int d = 0; d < 6; d++)
+            if (nbr(pb, d) == q) dq = d;
+        if (dq >= 0 && ((tm >> dq) & 1) && dm) return true;
+    }
+    return false;
+}
+
+// Per (state, legal slot): apply the move to a copy and report the child's
+// result, the number of occupied neighbours of the child's side-to-move
+// queen (0 if unplaced) and, optionally, whether that queen can escape.
+// Backs FNNMCTSOrchestrator._find_immediate_wins (fnn_mcts_orchestrator.py:
+// 446-493) and _queen_surround_qualifying_mask (:339-382).
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_child_probe(
+    const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal,
+    const int32_t* __restrict__ num_legal, int64_t batch, int want_escape,
+    int32_t* __restrict__ results, int32_t* __restrict__ surround, uint8_t* __restrict__ escape) {
+    WarpSmem* w = warp_slot();
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        int n = num_legal[p];
+        n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
+        for (int m = l; m < kMaxMoves; m += 32) {
+            if (m < n) continue;
+            results[p * kMaxMoves + m] = 0;
+            surround[p * kMaxMoves + m] = 0;
+            if (escape) escape[p * kMaxMoves + m] = 0;
+        }
+        for (int m = 0; m < n; m++) {
+            stage_state(w, states + p * kStateBytes);
+            if (l == 0) {
+                const uint8_t* x = legal + (p * kMaxMoves + m) * kMoveBytes;
+                st_apply(w->st, x[0], x[1], x[2] | (x[3] << 8), x[4] | (x[5] << 8));
+            }
+            __syncwarp();
+            Pos P{w};
+            const int color = P.turn() & 1;
+            // occupied (height > 0) neighbours of the queen cell field, as
+            // _queen_surround_count (fnn_mcts_orchestrator.py:318-337) reads it
+            int cnt = 0;
+            int qc = w->st[kOffQCell + 2 * color] | (w->st[kOffQCell + 2 * color + 1] << 8);
+            if (qc != 0xFFFF) {
+                const int q = c_to_p(qc < kCells ? qc : kCells - 1);
+                int nb = l < 6 ? nbr(q, l) : -1;
+                cnt = __popc(__ballot_sync(kFull, nb >= 0 && P.height(nb) > 0));
+            }
+            bool esc = want_escape ? queen_escape_staged(w) : false;
+            if (l == 0) {
+                results[p * kMaxMoves + m] = w->st[kOffResult];
+                surround[p * kMaxMoves + m] = cnt;
+                if (escape) escape[p * kMaxMoves + m] = esc ? 1 : 0;
+            }
+            __syncwarp();
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_queen_escape(
+    const uint8_t* __restrict__ states, int64_t batch, uint8_t* __restrict__ flags) {
+    WarpSmem* w = warp_slot();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        stage_state(w, states + p * kStateBytes);
+        bool esc = queen_escape_staged(w);
+        if (lane_id() == 0) flags[p] = esc ? 1 : 0;
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // MCTS tree kernels: one warp per game (hv_mcts.cuh)
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) k_mcts_select(TreeDev t, SelectArgs a) {
@@ -741,6 +842,34 @@ int hv_mcts_extract_policy(const hv_tree* tree, float* policies, const int32_t* 
     k_mcts_extract_policy<<<(B + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
         tree_dev(tree), policies, move_numbers, root_nodes, temperature, temp_drop_move,
         pruning_threshold, B);
+    return launch_status();
+}
+
+int hv_queen_escape_flags(const uint8_t* states, int64_t batch, uint8_t* flags, void* stream) {
+    if (batch < 0 || (batch && (!states || !flags || !aligned16(states)))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_queen_escape, batch, smem, &grid);
+    if (rc) return rc;
+    k_queen_escape<<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, batch, flags);
+    return launch_status();
+}
+
+int hv_child_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                   int64_t batch, int want_escape, int32_t* results, int32_t* surround,
+                   uint8_t* escape, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!states || !legal_moves || !num_legal || !results || !surround || !aligned16(states) ||
+        (want_escape && !escape))
+        return HV_EINVAL;
+    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_child_probe, batch, smem, &grid);
+    if (rc) return rc;
+    k_child_probe<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+        states, legal_moves, num_legal, batch, want_escape, results, surround, escape);
     return launch_status();
 }
 

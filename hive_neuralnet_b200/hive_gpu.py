@@ -185,6 +185,31 @@ class HiveGPUExtension:
                        "check_results_batch")
         return out
 
+    def queen_escape_flags_batch(self, states: torch.Tensor, batch_size: int) -> torch.Tensor:
+        states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
+        dev = states.device
+        out = torch.empty((batch_size,), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_queen_escape_flags(_ptr(states), batch_size, _ptr(out), _stream(dev)),
+                       "queen_escape_flags_batch")
+        return out
+
+    def child_probe_batch(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
+                          batch_size: int, want_escape: bool = False):
+        """(results, queen_surround, queen_escape) of every legal child, [B, 256] each."""
+        states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
+        legal_moves = _need(legal_moves, "legal_moves", torch.uint8, batch_size, (MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE))
+        num_legal = _need(num_legal, "num_legal", torch.int32, batch_size)
+        dev = states.device
+        res = torch.empty((batch_size, MAX_LEGAL_MOVES), dtype=torch.int32, device=dev)
+        sur = torch.empty((batch_size, MAX_LEGAL_MOVES), dtype=torch.int32, device=dev)
+        esc = torch.empty((batch_size, MAX_LEGAL_MOVES), dtype=torch.uint8, device=dev) if want_escape else None
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_child_probe(_ptr(states), _ptr(legal_moves), _ptr(num_legal), batch_size,
+                                                int(want_escape), _ptr(res), _ptr(sur), _ptr(esc), _stream(dev)),
+                       "child_probe")
+        return res, sur, esc
+
     def compute_centroids_batch(self, states: torch.Tensor, batch_size: int) -> torch.Tensor:
         states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
         dev = states.device

@@ -169,6 +169,22 @@ int hv_mcts_extract_policy(const hv_tree* tree, float* policies, const int32_t* 
                            const int32_t* root_nodes, float temperature, int temp_drop_move,
                            float pruning_threshold, int B, void* stream);
 
+/* queen_escape_flags_batch(states, batch_size) replaces bindings.cpp:339-342 /
+ * game_logic.cu:1538-1554: flags[b] = 1 when the side to move's queen has a
+ * slide or a pillbug / pillbug-adjacent mosquito throw (move_gen.cuh:771-821). */
+int hv_queen_escape_flags(const uint8_t* states, int64_t batch, uint8_t* flags, void* stream);
+
+/* Per (state b, legal slot m < num_legal[b]): the child after move m, its
+ * result (check_results), the occupied-neighbour count of the child's
+ * side-to-move queen and (want_escape) its queen-escape flag; outputs
+ * [batch, 256], zero past num_legal.  Replaces the per-successor
+ * apply_moves_batch + check_results_batch + queen_escape_flags_batch
+ * passes of FNNMCTSOrchestrator._find_immediate_wins and
+ * _queen_surround_qualifying_mask (hive_fnn/fnn_mcts_orchestrator.py:339-493). */
+int hv_child_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                   int64_t batch, int want_escape, int32_t* results, int32_t* surround,
+                   uint8_t* escape, void* stream);
+
 /* apply_moves_batch(states, moves, batch_size)
  * replaces bindings.cpp:272-274 / game_logic.cu:465-477.  moves: [batch, 6]. */
 int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream);
