@@ -132,3 +132,30 @@ def test_state_ops(ext, orc):
 
 def test_device_error_word_clean(ext):
     assert ext.device_error_word(clear=True) == 0
+
+
+def test_queen_escape_and_child_probe(ext, orc):
+    st = np.concatenate([orc.generate_positions(808, 0, 1024, 120, 7), orc.generate_positions(809, 0, 1024, 60, 0)])
+    qe = ext.queen_escape_flags_batch(_cuda(st), len(st)).cpu().numpy()
+    assert np.array_equal(qe, orc.queen_escape(st))
+    mo, no, _ = orc.legal_moves_features(st)
+    sub = st[:256]
+    res, sur, esc = (x.cpu().numpy() for x in ext.child_probe_batch(_cuda(sub), _cuda(mo[:256]), _cuda(no[:256]),
+                                                                     256, True))
+    for i in range(0, 256, 5):
+        n = no[i]
+        kids = orc.apply_moves(np.repeat(sub[i:i + 1], n, 0), mo[i, :n])
+        assert np.array_equal(res[i, :n], kids[:, 3415].astype(np.int32))
+        assert np.array_equal(esc[i, :n], orc.queen_escape(kids))
+        assert (res[i, n:] == 0).all() and (sur[i, n:] == 0).all()
+        for j in range(n):
+            k = kids[j]
+            color = int(k[3412]) & 1
+            qc = int(k[3392 + 2 * color]) | (int(k[3393 + 2 * color]) << 8)
+            want = 0
+            if qc != 0xFFFF:
+                r, c = divmod(qc, 23)
+                for dr, dc in ((0, 1), (-1, 1), (-1, 0), (0, -1), (1, -1), (1, 0)):
+                    if 0 <= r + dr < 23 and 0 <= c + dc < 23 and k[2645 + (r + dr) * 23 + c + dc] > 0:
+                        want += 1
+            assert sur[i, j] == want

@@ -16,10 +16,19 @@ pytestmark = pytest.mark.gpu
 
 
 def _start(B, seed, mask=7, max_ply=40):
+    """In-progress positions past the opening with no immediately winning
+    move (the reference PUCT driver skips the whole batch's search when any
+    game has one, fnn_puct_orchestrator.py:203-208)."""
     orc = O.oracle()
-    st = orc.generate_positions(seed, 0, 4 * B, max_ply, mask)
+    st = orc.generate_positions(seed, 0, 8 * B, max_ply, mask)
     mv, nl, _ = orc.legal_moves_features(st)
-    keep = np.where((st[:, 3415] == 0) & (nl > 3) & (st[:, 3412] >= 8))[0][:B]
+    keep = []
+    for i in np.where((st[:, 3415] == 0) & (nl > 3) & (st[:, 3412] >= 8))[0]:
+        kids = orc.apply_moves(np.repeat(st[i:i + 1], nl[i], 0), mv[i, :nl[i]])
+        if (kids[:, 3415] == 0).all():
+            keep.append(i)
+        if len(keep) == B:
+            break
     assert len(keep) == B
     return st[keep]
 
