@@ -346,9 +346,140 @@ def run_gpu(args) -> None:
         print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# secondary workloads (--workload mcts / fnn): BASELINE configs 4 and 3
+# --------------------------------------------------------------------------
+MCTS_GAMES = 512
+MCTS_SIMS = 4096
+
+
+def _mcts_start_states(ext, n, seed, device):
+    """Seeded in-progress base-game positions (ply U[0, 30]) as search roots."""
+    st = ext.generate_positions(seed, 0, n * 2, 30, 0, device=device)
+    res = ext.check_results_batch(st, n * 2)
+    keep = torch_nonzero(res == 0)[:n]
+    return st[keep].contiguous()
+
+
+def torch_nonzero(mask):
+    import torch
+    return torch.nonzero(mask, as_tuple=False).squeeze(1)
+
+
+def run_mcts(args) -> None:
+    """Config 4: Gumbel-root MCTS, 512 games/GPU, 4096 simulations per move,
+    16 considered actions, wave schedule (2, 4, 8, 16), FNN large random
+    init (seed 0), seeded Philox Gumbel noise, Dirichlet off.  One step =
+    one searched move of every game; metric = simulations per second."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from hive_neuralnet_b200.fnn import HiveFNN
+    from hive_neuralnet_b200.hive_gpu import load_extension
+    from hive_neuralnet_b200.orchestrator import FNNMCTSConfig, FNNMCTSOrchestrator
+    ext = load_extension()
+    torch.manual_seed(0)
+    net = HiveFNN()
+    games = args.games
+    cfg = FNNMCTSConfig(num_simulations=args.sims, batch_size=games, max_game_length=1, dirichlet_epsilon=0.0,
+                        seed=1234 + rank, max_tree_nodes=65536, expansion_mask=0)
+    orch = FNNMCTSOrchestrator(net, cfg, device=dev)
+    starts = [_mcts_start_states(ext, games, SEED + 97 * (rank * 1000 + i), dev) for i in range(args.warmup + args.steps)]
+    host_starts = [s.cpu() for s in starts]
+    torch.cuda.synchronize(dev)
+    for i in range(args.warmup):
+        orch.self_play_batch(host_starts[i])
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+    orch.sims_done.zero_()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, args.warmup + args.steps):
+        orch.self_play_batch(host_starts[i])  # host states in, training examples out
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    sims = orch.sims_done.to(torch.float64).reshape(1)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sims, op=dist.ReduceOp.SUM)
+    ms = float(t.item())
+    value = float(sims.item()) / (ms / 1e3)
+    if rank == 0:
+        line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": f"config4: Gumbel MCTS {games} games/GPU x {args.sims} sims/move, k=16, "
+                                       "waves (2,4,8,16), FNN large random init",
+                           "simulations": float(sims.item()), "games_per_gpu": games,
+                           "parallelism": f"games sharded dp{world}" if world > 1 else "single GPU",
+                           "l2": "tree arrays (1.6 GB/GPU) larger than L2"},
+                "e2e": {"value": value, "unit": "simulations/s",
+                        "h2d_bytes_per_step": games * STATE_BYTES, "d2h_bytes_per_step": None,
+                        "note": "start states come from host memory and training examples return to it "
+                                "inside every timed step"},
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def run_fnn(args) -> None:
+    """Config 3: fused leaf evaluation of 65,536 roots (all legal successors)
+    with FNN large (fp32, random init seed 0)."""
+    import torch
+
+    from hive_neuralnet_b200.fnn import FusedFNNEvaluator, HiveFNN
+    from hive_neuralnet_b200.hive_gpu import load_extension
+    ext = load_extension()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    ev = FusedFNNEvaluator(HiveFNN(), dev)
+    P = 65536
+    st = ext.generate_positions(SEED + 3, 0, P, MAX_PLY, EXPANSIONS, device=dev)
+    legal, nl, feats = ext.generate_legal_moves_and_fnn_features_batch(st, P)
+    for _ in range(args.warmup):
+        ev.eval_states(st, legal, nl, P, feats)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ev.eval_states(st, legal, nl, P, feats)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    succ = int(nl.sum().item())
+    flops = P * 2 * (122 * 64 + 64 * 64 + 64 + 64 * 64) + succ * 2 * (122 * 64 + 64 * 64 + 64 + 64 * 64 + 64)
+    print(json.dumps({"metric": "FNN leaf evaluations/sec", "value": P / (ms / 1e3), "unit": "roots/s",
+                      "successors_per_s": succ / (ms / 1e3), "ms_per_step": ms, "steps": args.steps,
+                      "warmup": args.warmup, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": "config3: 65536 roots x all legal successors, FNN large fp32",
+                                 "successors": succ},
+                      "mlp_tflops": flops / (ms / 1e3) / 1e12}), flush=True)
+
+
 def main() -> None:
     global POSITIONS
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=["movegen", "mcts", "fnn"], default="movegen")
+    ap.add_argument("--games", type=int, default=MCTS_GAMES)
+    ap.add_argument("--sims", type=int, default=MCTS_SIMS)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
@@ -362,6 +493,10 @@ def main() -> None:
     POSITIONS = args.positions
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "mcts":
+        run_mcts(args)
+    elif args.workload == "fnn":
+        run_fnn(args)
     else:
         run_gpu(args)
 

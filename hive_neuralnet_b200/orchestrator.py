@@ -162,6 +162,8 @@ class _SearchBase:
         else:
             self.gen.seed()
         self.trace: list | None = None  # set to a list to record per-wave evaluator outputs
+        # simulations executed (leaves with a node), accumulated on the device
+        self.sims_done = torch.zeros((), dtype=torch.int64, device=self.device)
 
     # -- tree ---------------------------------------------------------------
     def _alloc_tree(self, B: int) -> dict[str, torch.Tensor]:
@@ -377,6 +379,7 @@ class FNNMCTSOrchestrator(_SearchBase):
                     root_slots, C, self._max_legal, cfg.c_puct, B, aw, self._max_nodes, cfg.deterministic_non_root,
                     cfg.non_root_sigma, cfg.virtual_q_penalty)
             pri, vals, cq = self._eval_states(leaf_states, legal, nl, total, feats)
+            self.sims_done += (leaf >= 0).sum()
             if self.trace is not None:
                 self.trace.append(dict(kind="wave", root_slots=root_slots.clone(), W=aw, leaf=leaf.clone(),
                                        priors=pri.clone(),
@@ -564,6 +567,7 @@ class FNNPUCTOrchestrator(_SearchBase):
             results = self.ext.check_results_batch(ls, total)
             legal, nl, feats = self.ext.generate_legal_moves_and_fnn_features_batch(ls, total)
             pri, vals, cq = self._eval_states(ls, legal, nl, total, feats)
+            self.sims_done += (leaf >= 0).sum()
             if self.trace is not None:
                 self.trace.append(dict(kind="wave", W=aw, leaf=leaf.clone(), priors=pri.clone(),
                                        values=vals.clone(), child_q=cq.clone()))
