@@ -87,19 +87,20 @@ def _cpu_lib():
 
 
 def cpu_rate(states_np, threads: int, target_s: float = 12.0):
-    """positions/s of the CPU implementation over a bounded sample."""
+    """positions/s of the CPU implementation over a bounded sample: repeated
+    passes over the given positions until about target_s of work is done."""
     lib, kind = _cpu_lib()
-    probe = states_np[:2048]
+    lib.legal_moves_features(states_np[:2048], threads)  # warm-up
+    done, passes = 0, 0
     t0 = time.perf_counter()
-    lib.legal_moves_features(probe, threads)
-    dt = max(time.perf_counter() - t0, 1e-6)
-    est = len(probe) / dt
-    n = int(min(len(states_np), max(4096, est * target_s)))
-    sample = states_np[:n]
-    t0 = time.perf_counter()
-    lib.legal_moves_features(sample, threads)
-    dt = time.perf_counter() - t0
-    return n / dt, kind, n, dt
+    while True:
+        lib.legal_moves_features(states_np, threads)
+        done += len(states_np)
+        passes += 1
+        dt = time.perf_counter() - t0
+        if dt >= target_s or passes >= 1000:
+            break
+    return done / dt, kind, done, dt
 
 
 # --------------------------------------------------------------------------
