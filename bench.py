@@ -283,11 +283,9 @@ def run_gpu(args) -> None:
     e2e_steps = max(3, min(args.steps, 10))
 
     def e2e_step():
-        d_states = host_states.to(dev, non_blocking=True)
-        m, nl, f = ext.generate_legal_moves_and_fnn_features_batch(d_states, P)
-        h_moves.copy_(m, non_blocking=True)
-        h_nl.copy_(nl, non_blocking=True)
-        h_feat.copy_(f, non_blocking=True)
+        # host states in, host results out; chunked and overlapped over three streams
+        ext.generate_legal_moves_and_fnn_features_host(host_states, P, out=(h_moves, h_nl, h_feat),
+                                                       chunk=args.e2e_chunk, device=dev)
 
     for _ in range(2):
         e2e_step()
@@ -333,7 +331,9 @@ def run_gpu(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": workload_config(world),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
+                            f"{args.e2e_chunk}-position chunks over 3 streams"},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clocks,
@@ -370,7 +370,8 @@ def torch_nonzero(mask):
 def run_mcts(args) -> None:
     """Config 4: Gumbel-root MCTS, 512 games/GPU, 4096 simulations per move,
     16 considered actions, wave schedule (2, 4, 8, 16), FNN large random
-    init (seed 0), seeded Philox Gumbel noise, Dirichlet off.  One step =
+    init (seed 0), seeded Philox Gumbel noise, Dirichlet off, root tactical
+    probe on (the trainer's default).  One step =
     one searched move of every game; metric = simulations per second."""
     import torch
 
@@ -393,7 +394,8 @@ def run_mcts(args) -> None:
     net = HiveFNN()
     games = args.games
     cfg = FNNMCTSConfig(num_simulations=args.sims, batch_size=games, max_game_length=1, dirichlet_epsilon=0.0,
-                        seed=1234 + rank, max_tree_nodes=65536, expansion_mask=0)
+                        seed=1234 + rank, max_tree_nodes=65536, expansion_mask=0,
+                        short_forced_win_probe=True)
     orch = FNNMCTSOrchestrator(net, cfg, device=dev)
     starts = [_mcts_start_states(ext, games, SEED + 97 * (rank * 1000 + i), dev) for i in range(args.warmup + args.steps)]
     host_starts = [s.cpu() for s in starts]
@@ -486,6 +488,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--e2e-chunk", type=int, default=16384, help="positions per pipelined chunk of the e2e leg")
     ap.add_argument("--positions", type=int, default=POSITIONS,
                     help="positions per GPU (profiling runs use a smaller case)")
     args = ap.parse_args()

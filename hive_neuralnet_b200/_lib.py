@@ -81,6 +81,7 @@ _SIGNATURES = {
     "hv_fnn_weights_size": ([_int, _int, _int], _int),
     "hv_queen_escape_flags": ([_vp, _i64, _vp, _vp], _int),
     "hv_child_probe": ([_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _vp], _int),
+    "hv_root_tactical_probe": ([_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp, _vp, _vp], _int),
     "hv_apply_moves": ([_vp, _vp, _i64, _vp], _int),
     "hv_check_results": ([_vp, _i64, _vp, _vp], _int),
     "hv_compute_centroids": ([_vp, _i64, _vp, _vp], _int),

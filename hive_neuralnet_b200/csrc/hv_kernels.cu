@@ -17,6 +17,7 @@
 #include "hv_state.cuh"
 #include "hv_fnn.cuh"
 #include "hv_mcts.cuh"
+#include "hv_tactics.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -321,6 +322,199 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_queen_escape(
         bool esc = queen_escape_staged(w);
         if (lane_id() == 0) flags[p] = esc ? 1 : 0;
         __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// root tactical probe (game_logic.cu:290-397), five passes (hv_tactics.cuh)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int clamp_legal(int n) { return n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n); }
+
+// pass 1, warp per root: stage flags, winning = -1, allowed = slot < n
+__global__ void __launch_bounds__(kThreads) k_tac_flags(const uint8_t* __restrict__ states,
+                                                        const int32_t* __restrict__ num_legal,
+                                                        int64_t batch, int w1, int chk, int w2,
+                                                        int64_t* __restrict__ winning,
+                                                        uint8_t* __restrict__ allowed,
+                                                        uint8_t* __restrict__ flags) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        const int n = clamp_legal(num_legal[p]);
+        for (int i = l; i < kMaxMoves; i += 32) allowed[p * kMaxMoves + i] = i < n ? 1 : 0;
+        const uint8_t* st = states + p * kStateBytes;
+        const int me = st_u16(st, kOffTurn) & 1;
+        const int opp_s = surround_count(st, me ^ 1);
+        const int own_s = surround_count(st, me);
+        int f = opp_s << kTacOppShift;
+        if (n > 0 && st[kOffResult] == 0) {
+            if (w1 && opp_s == 5) f |= kTacS1;
+            if (chk && own_s == 5) f |= kTacS2;
+            if (w2 && (opp_s == 4 || opp_s == 5)) f |= kTacS3;
+        }
+        if (l == 0) {
+            winning[p] = -1;
+            flags[p] = (uint8_t)f;
+        }
+    }
+}
+
+// pass 2, warp per (root, child): does the child win at once (win-in-one
+// probe), can the opponent win at once from it (screen)?
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_tac_children(
+    const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal,
+    const int32_t* __restrict__ num_legal, int64_t batch, const uint8_t* __restrict__ flags,
+    uint8_t* __restrict__ allowed) {
+    WarpSmem* w = warp_slot();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); t < batch * kMaxMoves;
+         t += nwarps) {
+        const int64_t p = t >> 8;
+        const int i = (int)(t & 255);
+        const int f = flags[p];
+        if (!(f & (kTacS1 | kTacS2)) || i >= clamp_legal(num_legal[p])) continue;
+        const uint8_t* root = states + p * kStateBytes;
+        const uint8_t* mi = legal + (p * kMaxMoves + i) * kMoveBytes;
+        auto rebuild = [&]() {
+            stage_state(w, root);
+            if (lane_id() == 0) apply_bytes(w->st, mi);
+            __syncwarp();
+        };
+        rebuild();
+        const int me = (st_u16(w->st, kOffTurn) & 1) ^ 1;
+        int a = 1;
+        if ((f & kTacS1) && wins_for(w->st[kOffResult], me)) a |= 2;
+        if ((f & kTacS2) && immediate_win_staged(w, rebuild, &g_error)) a &= ~1;
+        if (lane_id() == 0) allowed[p * kMaxMoves + i] = (uint8_t)a;
+        __syncwarp();
+    }
+}
+
+// pass 3, warp per root: win-in-one by best prior (first of equal priors),
+// else the screen's "no safe move" verdict
+__global__ void __launch_bounds__(kThreads) k_tac_decide(const int32_t* __restrict__ num_legal,
+                                                         const float* __restrict__ priors, int64_t batch,
+                                                         int64_t* __restrict__ winning,
+                                                         uint8_t* __restrict__ allowed,
+                                                         uint8_t* __restrict__ flags) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        int f = flags[p];
+        if (!(f & (kTacS1 | kTacS2))) continue;
+        const int n = clamp_legal(num_legal[p]);
+        uint8_t* a = allowed + p * kMaxMoves;
+        int best = -1;
+        if (f & kTacS1) {
+            // sequential scan keeps the reference's comparison order exactly (NaN included)
+            if (l == 0) {
+                float bp = -1e30f;
+                for (int i = 0; i < n; i++)
+                    if ((a[i] & 2) && (best < 0 || priors[p * kMaxMoves + i] > bp)) {
+                        best = i;
+                        bp = priors[p * kMaxMoves + i];
+                    }
+            }
+            best = __shfl_sync(kFull, best, 0);
+        }
+        bool safe = false;
+        for (int i = l; i < n; i += 32) safe |= (a[i] & 1) != 0;
+        safe = __any_sync(kFull, safe);
+        if (best >= 0) {
+            f |= kTacDone;  // the probe returns before the screen: allowed stays "slot < n"
+            for (int i = l; i < kMaxMoves; i += 32) a[i] = i < n ? 1 : 0;
+            if (l == 0) winning[p] = best;
+        } else {
+            if ((f & kTacS2) && !safe) f |= kTacDone | kTacForced;
+            for (int i = l; i < kMaxMoves; i += 32) a[i] &= 1;
+        }
+        if (l == 0) flags[p] = (uint8_t)f;
+    }
+}
+
+// pass 4, warp per (root, allowed child): forced win in two -- every reply
+// keeps the opponent queen's surround from dropping and leaves a win at once
+__global__ void __launch_bounds__(kThreads, 2) k_tac_win2(const uint8_t* __restrict__ states,
+                                                          const uint8_t* __restrict__ legal,
+                                                          const int32_t* __restrict__ num_legal,
+                                                          int64_t batch, const uint8_t* __restrict__ flags,
+                                                          uint8_t* __restrict__ allowed) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    WarpSmem* w = warp_slot();
+    TacSmem* x = reinterpret_cast<TacSmem*>(smem_raw + sizeof(WarpSmem) * kWarpsPerBlock) + (threadIdx.x >> 5);
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); t < batch * kMaxMoves;
+         t += nwarps) {
+        const int64_t p = t >> 8;
+        const int i = (int)(t & 255);
+        const int f = flags[p];
+        if (!(f & kTacS3) || (f & kTacDone) || i >= clamp_legal(num_legal[p])) continue;
+        if (!(allowed[p * kMaxMoves + i] & 1)) continue;
+        stage_state(w, states + p * kStateBytes);
+        if (lane_id() == 0) apply_bytes(w->st, legal + (p * kMaxMoves + i) * kMoveBytes);
+        __syncwarp();
+        copy_state(x->child, w->st);
+        const int me = (st_u16(x->child, kOffTurn) & 1) ^ 1;
+        const int opp = me ^ 1;
+        const int opp_s = f >> kTacOppShift;
+        const int cs = surround_count(x->child, opp);
+        if (opp_s == 4 && cs <= opp_s) continue;
+        if (opp_s == 5 && cs < opp_s) continue;
+        Setup S = setup_position(w);
+        const int nr = gen_legal(w, S, &g_error);
+        for (int k = lane_id(); k < 3 * nr; k += 32) x->rep[k] = w->mv[k];
+        __syncwarp();
+        int r = 0;
+        auto rebuild = [&]() {
+            copy_state(w->st, x->child);
+            if (lane_id() == 0) apply_list(w->st, x->rep, r);
+            __syncwarp();
+        };
+        // generate_non_decreasing_surround_replies (move_gen.cuh:876-899)
+        bool ok = true;
+        for (r = 0; r < nr; r++) {
+            rebuild();
+            if (surround_count(w->st, opp) < cs) {
+                ok = false;
+                break;
+            }
+        }
+        for (r = 0; ok && r < nr; r++) {
+            rebuild();
+            if (wins_for(w->st[kOffResult], me)) continue;
+            if (!immediate_win_staged(w, rebuild, &g_error)) ok = false;
+        }
+        if (ok && lane_id() == 0) allowed[p * kMaxMoves + i] |= 4;
+        __syncwarp();
+    }
+}
+
+// pass 5, warp per root: first forced win in two; final 0/1 outputs
+__global__ void __launch_bounds__(kThreads) k_tac_final(const int32_t* __restrict__ num_legal,
+                                                        int64_t batch, int64_t* __restrict__ winning,
+                                                        uint8_t* __restrict__ allowed,
+                                                        uint8_t* __restrict__ flags) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        const int f = flags[p];
+        const int n = clamp_legal(num_legal[p]);
+        uint8_t* a = allowed + p * kMaxMoves;
+        if ((f & kTacS3) && !(f & kTacDone)) {
+            int first = -1;
+            for (int base = 0; base < n && first < 0; base += 32) {
+                const int i = base + l;
+                const uint32_t b = __ballot_sync(kFull, i < n && (a[i] & 4));
+                if (b) first = base + __ffs(b) - 1;
+            }
+            if (first >= 0 && l == 0) winning[p] = first;
+        }
+        __syncwarp();
+        for (int i = l; i < kMaxMoves; i += 32) a[i] &= 1;
+        if (l == 0) flags[p] = (f & kTacForced) ? 1 : 0;
     }
 }
 
@@ -737,6 +931,43 @@ int hv_fnn_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const 
     k_fnn_eval<<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, legal_moves, num_legal,
                                                                 root_features, count, weights, d,
                                                                 priors, values, child_q, logits);
+    return launch_status();
+}
+
+int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                           const float* priors, int64_t batch, int enable_win_in_one,
+                           int enable_check_opponent_wins, int enable_win_in_two, int64_t* winning_move,
+                           uint8_t* allowed_slots, uint8_t* forced_random, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!states || !legal_moves || !num_legal || !priors || !winning_move || !allowed_slots ||
+        !forced_random || !aligned16(states))
+        return HV_EINVAL;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t want = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    const int root_grid = (int)(want < 4096 ? want : 4096);  // warp-per-root passes stride the rest
+    k_tac_flags<<<root_grid, kThreads, 0, s>>>(states, num_legal, batch, enable_win_in_one != 0,
+                                              enable_check_opponent_wins != 0, enable_win_in_two != 0,
+                                              winning_move, allowed_slots, forced_random);
+    if (enable_win_in_one || enable_check_opponent_wins) {
+        size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+        int grid = 0;
+        int rc = grid_for(k_tac_children, batch * kMaxMoves, smem, &grid);
+        if (rc) return rc;
+        k_tac_children<<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, batch, forced_random,
+                                                   allowed_slots);
+        k_tac_decide<<<root_grid, kThreads, 0, s>>>(num_legal, priors, batch, winning_move, allowed_slots,
+                                                   forced_random);
+    }
+    if (enable_win_in_two) {
+        size_t smem = (sizeof(WarpSmem) + sizeof(TacSmem)) * kWarpsPerBlock;
+        int grid = 0;
+        int rc = grid_for(k_tac_win2, batch * kMaxMoves, smem, &grid);
+        if (rc) return rc;
+        k_tac_win2<<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, batch, forced_random,
+                                               allowed_slots);
+    }
+    k_tac_final<<<root_grid, kThreads, 0, s>>>(num_legal, batch, winning_move, allowed_slots, forced_random);
     return launch_status();
 }
 

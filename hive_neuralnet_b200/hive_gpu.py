@@ -136,6 +136,80 @@ class HiveGPUExtension:
                 "generate_legal_moves_and_fnn_features_batch")
         return moves, num_legal, feats
 
+    def generate_legal_moves_and_fnn_features_host(self, states: torch.Tensor, batch_size: int,
+                                                   out: tuple | None = None, chunk: int = 16384,
+                                                   device: torch.device | None = None):
+        """Host-buffer form of :meth:`generate_legal_moves_and_fnn_features_batch`.
+
+        ``states`` is a CPU uint8 ``[>=batch_size, 3424]`` tensor (pinned for
+        overlap); results land in CPU tensors ``(moves [B,256,6] u8, num_legal
+        [B] i32, features [B,122] f32)``, pinned when allocated here, or the
+        caller's ``out`` triple.  The batch is cut into chunks that cycle
+        through three streams and three device staging slots, so the
+        host-to-device copy of one chunk, the kernel of the next and the
+        device-to-host copy of a third overlap.  Returns after queuing; the
+        caller's current stream is ordered after every chunk, so
+        ``torch.cuda.current_stream().synchronize()`` makes the outputs valid.
+        """
+        if not isinstance(states, torch.Tensor) or states.is_cuda or states.dtype != torch.uint8:
+            raise ValueError("states: expected a CPU uint8 tensor")
+        if states.dim() != 2 or states.shape[0] < batch_size or states.shape[1] != SIZEOF_HIVE_STATE:
+            raise ValueError(f"states: expected [>= {batch_size}, {SIZEOF_HIVE_STATE}], got {tuple(states.shape)}")
+        if not states.is_contiguous():
+            raise ValueError("states: expected a contiguous tensor")
+        if chunk <= 0:
+            raise ValueError("chunk must be positive")
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if out is None:
+            pin = states.is_pinned()
+            out = (torch.empty((batch_size, MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE), dtype=torch.uint8, pin_memory=pin),
+                   torch.empty((batch_size,), dtype=torch.int32, pin_memory=pin),
+                   torch.empty((batch_size, FNN_FEAT_DIM), dtype=torch.float32, pin_memory=pin))
+        h_moves, h_nl, h_feat = out
+        for t, nm, dt, tail in ((h_moves, "moves", torch.uint8, (MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE)),
+                                (h_nl, "num_legal", torch.int32, ()),
+                                (h_feat, "features", torch.float32, (FNN_FEAT_DIM,))):
+            if t.is_cuda or t.dtype != dt or t.shape[0] < batch_size or tuple(t.shape[1:]) != tail \
+                    or not t.is_contiguous():
+                raise ValueError(f"out {nm}: expected a contiguous CPU {dt} tensor [>= {batch_size}, {tail}]")
+        chunk = min(chunk, max(batch_size, 1))
+        slots, streams = self._staging(dev, chunk)
+        cur = torch.cuda.current_stream(dev)
+        ready = cur.record_event()
+        with torch.cuda.device(dev):
+            for s in streams:
+                s.wait_event(ready)
+            for i, lo in enumerate(range(0, batch_size, chunk)):
+                n = min(chunk, batch_size - lo)
+                d_st, d_mv, d_nl, d_ft = slots[i % 3]
+                s = streams[i % 3]
+                with torch.cuda.stream(s):
+                    d_st[:n].copy_(states[lo:lo + n], non_blocking=True)
+                    _lib.check(self._lib.hv_generate_legal_moves_and_fnn_features(
+                        _ptr(d_st), n, _ptr(d_mv), _ptr(d_nl), _ptr(d_ft), s.cuda_stream),
+                        "generate_legal_moves_and_fnn_features_host")
+                    h_moves[lo:lo + n].copy_(d_mv[:n], non_blocking=True)
+                    h_nl[lo:lo + n].copy_(d_nl[:n], non_blocking=True)
+                    h_feat[lo:lo + n].copy_(d_ft[:n], non_blocking=True)
+            for s in streams:
+                cur.wait_stream(s)
+        return h_moves, h_nl, h_feat
+
+    def _staging(self, dev: torch.device, chunk: int):
+        """Three device staging slots and three streams per (device, chunk), kept for the process."""
+        cache = self.__dict__.setdefault("_staging_cache", {})
+        key = (dev.index, chunk)
+        if key not in cache:
+            with torch.cuda.device(dev):
+                slots = [(torch.empty((chunk, SIZEOF_HIVE_STATE), dtype=torch.uint8, device=dev),
+                          torch.empty((chunk, MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE), dtype=torch.uint8, device=dev),
+                          torch.empty((chunk,), dtype=torch.int32, device=dev),
+                          torch.empty((chunk, FNN_FEAT_DIM), dtype=torch.float32, device=dev))
+                         for _ in range(3)]
+                streams = [torch.cuda.Stream(dev) for _ in range(3)]
+            cache[key] = (slots, streams)
+        return cache[key]
+
     def extract_fnn_features_batch(self, states: torch.Tensor, legal_moves: torch.Tensor,
                                    num_legal: torch.Tensor, batch_size: int) -> torch.Tensor:
         states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
@@ -209,6 +283,25 @@ class HiveGPUExtension:
                                                 int(want_escape), _ptr(res), _ptr(sur), _ptr(esc), _stream(dev)),
                        "child_probe")
         return res, sur, esc
+
+    def root_tactical_probe_batch(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
+                                  priors: torch.Tensor, batch_size: int, enable_win_in_one: bool = True,
+                                  enable_check_opponent_wins: bool = True, enable_win_in_two: bool = True):
+        """(winning_move [B] i64, allowed_slots [B,256] u8, forced_random [B] u8), game_logic.cu:1579-1615."""
+        states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
+        legal_moves = _need(legal_moves, "legal_moves", torch.uint8, batch_size, (MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE))
+        num_legal = _need(num_legal, "num_legal", torch.int32, batch_size)
+        priors = _need(priors, "priors", torch.float32, batch_size, (MAX_LEGAL_MOVES,))
+        dev = states.device
+        win = torch.empty((batch_size,), dtype=torch.int64, device=dev)
+        allowed = torch.empty((batch_size, MAX_LEGAL_MOVES), dtype=torch.uint8, device=dev)
+        forced = torch.empty((batch_size,), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_root_tactical_probe(
+                _ptr(states), _ptr(legal_moves), _ptr(num_legal), _ptr(priors), batch_size,
+                int(bool(enable_win_in_one)), int(bool(enable_check_opponent_wins)), int(bool(enable_win_in_two)),
+                _ptr(win), _ptr(allowed), _ptr(forced), _stream(dev)), "root_tactical_probe_batch")
+        return win, allowed, forced
 
     def compute_centroids_batch(self, states: torch.Tensor, batch_size: int) -> torch.Tensor:
         states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))

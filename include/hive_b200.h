@@ -185,6 +185,17 @@ int hv_child_probe(const uint8_t* states, const uint8_t* legal_moves, const int3
                    int64_t batch, int want_escape, int32_t* results, int32_t* surround,
                    uint8_t* escape, void* stream);
 
+/* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
+ *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
+ * replaces bindings.cpp:91-100,336-339 / game_logic.cu:290-397,1579-1615.
+ * priors: [batch, 256] f32.  Outputs: winning_move [batch] i64 (-1 none),
+ * allowed_slots [batch, 256] u8, forced_random [batch] u8.  The outputs
+ * need no initialisation: every byte is written. */
+int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                           const float* priors, int64_t batch, int enable_win_in_one,
+                           int enable_check_opponent_wins, int enable_win_in_two, int64_t* winning_move,
+                           uint8_t* allowed_slots, uint8_t* forced_random, void* stream);
+
 /* apply_moves_batch(states, moves, batch_size)
  * replaces bindings.cpp:272-274 / game_logic.cu:465-477.  moves: [batch, 6]. */
 int hv_apply_moves(uint8_t* states, const uint8_t* moves, int64_t batch, void* stream);

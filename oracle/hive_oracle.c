@@ -1068,3 +1068,130 @@ void orc_queen_escape_batch(const uint8_t* states, int64_t count, uint8_t* flags
     for (int64_t i = 0; i < count; i++)
         flags[i] = (uint8_t)orc_queen_escape((const orc_state*)(states + i * ORC_STATE_BYTES));
 }
+
+/* ------------------------------------------------------------------ */
+/* Root tactical probe (game_logic.cu:290-397 root_tactical_probe_kernel */
+/* with move_gen.cuh:825-899 helpers)                                   */
+/* ------------------------------------------------------------------ */
+
+/* queen_surround_count_for_color_device, move_gen.cuh:825-831 */
+static int surround_count(const orc_state* s, int color) {
+    if (!((s->queen_placed >> color) & 1)) return 0;
+    return occupied_neighbours(s, s->queen_cell[color]);
+}
+
+/* lone_empty_neighbor_of_queen, move_gen.cuh:833-852 */
+static int lone_empty_neighbour(const orc_state* s, int target) {
+    if (!((s->queen_placed >> target) & 1)) return -1;
+    int q = s->queen_cell[target];
+    if (q >= ORC_CELLS) return -1;
+    if (occupied_neighbours(s, q) != 5) return -1;
+    int e = -1;
+    for (int d = 0; d < 6; d++) {
+        int nb = NB[q][d];
+        if (nb < 0) continue;
+        if (!OCC(s, nb)) {
+            if (e >= 0) return -1;
+            e = nb;
+        }
+    }
+    return e;
+}
+
+static inline int wins_for(int result, int color) { return result == (color == 0 ? 1 : 2); }
+
+/* has_immediate_surround_win_for_current_player, move_gen.cuh:854-874 */
+static int immediate_win(const orc_state* s) {
+    int player = s->turn & 1;
+    int cell = lone_empty_neighbour(s, player ^ 1);
+    if (cell < 0) return 0;
+    orc_move mv[ORC_MAX_MOVES];
+    int n = orc_legal_moves(s, mv);
+    for (int i = 0; i < n; i++) {
+        if (mv[i].to != cell) continue;
+        orc_state c = *s;
+        orc_apply_move(&c, &mv[i]);
+        if (wins_for(c.result, player)) return 1;
+    }
+    return 0;
+}
+
+void orc_tactical_probe(const orc_state* root, const orc_move* moves, int nlegal, const float* priors,
+                        int w1, int chk, int w2, int64_t* winning, uint8_t* allowed, uint8_t* forced) {
+    *winning = -1;
+    *forced = 0;
+    for (int i = 0; i < ORC_MAX_MOVES; i++) allowed[i] = i < nlegal;
+    if (nlegal <= 0 || root->result != 0) return;
+    int me = root->turn & 1, opp = me ^ 1;
+    int opp_s = surround_count(root, opp), own_s = surround_count(root, me);
+    if (w1 && opp_s == 5) {
+        int best = -1;
+        float bp = -1e30f;
+        for (int i = 0; i < nlegal; i++) {
+            orc_state c = *root;
+            orc_apply_move(&c, &moves[i]);
+            if (wins_for(c.result, me) && (best < 0 || priors[i] > bp)) {
+                best = i;
+                bp = priors[i];
+            }
+        }
+        if (best >= 0) {
+            *winning = best;
+            return;
+        }
+    }
+    if (chk && own_s == 5) {
+        int any_safe = 0;
+        for (int i = 0; i < nlegal; i++) {
+            orc_state c = *root;
+            orc_apply_move(&c, &moves[i]);
+            int bad = immediate_win(&c);
+            allowed[i] = !bad;
+            any_safe |= !bad;
+        }
+        if (!any_safe) {
+            *forced = 1;
+            return;
+        }
+    }
+    if (!w2 || !(opp_s == 4 || opp_s == 5)) return;
+    orc_move rep[ORC_MAX_MOVES];
+    for (int i = 0; i < nlegal; i++) {
+        if (!allowed[i]) continue;
+        orc_state c = *root;
+        orc_apply_move(&c, &moves[i]);
+        int cs = surround_count(&c, opp);
+        if (opp_s == 4 && cs <= opp_s) continue;
+        if (opp_s == 5 && cs < opp_s) continue;
+        /* generate_non_decreasing_surround_replies, move_gen.cuh:876-899 */
+        int nr = orc_legal_moves(&c, rep), ok = 1;
+        for (int r = 0; r < nr && ok; r++) {
+            orc_state g = c;
+            orc_apply_move(&g, &rep[r]);
+            if (surround_count(&g, opp) < cs) ok = 0;
+        }
+        if (!ok) continue;
+        for (int r = 0; r < nr && ok; r++) {
+            orc_state g = c;
+            orc_apply_move(&g, &rep[r]);
+            if (!wins_for(g.result, me) && !immediate_win(&g)) ok = 0;
+        }
+        if (ok) {
+            *winning = i;
+            return;
+        }
+    }
+}
+
+void orc_tactical_probe_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                              const float* priors, int64_t count, int w1, int chk, int w2,
+                              int64_t* winning, uint8_t* allowed, uint8_t* forced, int threads) {
+    orc_init_tables();
+    if (threads <= 0) threads = orc_num_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+    for (int64_t i = 0; i < count; i++)
+        orc_tactical_probe((const orc_state*)(states + i * ORC_STATE_BYTES),
+                           (const orc_move*)(moves + i * ORC_MAX_MOVES * 6), num_legal[i],
+                           priors + i * ORC_MAX_MOVES, w1, chk, w2, winning + i,
+                           allowed + i * ORC_MAX_MOVES, forced + i);
+}

@@ -100,6 +100,11 @@ void orc_actions_batch(const uint8_t* states, const uint8_t* moves,
                        const int32_t* num_legal, int64_t count,
                        int32_t* actions, int32_t* centroids);
 void orc_queen_escape_batch(const uint8_t* states, int64_t count, uint8_t* flags);
+void orc_tactical_probe(const orc_state* root, const orc_move* moves, int nlegal, const float* priors,
+                        int w1, int chk, int w2, int64_t* winning, uint8_t* allowed, uint8_t* forced);
+void orc_tactical_probe_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                              const float* priors, int64_t count, int w1, int chk, int w2,
+                              int64_t* winning, uint8_t* allowed, uint8_t* forced, int threads);
 int orc_num_threads(void);
 
 #ifdef __cplusplus

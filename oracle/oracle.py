@@ -65,6 +65,8 @@ class _Lib:
         self._ap = sig("articulation_batch", [_u8p, _i64, _u64p, _int])
         self._act = sig("actions_batch", [_u8p, _u8p, _i32p, _i64, _i32p, _i32p])
         self._qe = sig("queen_escape_batch", [_u8p, _i64, _u8p])
+        self._tac = sig("tactical_probe_batch", [_u8p, _u8p, _i32p, _f32p, _i64, _int, _int, _int,
+                                                 _i64p, _u8p, _u8p, _int])
         self._gen = sig("generate_positions",
                         [C.c_uint64, _i64, _i64, _int, _int, _u8p, _int])
 
@@ -133,6 +135,19 @@ class _Lib:
         out = np.zeros(states.shape[0], np.uint8)
         self._qe(states, states.shape[0], out)
         return out
+
+
+    def tactical_probe(self, states, moves, num_legal, priors, w1=True, chk=True, w2=True, threads: int = 0):
+        """root_tactical_probe_batch: (winning [B] i64, allowed [B,256] u8, forced [B] u8)."""
+        states = np.ascontiguousarray(states, np.uint8)
+        b = states.shape[0]
+        win = np.zeros(b, np.int64)
+        allowed = np.zeros((b, MAX_MOVES), np.uint8)
+        forced = np.zeros(b, np.uint8)
+        self._tac(states, np.ascontiguousarray(moves, np.uint8), np.ascontiguousarray(num_legal, np.int32),
+                  np.ascontiguousarray(priors, np.float32), b, int(w1), int(chk), int(w2), win, allowed,
+                  forced, threads)
+        return win, allowed, forced
 
 
 _oracle = None

@@ -387,3 +387,93 @@ void ref_mcts_root_noise(const ref_tree_ptrs* tp, const float* noise, const int3
 }
 
 }  // extern "C"
+
+// root_tactical_probe_kernel (game_logic.cu:290-397) lives in a .cu file
+// with torch host code, so its body is followed here step by step over the
+// reference's own helpers from move_gen.cuh / hive_state.cuh
+// (num_occupied_neighbors, has_immediate_surround_win_for_current_player,
+// generate_non_decreasing_surround_replies, apply_move).
+extern "C" void ref_tactical_probe_batch(const uint8_t* states, const uint8_t* moves,
+                                         const int32_t* num_legal, const float* priors, int64_t count,
+                                         int w1, int chk, int w2, int64_t* winning_out,
+                                         uint8_t* allowed_out, uint8_t* forced_out, int threads) {
+    tables_once();
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+    for (int64_t idx = 0; idx < count; idx++) {
+        HiveState root;
+        std::memcpy(&root, states + idx * sizeof(HiveState), sizeof(root));
+        const GPUMove* root_moves = reinterpret_cast<const GPUMove*>(moves) + idx * MAX_LEGAL_MOVES;
+        const float* root_priors = priors + idx * MAX_LEGAL_MOVES;
+        uint8_t* allowed = allowed_out + idx * MAX_LEGAL_MOVES;
+        int nlegal = num_legal[idx];
+        winning_out[idx] = -1;
+        forced_out[idx] = 0;
+        for (int i = 0; i < MAX_LEGAL_MOVES; ++i) allowed[i] = (i < nlegal) ? 1 : 0;
+        if (nlegal <= 0 || root.result != IN_PROGRESS) continue;
+        Color me = current_player(root);
+        Color opp = (me == WHITE) ? BLACK : WHITE;
+        int opp_s = queen_surround_count_for_color_device(root, opp);
+        int own_s = queen_surround_count_for_color_device(root, me);
+        auto won = [&](const HiveState& s) {
+            return (me == WHITE && s.result == WHITE_WINS) || (me == BLACK && s.result == BLACK_WINS);
+        };
+        bool done = false;
+        if (w1 && opp_s == 5) {
+            int best = -1;
+            float bp = -1e30f;
+            for (int i = 0; i < nlegal; ++i) {
+                HiveState c = root;
+                apply_move(c, root_moves[i]);
+                if (won(c) && (best < 0 || root_priors[i] > bp)) {
+                    best = i;
+                    bp = root_priors[i];
+                }
+            }
+            if (best >= 0) {
+                winning_out[idx] = best;
+                done = true;
+            }
+        }
+        if (!done && chk && own_s == 5) {
+            bool any_safe = false;
+            for (int i = 0; i < nlegal; ++i) {
+                HiveState c = root;
+                apply_move(c, root_moves[i]);
+                bool bad = has_immediate_surround_win_for_current_player(c);
+                allowed[i] = bad ? 0 : 1;
+                any_safe |= !bad;
+            }
+            if (!any_safe) {
+                forced_out[idx] = 1;
+                done = true;
+            }
+        }
+        if (done || !w2 || !(opp_s == 4 || opp_s == 5)) continue;
+        for (int i = 0; i < nlegal; ++i) {
+            if (!allowed[i]) continue;
+            HiveState c = root;
+            apply_move(c, root_moves[i]);
+            int cs = queen_surround_count_for_color_device(c, opp);
+            if (opp_s == 4 && cs <= opp_s) continue;
+            if (opp_s == 5 && cs < opp_s) continue;
+            GPUMove replies[MAX_LEGAL_MOVES];
+            bool all_nd = true;
+            int nr = generate_non_decreasing_surround_replies(c, opp, cs, replies, all_nd);
+            if (!all_nd) continue;
+            bool ok = true;
+            for (int r = 0; r < nr; ++r) {
+                HiveState g = c;
+                apply_move(g, replies[r]);
+                if (!won(g) && !has_immediate_surround_win_for_current_player(g)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok) {
+                winning_out[idx] = i;
+                break;
+            }
+        }
+    }
+}

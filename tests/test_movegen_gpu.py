@@ -159,3 +159,15 @@ def test_queen_escape_and_child_probe(ext, orc):
                     if 0 <= r + dr < 23 and 0 <= c + dc < 23 and k[2645 + (r + dr) * 23 + c + dc] > 0:
                         want += 1
             assert sur[i, j] == want
+
+
+def test_host_buffer_pipeline_matches_device_call(ext, orc):
+    """The chunked host-buffer form gives the same bytes as the device call (ragged last chunk)."""
+    st = orc.generate_positions(4711, 0, 5000, 120, 7)
+    host = torch.from_numpy(st).pin_memory()
+    mh, nh, fh = ext.generate_legal_moves_and_fnn_features_host(host, 5000, chunk=1024)
+    torch.cuda.current_stream().synchronize()
+    mg, ng, fg = ext.generate_legal_moves_and_fnn_features_batch(_cuda(st), 5000)
+    assert np.array_equal(mh.numpy(), mg.cpu().numpy())
+    assert np.array_equal(nh.numpy(), ng.cpu().numpy())
+    assert np.array_equal(_bits(fh.numpy()), _bits(fg.cpu().numpy()))

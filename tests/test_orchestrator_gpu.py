@@ -123,3 +123,44 @@ def test_self_play_games_deterministic_with_seed():
             assert np.array_equal(x.state_bytes, y.state_bytes)
             assert np.array_equal(x.policy_target, y.policy_target)
             assert x.value_target == y.value_target
+
+
+def test_gumbel_with_short_forced_win_probe():
+    """short_forced_win_probe=True (the trainer's default): rows the root
+    tactical probe decides are not searched, a found win is played with a
+    one-hot policy target, and the searched rows still replay bit-exact."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import make_tactical_golden as T
+    from hive_neuralnet_b200.fnn import HiveFNN
+    from hive_neuralnet_b200.orchestrator import FNNMCTSConfig, FNNMCTSOrchestrator
+    import json
+    orc = O.oracle()
+    st, sel = T.tactical_inputs(orc)
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_tactical.json")) as f:
+        case = json.load(f)["cases"]["111"]
+    w_all, f_all = np.array(case["winning"]), np.array(case["forced"])
+    rows = np.concatenate([np.where(w_all >= 0)[0][:6], np.where(f_all == 1)[0][:2],
+                           np.where((w_all < 0) & (f_all == 0))[0][:8]])
+    B, M = len(rows), 8192
+    start = st[sel[rows]]
+    torch.manual_seed(0)
+    cfg = FNNMCTSConfig(num_simulations=64, batch_size=B, max_game_length=1, dirichlet_epsilon=0.0, seed=7,
+                        max_tree_nodes=M, short_forced_win_probe=True, expansion_mask=7)
+    orch = FNNMCTSOrchestrator(HiveFNN(), cfg)
+    orch.trace = []
+    ex = orch.self_play_batch(torch.from_numpy(start).cuda())
+    root = next(x for x in orch.trace if x["kind"] == "root")
+    mv, nl, _ = orc.legal_moves_features(start)
+    win, _, forced = orc.tactical_probe(start, mv, nl, root["priors"].cpu().numpy())
+    ga = root["game_active"].cpu().numpy()
+    assert ((win >= 0) | (forced == 1)).any(), "fixture rows should include decided roots"
+    assert np.array_equal(ga != 0, (win < 0) & (forced == 0) & (nl > 0))
+    for b in range(B):
+        if win[b] >= 0:
+            (e,) = ex[b]
+            assert e.policy_target[win[b]] == 1.0 and e.policy_target.sum() == 1.0
+    if ga.any():
+        searched = next(x for x in orch.trace if x["kind"] == "searched")
+        assert _tree_np(searched["tree"], B, M).equal(_replay(orch.trace, B, M, 2, cfg.c_puct)) == []
