@@ -18,6 +18,7 @@
 #include "hv_fnn.cuh"
 #include "hv_mcts.cuh"
 #include "hv_tactics.cuh"
+#include "hv_hybrid.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -321,6 +322,88 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_queen_escape(
         stage_state(w, states + p * kStateBytes);
         bool esc = queen_escape_staged(w);
         if (lane_id() == 0) flags[p] = esc ? 1 : 0;
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// hybrid transformer inputs (game_logic.cu:93-131 generate_legal_moves_and_
+// hybrid_root_features_kernel, state_encoder.cuh:552-597): piece tokens,
+// move features, optionally fused with move generation and FNN features
+// ---------------------------------------------------------------------------
+struct HybridOut {
+    float* tf;
+    int32_t* tq;
+    int32_t* tr;
+    int32_t* tz;
+    uint8_t* tm;
+    float* gf;
+    int32_t* ntok;
+    float* mf;
+};
+
+template <bool GEN, bool TOKENS, bool MOVEF>
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_hybrid(const uint8_t* __restrict__ states,
+                                                                    const uint8_t* __restrict__ moves_in,
+                                                                    const int32_t* __restrict__ nl_in,
+                                                                    int64_t batch, uint8_t* __restrict__ moves_out,
+                                                                    int32_t* __restrict__ nl_out,
+                                                                    float* __restrict__ feats_out, HybridOut o) {
+    WarpSmem* w = warp_slot();
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
+         p += nwarps) {
+        stage_state(w, states + p * kStateBytes);
+        int n = 0;
+        if (GEN) {
+            zero_moves(w);
+            Setup S = setup_position(w);
+            n = gen_legal(w, S, &g_error);
+            store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes));
+            if (l == 0) nl_out[p] = n;
+            features(w, S, n, feats_out + p * kFeat);
+            if (TOKENS) {
+                // reads only the staged state and S, which features() leaves intact
+                int t = hybrid_tokens(w, S, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,
+                                      o.tr + p * kTokens, o.tz + p * kTokens, o.tm + p * kTokens,
+                                      o.gf + p * kGlobFeat);
+                if (l == 0) o.ntok[p] = t;
+            }
+        } else {
+            if (TOKENS) {
+                Setup S = setup_position(w);
+                int t = hybrid_tokens(w, S, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,
+                                      o.tr + p * kTokens, o.tz + p * kTokens, o.tm + p * kTokens,
+                                      o.gf + p * kGlobFeat);
+                if (l == 0) o.ntok[p] = t;
+            }
+            if (MOVEF) {
+                const uint4* s4 = reinterpret_cast<const uint4*>(moves_in + p * (kMaxMoves * kMoveBytes));
+                uint4* m4 = reinterpret_cast<uint4*>(w->mv);
+                for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
+                n = nl_in[p];
+                n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
+                __syncwarp();
+            }
+        }
+        if (MOVEF) {
+            Pos P{w};
+            const MoveCtx X = move_ctx(w);
+            for (int m = l; m < kMaxMoves; m += 32) {
+                float f[kMoveFeat];
+                if (m < n) {
+                    const uint16_t a = w->mv[3 * m];
+                    move_features(P, w->st, X, a & 0xFF, a >> 8, w->mv[3 * m + 1], w->mv[3 * m + 2], f);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < kMoveFeat; k++) f[k] = 0.0f;
+                }
+                float* row = o.mf + (p * kMaxMoves + m) * kMoveFeat;
+#pragma unroll
+                for (int k = 0; k < kMoveFeat; k++) row[k] = f[k];
+            }
+        }
         __syncwarp();
     }
 }
@@ -835,6 +918,25 @@ static int launch_root(const uint8_t* states, const uint8_t* mi, const int32_t* 
     return launch_status();
 }
 
+template <bool GEN, bool TOKENS, bool MOVEF>
+static int launch_hybrid(const uint8_t* states, const uint8_t* mi, const int32_t* nli, int64_t batch,
+                         uint8_t* mo, int32_t* nlo, float* fo, HybridOut o, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!states || !aligned16(states)) return HV_EINVAL;
+    if (GEN && (!mo || !nlo || !fo || !aligned16(mo))) return HV_EINVAL;
+    if (!GEN && MOVEF && (!mi || !nli || !aligned16(mi))) return HV_EINVAL;
+    if (TOKENS && (!o.tf || !o.tq || !o.tr || !o.tz || !o.tm || !o.gf || !o.ntok)) return HV_EINVAL;
+    if (MOVEF && !o.mf) return HV_EINVAL;
+    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_hybrid<GEN, TOKENS, MOVEF>, batch, smem, &grid);
+    if (rc) return rc;
+    k_hybrid<GEN, TOKENS, MOVEF><<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, mi, nli, batch, mo, nlo,
+                                                                                fo, o);
+    return launch_status();
+}
+
 }  // namespace hv
 
 using namespace hv;
@@ -932,6 +1034,30 @@ int hv_fnn_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const 
                                                                 root_features, count, weights, d,
                                                                 priors, values, child_q, logits);
     return launch_status();
+}
+
+int hv_hybrid_encode(const uint8_t* states, int64_t batch, float* token_features, int32_t* token_q,
+                     int32_t* token_r, int32_t* token_z, uint8_t* token_mask, float* global_features,
+                     int32_t* num_tokens, void* stream) {
+    HybridOut o{token_features, token_q, token_r, token_z, token_mask, global_features, num_tokens, nullptr};
+    return launch_hybrid<false, true, false>(states, nullptr, nullptr, batch, nullptr, nullptr, nullptr, o, stream);
+}
+
+int hv_hybrid_move_features(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            int64_t batch, float* move_features, void* stream) {
+    HybridOut o{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, move_features};
+    return launch_hybrid<false, false, true>(states, legal_moves, num_legal, batch, nullptr, nullptr, nullptr, o,
+                                             stream);
+}
+
+int hv_generate_legal_moves_and_hybrid_root_features(const uint8_t* states, int64_t batch, uint8_t* moves,
+                                                     int32_t* num_legal, float* fnn_features, float* token_features,
+                                                     int32_t* token_q, int32_t* token_r, int32_t* token_z,
+                                                     uint8_t* token_mask, float* global_features,
+                                                     int32_t* num_tokens, float* move_features, void* stream) {
+    HybridOut o{token_features, token_q, token_r, token_z, token_mask, global_features, num_tokens, move_features};
+    return launch_hybrid<true, true, true>(states, nullptr, nullptr, batch, moves, num_legal, fnn_features, o,
+                                           stream);
 }
 
 int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,

@@ -284,6 +284,58 @@ class HiveGPUExtension:
                        "child_probe")
         return res, sur, esc
 
+    # -- hybrid transformer inputs (bindings.cpp:48-52, 78-81, 110-114) ------
+    def _hybrid_tokens_out(self, B: int, dev):
+        return (torch.empty((B, HYBRID_MAX_PIECE_TOKENS, HYBRID_NODE_FEAT_DIM), dtype=torch.float32, device=dev),
+                torch.empty((B, HYBRID_MAX_PIECE_TOKENS), dtype=torch.int32, device=dev),
+                torch.empty((B, HYBRID_MAX_PIECE_TOKENS), dtype=torch.int32, device=dev),
+                torch.empty((B, HYBRID_MAX_PIECE_TOKENS), dtype=torch.int32, device=dev),
+                torch.empty((B, HYBRID_MAX_PIECE_TOKENS), dtype=torch.bool, device=dev),
+                torch.empty((B, HYBRID_GLOBAL_FEAT_DIM), dtype=torch.float32, device=dev),
+                torch.empty((B,), dtype=torch.int32, device=dev))
+
+    def hybrid_transformer_encode_with_moves_batch(self, states: torch.Tensor, legal_moves: torch.Tensor,
+                                                   num_legal: torch.Tensor, batch_size: int):
+        """(token_features [B,28,27], token_q, token_r, token_z [B,28] i32, token_mask [B,28] bool,
+        global_features [B,6], num_tokens [B] i32); game_logic.cu:652-702."""
+        states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
+        dev = states.device
+        out = self._hybrid_tokens_out(batch_size, dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_hybrid_encode(_ptr(states), batch_size, *(_ptr(t) for t in out), _stream(dev)),
+                       "hybrid_transformer_encode_with_moves_batch")
+        return out
+
+    def hybrid_transformer_move_features_batch(self, states: torch.Tensor, legal_moves: torch.Tensor,
+                                               num_legal: torch.Tensor, batch_size: int) -> torch.Tensor:
+        """[B, 256, 31] f32 move features; game_logic.cu:704-727."""
+        states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
+        legal_moves = _need(legal_moves, "legal_moves", torch.uint8, batch_size, (MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE))
+        num_legal = _need(num_legal, "num_legal", torch.int32, batch_size)
+        dev = states.device
+        mf = torch.empty((batch_size, MAX_LEGAL_MOVES, HYBRID_MOVE_FEAT_DIM), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_hybrid_move_features(_ptr(states), _ptr(legal_moves), _ptr(num_legal),
+                                                         batch_size, _ptr(mf), _stream(dev)),
+                       "hybrid_transformer_move_features_batch")
+        return mf
+
+    def generate_legal_moves_and_hybrid_root_features_batch(self, states: torch.Tensor, batch_size: int):
+        """(moves, num_legal, fnn_features, token_features, token_q, token_r, token_z, token_mask,
+        global_features, move_features); game_logic.cu:1469-1535."""
+        states = _need(states, "states", torch.uint8, batch_size, (SIZEOF_HIVE_STATE,))
+        dev = states.device
+        moves = torch.empty((batch_size, MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE), dtype=torch.uint8, device=dev)
+        num_legal = torch.empty((batch_size,), dtype=torch.int32, device=dev)
+        feats = torch.empty((batch_size, FNN_FEAT_DIM), dtype=torch.float32, device=dev)
+        tok = self._hybrid_tokens_out(batch_size, dev)
+        mf = torch.empty((batch_size, MAX_LEGAL_MOVES, HYBRID_MOVE_FEAT_DIM), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_generate_legal_moves_and_hybrid_root_features(
+                _ptr(states), batch_size, _ptr(moves), _ptr(num_legal), _ptr(feats), *(_ptr(t) for t in tok),
+                _ptr(mf), _stream(dev)), "generate_legal_moves_and_hybrid_root_features_batch")
+        return (moves, num_legal, feats) + tok[:6] + (mf,)
+
     def root_tactical_probe_batch(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
                                   priors: torch.Tensor, batch_size: int, enable_win_in_one: bool = True,
                                   enable_check_opponent_wins: bool = True, enable_win_in_two: bool = True):

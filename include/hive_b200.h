@@ -185,6 +185,32 @@ int hv_child_probe(const uint8_t* states, const uint8_t* legal_moves, const int3
                    int64_t batch, int want_escape, int32_t* results, int32_t* surround,
                    uint8_t* escape, void* stream);
 
+/* hybrid_transformer_encode_with_moves_batch(states, legal_moves, num_legal, batch_size)
+ * replaces bindings.cpp:48-52,361-363 / game_logic.cu:652-702 (the move list
+ * is not read by the token encoder, so it is not an argument here).
+ * token_features [batch, 28, 27] f32, token_q/r/z [batch, 28] i32 (column,
+ * row, stack level), token_mask [batch, 28] u8 (0/1, torch bool),
+ * global_features [batch, 6] f32, num_tokens [batch] i32.  Every element of
+ * every output is written. */
+int hv_hybrid_encode(const uint8_t* states, int64_t batch, float* token_features, int32_t* token_q,
+                     int32_t* token_r, int32_t* token_z, uint8_t* token_mask, float* global_features,
+                     int32_t* num_tokens, void* stream);
+
+/* hybrid_transformer_move_features_batch(states, legal_moves, num_legal, batch_size)
+ * replaces bindings.cpp:110-114,356-358 / game_logic.cu:704-727.
+ * move_features [batch, 256, 31] f32, zero past num_legal. */
+int hv_hybrid_move_features(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            int64_t batch, float* move_features, void* stream);
+
+/* generate_legal_moves_and_hybrid_root_features_batch(states, batch_size)
+ * replaces bindings.cpp:78-81,322-324 / game_logic.cu:93-131,1469-1535:
+ * legal moves, FNN features, piece tokens and move features in one pass. */
+int hv_generate_legal_moves_and_hybrid_root_features(const uint8_t* states, int64_t batch, uint8_t* moves,
+                                                     int32_t* num_legal, float* fnn_features, float* token_features,
+                                                     int32_t* token_q, int32_t* token_r, int32_t* token_z,
+                                                     uint8_t* token_mask, float* global_features,
+                                                     int32_t* num_tokens, float* move_features, void* stream);
+
 /* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
  *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
  * replaces bindings.cpp:91-100,336-339 / game_logic.cu:290-397,1579-1615.

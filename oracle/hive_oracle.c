@@ -1195,3 +1195,186 @@ void orc_tactical_probe_batch(const uint8_t* states, const uint8_t* moves, const
                            priors + i * ORC_MAX_MOVES, w1, chk, w2, winning + i,
                            allowed + i * ORC_MAX_MOVES, forced + i);
 }
+
+/* ------------------------------------------------------------------ */
+/* Hybrid transformer inputs (state_encoder.cuh:372-550)               */
+/* ------------------------------------------------------------------ */
+
+#define ORC_TOKENS 28
+#define ORC_TOK_FEAT 27
+#define ORC_MOVE_FEAT 31
+
+static int height_neighbours(const orc_state* s, int cell, int* flags) {
+    int n = 0;
+    for (int d = 0; d < 6; d++) {
+        int nb = NB[cell][d];
+        int f = nb >= 0 && s->height[nb] > 0;
+        if (flags) flags[d] = f;
+        n += f;
+    }
+    return n;
+}
+
+/* extract_hybrid_transformer_tokens_device, state_encoder.cuh:372-468 */
+int orc_hybrid_tokens(const orc_state* s, float* tf, int32_t* tq, int32_t* tr, int32_t* tz, uint8_t* tm,
+                      float* gf) {
+    memset(tf, 0, sizeof(float) * ORC_TOKENS * ORC_TOK_FEAT);
+    memset(tq, 0, sizeof(int32_t) * ORC_TOKENS);
+    memset(tr, 0, sizeof(int32_t) * ORC_TOKENS);
+    memset(tz, 0, sizeof(int32_t) * ORC_TOKENS);
+    memset(tm, 0, ORC_TOKENS);
+    memset(gf, 0, sizeof(float) * 6);
+    float qs[2] = {0.0f, 0.0f};
+    uint64_t ap[ORC_WORDS];
+    orc_articulation(s, ap);
+    for (int c = 0; c < 2; c++) {
+        int q = s->queen_cell[c];
+        if (q != 0xFFFF && q < ORC_CELLS) qs[c] = (float)height_neighbours(s, q, NULL) / 6.0f;
+    }
+    int n = 0;
+    for (int cell = 0; cell < ORC_CELLS; cell++) {
+        int h = s->height[cell];
+        if (h == 0) continue;
+        int fl[6];
+        int oc = height_neighbours(s, cell, fl);
+        for (int lv = 0; lv < h && lv < ORC_MAX_STACK; lv++) {
+            if (n >= ORC_TOKENS) break;
+            uint8_t b = s->pieces[lv][cell];
+            int pt = b & 0x0F, pc = BYTE_COLOR(b), top = lv == h - 1;
+            float* f = tf + n * ORC_TOK_FEAT;
+            if (pt >= 1 && pt <= 8) f[pt - 1] = 1.0f;
+            f[8 + pc] = 1.0f;
+            f[10] = lv == 0 ? 1.0f : 0.0f;
+            f[11] = top ? 1.0f : 0.0f;
+            f[12] = (float)h / 4.0f;
+            f[13] = pt == 1 ? 1.0f : 0.0f;
+            f[14] = qs[pc];
+            f[15] = (float)oc / 6.0f;
+            if (top)
+                for (int d = 0; d < 6; d++)
+                    if (!fl[d]) f[16 + d] = 1.0f;
+            f[24] = (float)lv * 0.25f;
+            f[25] = (s->stunned_cell != 0xFFFF && s->stunned_cell == cell) ? 1.0f : 0.0f;
+            if (top) f[26] = bb_get(ap, cell) ? 1.0f : 0.0f;
+            tq[n] = cell % ORC_BOARD;
+            tr[n] = cell / ORC_BOARD;
+            tz[n] = lv;
+            tm[n] = 1;
+            n++;
+        }
+    }
+    int cur = s->turn & 1, wh = 0, bh = 0;
+    gf[0] = cur == 0 ? 1.0f : 0.0f;
+    gf[1] = ((float)s->turn / 100.0f < 1.0f) ? (float)s->turn / 100.0f : 1.0f;
+    gf[2] = (s->queen_placed & 1) ? 1.0f : 0.0f;
+    gf[3] = (s->queen_placed & 2) ? 1.0f : 0.0f;
+    for (int p = 0; p < 8; p++) {
+        wh += s->hands[0][p];
+        bh += s->hands[1][p];
+    }
+    gf[4] = (float)wh / 14.0f;
+    gf[5] = (float)bh / 14.0f;
+    return n;
+}
+
+/* queen_surround_count_current, state_encoder.cuh:109-121 */
+static int qs_current(const orc_state* s, int color) {
+    if (!((s->queen_placed >> color) & 1)) return 0;
+    int q = s->queen_cell[color];
+    return q < ORC_CELLS ? height_neighbours(s, q, NULL) : 0;
+}
+
+/* queen_surround_count_after_move, state_encoder.cuh:123-165 */
+static int qs_after(const orc_state* s, const orc_move* m, int qc, int mover, int moved) {
+    int placed = (s->queen_placed >> qc) & 1;
+    int being_placed = m->type == 0 && m->pt == 1 && mover == qc && m->to < ORC_CELLS;
+    int being_moved = m->type == 1 && m->pt == 1 && moved == qc && m->to < ORC_CELLS;
+    if (!placed && !being_placed) return 0;
+    int q = placed ? (int)s->queen_cell[qc] : -1;
+    if (being_placed || being_moved) q = m->to;
+    if (q < 0 || q >= ORC_CELLS) return 0;
+    int has_src = m->type == 1 && m->from < ORC_CELLS;
+    int src = has_src ? m->from : -1;
+    int dst = m->to < ORC_CELLS ? m->to : -1;
+    int src_stays = has_src && s->height[src] > 1;
+    int n = 0;
+    for (int d = 0; d < 6; d++) {
+        int nb = NB[q][d];
+        if (nb < 0) continue;
+        int occ = s->height[nb] > 0;
+        if (has_src && nb == src) occ = src_stays;
+        if (dst >= 0 && nb == dst) occ = 1;
+        n += occ;
+    }
+    return n;
+}
+
+/* extract_hybrid_transformer_move_features_device, state_encoder.cuh:470-550 */
+void orc_hybrid_move_features(const orc_state* s, const orc_move* mv, int n, float* out) {
+    memset(out, 0, sizeof(float) * ORC_MAX_MOVES * ORC_MOVE_FEAT);
+    if (n > ORC_MAX_MOVES) n = ORC_MAX_MOVES;
+    int me = s->turn & 1, op = me ^ 1;
+    int oq = s->queen_cell[me], pq = s->queen_cell[op];
+    int oqc = oq != 0xFFFF ? oq % ORC_BOARD - ORC_HALF : 0, oqr = oq != 0xFFFF ? oq / ORC_BOARD - ORC_HALF : 0;
+    int pqc = pq != 0xFFFF ? pq % ORC_BOARD - ORC_HALF : 0, pqr = pq != 0xFFFF ? pq / ORC_BOARD - ORC_HALF : 0;
+    int os0 = qs_current(s, me), ps0 = qs_current(s, op);
+    const float H = (float)ORC_HALF;
+    for (int i = 0; i < n; i++) {
+        const orc_move* m = &mv[i];
+        float* f = out + i * ORC_MOVE_FEAT;
+        int moved = me;
+        if (m->type == 1 && m->from < ORC_CELLS && s->height[m->from] > 0)
+            moved = BYTE_COLOR(s->pieces[s->height[m->from] - 1][m->from]);
+        if (m->type < ORC_MOVE_FEAT) f[m->type] = 1.0f;
+        if (m->pt >= 1 && m->pt <= 8) f[3 + m->pt - 1] = 1.0f;
+        int src = m->type == 1;
+        f[11] = src ? 1.0f : 0.0f;
+        int sq = 0, sr = 0, dq = 0, dr = 0, ss = 0, ds = 0, docc = 0;
+        if (m->to < ORC_CELLS) {
+            dq = m->to % ORC_BOARD - ORC_HALF;
+            dr = m->to / ORC_BOARD - ORC_HALF;
+            ds = s->height[m->to];
+            docc = ds > 0;
+        }
+        if (src && m->from < ORC_CELLS) {
+            sq = m->from % ORC_BOARD - ORC_HALF;
+            sr = m->from / ORC_BOARD - ORC_HALF;
+            ss = s->height[m->from];
+        }
+        f[12] = src ? (float)(dq - sq) / H : 0.0f;
+        f[13] = src ? (float)(dr - sr) / H : 0.0f;
+        f[14] = (float)(dq - oqc) / H;
+        f[15] = (float)(dr - oqr) / H;
+        f[16] = (float)(dq - pqc) / H;
+        f[17] = (float)(dr - pqr) / H;
+        f[18] = src ? (float)(sq - oqc) / H : 0.0f;
+        f[19] = src ? (float)(sr - oqr) / H : 0.0f;
+        f[20] = src ? (float)(sq - pqc) / H : 0.0f;
+        f[21] = src ? (float)(sr - pqr) / H : 0.0f;
+        f[22] = (float)ss / 5.0f;
+        f[23] = (float)ds / 5.0f;
+        f[24] = (float)docc;
+        int od = qs_after(s, m, me, me, moved) - os0, pd = qs_after(s, m, op, me, moved) - ps0;
+        od = od < -1 ? -1 : (od > 1 ? 1 : od);
+        pd = pd < -1 ? -1 : (pd > 1 ? 1 : pd);
+        f[25 + od + 1] = 1.0f;
+        f[28 + pd + 1] = 1.0f;
+    }
+}
+
+void orc_hybrid_encode_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t count,
+                             float* tf, int32_t* tq, int32_t* tr, int32_t* tz, uint8_t* tm, float* gf,
+                             int32_t* ntok, float* mf, int threads) {
+    orc_init_tables();
+    if (threads <= 0) threads = orc_num_threads();
+#pragma omp parallel for schedule(static) num_threads(threads)
+    for (int64_t i = 0; i < count; i++) {
+        const orc_state* s = (const orc_state*)(states + i * ORC_STATE_BYTES);
+        int n = orc_hybrid_tokens(s, tf + i * ORC_TOKENS * ORC_TOK_FEAT, tq + i * ORC_TOKENS, tr + i * ORC_TOKENS,
+                                  tz + i * ORC_TOKENS, tm + i * ORC_TOKENS, gf + i * 6);
+        if (ntok) ntok[i] = n;
+        if (mf)
+            orc_hybrid_move_features(s, (const orc_move*)(moves + i * ORC_MAX_MOVES * 6), num_legal[i],
+                                     mf + i * ORC_MAX_MOVES * ORC_MOVE_FEAT);
+    }
+}

@@ -105,6 +105,12 @@ void orc_tactical_probe(const orc_state* root, const orc_move* moves, int nlegal
 void orc_tactical_probe_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
                               const float* priors, int64_t count, int w1, int chk, int w2,
                               int64_t* winning, uint8_t* allowed, uint8_t* forced, int threads);
+int orc_hybrid_tokens(const orc_state* s, float* tf, int32_t* tq, int32_t* tr, int32_t* tz, uint8_t* tm,
+                      float* gf);
+void orc_hybrid_move_features(const orc_state* s, const orc_move* mv, int n, float* out);
+void orc_hybrid_encode_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t count,
+                             float* tf, int32_t* tq, int32_t* tr, int32_t* tz, uint8_t* tm, float* gf,
+                             int32_t* ntok, float* mf, int threads);
 int orc_num_threads(void);
 
 #ifdef __cplusplus

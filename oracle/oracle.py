@@ -65,6 +65,8 @@ class _Lib:
         self._ap = sig("articulation_batch", [_u8p, _i64, _u64p, _int])
         self._act = sig("actions_batch", [_u8p, _u8p, _i32p, _i64, _i32p, _i32p])
         self._qe = sig("queen_escape_batch", [_u8p, _i64, _u8p])
+        self._hyb = sig("hybrid_encode_batch", [_u8p, _u8p, _i32p, _i64, _f32p, _i32p, _i32p, _i32p, _u8p,
+                                                _f32p, _i32p, _f32p, _int])
         self._tac = sig("tactical_probe_batch", [_u8p, _u8p, _i32p, _f32p, _i64, _int, _int, _int,
                                                  _i64p, _u8p, _u8p, _int])
         self._gen = sig("generate_positions",
@@ -148,6 +150,23 @@ class _Lib:
                   np.ascontiguousarray(priors, np.float32), b, int(w1), int(chk), int(w2), win, allowed,
                   forced, threads)
         return win, allowed, forced
+
+
+    def hybrid_encode(self, states, moves, num_legal, threads: int = 0):
+        """hybrid_transformer_encode_with_moves_batch + hybrid_transformer_move_features_batch outputs:
+        (token_features [B,28,27], q, r, z [B,28] i32, mask [B,28] u8, global [B,6], num_tokens [B],
+        move_features [B,256,31])."""
+        states = np.ascontiguousarray(states, np.uint8)
+        b = states.shape[0]
+        tf = np.zeros((b, 28, 27), np.float32)
+        tq, tr, tz = (np.zeros((b, 28), np.int32) for _ in range(3))
+        tm = np.zeros((b, 28), np.uint8)
+        gf = np.zeros((b, 6), np.float32)
+        nt = np.zeros(b, np.int32)
+        mf = np.zeros((b, MAX_MOVES, 31), np.float32)
+        self._hyb(states, np.ascontiguousarray(moves, np.uint8), np.ascontiguousarray(num_legal, np.int32), b,
+                  tf, tq, tr, tz, tm, gf, nt, mf, threads)
+        return tf, tq, tr, tz, tm, gf, nt, mf
 
 
 _oracle = None

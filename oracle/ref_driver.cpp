@@ -477,3 +477,29 @@ extern "C" void ref_tactical_probe_batch(const uint8_t* states, const uint8_t* m
         }
     }
 }
+
+// hybrid_transformer_encode_states_kernel / hybrid_transformer_move_features_kernel
+// (state_encoder.cuh:552-597): the reference's device functions run per state.
+extern "C" void ref_hybrid_encode_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                                        int64_t count, float* tf, int32_t* tq, int32_t* tr, int32_t* tz,
+                                        uint8_t* tm, float* gf, int32_t* ntok, float* mf, int threads) {
+    tables_once();
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(threads)
+    for (int64_t i = 0; i < count; i++) {
+        HiveState s;
+        std::memcpy(&s, states + i * sizeof(HiveState), sizeof(s));
+        bool mask[HYBRID_MAX_PIECE_TOKENS];
+        int n = 0;
+        extract_hybrid_transformer_tokens_device(s, tf + i * HYBRID_MAX_PIECE_TOKENS * HYBRID_NODE_FEAT_DIM,
+                                                 tq + i * HYBRID_MAX_PIECE_TOKENS, tr + i * HYBRID_MAX_PIECE_TOKENS,
+                                                 tz + i * HYBRID_MAX_PIECE_TOKENS, mask,
+                                                 gf + i * HYBRID_GLOBAL_FEAT_DIM, n);
+        for (int k = 0; k < HYBRID_MAX_PIECE_TOKENS; k++) tm[i * HYBRID_MAX_PIECE_TOKENS + k] = mask[k] ? 1 : 0;
+        if (ntok) ntok[i] = n;
+        if (mf)
+            extract_hybrid_transformer_move_features_device(
+                s, reinterpret_cast<const GPUMove*>(moves) + i * MAX_LEGAL_MOVES, num_legal[i],
+                mf + i * MAX_LEGAL_MOVES * HYBRID_MOVE_FEAT_DIM);
+    }
+}

@@ -8,7 +8,8 @@ on the host by oracle/ref_driver.cpp) and records its outputs:
   ply U[0,60]; 48 all expansions, ply U[0,120]): state bytes, full move lists,
   num_legal, features, compact lists, articulation points, centroids, action
   indices, queen-escape flags, and successor features of every legal move;
-* ``golden_digests.json`` -- SHA-256 digests of the same outputs for the
+* ``golden_digests.json`` -- SHA-256 digests of the same outputs (plus the
+  hybrid transformer's piece tokens and move features) for the
   BASELINE config-1 set (4,096 base positions) and an 8,192-position
   all-expansion set, so the larger parity sets are pinned without storing them.
 
@@ -61,6 +62,12 @@ def outputs(lib, states: np.ndarray) -> dict:
                 succ_roots=roots, succ_moves=idx, succ_features=succ)
 
 
+def hybrid(lib, states: np.ndarray, o: dict):
+    """Hybrid transformer inputs (state_encoder.cuh:372-550): tokens, q, r, z, mask, global,
+    num_tokens, move features."""
+    return lib.hybrid_encode(states, o["moves"], o["num_legal"])
+
+
 def main() -> None:
     O.build(ref=True)
     ref = O.ref()
@@ -86,6 +93,8 @@ def main() -> None:
             "actions": digest(o["actions"], o["centroids"]),
             "queen_escape": digest(o["queen_escape"]),
             "successor_features": digest(o["succ_features"]),
+            "hybrid_tokens": digest(*hybrid(ref, st, o)[:7]),
+            "hybrid_move_features": digest(hybrid(ref, st, o)[7]),
             "num_successors": int(len(o["succ_roots"])),
             "mean_legal": float(o["num_legal"].mean()),
         }

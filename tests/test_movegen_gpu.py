@@ -171,3 +171,28 @@ def test_host_buffer_pipeline_matches_device_call(ext, orc):
     assert np.array_equal(mh.numpy(), mg.cpu().numpy())
     assert np.array_equal(nh.numpy(), ng.cpu().numpy())
     assert np.array_equal(_bits(fh.numpy()), _bits(fg.cpu().numpy()))
+
+
+@pytest.mark.parametrize("mask,max_ply", [(0, 60), (7, 120), (7, 200)])
+def test_hybrid_transformer_inputs_bit_exact(ext, orc, mask, max_ply):
+    """Piece tokens, global and move features (state_encoder.cuh:372-550) against the oracle,
+    standalone and fused with move generation."""
+    st = orc.generate_positions(9090 + mask + max_ply, 0, 4096, max_ply, mask)
+    mo, no, fo = orc.legal_moves_features(st)
+    want = orc.hybrid_encode(st, mo, no)
+    d = _cuda(st)
+    tok = ext.hybrid_transformer_encode_with_moves_batch(d, _cuda(mo), _cuda(no), 4096)
+    mf = ext.hybrid_transformer_move_features_batch(d, _cuda(mo), _cuda(no), 4096)
+    fused = ext.generate_legal_moves_and_hybrid_root_features_batch(d, 4096)
+    assert tok[4].dtype == torch.bool
+    got = [t.cpu().numpy() for t in tok]
+    got[4] = got[4].astype(np.uint8)
+    for name, g, o in zip(("tf", "tq", "tr", "tz", "tm", "gf", "nt"), got, want[:7]):
+        assert np.array_equal(np.ascontiguousarray(g).view(np.uint8), np.ascontiguousarray(o).view(np.uint8)), name
+    assert np.array_equal(_bits(mf.cpu().numpy()), _bits(want[7]))
+    m, n, f = (x.cpu().numpy() for x in fused[:3])
+    assert np.array_equal(m, mo) and np.array_equal(n, no) and np.array_equal(_bits(f), _bits(fo))
+    assert np.array_equal(_bits(fused[3].cpu().numpy()), _bits(want[0]))
+    assert np.array_equal(fused[7].cpu().numpy().astype(np.uint8), want[4])
+    assert np.array_equal(_bits(fused[8].cpu().numpy()), _bits(want[5]))
+    assert np.array_equal(_bits(fused[9].cpu().numpy()), _bits(want[7]))

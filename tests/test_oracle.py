@@ -93,6 +93,9 @@ def test_oracle_matches_reference_digests(orc, name):
     assert _digest(o["actions"], o["centroids"]) == d["actions"]
     assert _digest(o["queen_escape"]) == d["queen_escape"]
     assert _digest(o["succ_features"]) == d["successor_features"]
+    hyb = orc.hybrid_encode(st, o["moves"], o["num_legal"])
+    assert _digest(*hyb[:7]) == d["hybrid_tokens"]
+    assert _digest(hyb[7]) == d["hybrid_move_features"]
 
 
 @pytest.mark.skipif(not O.ref_available(), reason="reference host build not present")
