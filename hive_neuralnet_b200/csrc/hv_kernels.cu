@@ -19,6 +19,7 @@
 #include "hv_mcts.cuh"
 #include "hv_tactics.cuh"
 #include "hv_hybrid.cuh"
+#include "hv_trunk.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -1058,6 +1059,40 @@ int hv_generate_legal_moves_and_hybrid_root_features(const uint8_t* states, int6
     HybridOut o{token_features, token_q, token_r, token_z, token_mask, global_features, num_tokens, move_features};
     return launch_hybrid<true, true, true>(states, nullptr, nullptr, batch, moves, num_legal, fnn_features, o,
                                            stream);
+}
+
+int hv_hybrid_trunk_sizes(int* image_elems, int* param_floats) {
+    if (!image_elems || !param_floats) return HV_EINVAL;
+    *image_elems = kImgTp + kTrLayers * kImgLayer;
+    *param_floats = kParLayer0 + kTrLayers * kLEnd;
+    return HV_OK;
+}
+
+int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                    const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                    const uint16_t* weight_image, const float* params, float* graph_summary, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!token_features || !token_q || !token_r || !token_z || !token_mask || !weight_image || !params ||
+        !graph_summary || !aligned16(weight_image) || !aligned16(graph_summary))
+        return HV_EINVAL;
+    if (node_feat_dim < 1 || node_feat_dim > 27) return HV_EINVAL;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HV_ECUDA;
+    DeviceInfo& d = g_dev[dev];
+    if (d.sms == 0 && cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return HV_ECUDA;
+    const size_t smem = sizeof(TrunkSmem);
+    if (cudaFuncSetAttribute(k_hybrid_trunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return HV_ECUDA;
+    const int64_t tiles = (batch + 3) / 4;
+    const int grid = (int)(tiles < d.sms ? tiles : d.sms);
+    uint32_t* err = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
+    k_hybrid_trunk<<<grid, 128, smem, (cudaStream_t)stream>>>(
+        token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim,
+        reinterpret_cast<const __nv_bfloat16*>(weight_image), params, graph_summary, err);
+    return launch_status();
 }
 
 int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,

@@ -1,0 +1,404 @@
+// hv_trunk.cuh -- the hybrid evaluator's relative transformer trunk
+// (fnn_transformer_net.py:75-209 RelativeSelfAttention /
+// RelativeTransformerBlock / HybridRelativeTransformerTrunk), hidden 64,
+// 8 heads of 8, GELU MLP 96, 4 pre-LayerNorm blocks, on sm_100a.
+//
+// One CTA of 4 warps owns a tile of 4 positions = 128 rows (a position is 32
+// rows: CLS, its 28 piece tokens, 3 padding rows), one row per thread, the
+// residual stream in registers.  The five linear layers of a block (token
+// projection once, then QKV, attention output, MLP in and out) are bf16
+// tcgen05.mma GEMMs with M = 128 and fp32 accumulators in TMEM, issued by one
+// thread; the per-head 32 x 32 attention (head width 8, too narrow for an MMA
+// K step) runs on the CUDA cores in fp32 out of shared memory, each warp on
+// its own position.  Block weights stream from global memory (L2-resident)
+// into a double-buffered shared image with bulk copies, one block ahead.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "hv_core.cuh"
+#include "hv_tc.cuh"
+
+namespace hv {
+
+constexpr int kTrH = 64, kTrHeads = 8, kTrFfn = 96, kTrLayers = 4;
+constexpr int kTrKin = 32;   // token features, zero-padded to two MMA K steps
+constexpr int kTrKStride = 68;  // fp32 row stride of the K / V tiles (conflict-free float4 stores)
+
+// bf16 image (elements): token projection, then per block Wqkv, Wo, W1, W2
+constexpr int kImgTp = kTrH * kTrKin;                      // 2048
+constexpr int kImgQkv = 3 * kTrH * kTrH, kImgO = kTrH * kTrH, kImgW1 = kTrFfn * kTrH, kImgW2 = kTrH * kTrFfn;
+constexpr int kImgLayer = kImgQkv + kImgO + kImgW1 + kImgW2;  // 28672
+constexpr uint32_t kImgLayerBytes = kImgLayer * 2;           // 57344
+
+// fp32 parameters: global block, then per transformer block
+constexpr int kParTpB = 0, kParCls = 64, kParFnG = 128, kParFnB = 192, kParLayer0 = 256;
+constexpr int kLLn1G = 0, kLLn1B = 64, kLBqkv = 128, kLBo = 320, kLLn2G = 384, kLLn2B = 448, kLB1 = 512,
+              kLB2 = 608, kLDq = 672, kLDr = 808, kLDz = 944, kLEnd = 984;
+
+struct __align__(16) TrunkSmem {
+    __nv_bfloat16 w[2][kImgLayer];            // block weights, double buffered
+    __nv_bfloat16 tp[kImgTp];                 // token projection weights
+    __nv_bfloat16 a[kTrFfn / 8][128][8];      // A operand (K <= 96)
+    float k[128 * kTrKStride];
+    float v[128 * kTrKStride];
+    int32_t cq[128], cr[128], cz[128];        // token coordinates (CLS and padding 0)
+    float par[kLEnd];                         // this block's fp32 parameters
+    uint64_t bar_w[2], bar_mma;
+    uint32_t tmem;
+    int err;
+};
+
+// 8 values of this thread's row -> slab c of the A operand (one 16-byte store)
+__device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int row, const float* x) {
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(x[0], x[1]);
+    __nv_bfloat162 p1 = __floats2bfloat162_rn(x[2], x[3]);
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(x[4], x[5]);
+    __nv_bfloat162 p3 = __floats2bfloat162_rn(x[6], x[7]);
+    uint4 u;
+    u.x = *reinterpret_cast<uint32_t*>(&p0);
+    u.y = *reinterpret_cast<uint32_t*>(&p1);
+    u.z = *reinterpret_cast<uint32_t*>(&p2);
+    u.w = *reinterpret_cast<uint32_t*>(&p3);
+    *reinterpret_cast<uint4*>(&s->a[c][row][0]) = u;
+}
+
+// write this thread's row (n values) into the A operand in slab layout
+__device__ __forceinline__ void put_row_bf16(TrunkSmem* s, int row, const float* x, int n) {
+#pragma unroll
+    for (int c = 0; c < n / 8; c++) put_chunk8(s, c, row, x + 8 * c);
+}
+
+// LayerNorm of a 64-vector (eps 1e-5, biased variance), gamma/beta from smem
+__device__ __forceinline__ void layer_norm64(const float* x, const float* g, const float* b, float* y) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i++) m += x[i];
+    m *= (1.0f / 64.0f);
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i++) {
+        const float d = x[i] - m;
+        var += d * d;
+    }
+    const float r = rsqrtf(var * (1.0f / 64.0f) + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < 64; i++) y[i] = (x[i] - m) * r * g[i] + b[i];
+}
+
+// one GEMM round: operands visible to the tensor core, issue, commit, wait
+// (uniform result: false if any thread's wait gave up)
+__device__ __forceinline__ bool trunk_gemm(TrunkSmem* s, uint32_t d_col, const void* b, int n, int k,
+                                           uint32_t& mphase) {
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        tc_fence_after();
+        gemm_m128(s->tmem + d_col, &s->a[0][0][0], b, n, k);
+        mma_commit(&s->bar_mma);
+    }
+    const bool ok = mbar_wait(&s->bar_mma, mphase);
+    mphase ^= 1u;
+    tc_fence_after();
+    return __syncthreads_and(ok) != 0;
+}
+
+__device__ __forceinline__ uint32_t lane_taddr(const TrunkSmem* s, int col) {
+    return s->tmem + ((uint32_t)((threadIdx.x >> 5) * 32) << 16) + (uint32_t)col;
+}
+
+__device__ __forceinline__ void prefetch_block(TrunkSmem* s, int buf, const __nv_bfloat16* img, int layer) {
+    const __nv_bfloat16* src = img + kImgTp + (size_t)layer * kImgLayer;
+    mbar_expect_tx(&s->bar_w[buf], kImgLayerBytes);
+    // four copies, one per matrix (each a multiple of 16 bytes)
+    bulk_g2s(&s->w[buf][0], src, kImgQkv * 2, &s->bar_w[buf]);
+    bulk_g2s(&s->w[buf][kImgQkv], src + kImgQkv, kImgO * 2, &s->bar_w[buf]);
+    bulk_g2s(&s->w[buf][kImgQkv + kImgO], src + kImgQkv + kImgO, kImgW1 * 2, &s->bar_w[buf]);
+    bulk_g2s(&s->w[buf][kImgQkv + kImgO + kImgW1], src + kImgQkv + kImgO + kImgW1, kImgW2 * 2, &s->bar_w[buf]);
+}
+
+__device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+// token_features [B,28,27] (first `nfeat` used), token_q/r/z [B,28], token_mask [B,28] (0/1),
+// img: bf16 weight image, par: fp32 parameters; out [B,64]: the normalised CLS row
+__global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict__ tf, const int32_t* __restrict__ tq,
+                                                         const int32_t* __restrict__ tr, const int32_t* __restrict__ tz,
+                                                         const uint8_t* __restrict__ tm, int64_t batch, int nfeat,
+                                                         const __nv_bfloat16* __restrict__ img,
+                                                         const float* __restrict__ par, float* __restrict__ out,
+                                                         uint32_t* err_word) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    TrunkSmem* s = reinterpret_cast<TrunkSmem*>(smem_raw);
+    const int t = threadIdx.x, w = t >> 5, l = t & 31;
+    const int64_t ntiles = (batch + 3) / 4;
+
+    if (t == 0) {
+        mbar_init(&s->bar_w[0], 1);
+        mbar_init(&s->bar_w[1], 1);
+        mbar_init(&s->bar_mma, 1);
+        s->err = 0;
+        fence_mbar_init();
+    }
+    if (w == 0) {
+        tmem_alloc(&s->tmem, 256);
+        tmem_relinquish();
+    }
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(img);
+        uint4* dst = reinterpret_cast<uint4*>(s->tp);
+        for (int i = t; i < kImgTp / 8; i += 128) dst[i] = __ldg(src + i);
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    uint32_t mphase = 0, wphase[2] = {0u, 0u};
+    bool wpend[2] = {false, false};
+    bool mpend = false;
+    bool failed = false;
+    int64_t slot = 0;
+    if (t == 0 && blockIdx.x < ntiles) {
+        prefetch_block(s, 0, img, 0);
+        wpend[0] = true;
+    }
+
+    for (int64_t tile = blockIdx.x; tile < ntiles && !failed; tile += gridDim.x) {
+        const int64_t b = tile * 4 + w;
+        const bool live = b < batch;
+        // ---- inputs of this row: token features (rows 1..28), CLS (row 0), padding (29..31)
+        const int tok = l - 1;
+        const bool is_tok = live && tok >= 0 && tok < 28;
+        const bool valid = (live && l == 0) || (is_tok && tm[b * 28 + tok] != 0);
+        s->cq[t] = is_tok ? tq[b * 28 + tok] : 0;
+        s->cr[t] = is_tok ? tr[b * 28 + tok] : 0;
+        s->cz[t] = is_tok ? tz[b * 28 + tok] : 0;
+        const uint32_t kmask = __ballot_sync(0xffffffffu, valid);
+        {
+            float f[kTrKin];
+#pragma unroll
+            for (int i = 0; i < kTrKin; i++) f[i] = (is_tok && i < nfeat) ? tf[(b * 28 + tok) * 27 + i] : 0.0f;
+            put_row_bf16(s, t, f, kTrKin);
+        }
+        float x[kTrH];
+        mpend = true;
+        if (!trunk_gemm(s, 192, s->tp, kTrH, kTrKin, mphase)) {
+            failed = true;
+            break;
+        }
+        mpend = false;
+        {
+            float d[32];
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const int j = 32 * c + i;
+                    // CLS row: the learned token; pieces: projection times mask; padding: 0
+                    x[j] = (l == 0) ? __ldg(par + kParCls + j)
+                                    : ((is_tok && valid) ? d[i] + __ldg(par + kParTpB + j) : 0.0f);
+                }
+            }
+        }
+
+        for (int layer = 0; layer < kTrLayers; layer++, slot++) {
+            const int buf = (int)(slot & 1);
+            // this block's fp32 parameters
+            __syncthreads();
+            for (int i = t; i < kLEnd; i += 128) s->par[i] = __ldg(par + kParLayer0 + layer * kLEnd + i);
+            // prefetch the next block (next layer, or layer 0 of this CTA's next tile)
+            if (t == 0) {
+                const bool more = layer + 1 < kTrLayers || tile + gridDim.x < ntiles;
+                if (more) {
+                    prefetch_block(s, buf ^ 1, img, (layer + 1) % kTrLayers);
+                    wpend[buf ^ 1] = true;
+                }
+            }
+            __syncthreads();
+            // ---- attention
+            float y[kTrH];
+            layer_norm64(x, s->par + kLLn1G, s->par + kLLn1B, y);
+            put_row_bf16(s, t, y, kTrH);
+            bool okw = true;
+            if (t == 0) {
+                okw = mbar_wait(&s->bar_w[buf], wphase[buf]);
+                wphase[buf] ^= 1u;
+                if (okw) wpend[buf] = false;
+            }
+            if (!__syncthreads_and(okw)) {
+                failed = true;
+                break;
+            }
+            const __nv_bfloat16* W = s->w[buf];
+            mpend = true;
+            if (!trunk_gemm(s, 0, W, 3 * kTrH, kTrH, mphase)) {
+                failed = true;
+                break;
+            }
+            mpend = false;
+            {
+                // keys and values to shared memory; queries stay in TMEM columns 0-63
+                float d[32];
+#pragma unroll
+                for (int c = 2; c < 6; c++) {
+                    tmem_ld32(lane_taddr(s, 32 * c), d);
+                    float* dst = (c < 4 ? s->k + 32 * (c - 2) : s->v + 32 * (c - 4)) + t * kTrKStride;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(dst + i) =
+                            make_float4(d[i] + s->par[kLBqkv + 32 * c + i], d[i + 1] + s->par[kLBqkv + 32 * c + i + 1],
+                                        d[i + 2] + s->par[kLBqkv + 32 * c + i + 2],
+                                        d[i + 3] + s->par[kLBqkv + 32 * c + i + 3]);
+                }
+            }
+            __syncwarp();
+            {
+                // per head: scores of this row's query against the 32 keys of
+                // its position, softmax over the valid ones, weighted values;
+                // the head's 8 outputs are one 16-byte chunk of the A operand
+                const int base = w * 32;
+                const int myq = s->cq[t], myr = s->cr[t], myz = s->cz[t];
+                const float scale = 0.35355339059327373f;  // 8 ** -0.5
+#pragma unroll
+                for (int h = 0; h < kTrHeads; h++) {
+                    float q[8];
+                    tmem_ld8(lane_taddr(s, 8 * h), q);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) q[e] += s->par[kLBqkv + 8 * h + e];
+                    float sc[32];
+                    float mx = -3.0e38f;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float4* kr = reinterpret_cast<const float4*>(s->k + (base + j) * kTrKStride + 8 * h);
+                        const float4 k0 = kr[0], k1 = kr[1];
+                        float dot = q[0] * k0.x;
+                        dot += q[1] * k0.y;
+                        dot += q[2] * k0.z;
+                        dot += q[3] * k0.w;
+                        dot += q[4] * k1.x;
+                        dot += q[5] * k1.y;
+                        dot += q[6] * k1.z;
+                        dot += q[7] * k1.w;
+                        const int dq = min(max(s->cq[base + j] - myq, -8), 8) + 8;
+                        const int dr = min(max(s->cr[base + j] - myr, -8), 8) + 8;
+                        const int dz = min(max(s->cz[base + j] - myz, -2), 2) + 2;
+                        const float sj = dot * scale + s->par[kLDq + dq * 8 + h] + s->par[kLDr + dr * 8 + h] +
+                                         s->par[kLDz + dz * 8 + h];
+                        sc[j] = sj;
+                        if ((kmask >> j) & 1u) mx = fmaxf(mx, sj);
+                    }
+                    float sum = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float p = ((kmask >> j) & 1u) ? __expf(sc[j] - mx) : 0.0f;
+                        sc[j] = p;
+                        sum += p;
+                    }
+                    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;  // no valid key: idle warp
+                    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float4* vr = reinterpret_cast<const float4*>(s->v + (base + j) * kTrKStride + 8 * h);
+                        const float4 v0 = vr[0], v1 = vr[1];
+                        o[0] += sc[j] * v0.x;
+                        o[1] += sc[j] * v0.y;
+                        o[2] += sc[j] * v0.z;
+                        o[3] += sc[j] * v0.w;
+                        o[4] += sc[j] * v1.x;
+                        o[5] += sc[j] * v1.y;
+                        o[6] += sc[j] * v1.z;
+                        o[7] += sc[j] * v1.w;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; e++) o[e] *= inv;
+                    put_chunk8(s, h, t, o);
+                }
+            }
+            mpend = true;
+            if (!trunk_gemm(s, 192, W + kImgQkv, kTrH, kTrH, mphase)) {
+                failed = true;
+                break;
+            }
+            mpend = false;
+            {
+                float d[32];
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) x[32 * c + i] += d[i] + s->par[kLBo + 32 * c + i];
+                }
+            }
+            // ---- MLP
+            layer_norm64(x, s->par + kLLn2G, s->par + kLLn2B, y);
+            put_row_bf16(s, t, y, kTrH);
+            mpend = true;
+            if (!trunk_gemm(s, 0, W + kImgQkv + kImgO, kTrFfn, kTrH, mphase)) {
+                failed = true;
+                break;
+            }
+            mpend = false;
+            {
+                float d[32];
+#pragma unroll
+                for (int c = 0; c < 3; c++) {
+                    tmem_ld32(lane_taddr(s, 32 * c), d);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) d[i] = gelu_exact(d[i] + s->par[kLB1 + 32 * c + i]);
+#pragma unroll
+                    for (int u = 0; u < 4; u++) put_chunk8(s, 4 * c + u, t, d + 8 * u);
+                }
+            }
+            mpend = true;
+            if (!trunk_gemm(s, 192, W + kImgQkv + kImgO + kImgW1, kTrH, kTrFfn, mphase)) {
+                failed = true;
+                break;
+            }
+            mpend = false;
+            {
+                float d[32];
+                const float keep = (l == 0) ? 1.0f : (valid ? 1.0f : 0.0f);
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) x[32 * c + i] = (x[32 * c + i] + d[i] + s->par[kLB2 + 32 * c + i]) * keep;
+                }
+            }
+        }
+        if (failed) break;
+        if (live && l == 0) {
+            float g[64], bb[64], y[64];
+#pragma unroll
+            for (int i = 0; i < 64; i++) {
+                g[i] = __ldg(par + kParFnG + i);
+                bb[i] = __ldg(par + kParFnB + i);
+            }
+            layer_norm64(x, g, bb, y);
+            float4* o4 = reinterpret_cast<float4*>(out + b * kTrH);
+#pragma unroll
+            for (int i = 0; i < 16; i++) o4[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+        }
+    }
+
+    if (failed) {
+        // a bounded wait gave up: record it, let this CTA's own copies and
+        // MMAs in flight finish (bounded again), free TMEM and return
+        if (t == 0) {
+            atomicOr(err_word, 4u);
+            for (int i = 0; i < 2; i++)
+                if (wpend[i]) mbar_wait(&s->bar_w[i], wphase[i]);
+        }
+        if (mpend) mbar_wait(&s->bar_mma, mphase ^ 1u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (w == 0) {
+        tc_fence_after();
+        tmem_dealloc(s->tmem, 256);
+    }
+}
+
+}  // namespace hv

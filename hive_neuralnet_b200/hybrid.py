@@ -200,3 +200,80 @@ class HiveHybridGNN(nn.Module):
 
 
 HiveFNNTransformer = HiveHybridGNN
+
+
+# ---------------------------------------------------------------------------
+# device weight images for the sm_100a kernels
+# ---------------------------------------------------------------------------
+TRUNK_HIDDEN, TRUNK_HEADS, TRUNK_FFN, TRUNK_LAYERS, TRUNK_KIN = 64, 8, 96, 4, 32
+
+
+def _slabs(w: torch.Tensor, k_pad: int | None = None) -> torch.Tensor:
+    """[N, K] row-major -> the kernels' K-major slab layout [K/8][N][8] (zero-padded K)."""
+    n, k = w.shape
+    kp = k_pad or k
+    if kp != k:
+        w = torch.cat([w, w.new_zeros((n, kp - k))], dim=1)
+    return w.reshape(n, kp // 8, 8).permute(1, 0, 2).contiguous().reshape(-1)
+
+
+def check_trunk_config(cfg: HybridGNNConfig) -> None:
+    if (cfg.graph_hidden_dim, cfg.num_heads, cfg.graph_mlp_hidden, cfg.graph_layers) != (
+            TRUNK_HIDDEN, TRUNK_HEADS, TRUNK_FFN, TRUNK_LAYERS):
+        raise NotImplementedError("the sm_100a trunk kernel implements the default and `small` presets "
+                                  "(hidden 64, 8 heads, MLP 96, 4 blocks)")
+    if cfg.rel_coord_clip != 8 or cfg.rel_height_clip != 2:
+        raise NotImplementedError("the sm_100a trunk kernel implements rel_coord_clip 8, rel_height_clip 2")
+
+
+def pack_trunk(trunk: HybridRelativeTransformerTrunk, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """(bf16 weight image as int16 storage, fp32 parameters) in the layout of hv_trunk.cuh."""
+    with torch.no_grad():
+        img = [_slabs(trunk.token_proj.weight.float(), TRUNK_KIN)]
+        par = [trunk.token_proj.bias, trunk.cls_token.reshape(-1), trunk.norm.weight, trunk.norm.bias]
+        for blk in trunk.layers:
+            a = blk.attn
+            img += [_slabs(a.qkv.weight.float()), _slabs(a.out_proj.weight.float()),
+                    _slabs(blk.ffn[0].weight.float()), _slabs(blk.ffn[2].weight.float())]
+            par += [blk.norm1.weight, blk.norm1.bias, a.qkv.bias, a.out_proj.bias, blk.norm2.weight,
+                    blk.norm2.bias, blk.ffn[0].bias, blk.ffn[2].bias, a.dq_bias.weight.reshape(-1),
+                    a.dr_bias.weight.reshape(-1), a.dz_bias.weight.reshape(-1)]
+        image = torch.cat(img).to(torch.bfloat16).view(torch.int16).to(device).contiguous()
+        params = torch.cat([p.detach().float().reshape(-1) for p in par]).to(device).contiguous()
+    return image, params
+
+
+class HybridTrunk:
+    """The relative transformer trunk on the tensor cores: piece tokens -> graph summary [B, 64]."""
+
+    def __init__(self, net: HiveHybridGNN, device="cuda"):
+        check_trunk_config(net.config)
+        self.net, self.device = net, torch.device(device)
+        self.lib = _lib.load()
+        self.refresh()
+
+    def refresh(self) -> None:
+        import ctypes
+        self.image, self.params = pack_trunk(self.net.graph_trunk, self.device)
+        ie, pf = ctypes.c_int(0), ctypes.c_int(0)
+        _lib.check(self.lib.hv_hybrid_trunk_sizes(ctypes.addressof(ie), ctypes.addressof(pf)), "trunk sizes")
+        if (ie.value, pf.value) != (self.image.numel(), self.params.numel()):
+            raise ValueError(f"packed ({self.image.numel()}, {self.params.numel()}), kernel expects "
+                             f"({ie.value}, {pf.value})")
+
+    def __call__(self, pb: HybridPieceTensorBatch) -> torch.Tensor:
+        tf = pb.token_features
+        B = tf.shape[0]
+        out = torch.empty((B, TRUNK_HIDDEN), dtype=torch.float32, device=tf.device)
+        if B == 0:
+            return out
+        if tf.shape[1:] != (MAX_PIECE_TOKENS, ARTICULATION_NODE_FEAT_DIM) or tf.dtype != torch.float32:
+            raise ValueError("token_features: expected float32 [B, 28, 27] (the encoder's full rows)")
+        tq, tr, tz = (t.to(torch.int32).contiguous() for t in (pb.token_q, pb.token_r, pb.token_z))
+        tm = pb.token_mask.to(torch.uint8).contiguous()
+        with torch.cuda.device(tf.device):
+            _lib.check(self.lib.hv_hybrid_trunk(
+                tf.contiguous().data_ptr(), tq.data_ptr(), tr.data_ptr(), tz.data_ptr(), tm.data_ptr(), B,
+                self.net.config.node_feat_dim, self.image.data_ptr(), self.params.data_ptr(), out.data_ptr(),
+                torch.cuda.current_stream(tf.device).cuda_stream), "hybrid_trunk")
+        return out

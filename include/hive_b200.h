@@ -211,6 +211,19 @@ int hv_generate_legal_moves_and_hybrid_root_features(const uint8_t* states, int6
                                                      uint8_t* token_mask, float* global_features,
                                                      int32_t* num_tokens, float* move_features, void* stream);
 
+/* Relative transformer trunk of the hybrid evaluator (hive_fnn_transformer/
+ * fnn_transformer_net.py:159-209 HybridRelativeTransformerTrunk.forward), the
+ * default / `small` presets: hidden 64, 8 heads, MLP 96, 4 blocks.  Inputs are
+ * hv_hybrid_encode's outputs (token_features [batch, 28, 27], first
+ * node_feat_dim columns used); weight_image (bf16 bits) and params (f32) are
+ * packed by hive_neuralnet_b200.hybrid.pack_trunk, sizes from
+ * hv_hybrid_trunk_sizes.  graph_summary [batch, 64] f32.  No reference
+ * counterpart as a single call: it replaces the torch module's forward. */
+int hv_hybrid_trunk_sizes(int* image_elems, int* param_floats);
+int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                    const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                    const uint16_t* weight_image, const float* params, float* graph_summary, void* stream);
+
 /* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
  *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
  * replaces bindings.cpp:91-100,336-339 / game_logic.cu:290-397,1579-1615.
