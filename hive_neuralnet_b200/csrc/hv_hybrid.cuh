@@ -229,3 +229,47 @@ __device__ __forceinline__ void move_features(const Pos& P, const uint8_t* st, c
 }
 
 }  // namespace hv
+
+namespace hv {
+
+// ---------------------------------------------------------------------------
+// hybrid policy / value heads (fnn_transformer_net.py:233-327), fp32:
+//   value  = tanh(vh2 . relu(vh1 [e_root ; g ; global6] + b) + b)
+//   g_ctx  = pg g + b                                   (policy_graph_proj)
+//   logit  = pf2 . sigmoid(pf1 [e_root ; g_ctx ; e_succ ; pm m + b] + b) + b
+// The move-projection block of pf1 is folded on the host:
+//   pf1[:, 3E:4E] (pm m + bm) = C m + c,  C = pf1[:, 3E:4E] pm,  c = pf1[:, 3E:4E] bm
+// Packed layout (transposed so lane o reads row k at column o):
+//   pgT [64][E]  pgb [E]  pf1T [3E][A]  cT [31][A]  pf1b' [A] (b + c)
+//   pf2 [A]  pf2b [1]  vh1T [E+70][V]  vh1b [V]  vh2 [V]  vh2b [1]
+// ---------------------------------------------------------------------------
+constexpr int kHybGraph = 64;
+constexpr int kHybMaxValue = 128;
+
+struct HybDims {
+    int E, A, V;
+};
+
+struct HybOffsets {
+    int pgT, pgb, pf1T, cT, pf1b, pf2, pf2b, vh1T, vh1b, vh2, vh2b, total;
+};
+
+__host__ __device__ inline HybOffsets hyb_offsets(HybDims d) {
+    HybOffsets o;
+    int p = 0;
+    o.pgT = p; p += kHybGraph * d.E;
+    o.pgb = p; p += d.E;
+    o.pf1T = p; p += 3 * d.E * d.A;
+    o.cT = p; p += kMoveFeat * d.A;
+    o.pf1b = p; p += d.A;
+    o.pf2 = p; p += d.A;
+    o.pf2b = p; p += 1;
+    o.vh1T = p; p += (d.E + kHybGraph + kGlobFeat) * d.V;
+    o.vh1b = p; p += d.V;
+    o.vh2 = p; p += d.V;
+    o.vh2b = p; p += 1;
+    o.total = p;
+    return o;
+}
+
+}  // namespace hv

@@ -227,6 +227,205 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
 }
 
 // ---------------------------------------------------------------------------
+// hybrid leaf evaluation (fnn_transformer_mcts_orchestrator.py:42-169
+// _eval_states): FNN encode of the root and of every successor (generated
+// in shared memory, as in k_fnn_eval), the transformer summary g from the
+// trunk kernel, value and hybrid action scores, masked softmax; child Q = 0
+// ---------------------------------------------------------------------------
+struct HybSmem {
+    float xm[kFnnChunk][32];  // move features of the chunk's moves
+};
+
+__device__ __forceinline__ HybSmem* hyb_slot() {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    return reinterpret_cast<HybSmem*>(smem_raw + (sizeof(WarpSmem) + sizeof(FnnSmem)) * kWarpsPerBlock) +
+           (threadIdx.x >> 5);
+}
+
+__global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
+    const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal_moves,
+    const int32_t* __restrict__ num_legal, const float* __restrict__ root_feats, const float* __restrict__ graph,
+    const float* __restrict__ glob, int64_t count, const float* __restrict__ fw, FnnDims fd,
+    const float* __restrict__ hw, HybDims hd, float* __restrict__ priors, float* __restrict__ values,
+    float* __restrict__ child_q, float* __restrict__ logits_out) {
+    WarpSmem* w = warp_slot();
+    FnnSmem* f = fnn_slot();
+    HybSmem* x = hyb_slot();
+    const FnnOffsets fo = fnn_offsets(fd);
+    const HybOffsets ho = hyb_offsets(hd);
+    const int E = hd.E, A = hd.A, V = hd.V;
+    const int l = lane_id();
+    const int o0 = l, o1 = l + 32;
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < count;
+         p += nwarps) {
+        int n = num_legal[p];
+        n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
+        const uint8_t* st_g = states + p * kStateBytes;
+        const uint8_t* mv_g = legal_moves + p * (kMaxMoves * kMoveBytes);
+        if (root_feats) {
+            for (int k = l; k < kFeat; k += 32) f->xs[0][k] = root_feats[p * kFeat + k];
+            __syncwarp();
+        } else {
+            stage_state(w, st_g);
+            const uint4* s4 = reinterpret_cast<const uint4*>(mv_g);
+            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
+            for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
+            __syncwarp();
+            Setup S = setup_position(w);
+            features(w, S, n, f->xs[0]);
+        }
+        float val[kFnnChunk], lg[kFnnChunk];
+        fnn_encode_chunk(fw, fd, fo, f, 1, val);
+        for (int k = l; k < E; k += 32) f->root_emb[k] = f->ys[0][k];
+        // per-leaf scratch in the (not yet used) logit row: g, global features, g_ctx
+        float* sg = f->logit;
+        float* sgl = f->logit + kHybGraph;
+        float* sgc = f->logit + kHybGraph + 8;
+        for (int k = l; k < kHybGraph; k += 32) sg[k] = graph[p * kHybGraph + k];
+        if (l < kGlobFeat) sgl[l] = glob[p * kGlobFeat + l];
+        __syncwarp();
+        // value head: lane owns hidden units l, l+32, l+64, l+96
+        float root_value;
+        {
+            float acc[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[i] = (l + 32 * i) < V ? __ldg(hw + ho.vh1b + l + 32 * i) : 0.0f;
+            const int nin = E + kHybGraph + kGlobFeat;
+#pragma unroll 2
+            for (int k = 0; k < nin; k++) {
+                const float in = k < E ? f->root_emb[k] : (k < E + kHybGraph ? sg[k - E] : sgl[k - E - kHybGraph]);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (l + 32 * i < V) acc[i] = fmaf(__ldg(hw + ho.vh1T + k * V + l + 32 * i), in, acc[i]);
+            }
+            float part = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (l + 32 * i < V) part += __ldg(hw + ho.vh2 + l + 32 * i) * fmaxf(acc[i], 0.0f);
+            root_value = tanhf(warp_sum(part) + __ldg(hw + ho.vh2b));
+        }
+        // graph context g_ctx = pg g + b
+        {
+            float a = o0 < E ? __ldg(hw + ho.pgb + o0) : 0.0f, b = o1 < E ? __ldg(hw + ho.pgb + o1) : 0.0f;
+            for (int k = 0; k < kHybGraph; k++) {
+                const float gk = sg[k];
+                if (o0 < E) a = fmaf(__ldg(hw + ho.pgT + k * E + o0), gk, a);
+                if (o1 < E) b = fmaf(__ldg(hw + ho.pgT + k * E + o1), gk, b);
+            }
+            __syncwarp();
+            if (o0 < E) sgc[o0] = a;
+            if (o1 < E) sgc[o1] = b;
+            __syncwarp();
+        }
+        // root half of policy_fc1: b' + W[:, 0:E] e_root + W[:, E:2E] g_ctx
+        {
+            float a = o0 < A ? __ldg(hw + ho.pf1b + o0) : 0.0f, b = o1 < A ? __ldg(hw + ho.pf1b + o1) : 0.0f;
+            for (int k = 0; k < E; k++) {
+                const float er = f->root_emb[k], gc = sgc[k];
+                if (o0 < A) a = fmaf(__ldg(hw + ho.pf1T + k * A + o0), er, fmaf(__ldg(hw + ho.pf1T + (E + k) * A + o0), gc, a));
+                if (o1 < A) b = fmaf(__ldg(hw + ho.pf1T + k * A + o1), er, fmaf(__ldg(hw + ho.pf1T + (E + k) * A + o1), gc, b));
+            }
+            if (o0 < A) f->root_pre[o0] = a;
+            if (o1 < A) f->root_pre[o1] = b;
+            __syncwarp();
+        }
+        float* cq = child_q + p * kMaxMoves;
+#pragma unroll 1
+        for (int base = 0; base < n; base += kFnnChunk) {
+            const int ns = min(kFnnChunk, n - base);
+            // move features of this chunk, read off the leaf position
+            stage_state(w, st_g);
+            {
+                Pos P{w};
+                const MoveCtx X = move_ctx(w);
+                if (l < ns) {
+                    const uint8_t* m = mv_g + (base + l) * kMoveBytes;
+                    float mf[kMoveFeat];
+                    move_features(P, w->st, X, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8), mf);
+#pragma unroll
+                    for (int k = 0; k < kMoveFeat; k++) x->xm[l][k] = mf[k];
+                }
+                __syncwarp();
+            }
+#pragma unroll 1
+            for (int s = 0; s < ns; s++) {
+                stage_state(w, st_g);
+                if (l == 0) {
+                    const uint8_t* m = mv_g + (base + s) * kMoveBytes;
+                    st_apply(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+                }
+                __syncwarp();
+                Setup S = setup_position(w);
+                int cn = gen_compact(w, S, &g_error);
+                features(w, S, cn, f->xs[s]);
+            }
+            fnn_encode_chunk(fw, fd, fo, f, ns, val);
+            // z = root_pre + W[:, 2E:3E] e_succ + C m
+            float z[kFnnChunk][2];
+            const float r0 = o0 < A ? f->root_pre[o0] : 0.0f, r1 = o1 < A ? f->root_pre[o1] : 0.0f;
+#pragma unroll
+            for (int s = 0; s < kFnnChunk; s++) {
+                z[s][0] = r0;
+                z[s][1] = r1;
+            }
+#pragma unroll 2
+            for (int k = 0; k < E; k++) {
+                const float w0 = o0 < A ? __ldg(hw + ho.pf1T + (2 * E + k) * A + o0) : 0.0f;
+                const float w1 = o1 < A ? __ldg(hw + ho.pf1T + (2 * E + k) * A + o1) : 0.0f;
+#pragma unroll
+                for (int s = 0; s < kFnnChunk; s++) {
+                    const float e = f->ys[s][k];
+                    z[s][0] = fmaf(w0, e, z[s][0]);
+                    z[s][1] = fmaf(w1, e, z[s][1]);
+                }
+            }
+#pragma unroll 1
+            for (int k = 0; k < kMoveFeat; k++) {
+                const float w0 = o0 < A ? __ldg(hw + ho.cT + k * A + o0) : 0.0f;
+                const float w1 = o1 < A ? __ldg(hw + ho.cT + k * A + o1) : 0.0f;
+#pragma unroll
+                for (int s = 0; s < kFnnChunk; s++) {
+                    const float mk = x->xm[s][k];
+                    z[s][0] = fmaf(w0, mk, z[s][0]);
+                    z[s][1] = fmaf(w1, mk, z[s][1]);
+                }
+            }
+            const float u0 = o0 < A ? __ldg(hw + ho.pf2 + o0) : 0.0f, u1 = o1 < A ? __ldg(hw + ho.pf2 + o1) : 0.0f;
+            const float b2 = __ldg(hw + ho.pf2b);
+#pragma unroll
+            for (int s = 0; s < kFnnChunk; s++) {
+                float t = (o0 < A ? u0 * sigmoidf_(z[s][0]) : 0.0f) + (o1 < A ? u1 * sigmoidf_(z[s][1]) : 0.0f);
+                lg[s] = warp_sum(t) + b2;
+            }
+            if (l < ns) {
+                float lv = lg[0];
+#pragma unroll
+                for (int s = 1; s < kFnnChunk; s++)
+                    if (l == s) lv = lg[s];
+                f->logit[base + l] = lv;
+            }
+            __syncwarp();
+        }
+        float mx = -INFINITY;
+        for (int i = l; i < n; i += 32) mx = fmaxf(mx, f->logit[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        float sum = 0.0f;
+        for (int i = l; i < n; i += 32) sum += expf(f->logit[i] - mx);
+        sum = warp_sum(sum);
+        float* pr = priors + p * kMaxMoves;
+        for (int i = l; i < kMaxMoves; i += 32) {
+            pr[i] = i < n ? expf(f->logit[i] - mx) / sum : 0.0f;
+            cq[i] = 0.0f;
+            if (logits_out) logits_out[p * kMaxMoves + i] = i < n ? f->logit[i] : 0.0f;
+        }
+        if (l == 0) values[p] = root_value;
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // queen escape flags (game_logic.cu:133-142, move_gen.cuh:771-821): can the
 // side to move's queen slide away, or be thrown by an own pillbug / a ground
 // mosquito next to a pillbug?
@@ -1129,6 +1328,34 @@ int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, co
                                                allowed_slots);
     }
     k_tac_final<<<root_grid, kThreads, 0, s>>>(num_legal, batch, winning_move, allowed_slots, forced_random);
+    return launch_status();
+}
+
+int hv_hybrid_head_weights_size(int embed, int action_hidden, int value_hidden) {
+    return hyb_offsets(HybDims{embed, action_hidden, value_hidden}).total;
+}
+
+int hv_hybrid_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                          const float* root_features, const float* graph_summary, const float* global_features,
+                          int64_t count, const float* fnn_weights, int hidden, int embed, int action_hidden,
+                          const float* head_weights, int value_hidden, float* priors, float* values,
+                          float* child_q, float* logits, void* stream) {
+    if (count < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!states || !legal_moves || !num_legal || !graph_summary || !global_features || !fnn_weights ||
+        !head_weights || !priors || !values || !child_q || !aligned16(states) || !aligned16(legal_moves))
+        return HV_EINVAL;
+    if (hidden < 1 || hidden > kFnnMaxDim || embed < 1 || embed > kFnnMaxDim || action_hidden < 1 ||
+        action_hidden > kFnnMaxDim || value_hidden < 1 || value_hidden > kHybMaxValue)
+        return HV_EINVAL;
+    size_t smem = (sizeof(WarpSmem) + sizeof(FnnSmem) + sizeof(HybSmem)) * kWarpsPerBlock;
+    int grid = 0;
+    int rc = grid_for(k_hybrid_eval, count, smem, &grid);
+    if (rc) return rc;
+    k_hybrid_eval<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+        states, legal_moves, num_legal, root_features, graph_summary, global_features, count, fnn_weights,
+        FnnDims{hidden, embed, action_hidden}, head_weights, HybDims{embed, action_hidden, value_hidden}, priors,
+        values, child_q, logits);
     return launch_status();
 }
 

@@ -277,3 +277,72 @@ class HybridTrunk:
                 self.net.config.node_feat_dim, self.image.data_ptr(), self.params.data_ptr(), out.data_ptr(),
                 torch.cuda.current_stream(tf.device).cuda_stream), "hybrid_trunk")
         return out
+
+
+def pack_heads(net: HiveHybridGNN, device) -> torch.Tensor:
+    """fp32 policy / value head weights in the layout of hv_hybrid.cuh (hyb_offsets); the
+    move-projection block of policy_fc1 is folded into a [A, 31] matrix on the host (float64)."""
+    e = net.fnn.config.embed_dim
+    with torch.no_grad():
+        w1 = net.policy_fc1.weight.double()
+        wm = w1[:, 3 * e:4 * e]
+        fold = wm @ net.policy_move_proj.weight.double()          # [A, 31]
+        b1 = net.policy_fc1.bias.double() + wm @ net.policy_move_proj.bias.double()
+        parts = [net.policy_graph_proj.weight.t(), net.policy_graph_proj.bias, w1[:, :3 * e].t(), fold.t(), b1,
+                 net.policy_fc2.weight.reshape(-1), net.policy_fc2.bias, net.value_head[0].weight.t(),
+                 net.value_head[0].bias, net.value_head[2].weight.reshape(-1), net.value_head[2].bias]
+        flat = torch.cat([p.detach().double().contiguous().reshape(-1) for p in parts]).float()
+    return flat.to(device).contiguous()
+
+
+class HybridEvaluator:
+    """Leaf evaluation of the hybrid network with the signature and outputs of the
+    reference's ``HybridMCTSOrchestrator._eval_states``: (priors [T,256], values [T],
+    child_q [T,256] = 0).  Piece tokens (k_hybrid), trunk (tcgen05), fused heads."""
+
+    def __init__(self, net: HiveHybridGNN, device="cuda"):
+        from .fnn import pack_weights
+        from .hive_gpu import load_extension
+        self.net, self.device = net, torch.device(device)
+        self.lib = _lib.load()
+        self.ext = load_extension()
+        self.trunk = HybridTrunk(net, self.device)
+        fc = net.fnn.config
+        self.fdims = (fc.hidden_dim, fc.embed_dim, fc.action_hidden)
+        self.vh = net.config.value_hidden
+        self._pack_weights = pack_weights
+        self.refresh()
+
+    def refresh(self) -> None:
+        """Re-pack every weight image (call after the network was trained)."""
+        self.trunk.refresh()
+        self.fnn_weights = self._pack_weights(self.net.fnn, self.device)
+        self.head_weights = pack_heads(self.net, self.device)
+        want = self.lib.hv_hybrid_head_weights_size(self.fdims[1], self.fdims[2], self.vh)
+        if want != self.head_weights.numel():
+            raise ValueError(f"packed {self.head_weights.numel()} head floats, kernel expects {want}")
+
+    def eval_states(self, states, legal_moves, num_legal, total, root_features=None, return_logits=False):
+        dev = states.device
+        priors = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
+        values = torch.empty((total,), dtype=torch.float32, device=dev)
+        child_q = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
+        logits = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev) if return_logits else None
+        if total == 0:
+            return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
+        tf, tq, tr, tz, tm, gf, nt = self.ext.hybrid_transformer_encode_with_moves_batch(
+            states, legal_moves, num_legal, total)
+        graph = self.trunk(HybridPieceTensorBatch(tf, tq, tr, tz, tm, gf, nt))
+        if root_features is not None and (root_features.dtype != torch.float32 or not root_features.is_contiguous()):
+            raise ValueError("root_features: expected contiguous float32")
+        with torch.cuda.device(dev):
+            _lib.check(self.lib.hv_hybrid_eval_leaves(
+                states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
+                None if root_features is None else root_features.data_ptr(), graph.data_ptr(), gf.data_ptr(),
+                total, self.fnn_weights.data_ptr(), *self.fdims, self.head_weights.data_ptr(), self.vh,
+                priors.data_ptr(), values.data_ptr(), child_q.data_ptr(),
+                None if logits is None else logits.data_ptr(), torch.cuda.current_stream(dev).cuda_stream),
+                "hybrid_eval_leaves")
+        if return_logits:
+            return priors, values, child_q, logits
+        return priors, values, child_q

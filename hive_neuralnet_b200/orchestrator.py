@@ -661,3 +661,37 @@ class FNNPUCTOrchestrator(_SearchBase):
                                                        float(cfg.final_value_weight) != 1.0) else 1.0
                 out[i].append(FNNTrainingExample(sb, pi, float(_result_to_value(winner, turn)), True, use_v, vw))
         return out
+
+
+# ---------------------------------------------------------------------------
+# hybrid FNN-transformer drivers
+# ---------------------------------------------------------------------------
+@dataclass
+class HybridMCTSConfig(FNNMCTSConfig):
+    """hive_fnn_transformer/fnn_transformer_mcts_orchestrator.py:20-22."""
+
+
+@dataclass
+class HybridPUCTConfig(FNNPUCTConfig):
+    """PUCT waves with the hybrid evaluator (the FNNPUCTConfig fields)."""
+
+
+class HybridMCTSOrchestrator(FNNMCTSOrchestrator):
+    """Gumbel-root MCTS with relative-transformer policy / value evaluation
+    (fnn_transformer_mcts_orchestrator.py:25-169): child initial Q is zero."""
+
+    def __init__(self, net, config: HybridMCTSConfig | None = None, device: str = "cuda") -> None:
+        from .hybrid import HybridEvaluator
+        super().__init__(net.fnn, config or HybridMCTSConfig(), device)
+        self.net = net
+        self.evaluator = HybridEvaluator(net, self.device)
+
+
+class HybridPUCTOrchestrator(FNNPUCTOrchestrator):
+    """PUCT MCTS (fnn_puct_orchestrator.py:140-386) with the hybrid evaluator."""
+
+    def __init__(self, net, config: HybridPUCTConfig | None = None, device: str = "cuda") -> None:
+        from .hybrid import HybridEvaluator
+        super().__init__(net.fnn, config or HybridPUCTConfig(), device)
+        self.net = net
+        self.evaluator = HybridEvaluator(net, self.device)

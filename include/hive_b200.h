@@ -224,6 +224,22 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
                     const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
                     const uint16_t* weight_image, const float* params, float* graph_summary, void* stream);
 
+/* Hybrid leaf evaluation: HybridMCTSOrchestrator._eval_states
+ * (hive_fnn_transformer/fnn_transformer_mcts_orchestrator.py:42-169) given
+ * the trunk's graph_summary [count, 64] and the encoder's global_features
+ * [count, 6]: FNN encode of the root (root_features [count, 122] or NULL to
+ * compute them) and of every legal successor, tanh value head, hybrid action
+ * scores, masked softmax.  priors / child_q / logits [count, 256] (child_q is
+ * zero, as in the reference), values [count].  fnn_weights as for
+ * hv_fnn_eval_leaves; head_weights packed by
+ * hive_neuralnet_b200.hybrid.pack_heads (hv_hybrid_head_weights_size floats). */
+int hv_hybrid_head_weights_size(int embed, int action_hidden, int value_hidden);
+int hv_hybrid_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                          const float* root_features, const float* graph_summary, const float* global_features,
+                          int64_t count, const float* fnn_weights, int hidden, int embed, int action_hidden,
+                          const float* head_weights, int value_hidden, float* priors, float* values,
+                          float* child_q, float* logits, void* stream);
+
 /* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
  *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
  * replaces bindings.cpp:91-100,336-339 / game_logic.cu:290-397,1579-1615.
