@@ -354,11 +354,21 @@ MCTS_GAMES = 512
 MCTS_SIMS = 4096
 
 
-def _mcts_start_states(ext, n, seed, device):
-    """Seeded in-progress base-game positions (ply U[0, 30]) as search roots."""
-    st = ext.generate_positions(seed, 0, n * 2, 30, 0, device=device)
-    res = ext.check_results_batch(st, n * 2)
-    keep = torch_nonzero(res == 0)[:n]
+def _mcts_start_states(ext, n, seed, device, no_immediate_end=False):
+    """Seeded in-progress base-game positions (ply U[0, 30]) as search roots.
+    ``no_immediate_end`` keeps only positions where no legal move ends the game
+    (the PUCT driver skips the whole batch's search when any game can win at
+    once, fnn_puct_orchestrator.py:203-208)."""
+    m = n * 4
+    st = ext.generate_positions(seed, 0, m, 30, 0, device=device)
+    ok = ext.check_results_batch(st, m) == 0
+    if no_immediate_end:
+        legal, nl = ext.generate_legal_moves_batch(st, m)
+        res, _, _ = ext.child_probe_batch(st, legal, nl, m, False)
+        ok &= (res == 0).all(dim=1) & (nl > 0)
+    keep = torch_nonzero(ok)[:n]
+    if keep.numel() < n:
+        raise RuntimeError(f"only {keep.numel()} of {n} start positions qualified")
     return st[keep].contiguous()
 
 
@@ -477,10 +487,119 @@ def run_fnn(args) -> None:
                       "mlp_tflops": flops / (ms / 1e3) / 1e12}), flush=True)
 
 
+HYBRID_GAMES = 256
+HYBRID_SIMS = 1024
+HYBRID_WAVE = 32  # 256 games x 32 = 8,192 leaves per wave
+TRUNK_FLOP_PER_LEAF = 7.61e6  # algorithmic trunk FLOPs per position (29 tokens, 4 blocks)
+
+
+def run_hybrid(args) -> None:
+    """Config 5: PUCT MCTS with the hybrid FNN-transformer evaluator, 256
+    games/GPU, 1,024 simulations per move, c_puct 1.5, 8,192 leaves per wave,
+    HybridGNNConfig() random init (seed 0), bf16 tensor-core trunk.  One step
+    = one searched move of every game; metric = simulations per second."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from hive_neuralnet_b200.hive_gpu import load_extension
+    from hive_neuralnet_b200.hybrid import HiveHybridGNN, HybridPieceTensorBatch
+    from hive_neuralnet_b200.orchestrator import HybridPUCTConfig, HybridPUCTOrchestrator
+    ext = load_extension()
+    torch.manual_seed(0)
+    net = HiveHybridGNN().eval()
+    games = args.games if args.games != MCTS_GAMES else HYBRID_GAMES
+    sims = args.sims if args.sims != MCTS_SIMS else HYBRID_SIMS
+    cfg = HybridPUCTConfig(num_simulations=sims, batch_size=games, max_game_length=1, dirichlet_epsilon=0.0,
+                           seed=4321 + rank, max_tree_nodes=65536, wave_size=HYBRID_WAVE, c_puct=1.5)
+    orch = HybridPUCTOrchestrator(net, cfg, device=dev)
+    starts = [_mcts_start_states(ext, games, SEED + 131 * (rank * 1000 + i), dev, no_immediate_end=True).cpu()
+              for i in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        orch.self_play_batch(starts[i])
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+    orch.sims_done.zero_()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, args.warmup + args.steps):
+        orch.self_play_batch(starts[i])
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    done = orch.sims_done.to(torch.float64).reshape(1)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(done, op=dist.ReduceOp.SUM)
+    ms = float(t.item())
+    value = float(done.item()) / (ms / 1e3)
+
+    # trunk kernel alone on one wave's worth of leaves (8,192 positions)
+    L = games * HYBRID_WAVE
+    st = ext.generate_positions(SEED + 5, 0, L, MAX_PLY, 0, device=dev)
+    mv, nl = ext.generate_legal_moves_batch(st, L)
+    pb = HybridPieceTensorBatch(*ext.hybrid_transformer_encode_with_moves_batch(st, mv, nl, L))
+    trunk = orch.evaluator.trunk
+    for _ in range(3):
+        trunk(pb)
+    torch.cuda.synchronize(dev)
+    reps = 20
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(reps):
+        trunk(pb)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    trunk_ms = t0.elapsed_time(t1) / reps
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, peak_kind = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    achieved = L * TRUNK_FLOP_PER_LEAF / (trunk_ms / 1e3) / 1e12
+    if rank == 0:
+        line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": f"config5: PUCT {games} games/GPU x {sims} sims/move, c_puct 1.5, "
+                                       f"{games * HYBRID_WAVE} leaves/wave, HybridGNNConfig() random init "
+                                       f"({net.count_parameters()} params)",
+                           "simulations": float(done.item()), "games_per_gpu": games,
+                           "parallelism": f"games sharded dp{world}" if world > 1 else "single GPU"},
+                "e2e": {"value": value, "unit": "simulations/s",
+                        "h2d_bytes_per_step": games * STATE_BYTES, "d2h_bytes_per_step": None,
+                        "note": "start states come from host memory and training examples return to it "
+                                "inside every timed step"},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                             "kernel": f"k_hybrid_trunk on {L} positions ({trunk_ms:.3f} ms)",
+                             "algorithmic_flop_per_position": TRUNK_FLOP_PER_LEAF},
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     global POSITIONS
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["movegen", "mcts", "fnn"], default="movegen")
+    ap.add_argument("--workload", choices=["movegen", "mcts", "fnn", "hybrid"], default="movegen")
     ap.add_argument("--games", type=int, default=MCTS_GAMES)
     ap.add_argument("--sims", type=int, default=MCTS_SIMS)
     ap.add_argument("--gpus", type=int, default=1)
@@ -501,6 +620,8 @@ def main() -> None:
         run_mcts(args)
     elif args.workload == "fnn":
         run_fnn(args)
+    elif args.workload == "hybrid":
+        run_hybrid(args)
     else:
         run_gpu(args)
 
