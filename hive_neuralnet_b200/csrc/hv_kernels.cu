@@ -995,6 +995,8 @@ __global__ void __launch_bounds__(kThreads) k_playouts(uint64_t seed, int64_t fi
     }
 }
 
+constexpr int kActionSpace = 85834;  // ENC_GRID 17: 8 x 289 placements + 289 x 289 moves + pass
+
 // round-half-to-even of sum / n (state_encoder.cuh:55-79)
 __device__ __forceinline__ int round_half_even(int sum, int n) {
     int q = sum / n, r = sum - q * n;
@@ -1011,7 +1013,8 @@ __global__ void __launch_bounds__(kThreads) k_actions(const uint8_t* __restrict_
                                                       const uint8_t* __restrict__ moves,
                                                       const int32_t* __restrict__ num_legal,
                                                       int64_t batch, int32_t* __restrict__ actions,
-                                                      int32_t* __restrict__ centroids) {
+                                                      int32_t* __restrict__ centroids,
+                                                      float* __restrict__ masks) {
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
     const int l = lane_id();
     for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
@@ -1034,8 +1037,16 @@ __global__ void __launch_bounds__(kThreads) k_actions(const uint8_t* __restrict_
             centroids[2 * p] = cq;
             centroids[2 * p + 1] = cr;
         }
-        if (actions) {
+        float* mrow = masks ? masks + p * (int64_t)kActionSpace : nullptr;
+        if (mrow) {
+            // zero the row (8-byte aligned: 85834 floats per row), then set the legal actions
+            float2* m2 = reinterpret_cast<float2*>(mrow);
+            for (int i = l; i < kActionSpace / 2; i += 32) m2[i] = make_float2(0.0f, 0.0f);
+            __syncwarp();
+        }
+        if (actions || mrow) {
             int nl = num_legal[p];
+            nl = nl < 0 ? 0 : (nl > kMaxMoves ? kMaxMoves : nl);
             const uint8_t* mv = moves + p * (kMaxMoves * kMoveBytes);
             for (int m = l; m < kMaxMoves; m += 32) {
                 int a = -1;
@@ -1054,9 +1065,11 @@ __global__ void __launch_bounds__(kThreads) k_actions(const uint8_t* __restrict_
                             a = 2312 + (srr * 17 + sc) * 289 + dr * 17 + dc;
                     }
                 }
-                actions[p * kMaxMoves + m] = a;
+                if (actions) actions[p * kMaxMoves + m] = a;
+                if (mrow && a >= 0 && a < kActionSpace) mrow[a] = 1.0f;
             }
         }
+        __syncwarp();
     }
 }
 
@@ -1294,6 +1307,77 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
     return launch_status();
 }
 
+// workspace of hv_hybrid_evaluate: per position tokens, coordinates, mask,
+// global features, token count and the trunk's summary, each array 256-byte aligned
+struct HybridWorkspace {
+    float* tf;
+    int32_t *tq, *tr, *tz;
+    uint8_t* tm;
+    float* gf;
+    int32_t* ntok;
+    float* graph;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static size_t hybrid_workspace_layout(int64_t count, uint8_t* base, HybridWorkspace* w) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t* p = base ? base + off : nullptr;
+        off += align256(bytes);
+        return p;
+    };
+    const size_t n = (size_t)count;
+    uint8_t* tf = take(n * kTokens * kTokFeat * sizeof(float));
+    uint8_t* tq = take(n * kTokens * sizeof(int32_t));
+    uint8_t* tr = take(n * kTokens * sizeof(int32_t));
+    uint8_t* tz = take(n * kTokens * sizeof(int32_t));
+    uint8_t* tm = take(n * kTokens);
+    uint8_t* gf = take(n * kGlobFeat * sizeof(float));
+    uint8_t* nt = take(n * sizeof(int32_t));
+    uint8_t* gr = take(n * kHybGraph * sizeof(float));
+    if (w) {
+        w->tf = reinterpret_cast<float*>(tf);
+        w->tq = reinterpret_cast<int32_t*>(tq);
+        w->tr = reinterpret_cast<int32_t*>(tr);
+        w->tz = reinterpret_cast<int32_t*>(tz);
+        w->tm = tm;
+        w->gf = reinterpret_cast<float*>(gf);
+        w->ntok = reinterpret_cast<int32_t*>(nt);
+        w->graph = reinterpret_cast<float*>(gr);
+    }
+    return off;
+}
+
+int hv_hybrid_workspace_bytes(int64_t count, size_t* bytes) {
+    if (count < 0 || !bytes) return HV_EINVAL;
+    *bytes = hybrid_workspace_layout(count, nullptr, nullptr);
+    return HV_OK;
+}
+
+int hv_hybrid_evaluate(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                       const float* root_features, int64_t count, int node_feat_dim, const uint16_t* trunk_image,
+                       const float* trunk_params, const float* fnn_weights, int hidden, int embed,
+                       int action_hidden, const float* head_weights, int value_hidden, float* priors,
+                       float* values, float* child_q, float* logits, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    if (count < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+        workspace_bytes < hybrid_workspace_layout(count, nullptr, nullptr))
+        return HV_EINVAL;
+    HybridWorkspace w;
+    hybrid_workspace_layout(count, static_cast<uint8_t*>(workspace), &w);
+    int rc = hv_hybrid_encode(states, count, w.tf, w.tq, w.tr, w.tz, w.tm, w.gf, w.ntok, stream);
+    if (rc) return rc;
+    rc = hv_hybrid_trunk(w.tf, w.tq, w.tr, w.tz, w.tm, count, node_feat_dim, trunk_image, trunk_params, w.graph,
+                         stream);
+    if (rc) return rc;
+    return hv_hybrid_eval_leaves(states, legal_moves, num_legal, root_features, w.graph, w.gf, count, fnn_weights,
+                                 hidden, embed, action_hidden, head_weights, value_hidden, priors, values, child_q,
+                                 logits, stream);
+}
+
 int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
                            const float* priors, int64_t batch, int enable_win_in_one,
                            int enable_check_opponent_wins, int enable_win_in_two, int64_t* winning_move,
@@ -1515,7 +1599,7 @@ int hv_compute_centroids(const uint8_t* states, int64_t batch, int32_t* centroid
     int rc = grid_for(k_actions, batch, 0, &grid);
     if (rc) return rc;
     k_actions<<<grid, kThreads, 0, (cudaStream_t)stream>>>(states, nullptr, nullptr, batch, nullptr,
-                                                            centroids);
+                                                            centroids, nullptr);
     return launch_status();
 }
 
@@ -1527,7 +1611,20 @@ int hv_legal_moves_to_actions(const uint8_t* states, const uint8_t* moves, const
     int rc = grid_for(k_actions, batch, 0, &grid);
     if (rc) return rc;
     k_actions<<<grid, kThreads, 0, (cudaStream_t)stream>>>(states, moves, num_legal, batch, actions,
-                                                            nullptr);
+                                                            nullptr, nullptr);
+    return launch_status();
+}
+
+int hv_legal_mask(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t batch,
+                  float* masks, void* stream) {
+    if (batch < 0 || (batch && (!states || !moves || !num_legal || !masks))) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (reinterpret_cast<uintptr_t>(masks) & 7) return HV_EINVAL;
+    int grid = 0;
+    int rc = grid_for(k_actions, batch, 0, &grid);
+    if (rc) return rc;
+    k_actions<<<grid, kThreads, 0, (cudaStream_t)stream>>>(states, moves, num_legal, batch, nullptr, nullptr,
+                                                            masks);
     return launch_status();
 }
 

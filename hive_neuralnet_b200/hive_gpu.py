@@ -336,6 +336,26 @@ class HiveGPUExtension:
                 _ptr(mf), _stream(dev)), "generate_legal_moves_and_hybrid_root_features_batch")
         return (moves, num_legal, feats) + tok[:6] + (mf,)
 
+    def _legal_mask(self, states, moves, num_legal, batch_size):
+        dev = states.device
+        masks = torch.empty((batch_size, ACTION_SPACE_SIZE), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_legal_mask(_ptr(states), _ptr(moves), _ptr(num_legal), batch_size, _ptr(masks),
+                                               _stream(dev)), "legal_mask")
+        return masks
+
+    def generate_legal_mask_batch(self, states: torch.Tensor, batch_size: int):
+        """(masks [B, 85834] f32, num_legal [B] i32); game_logic.cu:737-769."""
+        moves, num_legal = self.generate_legal_moves_batch(states, batch_size)
+        return self._legal_mask(_need(states, "states", torch.uint8, batch_size), moves, num_legal,
+                                batch_size), num_legal
+
+    def generate_legal_moves_and_mask_batch(self, states: torch.Tensor, batch_size: int):
+        """(moves [B,256,6] u8, num_legal [B] i32, masks [B, 85834] f32); game_logic.cu:782-809."""
+        moves, num_legal = self.generate_legal_moves_batch(states, batch_size)
+        return moves, num_legal, self._legal_mask(_need(states, "states", torch.uint8, batch_size), moves,
+                                                  num_legal, batch_size)
+
     def root_tactical_probe_batch(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
                                   priors: torch.Tensor, batch_size: int, enable_win_in_one: bool = True,
                                   enable_check_opponent_wins: bool = True, enable_win_in_two: bool = True):

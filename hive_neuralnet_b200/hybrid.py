@@ -298,7 +298,8 @@ def pack_heads(net: HiveHybridGNN, device) -> torch.Tensor:
 class HybridEvaluator:
     """Leaf evaluation of the hybrid network with the signature and outputs of the
     reference's ``HybridMCTSOrchestrator._eval_states``: (priors [T,256], values [T],
-    child_q [T,256] = 0).  Piece tokens (k_hybrid), trunk (tcgen05), fused heads."""
+    child_q [T,256] = 0).  One C-ABI call (hv_hybrid_evaluate): piece tokens, trunk
+    (tcgen05), fused heads; the tokens and summaries live in a cached workspace."""
 
     def __init__(self, net: HiveHybridGNN, device="cuda"):
         from .fnn import pack_weights
@@ -322,6 +323,15 @@ class HybridEvaluator:
         if want != self.head_weights.numel():
             raise ValueError(f"packed {self.head_weights.numel()} head floats, kernel expects {want}")
 
+    def _workspace(self, total: int, dev) -> torch.Tensor:
+        import ctypes
+        need = ctypes.c_size_t(0)
+        _lib.check(self.lib.hv_hybrid_workspace_bytes(total, ctypes.addressof(need)), "hybrid workspace size")
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.device != dev or ws.numel() < need.value:
+            self._ws = ws = torch.empty((max(need.value, 1),), dtype=torch.uint8, device=dev)
+        return ws
+
     def eval_states(self, states, legal_moves, num_legal, total, root_features=None, return_logits=False):
         dev = states.device
         priors = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
@@ -330,19 +340,21 @@ class HybridEvaluator:
         logits = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev) if return_logits else None
         if total == 0:
             return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
-        tf, tq, tr, tz, tm, gf, nt = self.ext.hybrid_transformer_encode_with_moves_batch(
-            states, legal_moves, num_legal, total)
-        graph = self.trunk(HybridPieceTensorBatch(tf, tq, tr, tz, tm, gf, nt))
+        for t, name, dt in ((states, "states", torch.uint8), (legal_moves, "legal_moves", torch.uint8),
+                            (num_legal, "num_legal", torch.int32)):
+            if t.dtype != dt or not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"{name}: expected contiguous CUDA {dt}")
         if root_features is not None and (root_features.dtype != torch.float32 or not root_features.is_contiguous()):
             raise ValueError("root_features: expected contiguous float32")
+        ws = self._workspace(total, dev)
         with torch.cuda.device(dev):
-            _lib.check(self.lib.hv_hybrid_eval_leaves(
+            _lib.check(self.lib.hv_hybrid_evaluate(
                 states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
-                None if root_features is None else root_features.data_ptr(), graph.data_ptr(), gf.data_ptr(),
-                total, self.fnn_weights.data_ptr(), *self.fdims, self.head_weights.data_ptr(), self.vh,
-                priors.data_ptr(), values.data_ptr(), child_q.data_ptr(),
-                None if logits is None else logits.data_ptr(), torch.cuda.current_stream(dev).cuda_stream),
-                "hybrid_eval_leaves")
+                None if root_features is None else root_features.data_ptr(), total, self.net.config.node_feat_dim,
+                self.trunk.image.data_ptr(), self.trunk.params.data_ptr(), self.fnn_weights.data_ptr(),
+                *self.fdims, self.head_weights.data_ptr(), self.vh, priors.data_ptr(), values.data_ptr(),
+                child_q.data_ptr(), None if logits is None else logits.data_ptr(), ws.data_ptr(), ws.numel(),
+                torch.cuda.current_stream(dev).cuda_stream), "hybrid_evaluate")
         if return_logits:
             return priors, values, child_q, logits
         return priors, values, child_q

@@ -240,6 +240,28 @@ int hv_hybrid_eval_leaves(const uint8_t* states, const uint8_t* legal_moves, con
                           const float* head_weights, int value_hidden, float* priors, float* values,
                           float* child_q, float* logits, void* stream);
 
+/* The whole hybrid leaf evaluation in one call (HybridMCTSOrchestrator._eval_states,
+ * hive_fnn_transformer/fnn_transformer_mcts_orchestrator.py:42-169): piece
+ * tokens (hv_hybrid_encode) -> trunk (hv_hybrid_trunk) -> heads
+ * (hv_hybrid_eval_leaves).  The intermediate tokens and summaries live in the
+ * caller's device workspace: 256-byte aligned, at least
+ * hv_hybrid_workspace_bytes(count) bytes.  Nothing is allocated. */
+int hv_hybrid_workspace_bytes(int64_t count, size_t* bytes);
+int hv_hybrid_evaluate(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                       const float* root_features, int64_t count, int node_feat_dim, const uint16_t* trunk_image,
+                       const float* trunk_params, const float* fnn_weights, int hidden, int embed,
+                       int action_hidden, const float* head_weights, int value_hidden, float* priors,
+                       float* values, float* child_q, float* logits, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Dense legal-action mask: legal_mask_kernel (state_encoder.cuh:908-976), the
+ * second half of generate_legal_mask_batch / generate_legal_moves_and_mask_batch
+ * (bindings.cpp:54-57, game_logic.cu:737-809).  masks [batch, 85834] f32
+ * (8-byte aligned): 1.0 at every legal move's action index inside the 17x17
+ * window around the centroid, 0 elsewhere; every element is written. */
+int hv_legal_mask(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t batch,
+                  float* masks, void* stream);
+
 /* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
  *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
  * replaces bindings.cpp:91-100,336-339 / game_logic.cu:290-397,1579-1615.

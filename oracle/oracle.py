@@ -67,6 +67,7 @@ class _Lib:
         self._qe = sig("queen_escape_batch", [_u8p, _i64, _u8p])
         self._hyb = sig("hybrid_encode_batch", [_u8p, _u8p, _i32p, _i64, _f32p, _i32p, _i32p, _i32p, _u8p,
                                                 _f32p, _i32p, _f32p, _int])
+        self._mask = sig("legal_mask_batch", [_u8p, _u8p, _i32p, _i64, _f32p])
         self._tac = sig("tactical_probe_batch", [_u8p, _u8p, _i32p, _f32p, _i64, _int, _int, _int,
                                                  _i64p, _u8p, _u8p, _int])
         self._gen = sig("generate_positions",
@@ -138,6 +139,14 @@ class _Lib:
         self._qe(states, states.shape[0], out)
         return out
 
+
+    def legal_mask(self, states, moves, num_legal):
+        """legal_mask_kernel outputs [B, 85834] f32 (reference build only)."""
+        states = np.ascontiguousarray(states, np.uint8)
+        out = np.zeros((states.shape[0], 85834), np.float32)
+        self._mask(states, np.ascontiguousarray(moves, np.uint8), np.ascontiguousarray(num_legal, np.int32),
+                   states.shape[0], out)
+        return out
 
     def tactical_probe(self, states, moves, num_legal, priors, w1=True, chk=True, w2=True, threads: int = 0):
         """root_tactical_probe_batch: (winning [B] i64, allowed [B,256] u8, forced [B] u8)."""

@@ -503,3 +503,15 @@ extern "C" void ref_hybrid_encode_batch(const uint8_t* states, const uint8_t* mo
                 mf + i * MAX_LEGAL_MOVES * HYBRID_MOVE_FEAT_DIM);
     }
 }
+
+// legal_mask_kernel (state_encoder.cuh:908-976) run per state (blockDim 1)
+extern "C" void ref_legal_mask_batch(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,
+                                     int64_t count, float* masks) {
+    tables_once();
+    std::memset(masks, 0, sizeof(float) * (size_t)count * ACTION_SPACE_SIZE);
+    for (int64_t i = 0; i < count; i++) {
+        as_thread((int)i);
+        legal_mask_kernel(reinterpret_cast<const HiveState*>(states), reinterpret_cast<const GPUMove*>(moves),
+                          num_legal, masks, (int)count);
+    }
+}

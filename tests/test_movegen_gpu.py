@@ -196,3 +196,19 @@ def test_hybrid_transformer_inputs_bit_exact(ext, orc, mask, max_ply):
     assert np.array_equal(fused[7].cpu().numpy().astype(np.uint8), want[4])
     assert np.array_equal(_bits(fused[8].cpu().numpy()), _bits(want[5]))
     assert np.array_equal(_bits(fused[9].cpu().numpy()), _bits(want[7]))
+
+
+def test_legal_mask_matches_action_indices(ext, orc):
+    """legal_mask_kernel (state_encoder.cuh:908-976): ones exactly at the oracle's action indices."""
+    st = np.concatenate([orc.generate_positions(515, 0, 256, 60, 0), orc.generate_positions(516, 0, 256, 150, 7)])
+    mo, no, _ = orc.legal_moves_features(st)
+    act, _ = orc.actions(st, mo, no)
+    masks, nl = ext.generate_legal_mask_batch(_cuda(st), len(st))
+    mv2, nl2, masks2 = ext.generate_legal_moves_and_mask_batch(_cuda(st), len(st))
+    want = np.zeros((len(st), 85834), np.float32)
+    for i in range(len(st)):
+        a = act[i, :no[i]]
+        want[i, a[a >= 0]] = 1.0
+    assert np.array_equal(nl.cpu().numpy(), no) and np.array_equal(nl2.cpu().numpy(), no)
+    assert np.array_equal(mv2.cpu().numpy(), mo)
+    assert np.array_equal(masks.cpu().numpy(), want) and np.array_equal(masks2.cpu().numpy(), want)

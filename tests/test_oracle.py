@@ -126,3 +126,17 @@ def test_oracle_apply_matches_golden_transitions(orc, small):
     for i in range(len(st)):
         bits = np.unpackbits(occ[i].view(np.uint8), bitorder="little")[:529]
         assert np.array_equal(bits.astype(bool), heights[i] > 0)
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference host build not present")
+def test_action_indices_give_the_reference_legal_mask(orc):
+    """The dense mask built from the oracle's action indices equals the reference's
+    legal_mask_kernel output (the GPU mask test builds its expectation the same way)."""
+    st = np.concatenate([orc.generate_positions(515, 0, 256, 60, 0), orc.generate_positions(516, 0, 256, 150, 7)])
+    mo, no, _ = orc.legal_moves_features(st)
+    act, _ = orc.actions(st, mo, no)
+    want = np.zeros((len(st), 85834), np.float32)
+    for i in range(len(st)):
+        a = act[i, :no[i]]
+        want[i, a[a >= 0]] = 1.0
+    assert np.array_equal(O.ref().legal_mask(st, mo, no), want)
