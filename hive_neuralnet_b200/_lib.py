@@ -93,6 +93,8 @@ _SIGNATURES = {
     "hv_hybrid_evaluate": ([_vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _int, _int, _int, _vp, _int, _vp, _vp,
                             _vp, _vp, _vp, C.c_size_t, _vp], _int),
     "hv_legal_mask": ([_vp, _vp, _vp, _i64, _vp, _vp], _int),
+    "hv_hybrid_evaluate_noalloc": ([_vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _int, _int, _int, _vp, _int,
+                                    _vp, _vp, _vp, _vp, _vp], _int),
     "hv_root_tactical_probe": ([_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp, _vp, _vp], _int),
     "hv_apply_moves": ([_vp, _vp, _i64, _vp], _int),
     "hv_check_results": ([_vp, _i64, _vp, _vp], _int),

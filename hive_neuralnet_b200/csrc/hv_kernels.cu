@@ -11,6 +11,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "hv_core.cuh"
 #include "hv_movegen.cuh"
@@ -1166,6 +1167,8 @@ const char* hv_status_string(int status) {
         case HV_ENOMEM_TREE: return "tree node pool exhausted";
         case HV_ETIMEOUT: return "bounded device wait gave up";
         case HV_EDEVICE: return "device error word set (a generator buffer overflowed)";
+        case HV_ESCRATCH:
+            return "request exceeds the fixed 32 MiB scratch of hv_hybrid_evaluate_noalloc (at most 9137 positions)";
         default: return "unknown status";
     }
 }
@@ -1376,6 +1379,38 @@ int hv_hybrid_evaluate(const uint8_t* states, const uint8_t* legal_moves, const 
     return hv_hybrid_eval_leaves(states, legal_moves, num_legal, root_features, w.graph, w.gf, count, fnn_weights,
                                  hidden, embed, action_hidden, head_weights, value_hidden, priors, values, child_q,
                                  logits, stream);
+}
+
+// Fixed scratch of hv_hybrid_evaluate_noalloc: enough for 9137 positions in
+// the hybrid_workspace_layout arrays.  Its address is resolved once per device.
+static __device__ __align__(256) uint8_t g_hybrid_scratch[32u << 20];
+static void* g_hybrid_scratch_ptr[64];
+static std::mutex g_hybrid_scratch_mu;
+
+int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                               const float* root_features, int64_t count, int node_feat_dim,
+                               const uint16_t* trunk_image, const float* trunk_params, const float* fnn_weights,
+                               int hidden, int embed, int action_hidden, const float* head_weights,
+                               int value_hidden, float* priors, float* values, float* child_q, float* logits,
+                               void* stream) {
+    if (count < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (hybrid_workspace_layout(count, nullptr, nullptr) > sizeof(g_hybrid_scratch)) return HV_ESCRATCH;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HV_ECUDA;
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_hybrid_scratch_mu);
+        if (!g_hybrid_scratch_ptr[dev]) {
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_hybrid_scratch) != cudaSuccess || !p) return HV_ECUDA;
+            g_hybrid_scratch_ptr[dev] = p;
+        }
+        scratch = g_hybrid_scratch_ptr[dev];
+    }
+    return hv_hybrid_evaluate(states, legal_moves, num_legal, root_features, count, node_feat_dim, trunk_image,
+                              trunk_params, fnn_weights, hidden, embed, action_hidden, head_weights, value_hidden,
+                              priors, values, child_q, logits, scratch, sizeof(g_hybrid_scratch), stream);
 }
 
 int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,

@@ -358,3 +358,22 @@ class HybridEvaluator:
         if return_logits:
             return priors, values, child_q, logits
         return priors, values, child_q
+
+    def eval_states_noalloc(self, states, legal_moves, num_legal, total, root_features=None):
+        """Same outputs as :meth:`eval_states` through ``hv_hybrid_evaluate_noalloc``: the
+        library uses its fixed device scratch (at most 9137 positions per call) instead
+        of this evaluator's workspace.  Calls on one device must not overlap."""
+        dev = states.device
+        priors = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
+        values = torch.empty((total,), dtype=torch.float32, device=dev)
+        child_q = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
+        if total == 0:
+            return priors, values, child_q
+        with torch.cuda.device(dev):
+            _lib.check(self.lib.hv_hybrid_evaluate_noalloc(
+                states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
+                None if root_features is None else root_features.data_ptr(), total, self.net.config.node_feat_dim,
+                self.trunk.image.data_ptr(), self.trunk.params.data_ptr(), self.fnn_weights.data_ptr(),
+                *self.fdims, self.head_weights.data_ptr(), self.vh, priors.data_ptr(), values.data_ptr(),
+                child_q.data_ptr(), None, torch.cuda.current_stream(dev).cuda_stream), "hybrid_evaluate_noalloc")
+        return priors, values, child_q

@@ -37,7 +37,8 @@ enum hv_status {
     HV_ECUDA = 2,       /* CUDA runtime or launch error */
     HV_ENOMEM_TREE = 3, /* MCTS node pool exhausted */
     HV_ETIMEOUT = 4,    /* a bounded device wait gave up */
-    HV_EDEVICE = 5      /* device error word set */
+    HV_EDEVICE = 5,     /* device error word set */
+    HV_ESCRATCH = 6     /* request larger than a no-alloc entry point's fixed scratch */
 };
 
 int hv_version(void);
@@ -261,6 +262,21 @@ int hv_hybrid_evaluate(const uint8_t* states, const uint8_t* legal_moves, const 
  * window around the centroid, 0 elsewhere; every element is written. */
 int hv_legal_mask(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t batch,
                   float* masks, void* stream);
+
+/* No-alloc variant of hv_hybrid_evaluate (no reference counterpart): the
+ * same evaluation, with the intermediate tokens and summaries in a fixed
+ * 32 MiB file-scope device array instead of a caller workspace, so a caller
+ * that owns no device allocator can still run it.  At most 9137 positions per
+ * call; larger requests return HV_ESCRATCH and launch nothing.  The scratch
+ * address is looked up once per device on the first call, so make the first
+ * call before any stream capture.  The scratch is shared by every call on a
+ * device: calls that overlap (other streams, other host threads) race. */
+int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                               const float* root_features, int64_t count, int node_feat_dim,
+                               const uint16_t* trunk_image, const float* trunk_params, const float* fnn_weights,
+                               int hidden, int embed, int action_hidden, const float* head_weights,
+                               int value_hidden, float* priors, float* values, float* child_q, float* logits,
+                               void* stream);
 
 /* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
  *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
