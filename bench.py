@@ -432,6 +432,10 @@ def run_mcts(args) -> None:
         dist.all_reduce(sims, op=dist.ReduceOp.SUM)
     ms = float(t.item())
     value = float(sims.item()) / (ms / 1e3)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = mcts_cpu_baseline(net, host_starts[0][:64].numpy(), sims=256, wave=16, c_puct=cfg.c_puct,
+                                hybrid=False)
     if rank == 0:
         line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -446,11 +450,32 @@ def run_mcts(args) -> None:
                         "h2d_bytes_per_step": games * STATE_BYTES, "d2h_bytes_per_step": None,
                         "note": "start states come from host memory and training examples return to it "
                                 "inside every timed step"},
+                "cpu_baseline": cpu,
                 "clocks": clocks}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def mcts_cpu_baseline(net, roots_np, sims, wave, c_puct, hybrid):
+    """CPU restatement of the search (oracle tree ops, oracle successor features,
+    fp32 torch CPU network on every host thread) timed on a bounded sample."""
+    import torch
+
+    from oracle import cpu_search as CS
+    from oracle import oracle as O
+    orc = O.oracle()
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    net_cpu = net.cpu().eval()
+    ev = ((lambda s, m, n, f: CS.hybrid_eval(net_cpu, orc, s, m, n, f)) if hybrid
+          else (lambda s, m, n, f: CS.fnn_eval(net_cpu, orc, s, m, n, f)))
+    rate, done, dt = CS.timed_search(ev, roots_np, sims, wave, c_puct, min_seconds=10.0)
+    return {"value": rate, "unit": "simulations/s", "cores": cores, "kind": "port",
+            "sample": f"{len(roots_np)} of the timed roots x {sims} PUCT simulations in waves of {wave}, repeated "
+                      f"for {dt:.1f} s ({done} simulations): C oracle tree ops / move generation / successor "
+                      f"features + fp32 torch CPU {'hybrid' if hybrid else 'FNN'} evaluator, {cpu_model()}"}
 
 
 def run_fnn(args) -> None:
@@ -479,12 +504,30 @@ def run_fnn(args) -> None:
     ms = e0.elapsed_time(e1) / args.steps
     succ = int(nl.sum().item())
     flops = P * 2 * (122 * 64 + 64 * 64 + 64 + 64 * 64) + succ * 2 * (122 * 64 + 64 * 64 + 64 + 64 * 64 + 64)
+    cpu = None
+    if not args.no_cpu:
+        from oracle import cpu_search as CS
+        from oracle import oracle as O
+        orc = O.oracle()
+        cores = host_cores()
+        torch.set_num_threads(cores)
+        net_cpu = ev.net.cpu().eval()
+        sample = st[:2048].cpu().numpy()
+        smv, snl, sft = (x[:2048].cpu().numpy() for x in (legal, nl, feats))
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0:
+            CS.fnn_eval(net_cpu, orc, sample, smv, snl, sft)
+            done += len(sample)
+        dt = time.perf_counter() - t0
+        cpu = {"value": done / dt, "unit": "roots/s", "cores": cores, "kind": "port",
+               "sample": f"first 2048 roots of the workload, repeated for {dt:.1f} s: C oracle successor "
+                         f"features + fp32 torch CPU HiveFNN, {cpu_model()}"}
     print(json.dumps({"metric": "FNN leaf evaluations/sec", "value": P / (ms / 1e3), "unit": "roots/s",
                       "successors_per_s": succ / (ms / 1e3), "ms_per_step": ms, "steps": args.steps,
                       "warmup": args.warmup, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
                       "config": {"workload": "config3: 65536 roots x all legal successors, FNN large fp32",
                                  "successors": succ},
-                      "mlp_tflops": flops / (ms / 1e3) / 1e12}), flush=True)
+                      "mlp_tflops": flops / (ms / 1e3) / 1e12, "cpu_baseline": cpu}), flush=True)
 
 
 HYBRID_GAMES = 256
@@ -571,6 +614,9 @@ def run_hybrid(args) -> None:
     except Exception:
         peak, peak_kind = 1590.0, "fallback"
     achieved = L * TRUNK_FLOP_PER_LEAF / (trunk_ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = mcts_cpu_baseline(net, starts[0][:32].numpy(), sims=128, wave=HYBRID_WAVE, c_puct=1.5, hybrid=True)
     if rank == 0:
         line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -589,6 +635,7 @@ def run_hybrid(args) -> None:
                              "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
                              "kernel": f"k_hybrid_trunk on {L} positions ({trunk_ms:.3f} ms)",
                              "algorithmic_flop_per_position": TRUNK_FLOP_PER_LEAF},
+                "cpu_baseline": cpu,
                 "clocks": clocks}
         print(json.dumps(line), flush=True)
     if dist is not None:
