@@ -539,7 +539,8 @@ TRUNK_FLOP_PER_LEAF = 7.61e6  # algorithmic trunk FLOPs per position (29 tokens,
 def run_hybrid(args) -> None:
     """Config 5: PUCT MCTS with the hybrid FNN-transformer evaluator, 256
     games/GPU, 1,024 simulations per move, c_puct 1.5, 8,192 leaves per wave,
-    HybridGNNConfig() random init (seed 0), bf16 tensor-core trunk.  One step
+    HybridGNNConfig() random init (seed 0), fp16-operand tensor-core trunk
+    (fp32 accumulation; the reference runs this network under fp16 autocast).  One step
     = one searched move of every game; metric = simulations per second."""
     import torch
 
@@ -620,7 +621,7 @@ def run_hybrid(args) -> None:
     if rank == 0:
         line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic",
                 "config": {"workload": f"config5: PUCT {games} games/GPU x {sims} sims/move, c_puct 1.5, "
                                        f"{games * HYBRID_WAVE} leaves/wave, HybridGNNConfig() random init "

@@ -1306,7 +1306,7 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
     k_hybrid_trunk<<<grid, 128, smem, (cudaStream_t)stream>>>(
         token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim,
-        reinterpret_cast<const __nv_bfloat16*>(weight_image), params, graph_summary, err);
+        reinterpret_cast<const __half*>(weight_image), params, graph_summary, err);
     return launch_status();
 }
 

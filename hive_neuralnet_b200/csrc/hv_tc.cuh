@@ -1,9 +1,9 @@
 // hv_tc.cuh -- thin inline-PTX wrappers for the sm_100a tensor-core path:
 // mbarriers, bulk global->shared copies, TMEM allocation, tcgen05.mma
-// (kind::f16, bf16 operands from shared memory, fp32 accumulator in TMEM)
+// (kind::f16, fp16 operands from shared memory, fp32 accumulator in TMEM)
 // and tcgen05.ld.  Every wait is bounded by wall time (%globaltimer).
 //
-// Operand layout used throughout (no swizzle, K-major): a [R x K] bf16
+// Operand layout used throughout (no swizzle, K-major): a [R x K] 16-bit
 // matrix is stored as K/8 slabs of R rows x 8 elements (16 bytes per row),
 // i.e. element (r, k) at index ((k / 8) * R + r) * 8 + k % 8.  Each 8x8 block
 // is one 128-byte "core matrix"; in the UMMA shared-memory descriptor the
@@ -94,12 +94,13 @@ __device__ __forceinline__ uint64_t sdesc(const void* p, uint32_t lbo, uint32_t 
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
-// instruction descriptor: bf16 x bf16 -> f32, A and B K-major, M = 128
-__host__ __device__ constexpr uint32_t idesc_bf16_m128(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// instruction descriptor: f16 x f16 -> f32 (A / B format 0 = F16, 1 = BF16;
+// both operands of one MMA share the type), A and B K-major, M = 128
+__host__ __device__ constexpr uint32_t idesc_f16_m128(int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -117,11 +118,11 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 // D[128 x n] = A[128 x k] * B[n x k]^T, both operands in the slab layout above
 __device__ __forceinline__ void gemm_m128(uint32_t d_tmem, const void* a, const void* b, int n, int k) {
-    const uint32_t id = idesc_bf16_m128(n);
+    const uint32_t id = idesc_f16_m128(n);
     const char* pa = static_cast<const char*>(a);
     const char* pb = static_cast<const char*>(b);
     for (int s = 0; s < k / 16; s++)
-        mma_bf16(d_tmem, sdesc(pa + s * 2 * 128 * 16, 128 * 16, 128), sdesc(pb + s * 2 * n * 16, n * 16, 128), id,
+        mma_f16(d_tmem, sdesc(pa + s * 2 * 128 * 16, 128 * 16, 128), sdesc(pb + s * 2 * n * 16, n * 16, 128), id,
                  s > 0 ? 1u : 0u);
 }
 

@@ -6,15 +6,16 @@
 // One CTA of 4 warps owns a tile of 4 positions = 128 rows (a position is 32
 // rows: CLS, its 28 piece tokens, 3 padding rows), one row per thread, the
 // residual stream in registers.  The five linear layers of a block (token
-// projection once, then QKV, attention output, MLP in and out) are bf16
+// projection once, then QKV, attention output, MLP in and out) are fp16
 // tcgen05.mma GEMMs with M = 128 and fp32 accumulators in TMEM, issued by one
-// thread; the per-head 32 x 32 attention (head width 8, too narrow for an MMA
-// K step) runs on the CUDA cores in fp32 out of shared memory, each warp on
-// its own position.  Block weights stream from global memory (L2-resident)
-// into a double-buffered shared image with bulk copies, one block ahead.
+// thread (fp16 operands as the reference's autocast, fp32 accumulation).  The per-head 32 x 32 attention of a position (head width 8, below
+// the tcgen05 K step and M tile) runs on warp-level fp16 MMAs inside the
+// warp that owns the position.  Block weights stream from global memory
+// (L2-resident) into a double-buffered shared image with bulk copies, one
+// block ahead.
 #pragma once
 
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "hv_core.cuh"
 #include "hv_tc.cuh"
@@ -23,9 +24,10 @@ namespace hv {
 
 constexpr int kTrH = 64, kTrHeads = 8, kTrFfn = 96, kTrLayers = 4;
 constexpr int kTrKin = 32;   // token features, zero-padded to two MMA K steps
-constexpr int kTrKStride = 68;  // fp32 row stride of the K / V tiles (conflict-free float4 stores)
+constexpr int kTrQkStride = 72;  // fp16 row stride of Q / K (conflict-free fragment loads)
+constexpr int kTrVtStride = 40;  // fp16 row stride of the transposed V of one position
 
-// bf16 image (elements): token projection, then per block Wqkv, Wo, W1, W2
+// fp16 image (elements): token projection, then per block Wqkv, Wo, W1, W2
 constexpr int kImgTp = kTrH * kTrKin;                      // 2048
 constexpr int kImgQkv = 3 * kTrH * kTrH, kImgO = kTrH * kTrH, kImgW1 = kTrFfn * kTrH, kImgW2 = kTrH * kTrFfn;
 constexpr int kImgLayer = kImgQkv + kImgO + kImgW1 + kImgW2;  // 28672
@@ -37,11 +39,12 @@ constexpr int kLLn1G = 0, kLLn1B = 64, kLBqkv = 128, kLBo = 320, kLLn2G = 384, k
               kLB2 = 608, kLDq = 672, kLDr = 808, kLDz = 944, kLEnd = 984;
 
 struct __align__(16) TrunkSmem {
-    __nv_bfloat16 w[2][kImgLayer];            // block weights, double buffered
-    __nv_bfloat16 tp[kImgTp];                 // token projection weights
-    __nv_bfloat16 a[kTrFfn / 8][128][8];      // A operand (K <= 96)
-    float k[128 * kTrKStride];
-    float v[128 * kTrKStride];
+    __half w[2][kImgLayer];            // block weights, double buffered
+    __half tp[kImgTp];                 // token projection weights
+    __half a[kTrFfn / 8][128][8];      // A operand (K <= 96)
+    __half q[128 * kTrQkStride];              // queries, row-major (bias added)
+    __half k[128 * kTrQkStride];              // keys
+    __half vt[4][kTrH * kTrVtStride];         // values, transposed per position [dim][key]
     int32_t cq[128], cr[128], cz[128];        // token coordinates (CLS and padding 0)
     float par[kLEnd];                         // this block's fp32 parameters
     uint64_t bar_w[2], bar_mma;
@@ -51,10 +54,10 @@ struct __align__(16) TrunkSmem {
 
 // 8 values of this thread's row -> slab c of the A operand (one 16-byte store)
 __device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int row, const float* x) {
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(x[0], x[1]);
-    __nv_bfloat162 p1 = __floats2bfloat162_rn(x[2], x[3]);
-    __nv_bfloat162 p2 = __floats2bfloat162_rn(x[4], x[5]);
-    __nv_bfloat162 p3 = __floats2bfloat162_rn(x[6], x[7]);
+    __half2 p0 = __floats2half2_rn(x[0], x[1]);
+    __half2 p1 = __floats2half2_rn(x[2], x[3]);
+    __half2 p2 = __floats2half2_rn(x[4], x[5]);
+    __half2 p3 = __floats2half2_rn(x[6], x[7]);
     uint4 u;
     u.x = *reinterpret_cast<uint32_t*>(&p0);
     u.y = *reinterpret_cast<uint32_t*>(&p1);
@@ -64,7 +67,7 @@ __device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int row, const f
 }
 
 // write this thread's row (n values) into the A operand in slab layout
-__device__ __forceinline__ void put_row_bf16(TrunkSmem* s, int row, const float* x, int n) {
+__device__ __forceinline__ void put_row_f16(TrunkSmem* s, int row, const float* x, int n) {
 #pragma unroll
     for (int c = 0; c < n / 8; c++) put_chunk8(s, c, row, x + 8 * c);
 }
@@ -108,8 +111,8 @@ __device__ __forceinline__ uint32_t lane_taddr(const TrunkSmem* s, int col) {
     return s->tmem + ((uint32_t)((threadIdx.x >> 5) * 32) << 16) + (uint32_t)col;
 }
 
-__device__ __forceinline__ void prefetch_block(TrunkSmem* s, int buf, const __nv_bfloat16* img, int layer) {
-    const __nv_bfloat16* src = img + kImgTp + (size_t)layer * kImgLayer;
+__device__ __forceinline__ void prefetch_block(TrunkSmem* s, int buf, const __half* img, int layer) {
+    const __half* src = img + kImgTp + (size_t)layer * kImgLayer;
     mbar_expect_tx(&s->bar_w[buf], kImgLayerBytes);
     // four copies, one per matrix (each a multiple of 16 bytes)
     bulk_g2s(&s->w[buf][0], src, kImgQkv * 2, &s->bar_w[buf]);
@@ -118,14 +121,136 @@ __device__ __forceinline__ void prefetch_block(TrunkSmem* s, int buf, const __nv
     bulk_g2s(&s->w[buf][kImgQkv + kImgO + kImgW1], src + kImgQkv + kImgO + kImgW1, kImgW2 * 2, &s->bar_w[buf]);
 }
 
+__device__ __forceinline__ uint32_t ld_b32(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// D += A(16x8, row) * B(8x8, col), fp16 in, fp32 accumulate
+__device__ __forceinline__ void mma_k8(float* d, uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// D += A(16x16, row) * B(16x8, col)
+__device__ __forceinline__ void mma_k16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Attention of one position (this warp's 32 rows): per head, S = Q K^T on
+// fp16 warp MMAs with fp32 accumulation (head width 8 = one k8 step; fp16
+// keeps the softmax weights to 11 significant bits), scale + relative bias + key mask,
+// row softmax on the accumulator fragments (quad shuffles), O = P V with the
+// score fragments reused as the A operand; O goes straight into the A
+// operand slab of the output projection.  Fragment coordinates: g = lane/4
+// selects rows g and g+8 of a 16-row tile, c = lane%4 selects columns 2c, 2c+1.
+__device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t kmask) {
+    const int g = l >> 2, c = l & 3, base = w * 32;
+    const float scale = 0.35355339059327373f;  // 8 ** -0.5
+    // relative-offset table indices of this thread's 32 (row, key) pairs
+    uint32_t rel[2][2][4][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            const int i = base + 16 * mt + g + 8 * hh;
+            const int qi = s->cq[i], ri = s->cr[i], zi = s->cz[i];
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int j = base + 8 * nt + 2 * c + e;
+                    const int dq = min(max(s->cq[j] - qi, -8), 8) + 8;
+                    const int dr = min(max(s->cr[j] - ri, -8), 8) + 8;
+                    const int dz = min(max(s->cz[j] - zi, -2), 2) + 2;
+                    rel[mt][hh][nt][e] = (uint32_t)(kLDq + dq * 8) | ((uint32_t)(kLDr + dr * 8) << 10) |
+                                         ((uint32_t)(kLDz + dz * 8) << 20);
+                }
+        }
+#pragma unroll 1
+    for (int h = 0; h < kTrHeads; h++) {
+        // S = Q_h K_h^T
+        float sc[2][4][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) {
+            const __half* qa = s->q + (base + 16 * mt + g) * kTrQkStride + 8 * h + 2 * c;
+            const uint32_t a0 = ld_b32(qa), a1 = ld_b32(qa + 8 * kTrQkStride);
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++) {
+                const uint32_t b0 = ld_b32(s->k + (base + 8 * nt + g) * kTrQkStride + 8 * h + 2 * c);
+                sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.0f;
+                mma_k8(sc[mt][nt], a0, a1, b0);
+            }
+        }
+        // scale, bias, mask; row max / sum over the quad
+        float rinv[2][2];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                float mx = -3.0e38f;
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const uint32_t r = rel[mt][hh][nt][e];
+                        const float b = s->par[(r & 1023u) + h] + s->par[((r >> 10) & 1023u) + h] +
+                                        s->par[(r >> 20) + h];
+                        float& v = sc[mt][nt][2 * hh + e];
+                        v = v * scale + b;
+                        if ((kmask >> (8 * nt + 2 * c + e)) & 1u) mx = fmaxf(mx, v);
+                    }
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                float sum = 0.0f;
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        float& v = sc[mt][nt][2 * hh + e];
+                        v = ((kmask >> (8 * nt + 2 * c + e)) & 1u) ? __expf(v - mx) : 0.0f;
+                        sum += v;
+                    }
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                rinv[mt][hh] = sum > 0.0f ? 1.0f / sum : 0.0f;  // no valid key: idle warp
+            }
+        // O = P V_h (k = 32 keys in two k16 steps), normalised, into the A slab of head h
+        const __half* vt = s->vt[w] + (8 * h + g) * kTrVtStride + 2 * c;
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) {
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kb = 0; kb < 2; kb++) {
+                const uint32_t a0 = pack_f16(sc[mt][2 * kb][0], sc[mt][2 * kb][1]);
+                const uint32_t a1 = pack_f16(sc[mt][2 * kb][2], sc[mt][2 * kb][3]);
+                const uint32_t a2 = pack_f16(sc[mt][2 * kb + 1][0], sc[mt][2 * kb + 1][1]);
+                const uint32_t a3 = pack_f16(sc[mt][2 * kb + 1][2], sc[mt][2 * kb + 1][3]);
+                mma_k16(o, a0, a1, a2, a3, ld_b32(vt + 16 * kb), ld_b32(vt + 16 * kb + 8));
+            }
+            const int r0 = base + 16 * mt + g;
+            *reinterpret_cast<uint32_t*>(&s->a[h][r0][2 * c]) = pack_f16(o[0] * rinv[mt][0], o[1] * rinv[mt][0]);
+            *reinterpret_cast<uint32_t*>(&s->a[h][r0 + 8][2 * c]) =
+                pack_f16(o[2] * rinv[mt][1], o[3] * rinv[mt][1]);
+        }
+    }
+}
+
 __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
 // token_features [B,28,27] (first `nfeat` used), token_q/r/z [B,28], token_mask [B,28] (0/1),
-// img: bf16 weight image, par: fp32 parameters; out [B,64]: the normalised CLS row
+// img: fp16 weight image, par: fp32 parameters; out [B,64]: the normalised CLS row
 __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict__ tf, const int32_t* __restrict__ tq,
                                                          const int32_t* __restrict__ tr, const int32_t* __restrict__ tz,
                                                          const uint8_t* __restrict__ tm, int64_t batch, int nfeat,
-                                                         const __nv_bfloat16* __restrict__ img,
+                                                         const __half* __restrict__ img,
                                                          const float* __restrict__ par, float* __restrict__ out,
                                                          uint32_t* err_word) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -179,7 +304,7 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             float f[kTrKin];
 #pragma unroll
             for (int i = 0; i < kTrKin; i++) f[i] = (is_tok && i < nfeat) ? tf[(b * 28 + tok) * 27 + i] : 0.0f;
-            put_row_bf16(s, t, f, kTrKin);
+            put_row_f16(s, t, f, kTrKin);
         }
         float x[kTrH];
         mpend = true;
@@ -220,7 +345,7 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             // ---- attention
             float y[kTrH];
             layer_norm64(x, s->par + kLLn1G, s->par + kLLn1B, y);
-            put_row_bf16(s, t, y, kTrH);
+            put_row_f16(s, t, y, kTrH);
             bool okw = true;
             if (t == 0) {
                 okw = mbar_wait(&s->bar_w[buf], wphase[buf]);
@@ -231,7 +356,7 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
                 failed = true;
                 break;
             }
-            const __nv_bfloat16* W = s->w[buf];
+            const __half* W = s->w[buf];
             mpend = true;
             if (!trunk_gemm(s, 0, W, 3 * kTrH, kTrH, mphase)) {
                 failed = true;
@@ -239,83 +364,28 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             }
             mpend = false;
             {
-                // keys and values to shared memory; queries stay in TMEM columns 0-63
+                // q, k (row-major) and v (transposed, per position) to shared memory in fp16
                 float d[32];
 #pragma unroll
-                for (int c = 2; c < 6; c++) {
+                for (int c = 0; c < 6; c++) {
                     tmem_ld32(lane_taddr(s, 32 * c), d);
-                    float* dst = (c < 4 ? s->k + 32 * (c - 2) : s->v + 32 * (c - 4)) + t * kTrKStride;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(dst + i) =
-                            make_float4(d[i] + s->par[kLBqkv + 32 * c + i], d[i + 1] + s->par[kLBqkv + 32 * c + i + 1],
-                                        d[i + 2] + s->par[kLBqkv + 32 * c + i + 2],
-                                        d[i + 3] + s->par[kLBqkv + 32 * c + i + 3]);
+                    for (int i = 0; i < 32; i += 2) {
+                        const int j = 32 * c + i;
+                        const float v0 = d[i] + s->par[kLBqkv + j], v1 = d[i + 1] + s->par[kLBqkv + j + 1];
+                        if (j < 128) {
+                            __half* row = (j < 64 ? s->q : s->k) + t * kTrQkStride + (j & 63);
+                            *reinterpret_cast<__half2*>(row) = __floats2half2_rn(v0, v1);
+                        } else {
+                            __half* vt = s->vt[w] + (j - 128) * kTrVtStride + l;
+                            vt[0] = __float2half_rn(v0);
+                            vt[kTrVtStride] = __float2half_rn(v1);
+                        }
+                    }
                 }
             }
             __syncwarp();
-            {
-                // per head: scores of this row's query against the 32 keys of
-                // its position, softmax over the valid ones, weighted values;
-                // the head's 8 outputs are one 16-byte chunk of the A operand
-                const int base = w * 32;
-                const int myq = s->cq[t], myr = s->cr[t], myz = s->cz[t];
-                const float scale = 0.35355339059327373f;  // 8 ** -0.5
-#pragma unroll
-                for (int h = 0; h < kTrHeads; h++) {
-                    float q[8];
-                    tmem_ld8(lane_taddr(s, 8 * h), q);
-#pragma unroll
-                    for (int e = 0; e < 8; e++) q[e] += s->par[kLBqkv + 8 * h + e];
-                    float sc[32];
-                    float mx = -3.0e38f;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const float4* kr = reinterpret_cast<const float4*>(s->k + (base + j) * kTrKStride + 8 * h);
-                        const float4 k0 = kr[0], k1 = kr[1];
-                        float dot = q[0] * k0.x;
-                        dot += q[1] * k0.y;
-                        dot += q[2] * k0.z;
-                        dot += q[3] * k0.w;
-                        dot += q[4] * k1.x;
-                        dot += q[5] * k1.y;
-                        dot += q[6] * k1.z;
-                        dot += q[7] * k1.w;
-                        const int dq = min(max(s->cq[base + j] - myq, -8), 8) + 8;
-                        const int dr = min(max(s->cr[base + j] - myr, -8), 8) + 8;
-                        const int dz = min(max(s->cz[base + j] - myz, -2), 2) + 2;
-                        const float sj = dot * scale + s->par[kLDq + dq * 8 + h] + s->par[kLDr + dr * 8 + h] +
-                                         s->par[kLDz + dz * 8 + h];
-                        sc[j] = sj;
-                        if ((kmask >> j) & 1u) mx = fmaxf(mx, sj);
-                    }
-                    float sum = 0.f;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const float p = ((kmask >> j) & 1u) ? __expf(sc[j] - mx) : 0.0f;
-                        sc[j] = p;
-                        sum += p;
-                    }
-                    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;  // no valid key: idle warp
-                    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const float4* vr = reinterpret_cast<const float4*>(s->v + (base + j) * kTrKStride + 8 * h);
-                        const float4 v0 = vr[0], v1 = vr[1];
-                        o[0] += sc[j] * v0.x;
-                        o[1] += sc[j] * v0.y;
-                        o[2] += sc[j] * v0.z;
-                        o[3] += sc[j] * v0.w;
-                        o[4] += sc[j] * v1.x;
-                        o[5] += sc[j] * v1.y;
-                        o[6] += sc[j] * v1.z;
-                        o[7] += sc[j] * v1.w;
-                    }
-#pragma unroll
-                    for (int e = 0; e < 8; e++) o[e] *= inv;
-                    put_chunk8(s, h, t, o);
-                }
-            }
+            attention_warp(s, w, l, kmask);
             mpend = true;
             if (!trunk_gemm(s, 192, W + kImgQkv, kTrH, kTrH, mphase)) {
                 failed = true;
@@ -333,7 +403,7 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             }
             // ---- MLP
             layer_norm64(x, s->par + kLLn2G, s->par + kLLn2B, y);
-            put_row_bf16(s, t, y, kTrH);
+            put_row_f16(s, t, y, kTrH);
             mpend = true;
             if (!trunk_gemm(s, 0, W + kImgQkv + kImgO, kTrFfn, kTrH, mphase)) {
                 failed = true;

@@ -8,7 +8,7 @@ statement of the network that the sm_100a kernels are checked against.
 
 ``HybridEvaluator`` replaces ``HybridMCTSOrchestrator._eval_states``
 (hive_fnn_transformer/fnn_transformer_mcts_orchestrator.py:42-169): piece
-tokens -> relative transformer trunk (bf16 tcgen05 GEMMs, fp32 attention)
+tokens -> relative transformer trunk (fp16 tcgen05 GEMMs and warp-MMA attention, fp32 accumulation)
 -> value head; successor generation + FNN encode + hybrid action scoring +
 masked softmax fused in one warp-per-leaf kernel.
 """
@@ -227,7 +227,7 @@ def check_trunk_config(cfg: HybridGNNConfig) -> None:
 
 
 def pack_trunk(trunk: HybridRelativeTransformerTrunk, device) -> tuple[torch.Tensor, torch.Tensor]:
-    """(bf16 weight image as int16 storage, fp32 parameters) in the layout of hv_trunk.cuh."""
+    """(fp16 weight image as int16 storage, fp32 parameters) in the layout of hv_trunk.cuh."""
     with torch.no_grad():
         img = [_slabs(trunk.token_proj.weight.float(), TRUNK_KIN)]
         par = [trunk.token_proj.bias, trunk.cls_token.reshape(-1), trunk.norm.weight, trunk.norm.bias]
@@ -238,7 +238,7 @@ def pack_trunk(trunk: HybridRelativeTransformerTrunk, device) -> tuple[torch.Ten
             par += [blk.norm1.weight, blk.norm1.bias, a.qkv.bias, a.out_proj.bias, blk.norm2.weight,
                     blk.norm2.bias, blk.ffn[0].bias, blk.ffn[2].bias, a.dq_bias.weight.reshape(-1),
                     a.dr_bias.weight.reshape(-1), a.dz_bias.weight.reshape(-1)]
-        image = torch.cat(img).to(torch.bfloat16).view(torch.int16).to(device).contiguous()
+        image = torch.cat(img).to(torch.float16).view(torch.int16).to(device).contiguous()
         params = torch.cat([p.detach().float().reshape(-1) for p in par]).to(device).contiguous()
     return image, params
 

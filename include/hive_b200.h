@@ -216,7 +216,7 @@ int hv_generate_legal_moves_and_hybrid_root_features(const uint8_t* states, int6
  * fnn_transformer_net.py:159-209 HybridRelativeTransformerTrunk.forward), the
  * default / `small` presets: hidden 64, 8 heads, MLP 96, 4 blocks.  Inputs are
  * hv_hybrid_encode's outputs (token_features [batch, 28, 27], first
- * node_feat_dim columns used); weight_image (bf16 bits) and params (f32) are
+ * node_feat_dim columns used); weight_image (fp16 bits) and params (f32) are
  * packed by hive_neuralnet_b200.hybrid.pack_trunk, sizes from
  * hv_hybrid_trunk_sizes.  graph_summary [batch, 64] f32.  No reference
  * counterpart as a single call: it replaces the torch module's forward. */

@@ -1,6 +1,6 @@
 """Hybrid FNN-transformer leaf evaluation on the B200 against the fp32 torch
 statement of the network on the same seeded positions (tolerance 1e-2: the
-trunk's GEMM operands are bf16), and the hybrid PUCT driver replaying
+trunk's GEMM operands are fp16), and the hybrid PUCT driver replaying
 bit-exact on the oracle's tree operations given the evaluator's outputs."""
 import numpy as np
 import pytest

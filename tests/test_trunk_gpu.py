@@ -1,6 +1,7 @@
-"""The hybrid evaluator's transformer trunk on the tensor cores (bf16 tcgen05
+"""The hybrid evaluator's transformer trunk on the tensor cores (fp16 tcgen05
 GEMMs, fp32 attention) against the fp32 torch statement of the network and
-the reference module's own outputs; tolerance 1e-2 (bf16 operands)."""
+the reference module's own outputs; tolerance 1e-2 (16-bit operands, the bound the
+reference's autocast network is held to)."""
 import os
 
 import numpy as np
