@@ -304,17 +304,33 @@ def run_gpu(args) -> None:
     h2d = P * STATE_BYTES
     d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
 
-    # ---- roofline: algorithmic bytes per launch / average launch time ----
+    # ---- roofline of the dominant kernel: the move generator k_root<gen>
+    # (one of the step's two launches), timed alone with CUDA events on the
+    # launching stream; algorithmic bytes per position = state read + move
+    # list (6 bytes per legal move) + num_legal written
     peak, peak_kind = measured_peak_gbs()
-    launch_s = (ms / args.steps) / 1e3
-    alg_bytes = P * (STATE_BYTES + 4 + FEAT * 4 + MOVE_BYTES * mean_legal)
-    achieved = alg_bytes / launch_s / 1e9
+    for _ in range(3):
+        ext.generate_legal_moves_batch(states, P)
+    torch.cuda.synchronize(dev)
+    reps = max(5, min(args.steps, 20))
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(reps):
+        ext.generate_legal_moves_batch(states, P)
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    gen_s = g0.elapsed_time(g1) / reps / 1e3
+    alg_bytes = P * (STATE_BYTES + 4 + MOVE_BYTES * mean_legal)
+    achieved = alg_bytes / gen_s / 1e9
     tpp = profiled_traffic_per_position()
+    step_bytes = P * (STATE_BYTES + 4 + FEAT * 4 + MOVE_BYTES * mean_legal)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": peak_kind,
                 "traffic": (tpp * P) if tpp else None,
                 "algorithmic_bytes_per_launch": alg_bytes,
-                "kernel": "k_root<gen,moves,features> (movegen+FNN features)"}
+                "kernel": f"k_root<1,1,0> move generator, {gen_s * 1e3:.3f} ms per launch",
+                "step": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / ((ms / args.steps) / 1e3) / 1e9,
+                         "launches": ["k_root<1,1,0> (legal moves)", "k_root<0,0,1> (FNN features)"]}}
 
     line = None
     if rank == 0:
@@ -337,7 +353,7 @@ def run_gpu(args) -> None:
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,
             "mean_legal_moves": mean_legal,
         }
     if dist is not None:
