@@ -95,6 +95,11 @@ _SIGNATURES = {
     "hv_legal_mask": ([_vp, _vp, _vp, _i64, _vp, _vp], _int),
     "hv_hybrid_evaluate_noalloc": ([_vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _int, _int, _int, _vp, _int,
                                     _vp, _vp, _vp, _vp, _vp], _int),
+    "hv_leaf_rows_workspace_bytes": ([_i64, _i64, _int, _vp], _int),
+    "hv_fnn_eval_leaves_rows": ([_vp, _vp, _vp, _vp, _i64, _i64, _vp, _int, _int, _int, _vp, _vp, _vp, _vp, _vp,
+                                 C.c_size_t, _vp], _int),
+    "hv_hybrid_evaluate_rows": ([_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp, _vp, _int, _int, _int, _vp, _int,
+                                 _vp, _vp, _vp, _vp, _vp, C.c_size_t, _vp], _int),
     "hv_root_tactical_probe": ([_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp, _vp, _vp], _int),
     "hv_apply_moves": ([_vp, _vp, _i64, _vp], _int),
     "hv_check_results": ([_vp, _i64, _vp, _vp], _int),

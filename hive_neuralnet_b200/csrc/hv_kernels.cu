@@ -21,6 +21,7 @@
 #include "hv_tactics.cuh"
 #include "hv_hybrid.cuh"
 #include "hv_trunk.cuh"
+#include "hv_mlp.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -106,9 +107,10 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
     const int64_t* __restrict__ action_to_root, const int64_t* __restrict__ move_indices,
-    int64_t num_actions, float* __restrict__ feats_out) {
+    int64_t num_actions, float* __restrict__ feats_out, const int64_t* __restrict__ n_actual) {
     WarpSmem* w = warp_slot();
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    if (n_actual) num_actions = min(num_actions, *n_actual);  // row pipeline: rows actually filled
     for (int64_t a = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); a < num_actions;
          a += nwarps) {
         int64_t root = action_to_root[a];
@@ -243,6 +245,76 @@ __device__ __forceinline__ HybSmem* hyb_slot() {
            (threadIdx.x >> 5);
 }
 
+// Root part of the hybrid evaluation for leaf p, root features in f->xs[0]:
+// FNN root embedding (f->root_emb), tanh value head over [e_root ; g ;
+// global6] (returned), graph context and the root half of policy_fc1
+// (f->root_pre).  Uses f->logit[0..136) as scratch.
+__device__ __noinline__ float hybrid_root(FnnSmem* f, int64_t p, const float* __restrict__ graph,
+                                      const float* __restrict__ glob, const float* __restrict__ fw, FnnDims fd,
+                                      const float* __restrict__ hw, HybDims hd) {
+    const FnnOffsets fo = fnn_offsets(fd);
+    const HybOffsets ho = hyb_offsets(hd);
+    const int E = hd.E, A = hd.A, V = hd.V;
+    const int l = lane_id();
+    const int o0 = l, o1 = l + 32;
+    float val[kFnnChunk];
+    fnn_encode_chunk(fw, fd, fo, f, 1, val);
+    for (int k = l; k < E; k += 32) f->root_emb[k] = f->ys[0][k];
+    // per-leaf scratch in the (not yet used) logit row: g, global features, g_ctx
+    float* sg = f->logit;
+    float* sgl = f->logit + kHybGraph;
+    float* sgc = f->logit + kHybGraph + 8;
+    for (int k = l; k < kHybGraph; k += 32) sg[k] = graph[p * kHybGraph + k];
+    if (l < kGlobFeat) sgl[l] = glob[p * kGlobFeat + l];
+    __syncwarp();
+    // value head: lane owns hidden units l, l+32, l+64, l+96
+    float root_value;
+    {
+        float acc[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[i] = (l + 32 * i) < V ? __ldg(hw + ho.vh1b + l + 32 * i) : 0.0f;
+        const int nin = E + kHybGraph + kGlobFeat;
+#pragma unroll 2
+        for (int k = 0; k < nin; k++) {
+            const float in = k < E ? f->root_emb[k] : (k < E + kHybGraph ? sg[k - E] : sgl[k - E - kHybGraph]);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (l + 32 * i < V) acc[i] = fmaf(__ldg(hw + ho.vh1T + k * V + l + 32 * i), in, acc[i]);
+        }
+        float part = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            if (l + 32 * i < V) part += __ldg(hw + ho.vh2 + l + 32 * i) * fmaxf(acc[i], 0.0f);
+        root_value = tanhf(warp_sum(part) + __ldg(hw + ho.vh2b));
+    }
+    // graph context g_ctx = pg g + b
+    {
+        float a = o0 < E ? __ldg(hw + ho.pgb + o0) : 0.0f, b = o1 < E ? __ldg(hw + ho.pgb + o1) : 0.0f;
+        for (int k = 0; k < kHybGraph; k++) {
+            const float gk = sg[k];
+            if (o0 < E) a = fmaf(__ldg(hw + ho.pgT + k * E + o0), gk, a);
+            if (o1 < E) b = fmaf(__ldg(hw + ho.pgT + k * E + o1), gk, b);
+        }
+        __syncwarp();
+        if (o0 < E) sgc[o0] = a;
+        if (o1 < E) sgc[o1] = b;
+        __syncwarp();
+    }
+    // root half of policy_fc1: b' + W[:, 0:E] e_root + W[:, E:2E] g_ctx
+    {
+        float a = o0 < A ? __ldg(hw + ho.pf1b + o0) : 0.0f, b = o1 < A ? __ldg(hw + ho.pf1b + o1) : 0.0f;
+        for (int k = 0; k < E; k++) {
+            const float er = f->root_emb[k], gc = sgc[k];
+            if (o0 < A) a = fmaf(__ldg(hw + ho.pf1T + k * A + o0), er, fmaf(__ldg(hw + ho.pf1T + (E + k) * A + o0), gc, a));
+            if (o1 < A) b = fmaf(__ldg(hw + ho.pf1T + k * A + o1), er, fmaf(__ldg(hw + ho.pf1T + (E + k) * A + o1), gc, b));
+        }
+        if (o0 < A) f->root_pre[o0] = a;
+        if (o1 < A) f->root_pre[o1] = b;
+        __syncwarp();
+    }
+    return root_value;
+}
+
 __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
     const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal_moves,
     const int32_t* __restrict__ num_legal, const float* __restrict__ root_feats, const float* __restrict__ graph,
@@ -277,60 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
             features(w, S, n, f->xs[0]);
         }
         float val[kFnnChunk], lg[kFnnChunk];
-        fnn_encode_chunk(fw, fd, fo, f, 1, val);
-        for (int k = l; k < E; k += 32) f->root_emb[k] = f->ys[0][k];
-        // per-leaf scratch in the (not yet used) logit row: g, global features, g_ctx
-        float* sg = f->logit;
-        float* sgl = f->logit + kHybGraph;
-        float* sgc = f->logit + kHybGraph + 8;
-        for (int k = l; k < kHybGraph; k += 32) sg[k] = graph[p * kHybGraph + k];
-        if (l < kGlobFeat) sgl[l] = glob[p * kGlobFeat + l];
-        __syncwarp();
-        // value head: lane owns hidden units l, l+32, l+64, l+96
-        float root_value;
-        {
-            float acc[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[i] = (l + 32 * i) < V ? __ldg(hw + ho.vh1b + l + 32 * i) : 0.0f;
-            const int nin = E + kHybGraph + kGlobFeat;
-#pragma unroll 2
-            for (int k = 0; k < nin; k++) {
-                const float in = k < E ? f->root_emb[k] : (k < E + kHybGraph ? sg[k - E] : sgl[k - E - kHybGraph]);
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    if (l + 32 * i < V) acc[i] = fmaf(__ldg(hw + ho.vh1T + k * V + l + 32 * i), in, acc[i]);
-            }
-            float part = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-                if (l + 32 * i < V) part += __ldg(hw + ho.vh2 + l + 32 * i) * fmaxf(acc[i], 0.0f);
-            root_value = tanhf(warp_sum(part) + __ldg(hw + ho.vh2b));
-        }
-        // graph context g_ctx = pg g + b
-        {
-            float a = o0 < E ? __ldg(hw + ho.pgb + o0) : 0.0f, b = o1 < E ? __ldg(hw + ho.pgb + o1) : 0.0f;
-            for (int k = 0; k < kHybGraph; k++) {
-                const float gk = sg[k];
-                if (o0 < E) a = fmaf(__ldg(hw + ho.pgT + k * E + o0), gk, a);
-                if (o1 < E) b = fmaf(__ldg(hw + ho.pgT + k * E + o1), gk, b);
-            }
-            __syncwarp();
-            if (o0 < E) sgc[o0] = a;
-            if (o1 < E) sgc[o1] = b;
-            __syncwarp();
-        }
-        // root half of policy_fc1: b' + W[:, 0:E] e_root + W[:, E:2E] g_ctx
-        {
-            float a = o0 < A ? __ldg(hw + ho.pf1b + o0) : 0.0f, b = o1 < A ? __ldg(hw + ho.pf1b + o1) : 0.0f;
-            for (int k = 0; k < E; k++) {
-                const float er = f->root_emb[k], gc = sgc[k];
-                if (o0 < A) a = fmaf(__ldg(hw + ho.pf1T + k * A + o0), er, fmaf(__ldg(hw + ho.pf1T + (E + k) * A + o0), gc, a));
-                if (o1 < A) b = fmaf(__ldg(hw + ho.pf1T + k * A + o1), er, fmaf(__ldg(hw + ho.pf1T + (E + k) * A + o1), gc, b));
-            }
-            if (o0 < A) f->root_pre[o0] = a;
-            if (o1 < A) f->root_pre[o1] = b;
-            __syncwarp();
-        }
+        const float root_value = hybrid_root(f, p, graph, glob, fw, fd, hw, hd);
         float* cq = child_q + p * kMaxMoves;
 #pragma unroll 1
         for (int base = 0; base < n; base += kFnnChunk) {
@@ -423,6 +442,160 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
         }
         if (l == 0) values[p] = root_value;
         __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// leaf evaluation as a row pipeline (the default evaluator path): successor
+// rows are compacted over all leaves, their features written by
+// k_successor_features, the network run by the tiled k_mlp_rows, the
+// per-leaf parts by warp-per-leaf kernels.  Launch order:
+//   k_row_offsets -> k_row_index -> k_successor_features (+ k_row_move_features)
+//   -> k_leaf_root_{fnn,hybrid} -> k_mlp_rows -> k_leaf_softmax
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t clamp_rows(int n) { return n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n); }
+
+// exclusive prefix sum of the clamped legal counts: row_start[T + 1] (one block)
+__global__ void __launch_bounds__(1024) k_row_offsets(const int32_t* __restrict__ num_legal, int64_t T,
+                                                      int64_t* __restrict__ row_start) {
+    __shared__ int64_t part[1024];
+    const int t = threadIdx.x;
+    const int64_t per = (T + 1023) / 1024;
+    const int64_t lo = min(T, (int64_t)t * per), hi = min(T, lo + per);
+    int64_t sum = 0;
+    for (int64_t i = lo; i < hi; i++) sum += clamp_rows(num_legal[i]);
+    part[t] = sum;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+        const int64_t v = t >= off ? part[t - off] : 0;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    int64_t run = part[t] - sum;
+    for (int64_t i = lo; i < hi; i++) {
+        row_start[i] = run;
+        run += clamp_rows(num_legal[i]);
+    }
+    if (t == 1023) row_start[T] = part[1023];
+}
+
+// leaf / slot of every row (rows past the capacity are dropped and flagged)
+__global__ void __launch_bounds__(kThreads) k_row_index(const int32_t* __restrict__ num_legal, int64_t T,
+                                                        const int64_t* __restrict__ row_start, int64_t cap,
+                                                        int64_t* __restrict__ atr, int64_t* __restrict__ mi) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < T; p += nwarps) {
+        const int64_t start = row_start[p], n = clamp_rows(num_legal[p]);
+        for (int64_t i = l; i < n; i += 32) {
+            if (start + i < cap) {
+                atr[start + i] = p;
+                mi[start + i] = i;
+            }
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0 && row_start[T] > cap) atomicOr(&g_error, kErrBuffer);
+}
+
+// hybrid: the 31 move features of every row, read off the leaf position
+__global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_row_move_features(
+    const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal_moves,
+    const int32_t* __restrict__ num_legal, int64_t T, const int64_t* __restrict__ row_start, int64_t cap,
+    float* __restrict__ mf) {
+    WarpSmem* w = warp_slot();
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < T; p += nwarps) {
+        const int64_t start = row_start[p], n = clamp_rows(num_legal[p]);
+        if (n == 0) continue;
+        stage_state(w, states + p * kStateBytes);
+        Pos P{w};
+        const MoveCtx X = move_ctx(w);
+        const uint8_t* mv = legal_moves + p * (kMaxMoves * kMoveBytes);
+        for (int64_t i = l; i < n; i += 32) {
+            if (start + i >= cap) continue;
+            const uint8_t* m = mv + i * kMoveBytes;
+            float f[kMoveFeat];
+            move_features(P, w->st, X, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8), f);
+            float* row = mf + (start + i) * kMoveFeat;
+#pragma unroll
+            for (int k = 0; k < kMoveFeat; k++) row[k] = f[k];
+        }
+        __syncwarp();
+    }
+}
+
+// per-leaf part: root features (given, or from the leaf's own list), FNN
+// root embedding, value, and the root half of the action layer -> root_pre[T][64]
+template <bool HYB>
+__global__ void __launch_bounds__(kThreads, 2) k_leaf_root(
+    const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal_moves,
+    const int32_t* __restrict__ num_legal, const float* __restrict__ root_feats, const float* __restrict__ graph,
+    const float* __restrict__ glob, int64_t count, const float* __restrict__ fw, FnnDims fd,
+    const float* __restrict__ hw, HybDims hd, float* __restrict__ values, float* __restrict__ root_pre) {
+    WarpSmem* w = warp_slot();
+    FnnSmem* f = fnn_slot();
+    const int l = lane_id();
+    const int A = HYB ? hd.A : fd.A;
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < count;
+         p += nwarps) {
+        if (root_feats) {
+            for (int k = l; k < kFeat; k += 32) f->xs[0][k] = root_feats[p * kFeat + k];
+            __syncwarp();
+        } else {
+            int n = (int)clamp_rows(num_legal[p]);
+            stage_state(w, states + p * kStateBytes);
+            const uint4* s4 = reinterpret_cast<const uint4*>(legal_moves + p * (kMaxMoves * kMoveBytes));
+            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
+            for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
+            __syncwarp();
+            Setup S = setup_position(w);
+            features(w, S, n, f->xs[0]);
+        }
+        float v;
+        if (HYB) {
+            v = hybrid_root(f, p, graph, glob, fw, fd, hw, hd);
+        } else {
+            float val[kFnnChunk];
+            const FnnOffsets fo = fnn_offsets(fd);
+            fnn_encode_chunk(fw, fd, fo, f, 1, val);
+            v = val[0];
+            fnn_root_pre(fw, fd, fo, f);
+        }
+        for (int k = l; k < 64; k += 32) root_pre[p * 64 + k] = k < A ? f->root_pre[k] : 0.0f;
+        if (l == 0) values[p] = v;
+        __syncwarp();
+    }
+}
+
+// per-leaf softmax over the legal slots (-inf padding, then zeroed); the
+// padding of child_q / logits is zeroed (the hybrid's child_q entirely)
+template <bool HYB>
+__global__ void __launch_bounds__(kThreads) k_leaf_softmax(const int32_t* __restrict__ num_legal, int64_t count,
+                                                           const int64_t* __restrict__ row_start, int64_t cap,
+                                                           float* __restrict__ logits, float* __restrict__ priors,
+                                                           float* __restrict__ child_q) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < count;
+         p += nwarps) {
+        int64_t n = clamp_rows(num_legal[p]);
+        n = min(n, max((int64_t)0, cap - row_start[p]));  // rows dropped at the capacity count as absent
+        float* lg = logits + p * kMaxMoves;
+        float mx = -INFINITY;
+        for (int i = l; i < n; i += 32) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        float sum = 0.0f;
+        for (int i = l; i < n; i += 32) sum += expf(lg[i] - mx);
+        sum = warp_sum(sum);
+        for (int i = l; i < kMaxMoves; i += 32) {
+            priors[p * kMaxMoves + i] = i < n ? expf(lg[i] - mx) / sum : 0.0f;
+            if (HYB || i >= n) child_q[p * kMaxMoves + i] = 0.0f;
+            if (i >= n) lg[i] = 0.0f;
+        }
     }
 }
 
@@ -1151,6 +1324,61 @@ static int launch_hybrid(const uint8_t* states, const uint8_t* mi, const int32_t
     return launch_status();
 }
 
+struct RowWorkspace {
+    int64_t* row_start;  // [count + 1]
+    int64_t* atr;        // [rows]
+    int64_t* mi;         // [rows]
+    float* x;            // [rows][122]
+    float* mf;           // [rows][31] (hybrid)
+    float* root_pre;     // [count][64]
+    float* logits;       // [count][256] (when the caller passes none)
+};
+
+template <bool HYB>
+static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            const float* root_features, const float* graph, const float* glob, int64_t count,
+                            int64_t rows, const float* fw, FnnDims fd, const float* hw, HybDims hd, float* priors,
+                            float* values, float* child_q, float* logits, RowWorkspace& w, cudaStream_t s) {
+    float* lg = logits ? logits : w.logits;
+    k_row_offsets<<<1, 1024, 0, s>>>(num_legal, count, w.row_start);
+    int grid = 0;
+    int rc = grid_for(k_row_index, count, 0, &grid);
+    if (rc) return rc;
+    k_row_index<<<grid, kThreads, 0, s>>>(num_legal, count, w.row_start, rows, w.atr, w.mi);
+    if (rows > 0) {
+        size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+        rc = grid_for(k_successor_features, rows, smem, &grid);
+        if (rc) return rc;
+        k_successor_features<<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows, w.x,
+                                                         w.row_start + count);
+        if (HYB) {
+            rc = grid_for(k_row_move_features, count, smem, &grid);
+            if (rc) return rc;
+            k_row_move_features<<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, count, w.row_start,
+                                                            rows, w.mf);
+        }
+    }
+    {
+        size_t smem = (sizeof(WarpSmem) + sizeof(FnnSmem)) * kWarpsPerBlock;
+        rc = grid_for(k_leaf_root<HYB>, count, smem, &grid);
+        if (rc) return rc;
+        k_leaf_root<HYB><<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, root_features, graph, glob,
+                                                      count, fw, fd, hw, hd, values, w.root_pre);
+    }
+    if (rows > 0) {
+        const size_t smem = sizeof(MlpSmem<HYB>);
+        const int64_t tiles = (rows + kMlpRows - 1) / kMlpRows;
+        rc = grid_for(k_mlp_rows<HYB>, tiles * kWarpsPerBlock, smem, &grid);
+        if (rc) return rc;
+        k_mlp_rows<HYB><<<grid, kMlpThreads, smem, s>>>(w.x, w.mf, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd,
+                                                        lg, child_q, w.row_start + count);
+    }
+    rc = grid_for(k_leaf_softmax<HYB>, count, 0, &grid);
+    if (rc) return rc;
+    k_leaf_softmax<HYB><<<grid, kThreads, 0, s>>>(num_legal, count, w.row_start, rows, lg, priors, child_q);
+    return launch_status();
+}
+
 }  // namespace hv
 
 using namespace hv;
@@ -1232,7 +1460,7 @@ int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const u
     int rc = grid_for(k_successor_features, num_actions, smem, &grid);
     if (rc) return rc;
     k_successor_features<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
-        states, num_states, legal_moves, action_to_root, move_indices, num_actions, features);
+        states, num_states, legal_moves, action_to_root, move_indices, num_actions, features, nullptr);
     return launch_status();
 }
 
@@ -1418,6 +1646,98 @@ int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves
     return hv_hybrid_evaluate(states, legal_moves, num_legal, root_features, count, node_feat_dim, trunk_image,
                               trunk_params, fnn_weights, hidden, embed, action_hidden, head_weights, value_hidden,
                               priors, values, child_q, logits, scratch, sizeof(g_hybrid_scratch), stream);
+}
+
+// ---- leaf evaluation as a row pipeline ------------------------------------
+
+static size_t row_workspace_layout(int64_t count, int64_t rows, bool hybrid, bool own_logits, uint8_t* base,
+                                   RowWorkspace* w) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t* p = base ? base + off : nullptr;
+        off += align256(bytes);
+        return p;
+    };
+    const size_t n = (size_t)count, r = (size_t)rows;
+    uint8_t* rs = take((n + 1) * sizeof(int64_t));
+    uint8_t* at = take(r * sizeof(int64_t));
+    uint8_t* mi = take(r * sizeof(int64_t));
+    uint8_t* x = take(r * kFeat * sizeof(float));
+    uint8_t* mf = hybrid ? take(r * kMoveFeat * sizeof(float)) : nullptr;
+    uint8_t* rp = take(n * 64 * sizeof(float));
+    uint8_t* lg = own_logits ? take(n * kMaxMoves * sizeof(float)) : nullptr;
+    if (w) {
+        w->row_start = reinterpret_cast<int64_t*>(rs);
+        w->atr = reinterpret_cast<int64_t*>(at);
+        w->mi = reinterpret_cast<int64_t*>(mi);
+        w->x = reinterpret_cast<float*>(x);
+        w->mf = reinterpret_cast<float*>(mf);
+        w->root_pre = reinterpret_cast<float*>(rp);
+        w->logits = reinterpret_cast<float*>(lg);
+    }
+    return off;
+}
+
+int hv_leaf_rows_workspace_bytes(int64_t count, int64_t rows, int hybrid, size_t* bytes) {
+    if (count < 0 || rows < 0 || !bytes) return HV_EINVAL;
+    *bytes = row_workspace_layout(count, rows, hybrid != 0, true, nullptr, nullptr);
+    if (hybrid) *bytes += hybrid_workspace_layout(count, nullptr, nullptr);
+    return HV_OK;
+}
+
+int hv_fnn_eval_leaves_rows(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            const float* root_features, int64_t count, int64_t rows, const float* weights,
+                            int hidden, int embed, int action_hidden, float* priors, float* values, float* child_q,
+                            float* logits, void* workspace, size_t workspace_bytes, void* stream) {
+    if (count < 0 || rows < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!states || !legal_moves || !num_legal || !weights || !priors || !values || !child_q ||
+        !aligned16(states) || !aligned16(legal_moves) || !workspace ||
+        (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return HV_EINVAL;
+    if (hidden < 1 || hidden > kFnnMaxDim || embed < 1 || embed > kFnnMaxDim || action_hidden < 1 ||
+        action_hidden > kFnnMaxDim)
+        return HV_EINVAL;
+    if (workspace_bytes < row_workspace_layout(count, rows, false, logits == nullptr, nullptr, nullptr))
+        return HV_EINVAL;
+    RowWorkspace w;
+    row_workspace_layout(count, rows, false, logits == nullptr, static_cast<uint8_t*>(workspace), &w);
+    return run_row_pipeline<false>(states, legal_moves, num_legal, root_features, nullptr, nullptr, count, rows,
+                                   weights, FnnDims{hidden, embed, action_hidden}, nullptr, HybDims{0, 0, 0}, priors,
+                                   values, child_q, logits, w, (cudaStream_t)stream);
+}
+
+int hv_hybrid_evaluate_rows(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            const float* root_features, int64_t count, int64_t rows, int node_feat_dim,
+                            const uint16_t* trunk_image, const float* trunk_params, const float* fnn_weights,
+                            int hidden, int embed, int action_hidden, const float* head_weights, int value_hidden,
+                            float* priors, float* values, float* child_q, float* logits, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+    if (count < 0 || rows < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!states || !legal_moves || !num_legal || !fnn_weights || !head_weights || !priors || !values ||
+        !child_q || !aligned16(states) || !aligned16(legal_moves) || !workspace ||
+        (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return HV_EINVAL;
+    if (hidden < 1 || hidden > kFnnMaxDim || embed < 1 || embed > kFnnMaxDim || action_hidden < 1 ||
+        action_hidden > kFnnMaxDim || value_hidden < 1 || value_hidden > kHybMaxValue)
+        return HV_EINVAL;
+    const size_t tok_bytes = hybrid_workspace_layout(count, nullptr, nullptr);
+    if (workspace_bytes < tok_bytes + row_workspace_layout(count, rows, true, logits == nullptr, nullptr, nullptr))
+        return HV_EINVAL;
+    HybridWorkspace hw;
+    hybrid_workspace_layout(count, static_cast<uint8_t*>(workspace), &hw);
+    RowWorkspace w;
+    row_workspace_layout(count, rows, true, logits == nullptr, static_cast<uint8_t*>(workspace) + tok_bytes, &w);
+    int rc = hv_hybrid_encode(states, count, hw.tf, hw.tq, hw.tr, hw.tz, hw.tm, hw.gf, hw.ntok, stream);
+    if (rc) return rc;
+    rc = hv_hybrid_trunk(hw.tf, hw.tq, hw.tr, hw.tz, hw.tm, count, node_feat_dim, trunk_image, trunk_params, hw.graph,
+                         stream);
+    if (rc) return rc;
+    return run_row_pipeline<true>(states, legal_moves, num_legal, root_features, hw.graph, hw.gf, count, rows,
+                                  fnn_weights, FnnDims{hidden, embed, action_hidden}, head_weights,
+                                  HybDims{embed, action_hidden, value_hidden}, priors, values, child_q, logits, w,
+                                  (cudaStream_t)stream);
 }
 
 int hv_root_tactical_probe(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,

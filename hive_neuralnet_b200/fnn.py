@@ -98,12 +98,33 @@ def pack_weights(net: HiveFNN, device: torch.device | str = "cuda") -> torch.Ten
     return flat.to(device).contiguous()
 
 
+def _rows(num_legal: torch.Tensor, total: int) -> int:
+    """Successor rows of a batch: sum of min(max(num_legal, 0), 256) (one device sync)."""
+    return int(num_legal[:total].clamp(0, MAX_LEGAL).sum().item())
+
+
+class _Workspace:
+    """Device scratch that only grows (256-byte aligned from the caching allocator)."""
+
+    def __init__(self):
+        self.buf = None
+
+    def get(self, nbytes: int, dev) -> torch.Tensor:
+        if self.buf is None or self.buf.device != dev or self.buf.numel() < nbytes:
+            self.buf = torch.empty((max(int(nbytes * 1.25), 256),), dtype=torch.uint8, device=dev)
+        return self.buf
+
+
 class FusedFNNEvaluator:
-    """Leaf evaluation with the fused successor + MLP kernel.
+    """Leaf evaluation on the device.
 
     ``eval_states`` has the signature and outputs of the reference's
     ``FNNMCTSOrchestrator._eval_states``: (priors_per_legal [T,256],
-    root_values [T], child_q_per_legal [T,256])."""
+    root_values [T], child_q_per_legal [T,256]).  It runs the row pipeline
+    (``hv_fnn_eval_leaves_rows``: successor features of all leaves, then the
+    network as a tiled fp32 GEMM over the successor rows); ``eval_states_fused``
+    runs the single warp-per-leaf kernel (``hv_fnn_eval_leaves``), which needs
+    no workspace."""
 
     def __init__(self, net: HiveFNN, device: torch.device | str = "cuda"):
         self.net = net
@@ -111,6 +132,7 @@ class FusedFNNEvaluator:
         self.lib = _lib.load()
         c = net.config
         self.dims = (c.hidden_dim, c.embed_dim, c.action_hidden)
+        self.ws = _Workspace()
         self.refresh()
 
     def refresh(self) -> None:
@@ -120,28 +142,51 @@ class FusedFNNEvaluator:
         if want != self.weights.numel():
             raise ValueError(f"packed {self.weights.numel()} floats, kernel expects {want}")
 
-    def eval_states(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
-                    total: int, root_features: torch.Tensor | None = None, return_logits: bool = False):
+    def _outputs(self, states, legal_moves, num_legal, total, root_features, return_logits):
         dev = states.device
         priors = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
         values = torch.empty((total,), dtype=torch.float32, device=dev)
         child_q = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
         logits = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev) if return_logits else None
-        if total == 0:
-            return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
         for t, name, dt in ((states, "states", torch.uint8), (legal_moves, "legal_moves", torch.uint8),
                             (num_legal, "num_legal", torch.int32)):
             if t.dtype != dt or not t.is_cuda or not t.is_contiguous():
                 raise ValueError(f"{name}: expected contiguous CUDA {dt}")
         if root_features is not None and (root_features.dtype != torch.float32 or not root_features.is_contiguous()):
             raise ValueError("root_features: expected contiguous float32")
-        with torch.cuda.device(dev):
-            _lib.check(self.lib.hv_fnn_eval_leaves(
-                states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
-                None if root_features is None else root_features.data_ptr(), total,
-                self.weights.data_ptr(), *self.dims, priors.data_ptr(), values.data_ptr(),
-                child_q.data_ptr(), None if logits is None else logits.data_ptr(),
-                torch.cuda.current_stream(dev).cuda_stream), "fnn_eval_leaves")
-        if return_logits:
-            return priors, values, child_q, logits
-        return priors, values, child_q
+        return priors, values, child_q, logits
+
+    def eval_states(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
+                    total: int, root_features: torch.Tensor | None = None, return_logits: bool = False):
+        import ctypes
+        priors, values, child_q, logits = self._outputs(states, legal_moves, num_legal, total, root_features,
+                                                        return_logits)
+        if total > 0:
+            dev = states.device
+            rows = _rows(num_legal, total)
+            need = ctypes.c_size_t(0)
+            _lib.check(self.lib.hv_leaf_rows_workspace_bytes(total, rows, 0, ctypes.addressof(need)), "workspace")
+            ws = self.ws.get(need.value, dev)
+            with torch.cuda.device(dev):
+                _lib.check(self.lib.hv_fnn_eval_leaves_rows(
+                    states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
+                    None if root_features is None else root_features.data_ptr(), total, rows,
+                    self.weights.data_ptr(), *self.dims, priors.data_ptr(), values.data_ptr(), child_q.data_ptr(),
+                    None if logits is None else logits.data_ptr(), ws.data_ptr(), ws.numel(),
+                    torch.cuda.current_stream(dev).cuda_stream), "fnn_eval_leaves_rows")
+        return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
+
+    def eval_states_fused(self, states: torch.Tensor, legal_moves: torch.Tensor, num_legal: torch.Tensor,
+                          total: int, root_features: torch.Tensor | None = None, return_logits: bool = False):
+        priors, values, child_q, logits = self._outputs(states, legal_moves, num_legal, total, root_features,
+                                                        return_logits)
+        if total > 0:
+            dev = states.device
+            with torch.cuda.device(dev):
+                _lib.check(self.lib.hv_fnn_eval_leaves(
+                    states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
+                    None if root_features is None else root_features.data_ptr(), total,
+                    self.weights.data_ptr(), *self.dims, priors.data_ptr(), values.data_ptr(),
+                    child_q.data_ptr(), None if logits is None else logits.data_ptr(),
+                    torch.cuda.current_stream(dev).cuda_stream), "fnn_eval_leaves")
+        return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)

@@ -333,6 +333,42 @@ class HybridEvaluator:
         return ws
 
     def eval_states(self, states, legal_moves, num_legal, total, root_features=None, return_logits=False):
+        """The row pipeline (``hv_hybrid_evaluate_rows``): tokens, trunk, successor
+        features and move features of all leaves, tiled fp32 heads over the rows."""
+        import ctypes
+
+        from .fnn import _rows
+        dev = states.device
+        priors = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
+        values = torch.empty((total,), dtype=torch.float32, device=dev)
+        child_q = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
+        logits = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev) if return_logits else None
+        if total == 0:
+            return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
+        for t, name, dt in ((states, "states", torch.uint8), (legal_moves, "legal_moves", torch.uint8),
+                            (num_legal, "num_legal", torch.int32)):
+            if t.dtype != dt or not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"{name}: expected contiguous CUDA {dt}")
+        if root_features is not None and (root_features.dtype != torch.float32 or not root_features.is_contiguous()):
+            raise ValueError("root_features: expected contiguous float32")
+        rows = _rows(num_legal, total)
+        need = ctypes.c_size_t(0)
+        _lib.check(self.lib.hv_leaf_rows_workspace_bytes(total, rows, 1, ctypes.addressof(need)), "workspace")
+        if getattr(self, "_rows_ws", None) is None or self._rows_ws.device != dev or self._rows_ws.numel() < need.value:
+            self._rows_ws = torch.empty((max(int(need.value * 1.25), 256),), dtype=torch.uint8, device=dev)
+        ws = self._rows_ws
+        with torch.cuda.device(dev):
+            _lib.check(self.lib.hv_hybrid_evaluate_rows(
+                states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),
+                None if root_features is None else root_features.data_ptr(), total, rows,
+                self.net.config.node_feat_dim, self.trunk.image.data_ptr(), self.trunk.params.data_ptr(),
+                self.fnn_weights.data_ptr(), *self.fdims, self.head_weights.data_ptr(), self.vh, priors.data_ptr(),
+                values.data_ptr(), child_q.data_ptr(), None if logits is None else logits.data_ptr(), ws.data_ptr(),
+                ws.numel(), torch.cuda.current_stream(dev).cuda_stream), "hybrid_evaluate_rows")
+        return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
+
+    def eval_states_fused(self, states, legal_moves, num_legal, total, root_features=None, return_logits=False):
+        """The single-call warp-per-leaf evaluation (``hv_hybrid_evaluate``)."""
         dev = states.device
         priors = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
         values = torch.empty((total,), dtype=torch.float32, device=dev)

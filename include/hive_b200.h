@@ -278,6 +278,28 @@ int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves
                                int value_hidden, float* priors, float* values, float* child_q, float* logits,
                                void* stream);
 
+/* Leaf evaluation as a row pipeline, the evaluators' default path: the
+ * successors of all `count` leaves are compacted into `rows` rows
+ * (rows = sum over leaves of min(max(num_legal, 0), 256)), their features
+ * written to the workspace, the network run as a tiled fp32 GEMM pipeline
+ * over rows, the per-leaf parts and the softmax by warp-per-leaf kernels.
+ * Same outputs as hv_fnn_eval_leaves / hv_hybrid_evaluate (fp32, a
+ * different summation order).  workspace: 256-byte aligned, at least
+ * hv_leaf_rows_workspace_bytes(count, rows, hybrid) bytes; with logits ==
+ * NULL the raw logits live in the workspace.  Rows beyond `rows` are dropped
+ * (device error word bit 0). */
+int hv_leaf_rows_workspace_bytes(int64_t count, int64_t rows, int hybrid, size_t* bytes);
+int hv_fnn_eval_leaves_rows(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            const float* root_features, int64_t count, int64_t rows, const float* weights,
+                            int hidden, int embed, int action_hidden, float* priors, float* values, float* child_q,
+                            float* logits, void* workspace, size_t workspace_bytes, void* stream);
+int hv_hybrid_evaluate_rows(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
+                            const float* root_features, int64_t count, int64_t rows, int node_feat_dim,
+                            const uint16_t* trunk_image, const float* trunk_params, const float* fnn_weights,
+                            int hidden, int embed, int action_hidden, const float* head_weights, int value_hidden,
+                            float* priors, float* values, float* child_q, float* logits, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* root_tactical_probe_batch(states, legal_moves, num_legal, priors, batch_size,
  *     enable_win_in_one, enable_check_opponent_wins, enable_win_in_two)
  * replaces bindings.cpp:91-100,336-339 / game_logic.cu:290-397,1579-1615.

@@ -22,7 +22,8 @@ def _close(a, b):
 
 @pytest.mark.parametrize("preset", ["large", "medium", "small"])
 @pytest.mark.parametrize("with_root_features", [True, False])
-def test_fused_eval_matches_reference(preset, with_root_features):
+@pytest.mark.parametrize("path", ["rows", "fused"])
+def test_fused_eval_matches_reference(preset, with_root_features, path):
     from hive_neuralnet_b200.fnn import FNNConfig, FusedFNNEvaluator, HiveFNN
     orc = O.oracle()
     torch.manual_seed(0)
@@ -35,8 +36,8 @@ def test_fused_eval_matches_reference(preset, with_root_features):
     pr, vr, cr, lr = eval_states_reference(net, fo, sf, no)
     ev = FusedFNNEvaluator(net)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-    out = ev.eval_states(t(st), t(mo), t(no), len(st), t(fo) if with_root_features else None,
-                         return_logits=True)
+    fn = ev.eval_states if path == "rows" else ev.eval_states_fused
+    out = fn(t(st), t(mo), t(no), len(st), t(fo) if with_root_features else None, return_logits=True)
     pg, vg, cg, lg = (x.cpu().numpy() for x in out)
     assert _close(vg, vr).all(), np.abs(vg - vr).max()
     valid = np.arange(256)[None, :] < no[:, None]
@@ -55,7 +56,8 @@ def test_terminal_and_empty_rows():
     st = torch.zeros((3, 3424), dtype=torch.uint8, device="cuda")
     mv = torch.zeros((3, 256, 6), dtype=torch.uint8, device="cuda")
     nl = torch.zeros((3,), dtype=torch.int32, device="cuda")
-    p, v, c = ev.eval_states(st, mv, nl, 3)
-    assert (p == 0).all() and (c == 0).all() and torch.isfinite(v).all()
+    for fn in (ev.eval_states, ev.eval_states_fused):
+        p, v, c = fn(st, mv, nl, 3)
+        assert (p == 0).all() and (c == 0).all() and torch.isfinite(v).all()
     p0, v0, c0 = ev.eval_states(st[:0], mv[:0], nl[:0], 0)
     assert p0.shape == (0, 256) and v0.shape == (0,)

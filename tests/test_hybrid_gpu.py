@@ -35,7 +35,8 @@ def _reference_eval(net, orc, st):
 
 @pytest.mark.parametrize("preset", ["default", "small"])
 @pytest.mark.parametrize("with_root_features", [True, False])
-def test_hybrid_eval_matches_fp32_statement(preset, with_root_features):
+@pytest.mark.parametrize("path", ["rows", "fused"])
+def test_hybrid_eval_matches_fp32_statement(preset, with_root_features, path):
     from hive_neuralnet_b200.hybrid import HiveHybridGNN, HybridEvaluator, HybridGNNConfig
     torch.manual_seed(11)
     net = HiveHybridGNN(HybridGNNConfig() if preset == "default" else HybridGNNConfig.small()).eval()
@@ -44,8 +45,8 @@ def test_hybrid_eval_matches_fp32_statement(preset, with_root_features):
     mo, no, fo, logits, pri, vals, valid = _reference_eval(net, orc, st)
     ev = HybridEvaluator(net)
     d = lambda a: torch.from_numpy(a).cuda()
-    p, v, cq, lg = ev.eval_states(d(st), d(mo), d(no), len(st), d(fo) if with_root_features else None,
-                                  return_logits=True)
+    fn = ev.eval_states if path == "rows" else ev.eval_states_fused
+    p, v, cq, lg = fn(d(st), d(mo), d(no), len(st), d(fo) if with_root_features else None, return_logits=True)
     p, v, cq, lg = (t.cpu().numpy() for t in (p, v, cq, lg))
     assert np.abs(lg - np.where(valid, logits, 0))[valid].max() < TOL
     assert np.abs(p - pri).max() < TOL

@@ -1,5 +1,5 @@
 """hv_hybrid_evaluate_noalloc (fixed file-scope device scratch) against the
-workspace entry point hv_hybrid_evaluate, on two calls in a row; and the
+workspace entry point hv_hybrid_evaluate (eval_states_fused), on two calls in a row; and the
 oversize rejection.  Collected last; needs nothing from other test files."""
 
 import numpy as np
@@ -24,13 +24,13 @@ def test_noalloc_matches_workspace_entry_point_twice():
     torch.manual_seed(21)
     ev = HybridEvaluator(HiveHybridGNN().eval())
     st, mo, no, fo = _inputs(700)
-    want = ev.eval_states(st, mo, no, len(st), fo)
+    want = ev.eval_states_fused(st, mo, no, len(st), fo)
     for _ in range(2):
         got = ev.eval_states_noalloc(st, mo, no, len(st), fo)
         for g, w in zip(got, want):
             assert torch.equal(g, w)
     # root features computed in the kernel, then a smaller call reusing the scratch
-    want2 = ev.eval_states(st[:123], mo[:123], no[:123], 123)
+    want2 = ev.eval_states_fused(st[:123], mo[:123], no[:123], 123)
     got2 = ev.eval_states_noalloc(st[:123], mo[:123], no[:123], 123)
     for g, w in zip(got2, want2):
         assert torch.equal(g, w)
