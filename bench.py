@@ -32,6 +32,7 @@ sys.path.insert(0, ROOT)
 METRIC = "movegen+encode positions/sec"
 UNIT = "positions/s"
 POSITIONS = 262144
+POSITIONS_DEFAULT = POSITIONS
 MAX_PLY = 120
 EXPANSIONS = 7
 SEED = 20260101
@@ -505,7 +506,7 @@ def run_fnn(args) -> None:
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     ev = FusedFNNEvaluator(HiveFNN(), dev)
-    P = 65536
+    P = 65536 if args.positions == POSITIONS_DEFAULT else args.positions
     st = ext.generate_positions(SEED + 3, 0, P, MAX_PLY, EXPANSIONS, device=dev)
     legal, nl, feats = ext.generate_legal_moves_and_fnn_features_batch(st, P)
     for _ in range(args.warmup):
@@ -541,7 +542,7 @@ def run_fnn(args) -> None:
     print(json.dumps({"metric": "FNN leaf evaluations/sec", "value": P / (ms / 1e3), "unit": "roots/s",
                       "successors_per_s": succ / (ms / 1e3), "ms_per_step": ms, "steps": args.steps,
                       "warmup": args.warmup, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
-                      "config": {"workload": "config3: 65536 roots x all legal successors, FNN large fp32",
+                      "config": {"workload": f"config3: {P} roots x all legal successors, FNN large fp32",
                                  "successors": succ},
                       "mlp_tflops": flops / (ms / 1e3) / 1e12, "cpu_baseline": cpu}), flush=True)
 
