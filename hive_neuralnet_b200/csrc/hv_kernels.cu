@@ -1535,11 +1535,11 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
     const size_t smem = sizeof(TrunkSmem);
     if (cudaFuncSetAttribute(k_hybrid_trunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return HV_ECUDA;
-    const int64_t tiles = (batch + 3) / 4;
-    const int grid = (int)(tiles < d.sms ? tiles : d.sms);
+    const int64_t passes = (batch + kTrWarps - 1) / kTrWarps;
+    const int grid = (int)(passes < d.sms ? passes : d.sms);
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
-    k_hybrid_trunk<<<grid, 128, smem, (cudaStream_t)stream>>>(
+    k_hybrid_trunk<<<grid, kTrThreads, smem, (cudaStream_t)stream>>>(
         token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim,
         reinterpret_cast<const __half*>(weight_image), params, graph_summary, err);
     return launch_status();

@@ -3,16 +3,19 @@
 // RelativeTransformerBlock / HybridRelativeTransformerTrunk), hidden 64,
 // 8 heads of 8, GELU MLP 96, 4 pre-LayerNorm blocks, on sm_100a.
 //
-// One CTA of 4 warps owns a tile of 4 positions = 128 rows (a position is 32
-// rows: CLS, its 28 piece tokens, 3 padding rows), one row per thread, the
-// residual stream in registers.  The five linear layers of a block (token
+// One CTA of 8 warps owns two tiles of 4 positions = 2 x 128 rows (a
+// position is 32 rows: CLS, its 28 piece tokens, 3 padding rows), one row per
+// thread, the residual stream in registers; each tile has its own 256 TMEM
+// columns, and one issuing thread drives both tiles' MMAs per GEMM.  The five linear layers of a block (token
 // projection once, then QKV, attention output, MLP in and out) are fp16
 // tcgen05.mma GEMMs with M = 128 and fp32 accumulators in TMEM, issued by one
-// thread (fp16 operands as the reference's autocast, fp32 accumulation).  The per-head 32 x 32 attention of a position (head width 8, below
-// the tcgen05 K step and M tile) runs on warp-level fp16 MMAs inside the
-// warp that owns the position.  Block weights stream from global memory
-// (L2-resident) into a double-buffered shared image with bulk copies, one
-// block ahead.
+// thread (fp16 operands as the reference's autocast, fp32 accumulation).
+// The per-head 32 x 32 attention of a position (head width 8, below the
+// tcgen05 K step and M tile) runs on warp-level fp16 MMAs inside the warp
+// that owns the position; the queries live in the A-operand slabs of the
+// output projection, which the heads overwrite one by one.  Block weights
+// stream from global memory (L2-resident) into shared memory with a bulk
+// copy issued as soon as the previous block's last GEMM has completed.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -23,6 +26,7 @@
 namespace hv {
 
 constexpr int kTrH = 64, kTrHeads = 8, kTrFfn = 96, kTrLayers = 4;
+constexpr int kTrWarps = 8, kTrThreads = kTrWarps * 32, kTrTiles = 2;  // 8 positions per CTA pass
 constexpr int kTrKin = 32;   // token features, zero-padded to two MMA K steps
 constexpr int kTrQkStride = 72;  // fp16 row stride of Q / K (conflict-free fragment loads)
 constexpr int kTrVtStride = 40;  // fp16 row stride of the transposed V of one position
@@ -39,21 +43,20 @@ constexpr int kLLn1G = 0, kLLn1B = 64, kLBqkv = 128, kLBo = 320, kLLn2G = 384, k
               kLB2 = 608, kLDq = 672, kLDr = 808, kLDz = 944, kLEnd = 984;
 
 struct __align__(16) TrunkSmem {
-    __half w[2][kImgLayer];            // block weights, double buffered
-    __half tp[kImgTp];                 // token projection weights
-    __half a[kTrFfn / 8][128][8];      // A operand (K <= 96)
-    __half q[128 * kTrQkStride];              // queries, row-major (bias added)
-    __half k[128 * kTrQkStride];              // keys
-    __half vt[4][kTrH * kTrVtStride];         // values, transposed per position [dim][key]
-    int32_t cq[128], cr[128], cz[128];        // token coordinates (CLS and padding 0)
-    float par[kLEnd];                         // this block's fp32 parameters
-    uint64_t bar_w[2], bar_mma;
+    __half w[kImgLayer];                           // this block's weights
+    __half tp[kImgTp];                             // token projection weights
+    __half a[kTrTiles][kTrFfn / 8][128][8];        // A operand per tile (K <= 96); queries during attention
+    __half k[kTrThreads * kTrQkStride];            // keys, row-major (bias added)
+    __half vt[kTrWarps][kTrH * kTrVtStride];       // values, transposed per position [dim][key]
+    int32_t cq[kTrThreads], cr[kTrThreads], cz[kTrThreads];  // token coordinates (CLS and padding 0)
+    float par[kLEnd];                              // this block's fp32 parameters
+    uint64_t bar_w, bar_mma;
     uint32_t tmem;
     int err;
 };
 
-// 8 values of this thread's row -> slab c of the A operand (one 16-byte store)
-__device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int row, const float* x) {
+// 8 values of this thread's row -> slab c of its tile's A operand (one 16-byte store)
+__device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int t, const float* x) {
     __half2 p0 = __floats2half2_rn(x[0], x[1]);
     __half2 p1 = __floats2half2_rn(x[2], x[3]);
     __half2 p2 = __floats2half2_rn(x[4], x[5]);
@@ -63,13 +66,13 @@ __device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int row, const f
     u.y = *reinterpret_cast<uint32_t*>(&p1);
     u.z = *reinterpret_cast<uint32_t*>(&p2);
     u.w = *reinterpret_cast<uint32_t*>(&p3);
-    *reinterpret_cast<uint4*>(&s->a[c][row][0]) = u;
+    *reinterpret_cast<uint4*>(&s->a[t >> 7][c][t & 127][0]) = u;
 }
 
-// write this thread's row (n values) into the A operand in slab layout
-__device__ __forceinline__ void put_row_f16(TrunkSmem* s, int row, const float* x, int n) {
+// write this thread's row (n values) into its tile's A operand in slab layout
+__device__ __forceinline__ void put_row_f16(TrunkSmem* s, int t, const float* x, int n) {
 #pragma unroll
-    for (int c = 0; c < n / 8; c++) put_chunk8(s, c, row, x + 8 * c);
+    for (int c = 0; c < n / 8; c++) put_chunk8(s, c, t, x + 8 * c);
 }
 
 // LayerNorm of a 64-vector (eps 1e-5, biased variance), gamma/beta from smem
@@ -98,7 +101,8 @@ __device__ __forceinline__ bool trunk_gemm(TrunkSmem* s, uint32_t d_col, const v
     __syncthreads();
     if (threadIdx.x == 0) {
         tc_fence_after();
-        gemm_m128(s->tmem + d_col, &s->a[0][0][0], b, n, k);
+#pragma unroll
+        for (int u = 0; u < kTrTiles; u++) gemm_m128(s->tmem + 256 * u + d_col, &s->a[u][0][0][0], b, n, k);
         mma_commit(&s->bar_mma);
     }
     const bool ok = mbar_wait(&s->bar_mma, mphase);
@@ -107,18 +111,20 @@ __device__ __forceinline__ bool trunk_gemm(TrunkSmem* s, uint32_t d_col, const v
     return __syncthreads_and(ok) != 0;
 }
 
+// TMEM address of this thread's row: warp w reads lanes 32 (w % 4) of tile w / 4's columns
 __device__ __forceinline__ uint32_t lane_taddr(const TrunkSmem* s, int col) {
-    return s->tmem + ((uint32_t)((threadIdx.x >> 5) * 32) << 16) + (uint32_t)col;
+    const int w = threadIdx.x >> 5;
+    return s->tmem + ((uint32_t)((w & 3) * 32) << 16) + (uint32_t)(256 * (w >> 2) + col);
 }
 
-__device__ __forceinline__ void prefetch_block(TrunkSmem* s, int buf, const __half* img, int layer) {
+__device__ __forceinline__ void prefetch_block(TrunkSmem* s, const __half* img, int layer) {
     const __half* src = img + kImgTp + (size_t)layer * kImgLayer;
-    mbar_expect_tx(&s->bar_w[buf], kImgLayerBytes);
+    mbar_expect_tx(&s->bar_w, kImgLayerBytes);
     // four copies, one per matrix (each a multiple of 16 bytes)
-    bulk_g2s(&s->w[buf][0], src, kImgQkv * 2, &s->bar_w[buf]);
-    bulk_g2s(&s->w[buf][kImgQkv], src + kImgQkv, kImgO * 2, &s->bar_w[buf]);
-    bulk_g2s(&s->w[buf][kImgQkv + kImgO], src + kImgQkv + kImgO, kImgW1 * 2, &s->bar_w[buf]);
-    bulk_g2s(&s->w[buf][kImgQkv + kImgO + kImgW1], src + kImgQkv + kImgO + kImgW1, kImgW2 * 2, &s->bar_w[buf]);
+    bulk_g2s(&s->w[0], src, kImgQkv * 2, &s->bar_w);
+    bulk_g2s(&s->w[kImgQkv], src + kImgQkv, kImgO * 2, &s->bar_w);
+    bulk_g2s(&s->w[kImgQkv + kImgO], src + kImgQkv + kImgO, kImgW1 * 2, &s->bar_w);
+    bulk_g2s(&s->w[kImgQkv + kImgO + kImgW1], src + kImgQkv + kImgO + kImgW1, kImgW2 * 2, &s->bar_w);
 }
 
 __device__ __forceinline__ uint32_t ld_b32(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
@@ -152,7 +158,7 @@ __device__ __forceinline__ void mma_k16(float* d, uint32_t a0, uint32_t a1, uint
 // operand slab of the output projection.  Fragment coordinates: g = lane/4
 // selects rows g and g+8 of a 16-row tile, c = lane%4 selects columns 2c, 2c+1.
 __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t kmask) {
-    const int g = l >> 2, c = l & 3, base = w * 32;
+    const int g = l >> 2, c = l & 3, base = w * 32, u = w >> 2, tb = (w & 3) * 32;
     const float scale = 0.35355339059327373f;  // 8 ** -0.5
     // relative-offset table indices of this thread's 32 (row, key) pairs
     uint32_t rel[2][2][4][2];
@@ -180,8 +186,8 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
         float sc[2][4][4];
 #pragma unroll
         for (int mt = 0; mt < 2; mt++) {
-            const __half* qa = s->q + (base + 16 * mt + g) * kTrQkStride + 8 * h + 2 * c;
-            const uint32_t a0 = ld_b32(qa), a1 = ld_b32(qa + 8 * kTrQkStride);
+            const __half* qa = &s->a[u][h][tb + 16 * mt + g][2 * c];
+            const uint32_t a0 = ld_b32(qa), a1 = ld_b32(qa + 8 * 8);
 #pragma unroll
             for (int nt = 0; nt < 4; nt++) {
                 const uint32_t b0 = ld_b32(s->k + (base + 8 * nt + g) * kTrQkStride + 8 * h + 2 * c);
@@ -235,9 +241,9 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                 const uint32_t a3 = pack_f16(sc[mt][2 * kb + 1][2], sc[mt][2 * kb + 1][3]);
                 mma_k16(o, a0, a1, a2, a3, ld_b32(vt + 16 * kb), ld_b32(vt + 16 * kb + 8));
             }
-            const int r0 = base + 16 * mt + g;
-            *reinterpret_cast<uint32_t*>(&s->a[h][r0][2 * c]) = pack_f16(o[0] * rinv[mt][0], o[1] * rinv[mt][0]);
-            *reinterpret_cast<uint32_t*>(&s->a[h][r0 + 8][2 * c]) =
+            const int r0 = tb + 16 * mt + g;
+            *reinterpret_cast<uint32_t*>(&s->a[u][h][r0][2 * c]) = pack_f16(o[0] * rinv[mt][0], o[1] * rinv[mt][0]);
+            *reinterpret_cast<uint32_t*>(&s->a[u][h][r0 + 8][2 * c]) =
                 pack_f16(o[2] * rinv[mt][1], o[3] * rinv[mt][1]);
         }
     }
@@ -247,7 +253,7 @@ __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f +
 
 // token_features [B,28,27] (first `nfeat` used), token_q/r/z [B,28], token_mask [B,28] (0/1),
 // img: fp16 weight image, par: fp32 parameters; out [B,64]: the normalised CLS row
-__global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict__ tf, const int32_t* __restrict__ tq,
+__global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __restrict__ tf, const int32_t* __restrict__ tq,
                                                          const int32_t* __restrict__ tr, const int32_t* __restrict__ tz,
                                                          const uint8_t* __restrict__ tm, int64_t batch, int nfeat,
                                                          const __half* __restrict__ img,
@@ -256,41 +262,39 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
     extern __shared__ __align__(16) uint8_t smem_raw[];
     TrunkSmem* s = reinterpret_cast<TrunkSmem*>(smem_raw);
     const int t = threadIdx.x, w = t >> 5, l = t & 31;
-    const int64_t ntiles = (batch + 3) / 4;
+    const int64_t npass = (batch + kTrWarps - 1) / kTrWarps;  // 8 positions per pass
 
     if (t == 0) {
-        mbar_init(&s->bar_w[0], 1);
-        mbar_init(&s->bar_w[1], 1);
+        mbar_init(&s->bar_w, 1);
         mbar_init(&s->bar_mma, 1);
         s->err = 0;
         fence_mbar_init();
     }
     if (w == 0) {
-        tmem_alloc(&s->tmem, 256);
+        tmem_alloc(&s->tmem, 512);
         tmem_relinquish();
     }
     {
         const uint4* src = reinterpret_cast<const uint4*>(img);
         uint4* dst = reinterpret_cast<uint4*>(s->tp);
-        for (int i = t; i < kImgTp / 8; i += 128) dst[i] = __ldg(src + i);
+        for (int i = t; i < kImgTp / 8; i += kTrThreads) dst[i] = __ldg(src + i);
     }
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
 
-    uint32_t mphase = 0, wphase[2] = {0u, 0u};
-    bool wpend[2] = {false, false};
+    uint32_t mphase = 0, wphase = 0;
+    bool wpend = false;
     bool mpend = false;
     bool failed = false;
-    int64_t slot = 0;
-    if (t == 0 && blockIdx.x < ntiles) {
-        prefetch_block(s, 0, img, 0);
-        wpend[0] = true;
+    if (t == 0 && blockIdx.x < npass) {
+        prefetch_block(s, img, 0);
+        wpend = true;
     }
 
-    for (int64_t tile = blockIdx.x; tile < ntiles && !failed; tile += gridDim.x) {
-        const int64_t b = tile * 4 + w;
+    for (int64_t pass = blockIdx.x; pass < npass && !failed; pass += gridDim.x) {
+        const int64_t b = pass * kTrWarps + w;
         const bool live = b < batch;
         // ---- inputs of this row: token features (rows 1..28), CLS (row 0), padding (29..31)
         const int tok = l - 1;
@@ -328,19 +332,10 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             }
         }
 
-        for (int layer = 0; layer < kTrLayers; layer++, slot++) {
-            const int buf = (int)(slot & 1);
+        for (int layer = 0; layer < kTrLayers; layer++) {
             // this block's fp32 parameters
             __syncthreads();
-            for (int i = t; i < kLEnd; i += 128) s->par[i] = __ldg(par + kParLayer0 + layer * kLEnd + i);
-            // prefetch the next block (next layer, or layer 0 of this CTA's next tile)
-            if (t == 0) {
-                const bool more = layer + 1 < kTrLayers || tile + gridDim.x < ntiles;
-                if (more) {
-                    prefetch_block(s, buf ^ 1, img, (layer + 1) % kTrLayers);
-                    wpend[buf ^ 1] = true;
-                }
-            }
+            for (int i = t; i < kLEnd; i += kTrThreads) s->par[i] = __ldg(par + kParLayer0 + layer * kLEnd + i);
             __syncthreads();
             // ---- attention
             float y[kTrH];
@@ -348,15 +343,15 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             put_row_f16(s, t, y, kTrH);
             bool okw = true;
             if (t == 0) {
-                okw = mbar_wait(&s->bar_w[buf], wphase[buf]);
-                wphase[buf] ^= 1u;
-                if (okw) wpend[buf] = false;
+                okw = mbar_wait(&s->bar_w, wphase);
+                wphase ^= 1u;
+                if (okw) wpend = false;
             }
             if (!__syncthreads_and(okw)) {
                 failed = true;
                 break;
             }
-            const __half* W = s->w[buf];
+            const __half* W = s->w;
             mpend = true;
             if (!trunk_gemm(s, 0, W, 3 * kTrH, kTrH, mphase)) {
                 failed = true;
@@ -364,17 +359,26 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
             }
             mpend = false;
             {
-                // q, k (row-major) and v (transposed, per position) to shared memory in fp16
+                // queries into the A slabs (one per head), keys row-major, values
+                // transposed per position; fp16, biases added
                 float d[32];
 #pragma unroll
-                for (int c = 0; c < 6; c++) {
+                for (int c = 0; c < 2; c++) {
+                    tmem_ld32(lane_taddr(s, 32 * c), d);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) d[i] += s->par[kLBqkv + 32 * c + i];
+#pragma unroll
+                    for (int hh = 0; hh < 4; hh++) put_chunk8(s, 4 * c + hh, t, d + 8 * hh);
+                }
+#pragma unroll
+                for (int c = 2; c < 6; c++) {
                     tmem_ld32(lane_taddr(s, 32 * c), d);
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         const int j = 32 * c + i;
                         const float v0 = d[i] + s->par[kLBqkv + j], v1 = d[i + 1] + s->par[kLBqkv + j + 1];
                         if (j < 128) {
-                            __half* row = (j < 64 ? s->q : s->k) + t * kTrQkStride + (j & 63);
+                            __half* row = s->k + t * kTrQkStride + (j - 64);
                             *reinterpret_cast<__half2*>(row) = __floats2half2_rn(v0, v1);
                         } else {
                             __half* vt = s->vt[w] + (j - 128) * kTrVtStride + l;
@@ -427,6 +431,12 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
                 break;
             }
             mpend = false;
+            // every MMA reading this block's weights has completed: fetch the
+            // next block (next layer, or layer 0 of this CTA's next pass)
+            if (t == 0 && (layer + 1 < kTrLayers || pass + gridDim.x < npass)) {
+                prefetch_block(s, img, (layer + 1) % kTrLayers);
+                wpend = true;
+            }
             {
                 float d[32];
                 const float keep = (l == 0) ? 1.0f : (valid ? 1.0f : 0.0f);
@@ -458,8 +468,7 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
         // MMAs in flight finish (bounded again), free TMEM and return
         if (t == 0) {
             atomicOr(err_word, 4u);
-            for (int i = 0; i < 2; i++)
-                if (wpend[i]) mbar_wait(&s->bar_w[i], wphase[i]);
+            if (wpend) mbar_wait(&s->bar_w, wphase);
         }
         if (mpend) mbar_wait(&s->bar_mma, mphase ^ 1u);
     }
@@ -467,7 +476,7 @@ __global__ void __launch_bounds__(128, 1) k_hybrid_trunk(const float* __restrict
     __syncthreads();
     if (w == 0) {
         tc_fence_after();
-        tmem_dealloc(s->tmem, 256);
+        tmem_dealloc(s->tmem, 512);
     }
 }
 
