@@ -28,10 +28,9 @@ constexpr int kMlpThreads = 256;
 constexpr int kMlpHs = 65;  // row stride of the hidden / embedding tile
 
 // Tile buffer (floats): the feature tile [64][122] at 0; once it is consumed,
-// the hidden rows h [64][65] at 0 and the embeddings e [64][65] at kMlpE;
-// the hybrid's move features [64][32] at kMlpM.
-constexpr int kMlpE = kMlpRows * kMlpHs;        // 4160
-constexpr int kMlpM = 2 * kMlpRows * kMlpHs;    // 8320 (>= 64 * 122)
+// the hidden rows h [64][65] at 0, then the embeddings e [64][65] over them;
+// the hybrid's move features [64][32] after the feature tile at kMlpM.
+constexpr int kMlpM = kMlpRows * kFeat;  // 7808
 template <bool HYB>
 struct MlpSmem {
     float w1[kFeat][64];     // W1^T, columns >= H zero
@@ -40,7 +39,7 @@ struct MlpSmem {
     float c[HYB ? 32 : 1][64];  // hybrid: folded move projection C^T, rows >= 31 zero
     float b1[64], g1[64], be1[64], b2[64], wv[64], a2[64];
     float bv, a2b, pad_[2];
-    float buf[kMlpM + (HYB ? kMlpRows * 32 : 0)];
+    float buf[kMlpM + (HYB ? kMlpRows * 32 : 0)];  // two 8-warp CTAs per SM for both variants
 };
 
 // sum over the 16 lanes (tx) that share a row
@@ -110,7 +109,7 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
     MlpSmem<HYB>* s = reinterpret_cast<MlpSmem<HYB>*>(mlp_raw);
     float* xs = s->buf;            // feature tile, row stride 122
     float* hs = s->buf;            // hidden rows, stride 65 (after the tile is consumed)
-    float* es = s->buf + kMlpE;    // embeddings, stride 65
+    float* es = s->buf;            // embeddings, stride 65 (after the hidden rows are consumed)
     float* ms = s->buf + kMlpM;    // hybrid move features, stride 32
     const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
     const int H = fd.H, E = fd.E;
@@ -191,6 +190,7 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
                 acc[i][3] = fmaf(h, w.w, acc[i][3]);
             }
         }
+        __syncthreads();  // the hidden rows are consumed: e overwrites them
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int r = 4 * ty + i;
