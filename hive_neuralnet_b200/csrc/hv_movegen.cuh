@@ -177,6 +177,49 @@ __device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out,
     return first_only ? 0 : cnt;
 }
 
+// The ant's full breadth-first search (move_gen.cuh:267-388), the hottest
+// walk (about half of the generator's time): the walk engine's ant path
+// without its mode dispatch and path bookkeeping.  Lanes take (queue item,
+// direction) pairs, five items per round; the queue is the output list.
+__device__ __noinline__ int ant_walk(WarpSmem* w, int cell, uint16_t* out, int cap) {
+    const int l = lane_id();
+    const uint32_t lt = lanemask_lt();
+    const int k = l / 6, d = l - 6 * (l / 6);
+    const uint32_t* slx = w->slx[d < 6 ? d : 0];
+    const int step = dstep(d < 6 ? d : 0);
+    set_clear(w->seen);
+    if (l == 0) set_add(w->seen, cell);
+    __syncwarp();
+    int rd = -1, cnt = 0;  // rd < 0: the seed round (the ant's own cell)
+#pragma unroll 1
+    while (true) {
+        const int items = rd < 0 ? 1 : min(5, cnt - rd);
+        if (items <= 0) break;
+        int dest = -1;
+        bool fin = false;
+        if (k < items) {
+            const int cur = rd < 0 ? cell : out[rd + k];
+            if (rowbit(slx, cur)) {
+                dest = cur + step;
+                fin = !set_has(w->seen, dest);
+            }
+        }
+        const uint32_t mm = __match_any_sync(kFull, fin ? dest : -1 - l);
+        const bool keep = fin && ((mm & lt) == 0u);
+        const uint32_t b = __ballot_sync(kFull, keep);
+        const int pos = cnt + __popc(b & lt);
+        if (keep && pos < cap) {
+            out[pos] = (uint16_t)dest;
+            set_add(w->seen, dest);
+        }
+        cnt = min(cap, cnt + __popc(b));
+        rd = rd < 0 ? 0 : rd + items;
+        __syncwarp();
+        if (cnt >= cap) break;
+    }
+    return cnt;
+}
+
 // top types of the six neighbours, mosquito excluded (move_gen.cuh:917-925)
 __device__ __forceinline__ uint32_t neighbour_types(WarpSmem* w, int cell) {
     Pos P{w};
@@ -218,7 +261,8 @@ __device__ __noinline__ int gen_mosquito(WarpSmem* w, int cell, bool first_only,
         const uint32_t need = part == 0 ? 0x102u : (part == 5 ? 0x80u : (1u << (part + 1)));
         if (!(t & need)) continue;
         const int mode = (int)((0x514230u >> (4 * part)) & 15u);
-        int k = walk(w, cell, mode, w->dst, mode == WM_ANT ? 128 : 32, first_only);
+        int k = (mode == WM_ANT && !first_only) ? ant_walk(w, cell, w->dst, 128)
+                                                : walk(w, cell, mode, w->dst, mode == WM_ANT ? 128 : 32, first_only);
         if (first_only) {
             if (k) return 1;
             continue;
@@ -254,6 +298,7 @@ __device__ __forceinline__ int piece_moves(WarpSmem* w, uint32_t occ_row, int ce
     if (pt < 1 || pt > 8) return 0;
     int mode = mode_of(pt);
     int c = mode == WM_ANT ? cap : (mode >= WM_SPIDER ? 32 : 6);
+    if (mode == WM_ANT && !first_only) return ant_walk(w, cell, w->dst, c);
     return walk(w, cell, mode, w->dst, c, first_only);
 }
 
