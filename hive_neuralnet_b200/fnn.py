@@ -60,6 +60,25 @@ class HiveFNN(nn.Module):
         self.action_fc1 = nn.Linear(c.embed_dim * 2, c.action_hidden)
         self.action_fc2 = nn.Linear(c.action_hidden, 1)
 
+    @staticmethod
+    def _pad_loaded_weight(old: torch.Tensor, new_template: torch.Tensor, *, noise_scale: float = 1e-3):
+        """A checkpoint's fc1 weight of another feature width: the overlap is
+        copied, the rest drawn from N(0, noise_scale) (fnn_network.py:74-85)."""
+        new = torch.empty_like(new_template)
+        new.normal_(mean=0.0, std=noise_scale)
+        rows, cols = min(old.shape[0], new.shape[0]), min(old.shape[1], new.shape[1])
+        new[:rows, :cols] = old[:rows, :cols]
+        return new
+
+    def load_state_dict(self, state_dict, strict: bool = True, assign: bool = False):
+        """fnn_network.py:87-94: checkpoints written with another feature width load."""
+        state = dict(state_dict)
+        cur = self.state_dict()
+        key = "fc1.weight"
+        if key in state and key in cur and state[key].shape != cur[key].shape:
+            state[key] = self._pad_loaded_weight(state[key], cur[key])
+        return super().load_state_dict(state, strict=strict, assign=assign)
+
     def encode(self, features: torch.Tensor) -> torch.Tensor:
         return self.fc2(self.ln1(torch.sigmoid(self.fc1(features))))
 

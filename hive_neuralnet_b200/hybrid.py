@@ -174,10 +174,53 @@ class HiveHybridGNN(nn.Module):
         self.value_head = nn.Sequential(nn.Linear(e + h + self.config.global_feat_dim, self.config.value_hidden),
                                         nn.ReLU(), nn.Linear(self.config.value_hidden, 1))
 
+    @staticmethod
+    def _resize_loaded_tensor(old: torch.Tensor, new_template: torch.Tensor, *, noise_scale: float = 1e-3):
+        """Overlap of a checkpoint tensor of another shape copied into the live
+        one; a resized floating tensor starts from N(0, noise_scale)
+        (fnn_transformer_net.py:244-270)."""
+        new = new_template.detach().clone()
+        if old.dtype.is_floating_point and new.dtype.is_floating_point and old.shape != new.shape:
+            new.normal_(mean=0.0, std=noise_scale)
+        overlap = tuple(slice(0, min(a, b)) for a, b in zip(old.shape, new.shape))
+        if overlap:
+            new[overlap] = old[overlap].to(dtype=new.dtype, device=new.device)
+        else:
+            new.copy_(old.to(dtype=new.dtype, device=new.device))
+        return new
+
+    def load_state_dict(self, state_dict, strict: bool = True, assign: bool = False):
+        """fnn_transformer_net.py:272-286: unknown keys dropped, missing keys
+        keep the live initialisation, resized tensors keep their overlap."""
+        state = dict(state_dict)
+        cur = self.state_dict()
+        for key in list(state.keys()):
+            if key not in cur:
+                state.pop(key)
+        for key, t in cur.items():
+            if key not in state:
+                state[key] = t
+            elif state[key].shape != t.shape:
+                state[key] = self._resize_loaded_tensor(state[key], t)
+        return super().load_state_dict(state, strict=strict, assign=assign)
+
+    def load_fnn_policy_weights(self, fnn: HiveFNN) -> None:
+        """fnn_transformer_net.py:359-365: the shared FNN encoder from a trained HiveFNN."""
+        self.fnn.load_state_dict(fnn.state_dict())
+
     def score_hybrid_actions(self, root_emb, root_graph_emb, successor_emb, move_features):
         combined = torch.cat([root_emb, self.policy_graph_proj(root_graph_emb), successor_emb,
                               self.policy_move_proj(move_features)], dim=1)
         return self.policy_fc2(torch.sigmoid(self.policy_fc1(combined))).squeeze(-1)
+
+    def policy_forward(self, root_features, successor_features, action_to_root, piece_batch, move_features):
+        """fnn_transformer_net.py:329-347"""
+        root_emb = self.fnn.encode(root_features)
+        if action_to_root.shape[0] == 0:
+            return root_features.new_zeros((0,))
+        g = self.graph_trunk(piece_batch)
+        return self.score_hybrid_actions(root_emb[action_to_root], g[action_to_root],
+                                         self.fnn.encode(successor_features), move_features)
 
     def value_forward(self, root_features, piece_batch):
         root_emb = self.fnn.encode(root_features)

@@ -185,6 +185,14 @@ class _SearchBase:
             "child_init_q": torch.zeros(B, M, dtype=torch.float32, device=dev),
         }
 
+    def _reset_tree(self, tree: dict[str, torch.Tensor]) -> None:
+        """fnn_mcts_orchestrator.py:216-230"""
+        for key, fill in (("visit_count", 0), ("total_value", 0.0), ("prior", 0.0), ("virtual_q_penalty", 0.0),
+                          ("parent_idx", -1), ("move_bytes", 0), ("action_idx", -1), ("first_child", -1),
+                          ("num_children", 0), ("is_terminal", 0), ("terminal_value", 0.0), ("node_count", 1),
+                          ("root_node", 0), ("child_init_q", 0.0)):
+            tree[key].fill_(fill)
+
     @staticmethod
     def _tree_args(tree: dict[str, torch.Tensor]) -> list[torch.Tensor]:
         return [tree["visit_count"], tree["total_value"], tree["prior"], tree["parent_idx"],
@@ -252,6 +260,37 @@ class _SearchBase:
         visits = torch.where(valid, v_raw, torch.zeros_like(v_raw))
         q = torch.where(valid & (v_raw > min_visits), -t_raw / v_raw.clamp(min=1).float(), torch.zeros_like(t_raw))
         return visits, q
+
+    def _gather_root_child_stats(self, tree, B: int):
+        """Visits and Q of every root child slot (fnn_mcts_orchestrator.py:1098-1120,
+        fnn_puct_orchestrator.py:388-410)."""
+        return self._root_stats(tree, B, self._slot_idx.expand(B, -1), int(getattr(self.config, "root_q_min_visits", 0)))
+
+    def _run_simulations(self, tree, root_states, game_active, alive_mask, B, num_sims, wave_size=None):
+        """Waves of root-mask select / replay / evaluate / expand + backup
+        (fnn_mcts_orchestrator.py:927-980, fnn_puct_orchestrator.py:341-386)."""
+        cfg = self.config
+        W = max(1, int(cfg.wave_size if wave_size is None else wave_size))
+        q_pen = float(cfg.virtual_q_penalty) if getattr(cfg, "deterministic_non_root", False) and W > 1 else 0.0
+        leaf_states = torch.zeros(W * B, root_states.shape[1], dtype=torch.uint8, device=self.device)
+        for wave in range((num_sims + W - 1) // W):
+            aw = min(W, num_sims - wave * W)
+            total = aw * B
+            leaf, paths, plen, vlp, vll = self.ext.mcts_select_with_root_mask_batch(
+                *self._tree_args(tree), tree["child_init_q"], game_active, tree["root_node"], alive_mask,
+                self._max_legal, cfg.c_puct, B, aw, self._max_nodes, False, 4.0, 0.0)
+            ls = leaf_states[:total]
+            self.ext.mcts_replay_batch(root_states, ls, paths, plen, leaf, B, total)
+            results = self.ext.check_results_batch(ls, total)
+            legal, nl, feats = self.ext.generate_legal_moves_and_fnn_features_batch(ls, total)
+            pri, vals, cq = self._eval_states(ls, legal, nl, total, feats)
+            self.sims_done += (leaf >= 0).sum()
+            if self.trace is not None:
+                self.trace.append(dict(kind="wave", W=aw, leaf=leaf.clone(), priors=pri.clone(),
+                                       values=vals.clone(), child_q=cq.clone()))
+            self.ext.mcts_expand_and_backprop_dense_priors_batch(
+                *self._tree_args(tree), tree["child_init_q"], cq, leaf, ls, legal, nl, pri, results, vals, vlp, vll,
+                B, total, self._max_nodes, q_pen)
 
     def _find_immediate_wins(self, states, legal_moves, num_legal, total, *, row_mask=None, slot_mask=None):
         """First winning legal slot per game or -1 (fnn_mcts_orchestrator.py:446-493)."""
@@ -550,30 +589,6 @@ class FNNPUCTOrchestrator(_SearchBase):
 
     def __init__(self, net: HiveFNN, config: FNNPUCTConfig | None = None, device: str = "cuda") -> None:
         self._setup(net, config or FNNPUCTConfig(), device)
-
-    # fnn_puct_orchestrator.py:341-386
-    def _run_simulations(self, tree, root_states, game_active, alive_mask, B, num_sims):
-        cfg = self.config
-        W = cfg.wave_size
-        leaf_states = torch.zeros(W * B, root_states.shape[1], dtype=torch.uint8, device=self.device)
-        for wave in range((num_sims + W - 1) // W):
-            aw = min(W, num_sims - wave * W)
-            total = aw * B
-            leaf, paths, plen, vlp, vll = self.ext.mcts_select_with_root_mask_batch(
-                *self._tree_args(tree), tree["child_init_q"], game_active, tree["root_node"], alive_mask,
-                self._max_legal, cfg.c_puct, B, aw, self._max_nodes, False, 4.0, 0.0)
-            ls = leaf_states[:total]
-            self.ext.mcts_replay_batch(root_states, ls, paths, plen, leaf, B, total)
-            results = self.ext.check_results_batch(ls, total)
-            legal, nl, feats = self.ext.generate_legal_moves_and_fnn_features_batch(ls, total)
-            pri, vals, cq = self._eval_states(ls, legal, nl, total, feats)
-            self.sims_done += (leaf >= 0).sum()
-            if self.trace is not None:
-                self.trace.append(dict(kind="wave", W=aw, leaf=leaf.clone(), priors=pri.clone(),
-                                       values=vals.clone(), child_q=cq.clone()))
-            self.ext.mcts_expand_and_backprop_dense_priors_batch(
-                *self._tree_args(tree), tree["child_init_q"], cq, leaf, ls, legal, nl, pri, results, vals, vlp, vll,
-                B, total, self._max_nodes, 0.0)
 
     def self_play_batch(self, start_states: torch.Tensor | None = None) -> list[list[FNNTrainingExample]]:
         """fnn_puct_orchestrator.py:140-298"""
