@@ -63,7 +63,6 @@ struct __align__(16) WarpSmem {
     uint32_t occ[24];            // occupied row words
     uint32_t own[24];            // side-to-move top-piece row words
     uint32_t sl[6][24];          // slide masks of the position
-    uint32_t slx[6][24];         // slide masks with the current mover lifted
     uint32_t seen[24];           // scratch cell set
     uint32_t prow[24];           // placement row words
     uint32_t adj[32];            // piece adjacency (piece-index space)
@@ -71,12 +70,23 @@ struct __align__(16) WarpSmem {
     uint16_t pref[24];           // piece index of the first occupied cell of row r
     uint16_t ppref[24];          // placement index of the first placement cell of row r
     uint8_t pflag[32];           // bit0: pinned
-    uint16_t dst[128];           // destination list of the running generator
-    uint16_t tmp[128];           // sub-generator list (mosquito)
-    uint16_t qcell[48];          // walk queue (spider / ladybug paths): cell
-    uint16_t qanc[48];           //                                      previous cell
-    int acc[112];                // feature accumulators
-    uint32_t bm[16 * 17 + 24];   // per (type, owner) source-cell sets + placement set
+    uint32_t pl[24];             // mosquito union set (generators) / placement-cell set (features)
+    // Generator scratch and feature accumulators are never live together
+    // (features run on a finished move list), so they share storage: 1.3 KB
+    // less per warp, one more resident block per SM.
+    union {
+        struct {
+            uint32_t slx[6][24];  // slide masks with the current mover lifted
+            uint16_t dst[128];    // destination list of the running generator
+            uint16_t tmp[128];    // sub-generator list (mosquito)
+            uint16_t qcell[48];   // walk queue (spider / ladybug paths): cell
+            uint16_t qanc[48];    //                                      previous cell
+        };
+        struct {
+            int acc[112];          // feature accumulators
+            uint32_t bm[16 * 17];  // per (type, owner) source-cell sets
+        };
+    };
 };
 
 // ---------------------------------------------------------------------------

@@ -26,10 +26,13 @@
 
 namespace hv {
 
-#ifndef HV_MIN_BLOCKS
-#define HV_MIN_BLOCKS 3  // resident blocks per SM the register budget is sized for
+#ifndef HV_WARPS_PER_BLOCK
+#define HV_WARPS_PER_BLOCK 4  // warps (positions in flight) per block of the warp-per-unit kernels
 #endif
-constexpr int kWarpsPerBlock = 8;
+#ifndef HV_MIN_BLOCKS
+#define HV_MIN_BLOCKS 7  // resident blocks per SM the register budget is sized for
+#endif
+constexpr int kWarpsPerBlock = HV_WARPS_PER_BLOCK;
 constexpr int kThreads = kWarpsPerBlock * 32;
 
 // device error word (sticky until read and cleared by hv_get_error)

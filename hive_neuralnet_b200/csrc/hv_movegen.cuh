@@ -151,7 +151,7 @@ __device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out,
         if (first_only) {
             if (__ballot_sync(kFull, fin)) return 1;
         } else {
-            uint32_t mm = __match_any_sync(kFull, fin ? dest : -1 - l);
+            uint32_t mm = __match_any_sync(kFull, fin ? dest : -1);  // one shared key for idle lanes
             bool keep = fin && ((mm & lt) == 0u);
             uint32_t b = __ballot_sync(kFull, keep);
             int pos = cnt + __popc(b & lt);
@@ -177,10 +177,15 @@ __device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out,
     return first_only ? 0 : cnt;
 }
 
-// The ant's full breadth-first search (move_gen.cuh:267-388), the hottest
-// walk (about half of the generator's time): the walk engine's ant path
-// without its mode dispatch and path bookkeeping.  Lanes take (queue item,
-// direction) pairs, five items per round; the queue is the output list.
+// The ant's breadth-first search (move_gen.cuh:267-388), the hottest walk:
+// the walk engine's ant path without its mode dispatch and path bookkeeping.
+// Lanes take (queue item, direction) pairs, five items per round; the queue
+// is the output list, as in the reference, and first occurrences are kept in
+// (item, direction) order -- the reference's sequential order.  Needs slx
+// built for this cell.  The duplicate test is one match over the lanes that
+// found a new cell: the idle lanes share one key, since a match costs the SM
+// about two cycles per distinct key (unique idle keys made it the ant's
+// dominant cost).
 __device__ __noinline__ int ant_walk(WarpSmem* w, int cell, uint16_t* out, int cap) {
     const int l = lane_id();
     const uint32_t lt = lanemask_lt();
@@ -193,7 +198,7 @@ __device__ __noinline__ int ant_walk(WarpSmem* w, int cell, uint16_t* out, int c
     int rd = -1, cnt = 0;  // rd < 0: the seed round (the ant's own cell)
 #pragma unroll 1
     while (true) {
-        const int items = rd < 0 ? 1 : min(5, cnt - rd);
+        const int items = cnt >= cap ? 0 : (rd < 0 ? 1 : min(5, cnt - rd));
         if (items <= 0) break;
         int dest = -1;
         bool fin = false;
@@ -204,7 +209,7 @@ __device__ __noinline__ int ant_walk(WarpSmem* w, int cell, uint16_t* out, int c
                 fin = !set_has(w->seen, dest);
             }
         }
-        const uint32_t mm = __match_any_sync(kFull, fin ? dest : -1 - l);
+        const uint32_t mm = __match_any_sync(kFull, fin ? dest : -1);
         const bool keep = fin && ((mm & lt) == 0u);
         const uint32_t b = __ballot_sync(kFull, keep);
         const int pos = cnt + __popc(b & lt);
@@ -215,7 +220,6 @@ __device__ __noinline__ int ant_walk(WarpSmem* w, int cell, uint16_t* out, int c
         cnt = min(cap, cnt + __popc(b));
         rd = rd < 0 ? 0 : rd + items;
         __syncwarp();
-        if (cnt >= cap) break;
     }
     return cnt;
 }
@@ -251,7 +255,7 @@ __device__ __noinline__ int gen_mosquito(WarpSmem* w, int cell, bool first_only,
     const uint32_t t = neighbour_types(w, cell);
     const int l = lane_id();
     const uint32_t lt = lanemask_lt();
-    uint32_t* uni = w->bm + 16 * 17;  // union set (free during generation)
+    uint32_t* uni = w->pl;  // union set
     if (!first_only) set_clear(uni);
     int cnt = 0;
     // part order Q/P, A, G, S, B, L: walk modes 0 3 2 4 1 5, and the
@@ -552,7 +556,8 @@ __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, f
 #pragma unroll 1
     for (int i = l; i < A_N; i += 32) w->acc[i] = 0;
 #pragma unroll 1
-    for (int i = l; i < 16 * 17 + 17; i += 32) w->bm[i] = 0u;
+    for (int i = l; i < 16 * 17; i += 32) w->bm[i] = 0u;
+    if (l < 17) w->pl[l] = 0u;
     __syncwarp();
     const int turn = P.turn(), cur = turn & 1, stun = P.stunned();
     const int q0 = P.queen_cell(0), q1 = P.queen_cell(1);
@@ -622,13 +627,13 @@ __device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, f
                 atomicOr(&w->bm[((mpt - 1) * 2 + owner) * 17 + (from >> 5)], 1u << (from & 31));
             }
         } else if (type == 0 && to < kCells) {
-            atomicOr(&w->bm[16 * 17 + (to >> 5)], 1u << (to & 31));
+            atomicOr(&w->pl[to >> 5], 1u << (to & 31));
         }
     }
     __syncwarp();
 #pragma unroll 1
     for (int i = l; i < 16 * 17 + 17; i += 32) {
-        int c = __popc(w->bm[i]);
+        int c = __popc(i < 16 * 17 ? w->bm[i] : w->pl[i - 16 * 17]);
         if (c) atomicAdd(&w->acc[i < 16 * 17 ? A_SRC + i / 17 : A_PLACE], c);
     }
     if (l == 0) {
