@@ -305,6 +305,29 @@ def run_gpu(args) -> None:
     h2d = P * STATE_BYTES
     d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
 
+    # ---- the host link the e2e leg runs against: plain pinned copies of the
+    # step's state bytes, each direction alone, CUDA events on this stream
+    dev_buf = torch.empty_like(states)
+
+    def link_gbs(copy):
+        for _ in range(2):
+            copy()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(3):
+            copy()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return 3 * h2d / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+    h2d_gbs = link_gbs(lambda: dev_buf.copy_(host_states, non_blocking=True))
+    d2h_gbs = link_gbs(lambda: host_states.copy_(dev_buf, non_blocking=True))
+    del dev_buf
+    e2e_step_s = float(t2.item()) / 1e3 / e2e_steps
+    link = {"h2d_gbs_measured": h2d_gbs, "d2h_gbs_measured": d2h_gbs,
+            "h2d_gbs_achieved": h2d / e2e_step_s / 1e9, "d2h_gbs_achieved": d2h / e2e_step_s / 1e9,
+            "frac": (h2d / e2e_step_s / 1e9) / h2d_gbs}
+
     # ---- roofline of the dominant kernel: the move generator k_root<gen>
     # (one of the step's two launches), timed alone with CUDA events on the
     # launching stream; algorithmic bytes per position = state read + move
@@ -350,7 +373,8 @@ def run_gpu(args) -> None:
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
-                            f"{args.e2e_chunk}-position chunks over 3 streams"},
+                            f"{args.e2e_chunk}-position chunks over 3 streams",
+                    "link": link},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clocks,

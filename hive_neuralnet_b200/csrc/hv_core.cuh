@@ -265,43 +265,11 @@ __device__ __forceinline__ uint32_t load_row(const uint8_t* st, int off, int lan
     return __funnelshift_r(lo, hi, b & 31) & kRowBits;
 }
 
-// Bitboards, piece list, slide masks, articulation points.
-__device__ __forceinline__ Setup setup_position(WarpSmem* w) {
-    Setup S;
+// Articulation flag of the piece lane: every lane removes its vertex and
+// floods the rest (the lane loops run for the longest flood).
+__device__ __forceinline__ bool articulation_flood(WarpSmem* w, const Setup& S) {
     Pos P{w};
-    int l = lane_id();
-    S.occ = load_row(w->st, kOffOcc, l);
-    uint32_t wt = load_row(w->st, kOffWTop, l), bt = load_row(w->st, kOffBTop, l);
-    S.color = P.turn() & 1;
-    S.own = S.color ? bt : wt;
-    S.opp = S.color ? wt : bt;
-    if (l < 24) {
-        w->occ[l] = S.occ;
-        w->own[l] = S.own;
-    }
-    int cnt = __popc(S.occ);
-    int pre = warp_excl_scan(cnt);
-    if (l < 24) w->pref[l] = (uint16_t)pre;
-    S.n = __shfl_sync(kFull, pre + cnt, 31);
-    if (S.n > 28) S.n = 28;
-    // cells of this row into the piece list (ascending order)
-    {
-        uint32_t bits = S.occ;
-        int k = pre;
-#pragma unroll 1
-        while (bits) {
-            int q = __ffs(bits) - 1;
-            bits &= bits - 1;
-            if (k < 32) w->pcell[k] = (uint16_t)((l << 5) + q);
-            k++;
-        }
-    }
-    build_slide_masks(S.occ, w->sl);
-    __syncwarp();
-    S.my_cell = l < S.n ? (int)w->pcell[l] : -1;
-    S.my_h = P.height(S.my_cell);
-    S.my_top = P.top(S.my_cell);
-
+    const int l = lane_id();
     // adjacency in piece-index space
     uint32_t adj = 0;
     if (S.my_cell >= 0) {
@@ -343,11 +311,116 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
         }
     }
     uint32_t comp = __shfl_sync(kFull, seen, 31);
-    S.my_ap = false;
+    bool ap = false;
     if (S.n > 2 && l < S.n && ((comp >> l) & 1u)) {
         uint32_t rest = comp & ~(1u << l);
-        S.my_ap = (l == 0) ? (adj0 != 0 && seen != rest) : (seen != rest);
+        ap = (l == 0) ? (adj0 != 0 && seen != rest) : (seen != rest);
     }
+    return ap;
+}
+
+// Articulation flag of the piece lane, flooding only from vertices whose
+// neighbours form two or more arcs of their ring.
+__device__ __forceinline__ bool articulation_arc(WarpSmem* w, const Setup& S) {
+    Pos P{w};
+    const int l = lane_id();
+    // adjacency in piece-index space, and the occupied neighbours of the
+    // piece's cell as a 6-bit ring in direction order
+    uint32_t adj = 0, ring = 0;
+    if (S.my_cell >= 0) {
+#pragma unroll 1
+        for (int d = 0; d < 6; d++) {
+            int nb = nbr(S.my_cell, d);
+            if (nb >= 0 && rowbit(w->occ, nb)) {
+                int j = P.pidx(nb);
+                if (j < S.n) {
+                    adj |= 1u << j;
+                    ring |= 1u << d;
+                }
+            }
+        }
+    }
+    w->adj[l] = adj;
+    __syncwarp();
+    // The component of the lowest occupied cell (the reference's Tarjan
+    // root) grows level by level, one warp OR-reduction per level.  A vertex
+    // x of it is an articulation point iff its neighbours are not all
+    // connected once x is removed (every other vertex of the component
+    // reaches x through one of them).  Neighbours forming one contiguous arc
+    // of x's six-cell ring are connected (consecutive ring cells touch), so
+    // only a vertex with two or more arcs floods, and it stops as soon as it
+    // has reached all its neighbours.
+    const uint32_t all = S.n >= 32 ? kFull : ((1u << S.n) - 1u);
+    uint32_t comp = S.n > 0 ? 1u : 0u;
+#pragma unroll 1
+    while (true) {
+        const uint32_t grow = (comp | __reduce_or_sync(kFull, ((comp >> l) & 1u) ? adj : 0u)) & all;
+        if (grow == comp) break;
+        comp = grow;
+    }
+    bool ap = false;
+    if (S.n > 2 && l < S.n && ((comp >> l) & 1u) && adj != 0u) {
+        const uint32_t starts = ring & ~(((ring << 1) | (ring >> 5)) & 63u);  // first cell of each arc
+        if (__popc(starts) >= 2) {
+            const uint32_t allowed = all & ~(1u << l);
+            uint32_t seen = 1u << (__ffs(adj) - 1), fr = seen;
+#pragma unroll 1
+            while (fr && (seen & adj) != adj) {
+                const int v = __ffs(fr) - 1;
+                fr &= fr - 1;
+                const uint32_t nw = w->adj[v] & allowed & ~seen;
+                seen |= nw;
+                fr |= nw;
+            }
+            ap = (seen & adj) != adj;
+        }
+    }
+    return ap;
+}
+
+// Bitboards, piece list, slide masks, articulation points.  SLIDES = false
+// skips the slide masks (a caller that generates no moves); ARC selects the
+// articulation test that floods only from vertices whose neighbours form
+// two or more arcs of their ring (shorter, faster where the kernel is not
+// bound by branch issue; the result is the same).
+template <bool SLIDES = true, bool ARC = false>
+__device__ __forceinline__ Setup setup_position(WarpSmem* w) {
+    Setup S;
+    Pos P{w};
+    int l = lane_id();
+    S.occ = load_row(w->st, kOffOcc, l);
+    uint32_t wt = load_row(w->st, kOffWTop, l), bt = load_row(w->st, kOffBTop, l);
+    S.color = P.turn() & 1;
+    S.own = S.color ? bt : wt;
+    S.opp = S.color ? wt : bt;
+    if (l < 24) {
+        w->occ[l] = S.occ;
+        w->own[l] = S.own;
+    }
+    int cnt = __popc(S.occ);
+    int pre = warp_excl_scan(cnt);
+    if (l < 24) w->pref[l] = (uint16_t)pre;
+    S.n = __shfl_sync(kFull, pre + cnt, 31);
+    if (S.n > 28) S.n = 28;
+    // cells of this row into the piece list (ascending order)
+    {
+        uint32_t bits = S.occ;
+        int k = pre;
+#pragma unroll 1
+        while (bits) {
+            int q = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (k < 32) w->pcell[k] = (uint16_t)((l << 5) + q);
+            k++;
+        }
+    }
+    if (SLIDES) build_slide_masks(S.occ, w->sl);
+    __syncwarp();
+    S.my_cell = l < S.n ? (int)w->pcell[l] : -1;
+    S.my_h = P.height(S.my_cell);
+    S.my_top = P.top(S.my_cell);
+
+    S.my_ap = ARC ? articulation_arc(w, S) : articulation_flood(w, S);
     w->pflag[l] = (S.my_ap && S.my_h == 1) ? 1 : 0;
     __syncwarp();
     return S;

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
             n = nl_in[p];
             n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
             __syncwarp();
-            Setup S = setup_position(w);
+            Setup S = setup_position<false, true>(w);  // no moves generated here
             features(w, S, n, feats_out + p * kFeat);
         }
         __syncwarp();
