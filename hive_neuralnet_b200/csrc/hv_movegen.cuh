@@ -493,7 +493,13 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
         uint32_t bit = 1u << ((pt - 1) * 2 + color);
         if (seen & bit) continue;
         const uint16_t* list;
-        if (piece_moves(w, S.occ, cell, pt, 128, true, err, &list)) {
+        // queen, ant, pillbug: a move exists iff one slide out of the cell is
+        // legal (the first step of each; lifting the piece does not change
+        // slides out of its own cell), read from the position's slide masks
+        const bool slider = pt == 1 || pt == 2 || pt == 8;
+        const bool has = slider ? __ballot_sync(kFull, l < 6 && rowbit(w->sl[l < 6 ? l : 0], cell)) != 0u
+                                : piece_moves(w, S.occ, cell, pt, 128, true, err, &list) != 0;
+        if (has) {
             seen |= bit;
             if (l == 0) put_move(w, count, 1, pt, p_to_c(cell), 0);
             count++;
