@@ -251,8 +251,13 @@ struct HybDims {
 };
 
 struct HybOffsets {
-    int pgT, pgb, pf1T, cT, pf1b, pf2, pf2b, vh1T, vh1b, vh2, vh2b, total;
+    int pgT, pgb, pf1T, cT, pf1b, pf2, pf2b, vh1T, vh1b, vh2, vh2b, tcimg, total;
 };
+
+// fp16 operand image of the per-successor network for the tensor-core row
+// kernel (hv_mlp_tc.cuh), at the end of the head weights: W1 [64 x 128],
+// W2 [64 x 64], [A1s | C] [64 x 96] in the K-major slab layout, zero padded
+constexpr int kTcImgHalves = 64 * 128 + 64 * 64 + 64 * 96;  // 18432
 
 __host__ __device__ inline HybOffsets hyb_offsets(HybDims d) {
     HybOffsets o;
@@ -268,6 +273,8 @@ __host__ __device__ inline HybOffsets hyb_offsets(HybDims d) {
     o.vh1b = p; p += d.V;
     o.vh2 = p; p += d.V;
     o.vh2b = p; p += 1;
+    p = (p + 3) & ~3;  // 16-byte aligned image
+    o.tcimg = p; p += kTcImgHalves / 2;
     o.total = p;
     return o;
 }

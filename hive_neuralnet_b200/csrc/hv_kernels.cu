@@ -22,6 +22,7 @@
 #include "hv_hybrid.cuh"
 #include "hv_trunk.cuh"
 #include "hv_mlp.cuh"
+#include "hv_mlp_tc.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -1380,7 +1381,17 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         k_leaf_root<HYB><<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, root_features, graph, glob,
                                                       count, fw, fd, hw, hd, values, w.root_pre);
     }
-    if (rows > 0) {
+    if (rows > 0 && HYB) {
+        // the hybrid network on the tensor cores (fp16 operands, as the reference's autocast)
+        uint32_t* err = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
+        const size_t smem = sizeof(MlpTcSmem);
+        const int64_t tiles = (rows + kTcRows - 1) / kTcRows;
+        rc = grid_for(k_mlp_rows_tc, tiles * kWarpsPerBlock, smem, &grid);
+        if (rc) return rc;
+        k_mlp_rows_tc<<<grid, kTcThreads, smem, s>>>(w.x, w.mf, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd, lg,
+                                                     w.row_start + count, err);
+    } else if (rows > 0) {
         const size_t smem = sizeof(MlpSmem<HYB>);
         const int64_t tiles = (rows + kMlpRows - 1) / kMlpRows;
         rc = grid_for(k_mlp_rows<HYB>, tiles * kWarpsPerBlock, smem, &grid);

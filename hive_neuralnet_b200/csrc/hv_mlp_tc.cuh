@@ -1,0 +1,301 @@
+// hv_mlp_tc.cuh -- the hybrid evaluator's per-successor network on the
+// sm_100a tensor cores (fnn_network.py:98-117 HiveFNN.encode;
+// fnn_transformer_net.py:316-327 score_hybrid_actions), over the successor
+// rows of a wave:
+//   h = LayerNorm(sigmoid(X W1 + b1)),  e = h W2 + b2,
+//   logit = pf2 . sigmoid(root_pre[leaf] + [e | m] [A1s | C]^T) + pf2b
+// with X the row's 122 successor features, m its 31 move features and
+// root_pre the per-leaf half of the action layer (bias, root and graph
+// terms, from the leaf-root kernel).
+//
+// One CTA of 4 warps owns 128 rows at a time: one thread and one TMEM lane
+// per row.  The three linear layers are fp16 tcgen05.mma GEMMs (M = 128,
+// N = 64, K = 128 / 64 / 64 + 32) with fp32 accumulators in TMEM, issued by
+// one thread; sigmoid, LayerNorm and the output head run in fp32 on the
+// row's thread straight from TMEM.  fp16 operands with fp32 accumulation
+// are the reference's own arithmetic for this network (it evaluates under
+// CUDA autocast).  The weights are converted once per CTA from the fp32
+// buffers the fp32 kernel reads into the K-major slab layout of hv_tc.cuh.
+// Every wait is bounded; a CTA that gives up sets 8 (bit 3) in the error word,
+// lets its own MMAs finish, frees its TMEM and returns.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "hv_fnn.cuh"
+#include "hv_hybrid.cuh"
+#include "hv_tc.cuh"
+
+namespace hv {
+
+constexpr int kTcRows = 128, kTcThreads = 128;
+constexpr uint32_t kErrMlpWait = 8u;
+
+struct __align__(128) MlpTcSmem {
+    __half w1[16][64][8];   // W1 [64 x 128] (features padded 122 -> 128), slab layout
+    __half w2[8][64][8];    // W2 [64 x 64]
+    __half w3[12][64][8];   // [A1s | C] [64 x 96]: successor block, then the folded move projection
+    __half a[16][kTcRows][8];  // A operand: X, then h, then e
+    __half m[4][kTcRows][8];   // move features (31, padded to 32)
+    float xs[kTcRows * kFeat];      // staging: the tile's feature rows as stored in global memory
+    float ms[kTcRows * kMoveFeat];  // staging: its move-feature rows
+    float b1[64], g1[64], be1[64], b2[64], a2[64];
+    float a2b;
+    uint64_t bar_w, bar_x, bar;
+    uint32_t tmem;
+};
+static_assert(sizeof(__half) * kTcImgHalves == sizeof(MlpTcSmem::w1) + sizeof(MlpTcSmem::w2) + sizeof(MlpTcSmem::w3),
+              "weight image size");
+
+// 8 values -> one 16-byte slab row (row r of chunk c)
+__device__ __forceinline__ void tc_put8(__half (*slab)[kTcRows][8], int c, int r, const float* x) {
+    __half2 p0 = __floats2half2_rn(x[0], x[1]);
+    __half2 p1 = __floats2half2_rn(x[2], x[3]);
+    __half2 p2 = __floats2half2_rn(x[4], x[5]);
+    __half2 p3 = __floats2half2_rn(x[6], x[7]);
+    uint4 u;
+    u.x = *reinterpret_cast<uint32_t*>(&p0);
+    u.y = *reinterpret_cast<uint32_t*>(&p1);
+    u.z = *reinterpret_cast<uint32_t*>(&p2);
+    u.w = *reinterpret_cast<uint32_t*>(&p3);
+    *reinterpret_cast<uint4*>(&slab[c][r][0]) = u;
+}
+
+// issue K/16 MMA steps D (+)= A[128 x k] B[64 x k]^T, both in slab layout
+// (A: 128 rows per 8-wide K chunk, B: 64 rows)
+__device__ __forceinline__ void tc_gemm(uint32_t d, const void* a, const void* b, int k, bool acc) {
+    const uint32_t id = idesc_f16_m128(64);
+    const char* pa = static_cast<const char*>(a);
+    const char* pb = static_cast<const char*>(b);
+    for (int s = 0; s < k / 16; s++)
+        mma_f16(d, sdesc(pa + s * 2 * kTcRows * 16, kTcRows * 16, 128), sdesc(pb + s * 2 * 64 * 16, 64 * 16, 128), id,
+                (acc || s > 0) ? 1u : 0u);
+}
+
+// all threads: make the slab writes visible to the tensor core, thread 0
+// issues `issue`, commits; everyone waits (bounded).  Uniform result.
+template <typename F>
+__device__ __forceinline__ bool tc_round(MlpTcSmem* s, uint32_t& phase, F issue) {
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        tc_fence_after();
+        issue();
+        mma_commit(&s->bar);
+    }
+    const bool ok = mbar_wait(&s->bar, phase);
+    phase ^= 1u;
+    tc_fence_after();
+    return __syncthreads_and(ok) != 0;
+}
+
+// bytes of a tile's rows that one bulk copy moves (a multiple of 16; the
+// remaining 0-12 bytes are read directly)
+__device__ __forceinline__ uint32_t tc_bulk_bytes(int nrows, int row_floats) {
+    return ((uint32_t)nrows * (uint32_t)row_floats * 4u) & ~15u;
+}
+
+// thread 0: start the bulk copies of a tile's feature and move-feature rows
+__device__ __forceinline__ void tc_fetch(MlpTcSmem* s, const float* X, const float* MF, int64_t r0, int nrows) {
+    const uint32_t bx = tc_bulk_bytes(nrows, kFeat), bm = tc_bulk_bytes(nrows, kMoveFeat);
+    mbar_expect_tx(&s->bar_x, bx + bm);
+    if (bx) bulk_g2s(s->xs, X + r0 * kFeat, bx, &s->bar_x);
+    if (bm) bulk_g2s(s->ms, MF + r0 * kMoveFeat, bm, &s->bar_x);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __restrict__ X,
+                                                               const float* __restrict__ MF,
+                                                               const int64_t* __restrict__ atr,
+                                                               const int64_t* __restrict__ mi, int64_t N,
+                                                               const float* __restrict__ root_pre,
+                                                               const float* __restrict__ fw, FnnDims fd,
+                                                               const float* __restrict__ hw, HybDims hd,
+                                                               float* __restrict__ logits,
+                                                               const int64_t* __restrict__ n_actual,
+                                                               uint32_t* __restrict__ err_word) {
+    extern __shared__ __align__(128) uint8_t tc_raw[];
+    MlpTcSmem* s = reinterpret_cast<MlpTcSmem*>(tc_raw);
+    const int t = threadIdx.x, w = t >> 5;
+    const int H = fd.H, E = fd.E, A = hd.A;
+    const FnnOffsets fo = fnn_offsets(fd);
+    const HybOffsets ho = hyb_offsets(hd);
+    if (n_actual) N = min(N, *n_actual);  // rows actually filled
+    const int64_t tiles = (N + kTcRows - 1) / kTcRows;
+
+    for (int o = t; o < 64; o += kTcThreads) {
+        s->b1[o] = o < H ? __ldg(fw + fo.b1 + o) : 0.0f;
+        s->g1[o] = o < H ? __ldg(fw + fo.g1 + o) : 0.0f;
+        s->be1[o] = o < H ? __ldg(fw + fo.be1 + o) : 0.0f;
+        s->b2[o] = o < E ? __ldg(fw + fo.b2 + o) : 0.0f;
+        s->a2[o] = o < A ? __ldg(hw + ho.pf2 + o) : 0.0f;
+    }
+    // the operand slabs start at zero (their padding columns are never written again)
+    {
+        uint4* z = reinterpret_cast<uint4*>(&s->a[0][0][0]);
+        for (int i = t; i < (16 + 4) * kTcRows; i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
+    }
+    bool wpend = false, xpend = false;
+    if (t == 0) {
+        s->a2b = __ldg(hw + ho.pf2b);
+        mbar_init(&s->bar_w, 1);
+        mbar_init(&s->bar_x, 1);
+        mbar_init(&s->bar, 1);
+        fence_mbar_init();
+        if (blockIdx.x < tiles) {
+            // the weight image (host-packed fp16 slabs) and the first tile's rows
+            mbar_expect_tx(&s->bar_w, (uint32_t)(kTcImgHalves * 2));
+            bulk_g2s(&s->w1[0][0][0], hw + ho.tcimg, (uint32_t)(kTcImgHalves * 2), &s->bar_w);
+            tc_fetch(s, X, MF, (int64_t)blockIdx.x * kTcRows, (int)min((int64_t)kTcRows, N - (int64_t)blockIdx.x * kTcRows));
+            wpend = xpend = true;
+        }
+    }
+    if (w == 0) {
+        tmem_alloc(&s->tmem, 128);
+        tmem_relinquish();
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const uint32_t lane = s->tmem + ((uint32_t)(w * 32) << 16);  // this thread's TMEM lane (row t)
+    uint32_t phase = 0, xphase = 0;
+    bool failed = false, pending = false;
+    if (t == 0 && wpend) {
+        failed = !mbar_wait(&s->bar_w, 0);
+        if (!failed) wpend = false;
+    }
+    if (!__syncthreads_and(!failed)) failed = true;
+    for (int64_t tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x) {
+        const int64_t r0 = tile * kTcRows;
+        const int nrows = (int)min((int64_t)kTcRows, N - r0);
+        // ---- this tile's rows: staged by the bulk copy, the last bytes read directly
+        {
+            const bool ok = mbar_wait(&s->bar_x, xphase);
+            if (!__syncthreads_and(ok)) {
+                failed = true;
+                break;
+            }
+            xphase ^= 1u;
+            xpend = false;
+            const int nx = nrows * kFeat, nm = nrows * kMoveFeat;
+            const int cx = (int)(tc_bulk_bytes(nrows, kFeat) / 4), cm = (int)(tc_bulk_bytes(nrows, kMoveFeat) / 4);
+            for (int i = cx + t; i < nx; i += kTcThreads) s->xs[i] = __ldg(X + r0 * kFeat + i);
+            for (int i = cm + t; i < nm; i += kTcThreads) s->ms[i] = __ldg(MF + r0 * kMoveFeat + i);
+            __syncthreads();
+            for (int i = t; i < nrows * (kFeat / 2); i += kTcThreads) {
+                const int r = i / (kFeat / 2), k = 2 * (i - r * (kFeat / 2));
+                const float2 v = *reinterpret_cast<const float2*>(&s->xs[r * kFeat + k]);
+                *reinterpret_cast<__half2*>(&s->a[k >> 3][r][k & 7]) = __floats2half2_rn(v.x, v.y);
+            }
+            for (int i = t; i < nm; i += kTcThreads) {
+                const int r = i / kMoveFeat, k = i - r * kMoveFeat;
+                s->m[k >> 3][r][k & 7] = __float2half_rn(s->ms[i]);
+            }
+            // the staging is consumed: start the next tile's copy under this tile's GEMMs
+            fence_proxy_async();
+            __syncthreads();
+            const int64_t next = tile + gridDim.x;
+            if (t == 0 && next < tiles) {
+                tc_fetch(s, X, MF, next * kTcRows, (int)min((int64_t)kTcRows, N - next * kTcRows));
+                xpend = true;
+            }
+        }
+        // ---- D[0:64] = X W1^T
+        pending = true;
+        if (!tc_round(s, phase, [&] { tc_gemm(s->tmem, &s->a[0][0][0], &s->w1[0][0][0], 128, false); })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane, d);
+            tmem_ld32(lane + 32, d + 32);
+            float mean = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 64; j++) {
+                d[j] = j < H ? sigmoidf_(d[j] + s->b1[j]) : 0.0f;
+                mean += d[j];
+            }
+            mean /= (float)H;
+            float var = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 64; j++) {
+                d[j] = j < H ? d[j] - mean : 0.0f;
+                var += d[j] * d[j];
+            }
+            const float rstd = 1.0f / sqrtf(var / (float)H + 1e-5f);
+#pragma unroll
+            for (int j = 0; j < 64; j++) d[j] = d[j] * rstd * s->g1[j] + s->be1[j];
+#pragma unroll
+            for (int c = 0; c < 8; c++) tc_put8(s->a, c, t, d + 8 * c);
+        }
+        // ---- D[64:128] = h W2^T
+        pending = true;
+        if (!tc_round(s, phase, [&] { tc_gemm(s->tmem + 64, &s->a[0][0][0], &s->w2[0][0][0], 64, false); })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane + 64, d);
+            tmem_ld32(lane + 96, d + 32);
+#pragma unroll
+            for (int j = 0; j < 64; j++) d[j] += s->b2[j];
+#pragma unroll
+            for (int c = 0; c < 8; c++) tc_put8(s->a, c, t, d + 8 * c);
+        }
+        // ---- D[0:64] = e A1s^T + m C^T
+        pending = true;
+        if (!tc_round(s, phase, [&] {
+                tc_gemm(s->tmem, &s->a[0][0][0], &s->w3[0][0][0], 64, false);
+                tc_gemm(s->tmem, &s->m[0][0][0], &s->w3[8][0][0], 32, true);
+            })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane, d);
+            tmem_ld32(lane + 32, d + 32);
+            if (t < nrows) {
+                const int64_t leaf = atr[r0 + t];
+                const float4* rp = reinterpret_cast<const float4*>(root_pre + leaf * 64);
+                float p = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    const float4 v = __ldg(rp + q);
+                    const float pre[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int j = 4 * q + u;
+                        if (j < A) p += s->a2[j] * sigmoidf_(pre[u] + d[j]);
+                    }
+                }
+                logits[leaf * kMaxMoves + mi[r0 + t]] = p + s->a2b;
+            }
+        }
+    }
+    if (failed) {
+        // a bounded wait gave up: record it, let this CTA's copies and MMAs
+        // in flight finish (bounded again), free TMEM and return
+        if (t == 0) {
+            atomicOr(err_word, kErrMlpWait);
+            if (wpend) mbar_wait(&s->bar_w, 0);
+            if (xpend) mbar_wait(&s->bar_x, xphase);
+        }
+        if (pending) mbar_wait(&s->bar, phase ^ 1u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (w == 0) {
+        tc_fence_after();
+        tmem_dealloc(s->tmem, 128);
+    }
+}
+
+}  // namespace hv

@@ -335,7 +335,26 @@ def pack_heads(net: HiveHybridGNN, device) -> torch.Tensor:
                  net.policy_fc2.weight.reshape(-1), net.policy_fc2.bias, net.value_head[0].weight.t(),
                  net.value_head[0].bias, net.value_head[2].weight.reshape(-1), net.value_head[2].bias]
         flat = torch.cat([p.detach().double().contiguous().reshape(-1) for p in parts]).float()
+        # fp16 slab image for the tensor-core row kernel (hv_mlp_tc.cuh), 16-byte aligned
+        fnn = net.fnn
+        img = torch.cat([_slabs_b(fnn.fc1.weight.float(), 128), _slabs_b(fnn.fc2.weight.float(), 64),
+                         _slabs_b(torch.cat([w1[:, 2 * e:3 * e].float(), fold.float()], dim=1), 96, split=e)])
+        pad = (-flat.numel()) % 4
+        flat = torch.cat([flat, flat.new_zeros(pad), img.view(torch.float32)])
     return flat.to(device).contiguous()
+
+
+def _slabs_b(w: torch.Tensor, k_pad: int, split: int | None = None) -> torch.Tensor:
+    """[N <= 64, K] fp32 weight -> fp16 B operand [64 x k_pad] in the K-major
+    slab layout (element (n, k) at ((k / 8) * 64 + n) * 8 + k % 8), zero padded.
+    With ``split``, columns [split:] start at K = 64 (the [A1s | C] layout)."""
+    out = torch.zeros(64, k_pad, dtype=torch.float32)
+    if split is None:
+        out[:w.shape[0], :w.shape[1]] = w
+    else:
+        out[:w.shape[0], :split] = w[:, :split]
+        out[:w.shape[0], 64:64 + w.shape[1] - split] = w[:, split:]
+    return out.half().reshape(64, k_pad // 8, 8).permute(1, 0, 2).contiguous().reshape(-1)
 
 
 class HybridEvaluator:
