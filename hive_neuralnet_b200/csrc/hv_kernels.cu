@@ -80,6 +80,18 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
     for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
          p += nwarps) {
         stage_state(w, states + p * kStateBytes);
+        {
+            // the warp's next position into L2 while this one is computed
+            // (the feature launch waits on these loads otherwise)
+            const int64_t q = p + nwarps;
+            const int l = lane_id();
+            if (q < batch) {
+                if (l < kStateBytes / 128 + 1)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(states + q * kStateBytes + 128 * l));
+                if (!GEN && l < kMaxMoves * kMoveBytes / 128)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(moves_in + q * (kMaxMoves * kMoveBytes) + 128 * l));
+            }
+        }
         int n;
         if (GEN) {
             zero_moves(w);
