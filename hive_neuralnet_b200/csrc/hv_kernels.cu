@@ -1398,8 +1398,8 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         uint32_t* err = nullptr;
         if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
         const size_t smem = sizeof(MlpTcSmem);
-        const int64_t tiles = (rows + kTcRows - 1) / kTcRows;
-        rc = grid_for(k_mlp_rows_tc, tiles * kWarpsPerBlock, smem, &grid);
+        const int64_t tiles = (rows + kTcRows - 1) / kTcRows, ctas = (tiles + kTcGroups - 1) / kTcGroups;
+        rc = grid_for(k_mlp_rows_tc, ctas * kWarpsPerBlock, smem, &grid);  // one CTA per SM (shared memory)
         if (rc) return rc;
         k_mlp_rows_tc<<<grid, kTcThreads, smem, s>>>(w.x, w.mf, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd, lg,
                                                      w.row_start + count, err);

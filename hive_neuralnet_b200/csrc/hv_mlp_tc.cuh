@@ -8,14 +8,17 @@
 // root_pre the per-leaf half of the action layer (bias, root and graph
 // terms, from the leaf-root kernel).
 //
-// One CTA of 4 warps owns 128 rows at a time: one thread and one TMEM lane
-// per row.  The three linear layers are fp16 tcgen05.mma GEMMs (M = 128,
+// A CTA holds four independent groups of 4 warps; a group owns 128 rows at a
+// time (one thread and one TMEM lane per row) with its own operands, MMA
+// barrier, named barrier and 128 TMEM columns, so an SM overlaps four tiles'
+// copies, GEMMs and epilogues.  The three linear layers are fp16 tcgen05.mma GEMMs (M = 128,
 // N = 64, K = 128 / 64 / 64 + 32) with fp32 accumulators in TMEM, issued by
 // one thread; sigmoid, LayerNorm and the output head run in fp32 on the
 // row's thread straight from TMEM.  fp16 operands with fp32 accumulation
 // are the reference's own arithmetic for this network (it evaluates under
-// CUDA autocast).  The weights are converted once per CTA from the fp32
-// buffers the fp32 kernel reads into the K-major slab layout of hv_tc.cuh.
+// CUDA autocast).  The weights arrive once per CTA as the host-packed fp16
+// image (K-major slab layout of hv_tc.cuh) by one bulk copy; a group's rows
+// are read straight from global memory into its slabs.
 // Every wait is bounded; a CTA that gives up sets 8 (bit 3) in the error word,
 // lets its own MMAs finish, frees its TMEM and returns.
 #pragma once
@@ -28,21 +31,24 @@
 
 namespace hv {
 
-constexpr int kTcRows = 128, kTcThreads = 128;
+constexpr int kTcRows = 128, kTcGroups = 4, kTcGroupThreads = 128, kTcThreads = kTcGroups * kTcGroupThreads;
 constexpr uint32_t kErrMlpWait = 8u;
+
+struct __align__(128) MlpTcGroup {
+    __half a[16][kTcRows][8];  // A operand: X, then h, then e
+    __half m[4][kTcRows][8];   // move features (31, padded to 32)
+};
 
 struct __align__(128) MlpTcSmem {
     __half w1[16][64][8];   // W1 [64 x 128] (features padded 122 -> 128), slab layout
     __half w2[8][64][8];    // W2 [64 x 64]
     __half w3[12][64][8];   // [A1s | C] [64 x 96]: successor block, then the folded move projection
-    __half a[16][kTcRows][8];  // A operand: X, then h, then e
-    __half m[4][kTcRows][8];   // move features (31, padded to 32)
-    float xs[kTcRows * kFeat];      // staging: the tile's feature rows as stored in global memory
-    float ms[kTcRows * kMoveFeat];  // staging: its move-feature rows
+    MlpTcGroup g[kTcGroups];
     float b1[64], g1[64], be1[64], b2[64], a2[64];
     float a2b;
-    uint64_t bar_w, bar_x, bar;
+    uint64_t bar_w, bar[kTcGroups];
     uint32_t tmem;
+    int fail[kTcGroups];
 };
 static_assert(sizeof(__half) * kTcImgHalves == sizeof(MlpTcSmem::w1) + sizeof(MlpTcSmem::w2) + sizeof(MlpTcSmem::w3),
               "weight image size");
@@ -72,36 +78,30 @@ __device__ __forceinline__ void tc_gemm(uint32_t d, const void* a, const void* b
                 (acc || s > 0) ? 1u : 0u);
 }
 
-// all threads: make the slab writes visible to the tensor core, thread 0
-// issues `issue`, commits; everyone waits (bounded).  Uniform result.
+// barrier of one group's 128 threads (named barrier 1 + g)
+__device__ __forceinline__ void group_sync(int g) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kTcGroupThreads) : "memory");
+}
+
+// one group: make the slab writes visible to the tensor core, the group's
+// thread 0 issues `issue` and commits; the group waits (bounded).  Uniform
+// over the group: false if any of its threads' waits gave up.
 template <typename F>
-__device__ __forceinline__ bool tc_round(MlpTcSmem* s, uint32_t& phase, F issue) {
+__device__ __forceinline__ bool tc_round(MlpTcSmem* s, int g, int gt, uint32_t& phase, F issue) {
     fence_proxy_async();
     tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x == 0) {
+    group_sync(g);
+    if (gt == 0) {
         tc_fence_after();
         issue();
-        mma_commit(&s->bar);
+        mma_commit(&s->bar[g]);
     }
-    const bool ok = mbar_wait(&s->bar, phase);
+    const bool ok = mbar_wait(&s->bar[g], phase);
     phase ^= 1u;
     tc_fence_after();
-    return __syncthreads_and(ok) != 0;
-}
-
-// bytes of a tile's rows that one bulk copy moves (a multiple of 16; the
-// remaining 0-12 bytes are read directly)
-__device__ __forceinline__ uint32_t tc_bulk_bytes(int nrows, int row_floats) {
-    return ((uint32_t)nrows * (uint32_t)row_floats * 4u) & ~15u;
-}
-
-// thread 0: start the bulk copies of a tile's feature and move-feature rows
-__device__ __forceinline__ void tc_fetch(MlpTcSmem* s, const float* X, const float* MF, int64_t r0, int nrows) {
-    const uint32_t bx = tc_bulk_bytes(nrows, kFeat), bm = tc_bulk_bytes(nrows, kMoveFeat);
-    mbar_expect_tx(&s->bar_x, bx + bm);
-    if (bx) bulk_g2s(s->xs, X + r0 * kFeat, bx, &s->bar_x);
-    if (bm) bulk_g2s(s->ms, MF + r0 * kMoveFeat, bm, &s->bar_x);
+    if (!ok) s->fail[g] = 1;
+    group_sync(g);
+    return s->fail[g] == 0;
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __restrict__ X,
@@ -117,6 +117,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
     extern __shared__ __align__(128) uint8_t tc_raw[];
     MlpTcSmem* s = reinterpret_cast<MlpTcSmem*>(tc_raw);
     const int t = threadIdx.x, w = t >> 5;
+    const int g = t / kTcGroupThreads, gt = t - g * kTcGroupThreads;  // group, row within the tile
+    MlpTcGroup* G = &s->g[g];
     const int H = fd.H, E = fd.E, A = hd.A;
     const FnnOffsets fo = fnn_offsets(fd);
     const HybOffsets ho = hyb_offsets(hd);
@@ -132,79 +134,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
     }
     // the operand slabs start at zero (their padding columns are never written again)
     {
-        uint4* z = reinterpret_cast<uint4*>(&s->a[0][0][0]);
-        for (int i = t; i < (16 + 4) * kTcRows; i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
+        uint4* z = reinterpret_cast<uint4*>(&s->g[0]);
+        for (int i = t; i < (int)(sizeof(s->g) / 16); i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
     }
-    bool wpend = false, xpend = false;
+    if (t < kTcGroups) s->fail[t] = 0;
+    const bool live = (int64_t)blockIdx.x * kTcGroups < tiles;
     if (t == 0) {
         s->a2b = __ldg(hw + ho.pf2b);
         mbar_init(&s->bar_w, 1);
-        mbar_init(&s->bar_x, 1);
-        mbar_init(&s->bar, 1);
+        for (int i = 0; i < kTcGroups; i++) mbar_init(&s->bar[i], 1);
         fence_mbar_init();
-        if (blockIdx.x < tiles) {
-            // the weight image (host-packed fp16 slabs) and the first tile's rows
+        if (live) {
+            // the weight image (host-packed fp16 slabs)
             mbar_expect_tx(&s->bar_w, (uint32_t)(kTcImgHalves * 2));
             bulk_g2s(&s->w1[0][0][0], hw + ho.tcimg, (uint32_t)(kTcImgHalves * 2), &s->bar_w);
-            tc_fetch(s, X, MF, (int64_t)blockIdx.x * kTcRows, (int)min((int64_t)kTcRows, N - (int64_t)blockIdx.x * kTcRows));
-            wpend = xpend = true;
         }
     }
     if (w == 0) {
-        tmem_alloc(&s->tmem, 128);
+        tmem_alloc(&s->tmem, 512);
         tmem_relinquish();
     }
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-
-    const uint32_t lane = s->tmem + ((uint32_t)(w * 32) << 16);  // this thread's TMEM lane (row t)
-    uint32_t phase = 0, xphase = 0;
     bool failed = false, pending = false;
-    if (t == 0 && wpend) {
-        failed = !mbar_wait(&s->bar_w, 0);
-        if (!failed) wpend = false;
+    if (live) {
+        const bool ok = mbar_wait(&s->bar_w, 0);  // every thread, bounded
+        failed = __syncthreads_or(!ok) != 0;
     }
-    if (!__syncthreads_and(!failed)) failed = true;
-    for (int64_t tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x) {
+    const uint32_t tcol = s->tmem + 128u * (uint32_t)g;
+    const uint32_t lane = tcol + ((uint32_t)((w & 3) * 32) << 16);  // this thread's TMEM lane (row gt)
+    uint32_t phase = 0;
+    for (int64_t tile = (int64_t)blockIdx.x * kTcGroups + g; tile < tiles && !failed;
+         tile += (int64_t)gridDim.x * kTcGroups) {
         const int64_t r0 = tile * kTcRows;
         const int nrows = (int)min((int64_t)kTcRows, N - r0);
-        // ---- this tile's rows: staged by the bulk copy, the last bytes read directly
+        // ---- this tile's rows straight into the slabs (two floats at a time; 122 is even)
         {
-            const bool ok = mbar_wait(&s->bar_x, xphase);
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
-            xphase ^= 1u;
-            xpend = false;
-            const int nx = nrows * kFeat, nm = nrows * kMoveFeat;
-            const int cx = (int)(tc_bulk_bytes(nrows, kFeat) / 4), cm = (int)(tc_bulk_bytes(nrows, kMoveFeat) / 4);
-            for (int i = cx + t; i < nx; i += kTcThreads) s->xs[i] = __ldg(X + r0 * kFeat + i);
-            for (int i = cm + t; i < nm; i += kTcThreads) s->ms[i] = __ldg(MF + r0 * kMoveFeat + i);
-            __syncthreads();
-            for (int i = t; i < nrows * (kFeat / 2); i += kTcThreads) {
+            const float2* xg = reinterpret_cast<const float2*>(X + r0 * kFeat);
+            const int nx = nrows * (kFeat / 2);
+#pragma unroll 4
+            for (int i = gt; i < nx; i += kTcGroupThreads) {
                 const int r = i / (kFeat / 2), k = 2 * (i - r * (kFeat / 2));
-                const float2 v = *reinterpret_cast<const float2*>(&s->xs[r * kFeat + k]);
-                *reinterpret_cast<__half2*>(&s->a[k >> 3][r][k & 7]) = __floats2half2_rn(v.x, v.y);
+                const float2 v = __ldg(xg + i);
+                *reinterpret_cast<__half2*>(&G->a[k >> 3][r][k & 7]) = __floats2half2_rn(v.x, v.y);
             }
-            for (int i = t; i < nm; i += kTcThreads) {
+            const float* mg = MF + r0 * kMoveFeat;
+            const int nm = nrows * kMoveFeat;
+#pragma unroll 4
+            for (int i = gt; i < nm; i += kTcGroupThreads) {
                 const int r = i / kMoveFeat, k = i - r * kMoveFeat;
-                s->m[k >> 3][r][k & 7] = __float2half_rn(s->ms[i]);
-            }
-            // the staging is consumed: start the next tile's copy under this tile's GEMMs
-            fence_proxy_async();
-            __syncthreads();
-            const int64_t next = tile + gridDim.x;
-            if (t == 0 && next < tiles) {
-                tc_fetch(s, X, MF, next * kTcRows, (int)min((int64_t)kTcRows, N - next * kTcRows));
-                xpend = true;
+                G->m[k >> 3][r][k & 7] = __float2half_rn(__ldg(mg + i));
             }
         }
         // ---- D[0:64] = X W1^T
         pending = true;
-        if (!tc_round(s, phase, [&] { tc_gemm(s->tmem, &s->a[0][0][0], &s->w1[0][0][0], 128, false); })) {
+        if (!tc_round(s, g, gt, phase, [&] { tc_gemm(tcol, &G->a[0][0][0], &s->w1[0][0][0], 128, false); })) {
             failed = true;
             break;
         }
@@ -230,11 +216,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
 #pragma unroll
             for (int j = 0; j < 64; j++) d[j] = d[j] * rstd * s->g1[j] + s->be1[j];
 #pragma unroll
-            for (int c = 0; c < 8; c++) tc_put8(s->a, c, t, d + 8 * c);
+            for (int c = 0; c < 8; c++) tc_put8(G->a, c, gt, d + 8 * c);
         }
         // ---- D[64:128] = h W2^T
         pending = true;
-        if (!tc_round(s, phase, [&] { tc_gemm(s->tmem + 64, &s->a[0][0][0], &s->w2[0][0][0], 64, false); })) {
+        if (!tc_round(s, g, gt, phase, [&] { tc_gemm(tcol + 64, &G->a[0][0][0], &s->w2[0][0][0], 64, false); })) {
             failed = true;
             break;
         }
@@ -246,13 +232,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
 #pragma unroll
             for (int j = 0; j < 64; j++) d[j] += s->b2[j];
 #pragma unroll
-            for (int c = 0; c < 8; c++) tc_put8(s->a, c, t, d + 8 * c);
+            for (int c = 0; c < 8; c++) tc_put8(G->a, c, gt, d + 8 * c);
         }
         // ---- D[0:64] = e A1s^T + m C^T
         pending = true;
-        if (!tc_round(s, phase, [&] {
-                tc_gemm(s->tmem, &s->a[0][0][0], &s->w3[0][0][0], 64, false);
-                tc_gemm(s->tmem, &s->m[0][0][0], &s->w3[8][0][0], 32, true);
+        if (!tc_round(s, g, gt, phase, [&] {
+                tc_gemm(tcol, &G->a[0][0][0], &s->w3[0][0][0], 64, false);
+                tc_gemm(tcol, &G->m[0][0][0], &s->w3[8][0][0], 32, true);
             })) {
             failed = true;
             break;
@@ -262,8 +248,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
             float d[64];
             tmem_ld32(lane, d);
             tmem_ld32(lane + 32, d + 32);
-            if (t < nrows) {
-                const int64_t leaf = atr[r0 + t];
+            if (gt < nrows) {
+                const int64_t leaf = atr[r0 + gt];
                 const float4* rp = reinterpret_cast<const float4*>(root_pre + leaf * 64);
                 float p = 0.0f;
 #pragma unroll
@@ -276,25 +262,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
                         if (j < A) p += s->a2[j] * sigmoidf_(pre[u] + d[j]);
                     }
                 }
-                logits[leaf * kMaxMoves + mi[r0 + t]] = p + s->a2b;
+                logits[leaf * kMaxMoves + mi[r0 + gt]] = p + s->a2b;
             }
         }
+        // the slabs are rewritten by the next tile only after every thread of
+        // the group has read its TMEM lane (the next round's group barrier)
     }
     if (failed) {
-        // a bounded wait gave up: record it, let this CTA's copies and MMAs
-        // in flight finish (bounded again), free TMEM and return
-        if (t == 0) {
-            atomicOr(err_word, kErrMlpWait);
-            if (wpend) mbar_wait(&s->bar_w, 0);
-            if (xpend) mbar_wait(&s->bar_x, xphase);
-        }
-        if (pending) mbar_wait(&s->bar, phase ^ 1u);
+        // a bounded wait gave up: record it, let the group's MMAs finish
+        // (bounded again), free TMEM and return
+        if (gt == 0) atomicOr(err_word, kErrMlpWait);
+        if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
     }
     tc_fence_before();
     __syncthreads();
     if (w == 0) {
         tc_fence_after();
-        tmem_dealloc(s->tmem, 128);
+        tmem_dealloc(s->tmem, 512);
     }
 }
 
