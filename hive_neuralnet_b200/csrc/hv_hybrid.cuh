@@ -251,13 +251,19 @@ struct HybDims {
 };
 
 struct HybOffsets {
-    int pgT, pgb, pf1T, cT, pf1b, pf2, pf2b, vh1T, vh1b, vh2, vh2b, tcimg, total;
+    int pgT, pgb, pf1T, cT, pf1b, pf2, pf2b, vh1T, vh1b, vh2, vh2b, tcimg, rootimg, total;
 };
 
 // fp16 operand image of the per-successor network for the tensor-core row
 // kernel (hv_mlp_tc.cuh), at the end of the head weights: W1 [64 x 128],
 // W2 [64 x 64], [A1s | C] [64 x 96] in the K-major slab layout, zero padded
 constexpr int kTcImgHalves = 64 * 128 + 64 * 64 + 64 * 96;  // 18432
+// fp16 operand image of the per-leaf root network (k_leaf_root_tc), after
+// it: W1 [64 x 128], W2 [64 x 64], the value layer's three K blocks
+// VH1e / VH1g / VH1x [128 x 64, 128 x 64, 128 x 16] (embedding, graph,
+// global features), PG [64 x 64], PF1e / PF1g [64 x 64 each] (the root and
+// graph-context blocks of the action layer)
+constexpr int kRootImgHalves = 64 * 128 + 64 * 64 + 128 * 64 + 128 * 64 + 128 * 16 + 64 * 64 + 2 * 64 * 64;  // 43008
 
 __host__ __device__ inline HybOffsets hyb_offsets(HybDims d) {
     HybOffsets o;
@@ -275,6 +281,7 @@ __host__ __device__ inline HybOffsets hyb_offsets(HybDims d) {
     o.vh2b = p; p += 1;
     p = (p + 3) & ~3;  // 16-byte aligned image
     o.tcimg = p; p += kTcImgHalves / 2;
+    o.rootimg = p; p += kRootImgHalves / 2;
     o.total = p;
     return o;
 }

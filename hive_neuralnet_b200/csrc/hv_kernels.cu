@@ -1386,7 +1386,17 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
                                                             rows, w.mf);
         }
     }
-    {
+    if (HYB && root_features) {
+        // the hybrid's per-leaf network on the tensor cores
+        uint32_t* err = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
+        const size_t smem = sizeof(RootTcSmem);
+        const int64_t tiles = (count + kTcRows - 1) / kTcRows, ctas = (tiles + kRtGroups - 1) / kRtGroups;
+        rc = grid_for(k_leaf_root_tc, ctas * kWarpsPerBlock, smem, &grid);  // one CTA per SM (shared memory)
+        if (rc) return rc;
+        k_leaf_root_tc<<<grid, kRtThreads, smem, s>>>(root_features, graph, glob, count, fw, fd, hw, hd, values,
+                                                      w.root_pre, err);
+    } else {
         size_t smem = (sizeof(WarpSmem) + sizeof(FnnSmem)) * kWarpsPerBlock;
         rc = grid_for(k_leaf_root<HYB>, count, smem, &grid);
         if (rc) return rc;

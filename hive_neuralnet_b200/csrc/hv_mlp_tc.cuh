@@ -25,6 +25,8 @@
 
 #include <cuda_fp16.h>
 
+#include <cstddef>
+
 #include "hv_fnn.cuh"
 #include "hv_hybrid.cuh"
 #include "hv_tc.cuh"
@@ -271,6 +273,286 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
     if (failed) {
         // a bounded wait gave up: record it, let the group's MMAs finish
         // (bounded again), free TMEM and return
+        if (gt == 0) atomicOr(err_word, kErrMlpWait);
+        if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (w == 0) {
+        tc_fence_after();
+        tmem_dealloc(s->tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// per-leaf root network (the hybrid's part of HybridMCTSOrchestrator.
+// _eval_states that depends on the leaf alone, fnn_transformer_net.py:
+// 316-357): e = encode(root features), value = tanh(vh2 . relu(VH1 [e | g |
+// global] + vh1b) + vh2b), g_ctx = PG g + pgb, root_pre = pf1b' + PF1e e +
+// PF1g g_ctx.  Three independent 4-warp groups per CTA, 128 leaves per
+// group tile, five fp16 tcgen05 GEMMs with fp32 accumulators in TMEM.
+// ---------------------------------------------------------------------------
+constexpr int kRtGroups = 3, kRtThreads = kRtGroups * kTcGroupThreads;
+
+struct __align__(128) RootTcGroup {
+    __half a[16][kTcRows][8];  // X; then h | g; then e | g; then e | g_ctx
+    __half x[2][kTcRows][8];   // global features (6, padded to 16)
+};
+
+struct __align__(128) RootTcSmem {
+    __half w1[16][64][8], w2[8][64][8];
+    __half vhe[8][128][8], vhg[8][128][8], vhx[2][128][8];
+    __half pg[8][64][8], pfe[8][64][8], pfg[8][64][8];
+    RootTcGroup g[kRtGroups];
+    float b1[64], g1[64], be1[64], b2[64], vh1b[128], vh2[128], pgb[64], pf1b[64];
+    float vh2b;
+    uint64_t bar_w, bar[kRtGroups];
+    uint32_t tmem;
+    int fail[kRtGroups];
+};
+static_assert(sizeof(__half) * kRootImgHalves ==
+                  offsetof(RootTcSmem, g) - offsetof(RootTcSmem, w1), "root weight image size");
+
+// D (+)= A[128 x k] B[n x k]^T, both in slab layout (A 128 rows, B n rows)
+__device__ __forceinline__ void tc_gemm_n(uint32_t d, const void* a, const void* b, int k, int n, bool acc) {
+    const uint32_t id = idesc_f16_m128(n);
+    const char* pa = static_cast<const char*>(a);
+    const char* pb = static_cast<const char*>(b);
+    for (int s = 0; s < k / 16; s++)
+        mma_f16(d, sdesc(pa + s * 2 * kTcRows * 16, kTcRows * 16, 128), sdesc(pb + s * 2 * n * 16, n * 16, 128), id,
+                (acc || s > 0) ? 1u : 0u);
+}
+
+template <typename F>
+__device__ __forceinline__ bool rt_round(RootTcSmem* s, int g, int gt, uint32_t& phase, F issue) {
+    fence_proxy_async();
+    tc_fence_before();
+    group_sync(g);
+    if (gt == 0) {
+        tc_fence_after();
+        issue();
+        mma_commit(&s->bar[g]);
+    }
+    const bool ok = mbar_wait(&s->bar[g], phase);
+    phase ^= 1u;
+    tc_fence_after();
+    if (!ok) s->fail[g] = 1;
+    group_sync(g);
+    return s->fail[g] == 0;
+}
+
+__global__ void __launch_bounds__(kRtThreads, 1) k_leaf_root_tc(const float* __restrict__ root_feats,
+                                                                const float* __restrict__ graph,
+                                                                const float* __restrict__ glob, int64_t count,
+                                                                const float* __restrict__ fw, FnnDims fd,
+                                                                const float* __restrict__ hw, HybDims hd,
+                                                                float* __restrict__ values,
+                                                                float* __restrict__ root_pre,
+                                                                uint32_t* __restrict__ err_word) {
+    extern __shared__ __align__(128) uint8_t rt_raw[];
+    RootTcSmem* s = reinterpret_cast<RootTcSmem*>(rt_raw);
+    const int t = threadIdx.x, w = t >> 5;
+    const int g = t / kTcGroupThreads, gt = t - g * kTcGroupThreads;
+    RootTcGroup* G = &s->g[g];
+    const int H = fd.H, E = fd.E, A = hd.A, V = hd.V;
+    const FnnOffsets fo = fnn_offsets(fd);
+    const HybOffsets ho = hyb_offsets(hd);
+    const int64_t tiles = (count + kTcRows - 1) / kTcRows;
+
+    for (int o = t; o < 128; o += kRtThreads) {
+        if (o < 64) {
+            s->b1[o] = o < H ? __ldg(fw + fo.b1 + o) : 0.0f;
+            s->g1[o] = o < H ? __ldg(fw + fo.g1 + o) : 0.0f;
+            s->be1[o] = o < H ? __ldg(fw + fo.be1 + o) : 0.0f;
+            s->b2[o] = o < E ? __ldg(fw + fo.b2 + o) : 0.0f;
+            s->pgb[o] = o < E ? __ldg(hw + ho.pgb + o) : 0.0f;
+            s->pf1b[o] = o < A ? __ldg(hw + ho.pf1b + o) : 0.0f;
+        }
+        s->vh1b[o] = o < V ? __ldg(hw + ho.vh1b + o) : 0.0f;
+        s->vh2[o] = o < V ? __ldg(hw + ho.vh2 + o) : 0.0f;
+    }
+    {
+        uint4* z = reinterpret_cast<uint4*>(&s->g[0]);
+        for (int i = t; i < (int)(sizeof(s->g) / 16); i += kRtThreads) z[i] = make_uint4(0, 0, 0, 0);
+    }
+    if (t < kRtGroups) s->fail[t] = 0;
+    const bool live = (int64_t)blockIdx.x * kRtGroups < tiles;
+    if (t == 0) {
+        s->vh2b = __ldg(hw + ho.vh2b);
+        mbar_init(&s->bar_w, 1);
+        for (int i = 0; i < kRtGroups; i++) mbar_init(&s->bar[i], 1);
+        fence_mbar_init();
+        if (live) {
+            mbar_expect_tx(&s->bar_w, (uint32_t)(kRootImgHalves * 2));
+            bulk_g2s(&s->w1[0][0][0], hw + ho.rootimg, (uint32_t)(kRootImgHalves * 2), &s->bar_w);
+        }
+    }
+    if (w == 0) {
+        tmem_alloc(&s->tmem, 512);
+        tmem_relinquish();
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    bool failed = false, pending = false;
+    if (live) {
+        const bool ok = mbar_wait(&s->bar_w, 0);
+        failed = __syncthreads_or(!ok) != 0;
+    }
+    const uint32_t tcol = s->tmem + 128u * (uint32_t)g;
+    const uint32_t lane = tcol + ((uint32_t)((w & 3) * 32) << 16);
+    uint32_t phase = 0;
+    for (int64_t tile = (int64_t)blockIdx.x * kRtGroups + g; tile < tiles && !failed;
+         tile += (int64_t)gridDim.x * kRtGroups) {
+        const int64_t p0 = tile * kTcRows;
+        const int nl = (int)min((int64_t)kTcRows, count - p0);
+        const int64_t p = p0 + gt;
+        const bool mine = gt < nl;
+        {
+            const float2* xg = reinterpret_cast<const float2*>(root_feats + p0 * kFeat);
+            const int nx = nl * (kFeat / 2);
+#pragma unroll 4
+            for (int i = gt; i < nx; i += kTcGroupThreads) {
+                const int r = i / (kFeat / 2), k = 2 * (i - r * (kFeat / 2));
+                const float2 v = __ldg(xg + i);
+                *reinterpret_cast<__half2*>(&G->a[k >> 3][r][k & 7]) = __floats2half2_rn(v.x, v.y);
+            }
+            if (mine) {
+#pragma unroll
+                for (int k = 0; k < kGlobFeat; k++) G->x[0][gt][k] = __float2half_rn(__ldg(glob + p * kGlobFeat + k));
+            }
+        }
+        // ---- encode: D[0:64] = X W1^T, h = LayerNorm(sigmoid(. + b1))
+        pending = true;
+        if (!rt_round(s, g, gt, phase, [&] { tc_gemm_n(tcol, &G->a[0][0][0], &s->w1[0][0][0], 128, 64, false); })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane, d);
+            tmem_ld32(lane + 32, d + 32);
+            float mean = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 64; j++) {
+                d[j] = j < H ? sigmoidf_(d[j] + s->b1[j]) : 0.0f;
+                mean += d[j];
+            }
+            mean /= (float)H;
+            float var = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 64; j++) {
+                d[j] = j < H ? d[j] - mean : 0.0f;
+                var += d[j] * d[j];
+            }
+            const float rstd = 1.0f / sqrtf(var / (float)H + 1e-5f);
+#pragma unroll
+            for (int j = 0; j < 64; j++) d[j] = d[j] * rstd * s->g1[j] + s->be1[j];
+#pragma unroll
+            for (int c = 0; c < 8; c++) tc_put8(G->a, c, gt, d + 8 * c);
+            // the trunk's graph summary into K 64..127
+            if (mine) {
+                const float4* gp = reinterpret_cast<const float4*>(graph + p * kHybGraph);
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    const float4 v = __ldg(gp + q);
+                    d[4 * q] = v.x;
+                    d[4 * q + 1] = v.y;
+                    d[4 * q + 2] = v.z;
+                    d[4 * q + 3] = v.w;
+                }
+#pragma unroll
+                for (int c = 0; c < 8; c++) tc_put8(G->a, 8 + c, gt, d + 8 * c);
+            }
+        }
+        // ---- D[64:128] = h W2^T, e = . + b2
+        pending = true;
+        if (!rt_round(s, g, gt, phase, [&] { tc_gemm_n(tcol + 64, &G->a[0][0][0], &s->w2[0][0][0], 64, 64, false); })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane + 64, d);
+            tmem_ld32(lane + 96, d + 32);
+#pragma unroll
+            for (int j = 0; j < 64; j++) d[j] += s->b2[j];
+#pragma unroll
+            for (int c = 0; c < 8; c++) tc_put8(G->a, c, gt, d + 8 * c);
+        }
+        // ---- value hidden: D[0:128] = e VH1e^T + g VH1g^T + x VH1x^T
+        pending = true;
+        if (!rt_round(s, g, gt, phase, [&] {
+                tc_gemm_n(tcol, &G->a[0][0][0], &s->vhe[0][0][0], 64, 128, false);
+                tc_gemm_n(tcol, &G->a[8][0][0], &s->vhg[0][0][0], 64, 128, true);
+                tc_gemm_n(tcol, &G->x[0][0][0], &s->vhx[0][0][0], 16, 128, true);
+            })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float part = 0.0f, d[32];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                tmem_ld32(lane + 32 * c, d);
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const int j = 32 * c + i;
+                    if (j < V) part += s->vh2[j] * fmaxf(d[i] + s->vh1b[j], 0.0f);
+                }
+            }
+            if (mine) values[p] = tanhf(part + s->vh2b);
+        }
+        // ---- graph context: D[0:64] = g PG^T, g_ctx = . + pgb (over g in K 64..127)
+        pending = true;
+        if (!rt_round(s, g, gt, phase, [&] { tc_gemm_n(tcol, &G->a[8][0][0], &s->pg[0][0][0], 64, 64, false); })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane, d);
+            tmem_ld32(lane + 32, d + 32);
+#pragma unroll
+            for (int j = 0; j < 64; j++) d[j] += s->pgb[j];
+#pragma unroll
+            for (int c = 0; c < 8; c++) tc_put8(G->a, 8 + c, gt, d + 8 * c);
+        }
+        // ---- root half of the action layer: D[64:128] = e PF1e^T + g_ctx PF1g^T
+        pending = true;
+        if (!rt_round(s, g, gt, phase, [&] {
+                tc_gemm_n(tcol + 64, &G->a[0][0][0], &s->pfe[0][0][0], 64, 64, false);
+                tc_gemm_n(tcol + 64, &G->a[8][0][0], &s->pfg[0][0][0], 64, 64, true);
+            })) {
+            failed = true;
+            break;
+        }
+        pending = false;
+        {
+            float d[64];
+            tmem_ld32(lane + 64, d);
+            tmem_ld32(lane + 96, d + 32);
+            if (mine) {
+                float4* rp = reinterpret_cast<float4*>(root_pre + p * 64);
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    float v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int j = 4 * q + u;
+                        v[u] = j < A ? d[j] + s->pf1b[j] : 0.0f;
+                    }
+                    rp[q] = make_float4(v[0], v[1], v[2], v[3]);
+                }
+            }
+        }
+    }
+    if (failed) {
         if (gt == 0) atomicOr(err_word, kErrMlpWait);
         if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
     }

@@ -339,22 +339,30 @@ def pack_heads(net: HiveHybridGNN, device) -> torch.Tensor:
         fnn = net.fnn
         img = torch.cat([_slabs_b(fnn.fc1.weight.float(), 128), _slabs_b(fnn.fc2.weight.float(), 64),
                          _slabs_b(torch.cat([w1[:, 2 * e:3 * e].float(), fold.float()], dim=1), 96, split=e)])
+        # the per-leaf root network (k_leaf_root_tc): encode, value layer in
+        # three K blocks, graph projection, root half of the action layer
+        vh1 = net.value_head[0].weight.float()  # [V, E + 64 + 6]
+        g = net.graph_trunk.out_dim
+        root = torch.cat([_slabs_b(fnn.fc1.weight.float(), 128), _slabs_b(fnn.fc2.weight.float(), 64),
+                          _slabs_b(vh1[:, :e], 64, rows=128), _slabs_b(vh1[:, e:e + g], 64, rows=128),
+                          _slabs_b(vh1[:, e + g:], 16, rows=128), _slabs_b(net.policy_graph_proj.weight.float(), 64),
+                          _slabs_b(w1[:, :e].float(), 64), _slabs_b(w1[:, e:2 * e].float(), 64)])
         pad = (-flat.numel()) % 4
-        flat = torch.cat([flat, flat.new_zeros(pad), img.view(torch.float32)])
+        flat = torch.cat([flat, flat.new_zeros(pad), img.view(torch.float32), root.view(torch.float32)])
     return flat.to(device).contiguous()
 
 
-def _slabs_b(w: torch.Tensor, k_pad: int, split: int | None = None) -> torch.Tensor:
-    """[N <= 64, K] fp32 weight -> fp16 B operand [64 x k_pad] in the K-major
-    slab layout (element (n, k) at ((k / 8) * 64 + n) * 8 + k % 8), zero padded.
+def _slabs_b(w: torch.Tensor, k_pad: int, split: int | None = None, rows: int = 64) -> torch.Tensor:
+    """[N <= rows, K] fp32 weight -> fp16 B operand [rows x k_pad] in the K-major
+    slab layout (element (n, k) at ((k / 8) * rows + n) * 8 + k % 8), zero padded.
     With ``split``, columns [split:] start at K = 64 (the [A1s | C] layout)."""
-    out = torch.zeros(64, k_pad, dtype=torch.float32)
+    out = torch.zeros(rows, k_pad, dtype=torch.float32)
     if split is None:
         out[:w.shape[0], :w.shape[1]] = w
     else:
         out[:w.shape[0], :split] = w[:, :split]
         out[:w.shape[0], 64:64 + w.shape[1] - split] = w[:, split:]
-    return out.half().reshape(64, k_pad // 8, 8).permute(1, 0, 2).contiguous().reshape(-1)
+    return out.half().reshape(rows, k_pad // 8, 8).permute(1, 0, 2).contiguous().reshape(-1)
 
 
 class HybridEvaluator:
