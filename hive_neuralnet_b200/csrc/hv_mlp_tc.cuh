@@ -271,10 +271,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
         // the group has read its TMEM lane (the next round's group barrier)
     }
     if (failed) {
-        // a bounded wait gave up: record it, let the group's MMAs finish
-        // (bounded again), free TMEM and return
+        // a bounded wait gave up: record it, let the group's MMAs and the
+        // weight copy finish (bounded again), free TMEM and return
         if (gt == 0) atomicOr(err_word, kErrMlpWait);
         if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
+        if (t == 0 && live) mbar_wait(&s->bar_w, 0);
     }
     tc_fence_before();
     __syncthreads();
@@ -553,8 +554,10 @@ __global__ void __launch_bounds__(kRtThreads, 1) k_leaf_root_tc(const float* __r
         }
     }
     if (failed) {
+        // as in k_mlp_rows_tc: record, drain this group's MMAs and the weight copy (bounded)
         if (gt == 0) atomicOr(err_word, kErrMlpWait);
         if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
+        if (t == 0 && live) mbar_wait(&s->bar_w, 0);
     }
     tc_fence_before();
     __syncthreads();

@@ -344,8 +344,10 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             bool okw = true;
             if (t == 0) {
                 okw = mbar_wait(&s->bar_w, wphase);
-                wphase ^= 1u;
-                if (okw) wpend = false;
+                if (okw) {
+                    wphase ^= 1u;  // on failure the parity stays: the exit path waits for this copy
+                    wpend = false;
+                }
             }
             if (!__syncthreads_and(okw)) {
                 failed = true;
