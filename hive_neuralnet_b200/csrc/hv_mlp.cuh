@@ -124,8 +124,10 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
         const int nrows = (int)min((int64_t)kMlpRows, N - r0);
         // feature tile (rows past N are zero)
         const float* xg = X + r0 * kFeat;
-        for (int i = t; i < kMlpRows * kFeat; i += kMlpThreads) xs[i] = i < nrows * kFeat ? xg[i] : 0.0f;
+#pragma unroll 8
+        for (int i = t; i < kMlpRows * kFeat; i += kMlpThreads) xs[i] = i < nrows * kFeat ? __ldg(xg + i) : 0.0f;
         if (HYB) {
+#pragma unroll 8
             for (int i = t; i < kMlpRows * 32; i += kMlpThreads) {
                 const int r = i >> 5, k = i & 31;
                 ms[i] = (r < nrows && k < kMoveFeat) ? MF[(r0 + r) * kMoveFeat + k] : 0.0f;
