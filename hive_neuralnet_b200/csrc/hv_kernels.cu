@@ -51,6 +51,11 @@ __device__ __forceinline__ void stage_state(WarpSmem* w, const uint8_t* src) {
     __syncwarp();
 }
 
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
 __device__ __forceinline__ void zero_moves(WarpSmem* w) {
     uint4* m4 = reinterpret_cast<uint4*>(w->mv);
     for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = make_uint4(0, 0, 0, 0);
@@ -120,10 +125,17 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
 // successor features: apply one root move, compact list, features
 // (game_logic.cu:182-229 fnn_successor_features_kernel)
 // ---------------------------------------------------------------------------
+// SLAB: rows go out as fp16 in the K-major slab layout of 128-row tiles that
+// the hybrid's tensor-core row network copies straight into its A operand
+// (row r: tile r / 128, chunk c of 8 features at ((tile * 16 + c) * 128 +
+// r % 128) * 8 halves, features 122..127 zero); otherwise fp32 [rows][122].
+template <bool SLAB>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
     const int64_t* __restrict__ action_to_root, const int64_t* __restrict__ move_indices,
-    int64_t num_actions, float* __restrict__ feats_out, const int64_t* __restrict__ n_actual) {
+    int64_t num_actions, void* __restrict__ out, const int64_t* __restrict__ n_actual) {
+    float* feats_out = static_cast<float*>(out);
+    __half* slab = static_cast<__half*>(out);
     WarpSmem* w = warp_slot();
     if (n_actual) num_actions = min(num_actions, *n_actual);  // row pipeline: rows actually filled
     // The block's warps take consecutive rows and cross one block barrier
@@ -140,7 +152,13 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             mi = move_indices[a];
             if (root < 0 || root >= num_states || mi < 0 || mi >= kMaxMoves) {
                 // out-of-range request: zero row, flag it, touch nothing else
-                for (int k = lane_id(); k < kFeat; k += 32) feats_out[a * kFeat + k] = 0.0f;
+                if (SLAB) {
+                    if (lane_id() < 16)
+                        *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + lane_id()) * 128 + (a & 127)) * 8) =
+                            make_uint4(0, 0, 0, 0);
+                } else {
+                    for (int k = lane_id(); k < kFeat; k += 32) feats_out[a * kFeat + k] = 0.0f;
+                }
                 if (lane_id() == 0) atomicOr(&g_error, kErrIndex);
                 ok = false;
             }
@@ -158,7 +176,28 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             n = gen_compact(w, S, &g_error);
         }
         __syncthreads();
-        if (ok) features(w, S, n, feats_out + a * kFeat);
+        if (ok) {
+            if (SLAB) {
+                // the move list is consumed once the features are written: stage them there
+                float* f = reinterpret_cast<float*>(w->mv);
+                features(w, S, n, f);
+                __syncwarp();
+                const int c = lane_id();
+                if (c < 16) {
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = 8 * c + i < kFeat ? f[8 * c + i] : 0.0f;
+                    uint4 u;
+                    u.x = pack_half2(v[0], v[1]);
+                    u.y = pack_half2(v[2], v[3]);
+                    u.z = pack_half2(v[4], v[5]);
+                    u.w = pack_half2(v[6], v[7]);
+                    *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + c) * 128 + (a & 127)) * 8) = u;
+                }
+            } else {
+                features(w, S, n, feats_out + a * kFeat);
+            }
+        }
         __syncwarp();
     }
 }
@@ -530,7 +569,7 @@ __global__ void __launch_bounds__(kThreads) k_row_index(const int32_t* __restric
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_row_move_features(
     const uint8_t* __restrict__ states, const uint8_t* __restrict__ legal_moves,
     const int32_t* __restrict__ num_legal, int64_t T, const int64_t* __restrict__ row_start, int64_t cap,
-    float* __restrict__ mf) {
+    __half* __restrict__ mf) {
     WarpSmem* w = warp_slot();
     const int l = lane_id();
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
@@ -544,11 +583,20 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_row_move_features(
         for (int64_t i = l; i < n; i += 32) {
             if (start + i >= cap) continue;
             const uint8_t* m = mv + i * kMoveBytes;
-            float f[kMoveFeat];
+            float f[32];
             move_features(P, w->st, X, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8), f);
-            float* row = mf + (start + i) * kMoveFeat;
+            f[31] = 0.0f;
+            // fp16, slab layout of 128-row tiles (4 chunks of 8; feature 31 zero)
+            const int64_t r = start + i;
 #pragma unroll
-            for (int k = 0; k < kMoveFeat; k++) row[k] = f[k];
+            for (int c = 0; c < 4; c++) {
+                uint4 u;
+                u.x = pack_half2(f[8 * c], f[8 * c + 1]);
+                u.y = pack_half2(f[8 * c + 2], f[8 * c + 3]);
+                u.z = pack_half2(f[8 * c + 4], f[8 * c + 5]);
+                u.w = pack_half2(f[8 * c + 6], f[8 * c + 7]);
+                *reinterpret_cast<uint4*>(mf + (((r >> 7) * 4 + c) * 128 + (r & 127)) * 8) = u;
+            }
         }
         __syncwarp();
     }
@@ -1356,8 +1404,9 @@ struct RowWorkspace {
     int64_t* row_start;  // [count + 1]
     int64_t* atr;        // [rows]
     int64_t* mi;         // [rows]
-    float* x;            // [rows][122]
-    float* mf;           // [rows][31] (hybrid)
+    float* x;            // [rows][122] (FNN)
+    __half* xh;          // hybrid: fp16 slab tiles of the successor features, 256 bytes per row
+    __half* mfh;         // hybrid: fp16 slab tiles of the move features, 64 bytes per row
     float* root_pre;     // [count][64]
     float* logits;       // [count][256] (when the caller passes none)
 };
@@ -1375,15 +1424,16 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
     k_row_index<<<grid, kThreads, 0, s>>>(num_legal, count, w.row_start, rows, w.atr, w.mi);
     if (rows > 0) {
         size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
-        rc = grid_for(k_successor_features, rows, smem, &grid);
+        rc = grid_for(k_successor_features<HYB>, rows, smem, &grid);
         if (rc) return rc;
-        k_successor_features<<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows, w.x,
-                                                         w.row_start + count);
+        k_successor_features<HYB><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows,
+                                                              HYB ? static_cast<void*>(w.xh) : static_cast<void*>(w.x),
+                                                              w.row_start + count);
         if (HYB) {
             rc = grid_for(k_row_move_features, count, smem, &grid);
             if (rc) return rc;
             k_row_move_features<<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, count, w.row_start,
-                                                            rows, w.mf);
+                                                            rows, w.mfh);
         }
     }
     if (HYB && root_features) {
@@ -1403,7 +1453,8 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         k_leaf_root<HYB><<<grid, kThreads, smem, s>>>(states, legal_moves, num_legal, root_features, graph, glob,
                                                       count, fw, fd, hw, hd, values, w.root_pre);
     }
-    if (rows > 0 && HYB) {
+    if constexpr (HYB) {
+      if (rows > 0) {
         // the hybrid network on the tensor cores (fp16 operands, as the reference's autocast)
         uint32_t* err = nullptr;
         if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
@@ -1411,14 +1462,15 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         const int64_t tiles = (rows + kTcRows - 1) / kTcRows, ctas = (tiles + kTcGroups - 1) / kTcGroups;
         rc = grid_for(k_mlp_rows_tc, ctas * kWarpsPerBlock, smem, &grid);  // one CTA per SM (shared memory)
         if (rc) return rc;
-        k_mlp_rows_tc<<<grid, kTcThreads, smem, s>>>(w.x, w.mf, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd, lg,
+        k_mlp_rows_tc<<<grid, kTcThreads, smem, s>>>(w.xh, w.mfh, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd, lg,
                                                      w.row_start + count, err);
+      }
     } else if (rows > 0) {
         const size_t smem = sizeof(MlpSmem<HYB>);
         const int64_t tiles = (rows + kMlpRows - 1) / kMlpRows;
         rc = grid_for(k_mlp_rows<HYB>, tiles * kWarpsPerBlock, smem, &grid);
         if (rc) return rc;
-        k_mlp_rows<HYB><<<grid, kMlpThreads, smem, s>>>(w.x, w.mf, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd,
+        k_mlp_rows<HYB><<<grid, kMlpThreads, smem, s>>>(w.x, nullptr, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd,
                                                         lg, child_q, w.row_start + count);
     }
     rc = grid_for(k_leaf_softmax<HYB>, count, 0, &grid);
@@ -1505,9 +1557,9 @@ int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const u
         return HV_EINVAL;
     size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
     int grid = 0;
-    int rc = grid_for(k_successor_features, num_actions, smem, &grid);
+    int rc = grid_for(k_successor_features<false>, num_actions, smem, &grid);
     if (rc) return rc;
-    k_successor_features<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+    k_successor_features<false><<<grid, kThreads, smem, (cudaStream_t)stream>>>(
         states, num_states, legal_moves, action_to_root, move_indices, num_actions, features, nullptr);
     return launch_status();
 }
@@ -1710,8 +1762,10 @@ static size_t row_workspace_layout(int64_t count, int64_t rows, bool hybrid, boo
     uint8_t* rs = take((n + 1) * sizeof(int64_t));
     uint8_t* at = take(r * sizeof(int64_t));
     uint8_t* mi = take(r * sizeof(int64_t));
-    uint8_t* x = take(r * kFeat * sizeof(float));
-    uint8_t* mf = hybrid ? take(r * kMoveFeat * sizeof(float)) : nullptr;
+    const size_t rt = (r + 127) / 128 * 128;  // whole 128-row tiles
+    uint8_t* x = hybrid ? nullptr : take(r * kFeat * sizeof(float));
+    uint8_t* xh = hybrid ? take(rt * 128 * 2) : nullptr;
+    uint8_t* mf = hybrid ? take(rt * 32 * 2) : nullptr;
     uint8_t* rp = take(n * 64 * sizeof(float));
     uint8_t* lg = own_logits ? take(n * kMaxMoves * sizeof(float)) : nullptr;
     if (w) {
@@ -1719,7 +1773,8 @@ static size_t row_workspace_layout(int64_t count, int64_t rows, bool hybrid, boo
         w->atr = reinterpret_cast<int64_t*>(at);
         w->mi = reinterpret_cast<int64_t*>(mi);
         w->x = reinterpret_cast<float*>(x);
-        w->mf = reinterpret_cast<float*>(mf);
+        w->xh = reinterpret_cast<__half*>(xh);
+        w->mfh = reinterpret_cast<__half*>(mf);
         w->root_pre = reinterpret_cast<float*>(rp);
         w->logits = reinterpret_cast<float*>(lg);
     }

@@ -48,7 +48,7 @@ struct __align__(128) MlpTcSmem {
     MlpTcGroup g[kTcGroups];
     float b1[64], g1[64], be1[64], b2[64], a2[64];
     float a2b;
-    uint64_t bar_w, bar[kTcGroups];
+    uint64_t bar_w, bar[kTcGroups], bar_x[kTcGroups];
     uint32_t tmem;
     int fail[kTcGroups];
 };
@@ -106,8 +106,12 @@ __device__ __forceinline__ bool tc_round(MlpTcSmem* s, int g, int gt, uint32_t& 
     return s->fail[g] == 0;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __restrict__ X,
-                                                               const float* __restrict__ MF,
+// X / MF: the rows' successor and move features as fp16 slab tiles (written
+// so by k_successor_features<true> / k_row_move_features): one tile is
+// 16 x 128 x 8 and 4 x 128 x 8 halves, copied as they are into the group's
+// A operands
+__global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const __half* __restrict__ X,
+                                                               const __half* __restrict__ MF,
                                                                const int64_t* __restrict__ atr,
                                                                const int64_t* __restrict__ mi, int64_t N,
                                                                const float* __restrict__ root_pre,
@@ -134,17 +138,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
         s->b2[o] = o < E ? __ldg(fw + fo.b2 + o) : 0.0f;
         s->a2[o] = o < A ? __ldg(hw + ho.pf2 + o) : 0.0f;
     }
-    // the operand slabs start at zero (their padding columns are never written again)
-    {
-        uint4* z = reinterpret_cast<uint4*>(&s->g[0]);
-        for (int i = t; i < (int)(sizeof(s->g) / 16); i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
-    }
     if (t < kTcGroups) s->fail[t] = 0;
     const bool live = (int64_t)blockIdx.x * kTcGroups < tiles;
     if (t == 0) {
         s->a2b = __ldg(hw + ho.pf2b);
         mbar_init(&s->bar_w, 1);
-        for (int i = 0; i < kTcGroups; i++) mbar_init(&s->bar[i], 1);
+        for (int i = 0; i < kTcGroups; i++) {
+            mbar_init(&s->bar[i], 1);
+            mbar_init(&s->bar_x[i], 1);
+        }
         fence_mbar_init();
         if (live) {
             // the weight image (host-packed fp16 slabs)
@@ -167,28 +169,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
     }
     const uint32_t tcol = s->tmem + 128u * (uint32_t)g;
     const uint32_t lane = tcol + ((uint32_t)((w & 3) * 32) << 16);  // this thread's TMEM lane (row gt)
-    uint32_t phase = 0;
+    uint32_t phase = 0, xphase = 0;
+    bool xpend = false;
     for (int64_t tile = (int64_t)blockIdx.x * kTcGroups + g; tile < tiles && !failed;
          tile += (int64_t)gridDim.x * kTcGroups) {
         const int64_t r0 = tile * kTcRows;
         const int nrows = (int)min((int64_t)kTcRows, N - r0);
-        // ---- this tile's rows straight into the slabs (two floats at a time; 122 is even)
+        // ---- this tile's slabs, as written by the feature kernels (the
+        // previous tile's MMAs reading the operands have completed)
         {
-            const float2* xg = reinterpret_cast<const float2*>(X + r0 * kFeat);
-            const int nx = nrows * (kFeat / 2);
-#pragma unroll 4
-            for (int i = gt; i < nx; i += kTcGroupThreads) {
-                const int r = i / (kFeat / 2), k = 2 * (i - r * (kFeat / 2));
-                const float2 v = __ldg(xg + i);
-                *reinterpret_cast<__half2*>(&G->a[k >> 3][r][k & 7]) = __floats2half2_rn(v.x, v.y);
+            constexpr uint32_t bx = sizeof(G->a), bm = sizeof(G->m);
+            if (gt == 0) {
+                mbar_expect_tx(&s->bar_x[g], bx + bm);
+                bulk_g2s(&G->a[0][0][0], X + tile * (bx / 2), bx, &s->bar_x[g]);
+                bulk_g2s(&G->m[0][0][0], MF + tile * (bm / 2), bm, &s->bar_x[g]);
             }
-            const float* mg = MF + r0 * kMoveFeat;
-            const int nm = nrows * kMoveFeat;
-#pragma unroll 4
-            for (int i = gt; i < nm; i += kTcGroupThreads) {
-                const int r = i / kMoveFeat, k = i - r * kMoveFeat;
-                G->m[k >> 3][r][k & 7] = __float2half_rn(__ldg(mg + i));
+            xpend = true;
+            const bool ok = mbar_wait(&s->bar_x[g], xphase);
+            if (!ok) s->fail[g] = 1;
+            group_sync(g);
+            if (s->fail[g]) {
+                failed = true;
+                break;
             }
+            xphase ^= 1u;
+            xpend = false;
         }
         // ---- D[0:64] = X W1^T
         pending = true;
@@ -275,6 +280,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const float* __re
         // weight copy finish (bounded again), free TMEM and return
         if (gt == 0) atomicOr(err_word, kErrMlpWait);
         if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
+        if (gt == 0 && xpend) mbar_wait(&s->bar_x[g], xphase);
         if (t == 0 && live) mbar_wait(&s->bar_w, 0);
     }
     tc_fence_before();
