@@ -1446,6 +1446,15 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         if (rc) return rc;
         k_leaf_root_tc<<<grid, kRtThreads, smem, s>>>(root_features, graph, glob, count, fw, fd, hw, hd, values,
                                                       w.root_pre, err);
+    } else if (!HYB && root_features) {
+        // the FNN's per-leaf network tiled like the successor rows (fp32)
+        const size_t smem = sizeof(MlpSmem<false>);
+        const int64_t tiles = (count + kMlpRows - 1) / kMlpRows;
+        rc = grid_for(k_mlp_rows<false, true>, tiles * kWarpsPerBlock, smem, &grid);
+        if (rc) return rc;
+        k_mlp_rows<false, true><<<grid, kMlpThreads, smem, s>>>(root_features, nullptr, nullptr, nullptr, count,
+                                                                nullptr, fw, fd, hw, hd, w.root_pre, values,
+                                                                nullptr);
     } else {
         size_t smem = (sizeof(WarpSmem) + sizeof(FnnSmem)) * kWarpsPerBlock;
         rc = grid_for(k_leaf_root<HYB>, count, smem, &grid);

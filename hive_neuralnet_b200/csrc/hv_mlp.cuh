@@ -49,7 +49,7 @@ __device__ __forceinline__ float row_sum16(float v) {
     return v;
 }
 
-template <bool HYB>
+template <bool HYB, bool ROOT = false>
 __device__ void mlp_load_weights(MlpSmem<HYB>* s, const float* __restrict__ fw, FnnDims fd, const float* __restrict__ hw,
                                  HybDims hd) {
     const FnnOffsets fo = fnn_offsets(fd);
@@ -66,7 +66,7 @@ __device__ void mlp_load_weights(MlpSmem<HYB>* s, const float* __restrict__ fw, 
         float a = 0.0f;
         if (k < E && o < A) {
             if (HYB) a = __ldg(hw + hyb_offsets(hd).pf1T + (2 * E + k) * A + o);
-            else a = __ldg(fw + fo.a1t + (E + k) * A + o);
+            else a = __ldg(fw + fo.a1t + ((ROOT ? 0 : E) + k) * A + o);  // root or successor half
         }
         s->a1[k][o] = a;
     }
@@ -84,6 +84,7 @@ __device__ void mlp_load_weights(MlpSmem<HYB>* s, const float* __restrict__ fw, 
         s->b2[o] = o < E ? __ldg(fw + fo.b2 + o) : 0.0f;
         s->wv[o] = o < E ? __ldg(fw + fo.wv + o) : 0.0f;
         if (HYB) s->a2[o] = o < A ? __ldg(hw + hyb_offsets(hd).pf2 + o) : 0.0f;
+        else if (ROOT) s->a2[o] = o < A ? __ldg(fw + fo.a1b + o) : 0.0f;  // ROOT: the action layer's bias
         else s->a2[o] = o < A ? __ldg(fw + fo.a2 + o) : 0.0f;
     }
     if (t == 0) {
@@ -94,8 +95,12 @@ __device__ void mlp_load_weights(MlpSmem<HYB>* s, const float* __restrict__ fw, 
 
 // rows [0, N): features X [N][122] (+ move features MF [N][31] for the hybrid),
 // leaf / slot of each row, per-leaf action pre-activations root_pre [T][64];
-// writes logits[leaf * 256 + slot] and (FNN) child_q[leaf * 256 + slot]
-template <bool HYB>
+// writes logits[leaf * 256 + slot] and (FNN) child_q[leaf * 256 + slot].
+// ROOT (FNN): the rows are the leaves' own root features; writes the value
+// (child_q: values [N]) and the root half of the action layer
+// (root_pre [N][64]: a1b + A1[:, 0:E] e, zero past A) -- the per-leaf part of
+// the evaluator (fnn_network.py:98-143), tiled.
+template <bool HYB, bool ROOT = false>
 __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __restrict__ X,
                                                             const float* __restrict__ MF,
                                                             const int64_t* __restrict__ atr,
@@ -115,7 +120,7 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
     const int H = fd.H, E = fd.E;
     const int A = HYB ? hd.A : fd.A;
     const float invH = 1.0f / (float)H;
-    mlp_load_weights<HYB>(s, fw, fd, hw, hd);
+    mlp_load_weights<HYB, ROOT>(s, fw, fd, hw, hd);
     __syncthreads();
     if (n_actual) N = min(N, *n_actual);  // rows actually filled
     const int64_t tiles = (N + kMlpRows - 1) / kMlpRows;
@@ -203,7 +208,11 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
 #pragma unroll
                 for (int j = 0; j < 4; j++) pv += s->wv[4 * tx + j] * acc[i][j];
                 pv = row_sum16(pv);
-                if (tx == 0 && r < nrows) child_q[atr[r0 + r] * kMaxMoves + mi[r0 + r]] = -tanhf(pv + s->bv);
+                if (ROOT) {
+                    if (tx == 0 && r < nrows) child_q[r0 + r] = tanhf(pv + s->bv);
+                } else if (tx == 0 && r < nrows) {
+                    child_q[atr[r0 + r] * kMaxMoves + mi[r0 + r]] = -tanhf(pv + s->bv);
+                }
             }
         }
         __syncthreads();
@@ -212,10 +221,10 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int r = 4 * ty + i;
-            leaf[i] = r < nrows ? atr[r0 + r] : 0;
+            leaf[i] = ROOT ? 0 : (r < nrows ? atr[r0 + r] : 0);
 #pragma unroll
             for (int j = 0; j < 4; j++)
-                acc[i][j] = (4 * tx + j) < A ? root_pre[leaf[i] * 64 + 4 * tx + j] : 0.0f;
+                acc[i][j] = (4 * tx + j) < A ? (ROOT ? s->a2[4 * tx + j] : root_pre[leaf[i] * 64 + 4 * tx + j]) : 0.0f;
         }
 #pragma unroll 2
         for (int k = 0; k < E; k++) {
@@ -243,15 +252,26 @@ __global__ void __launch_bounds__(kMlpThreads, 2) k_mlp_rows(const float* __rest
                 }
             }
         }
+        if (ROOT) {
+            float* rp = logits;  // ROOT: root_pre [N][64]
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int r = 4 * ty + i;
-            float p = 0.0f;
+            for (int i = 0; i < 4; i++) {
+                const int r = 4 * ty + i;
+                if (r < nrows)
+                    *reinterpret_cast<float4*>(rp + (r0 + r) * 64 + 4 * tx) = make_float4(acc[i][0], acc[i][1],
+                                                                                       acc[i][2], acc[i][3]);
+            }
+        } else {
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                if ((4 * tx + j) < A) p += s->a2[4 * tx + j] * sigmoidf_(acc[i][j]);
-            p = row_sum16(p);
-            if (tx == 0 && r < nrows) logits[leaf[i] * kMaxMoves + mi[r0 + r]] = p + s->a2b;
+            for (int i = 0; i < 4; i++) {
+                const int r = 4 * ty + i;
+                float p = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if ((4 * tx + j) < A) p += s->a2[4 * tx + j] * sigmoidf_(acc[i][j]);
+                p = row_sum16(p);
+                if (tx == 0 && r < nrows) logits[leaf[i] * kMaxMoves + mi[r0 + r]] = p + s->a2b;
+            }
         }
         __syncthreads();
     }
