@@ -162,6 +162,25 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # roofline helpers
 # --------------------------------------------------------------------------
+def staged_upload_bytes(states):
+    """Host->device bytes of hv_stage_host_states for these states: bytes
+    2645..3423 of each, and per stack level L the 16-byte words spanning the
+    board rows that hold a cell higher than L."""
+    import torch
+    n = states.shape[0]
+    rowmax = states[:, 2645:2645 + 529].reshape(n, 23, 23).amax(2).long()
+    rows = torch.arange(23, device=states.device)
+    total = n * (STATE_BYTES - 2645)
+    for lv in range(5):
+        has = rowmax > lv
+        r0 = torch.where(has, rows, 23).amin(1)
+        r1 = torch.where(has, rows + 1, 0).amax(1)
+        w0 = (lv * 529 + r0 * 23) // 16
+        w1 = (lv * 529 + r1 * 23 + 15) // 16
+        total += int((16 * (w1 - w0) * has.any(1)).sum().item())
+    return total
+
+
 def measured_peak_gbs():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -302,14 +321,15 @@ def run_gpu(args) -> None:
     if dist is not None:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = world * P * e2e_steps / (float(t2.item()) / 1e3)
-    h2d = P * STATE_BYTES
+    h2d = staged_upload_bytes(states)
+    n_tall = int((states[:, 2645:2645 + 529].amax(1) >= 3).sum().item())
     d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
 
     # ---- the host link the e2e leg runs against: plain pinned copies of the
     # step's state bytes, each direction alone, CUDA events on this stream
     dev_buf = torch.empty_like(states)
 
-    def link_gbs(copy):
+    def link_gbs(copy, nbytes):
         for _ in range(2):
             copy()
         torch.cuda.synchronize(dev)
@@ -318,15 +338,27 @@ def run_gpu(args) -> None:
             copy()
         e1.record(stream)
         torch.cuda.synchronize(dev)
-        return 3 * h2d / (e0.elapsed_time(e1) / 1e3) / 1e9
+        return 3 * nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9
 
-    h2d_gbs = link_gbs(lambda: dev_buf.copy_(host_states, non_blocking=True))
-    d2h_gbs = link_gbs(lambda: host_states.copy_(dev_buf, non_blocking=True))
+    side = torch.cuda.Stream(dev)
+
+    def both_ways():
+        # the state upload and the move-list download at once, on two streams
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            h_moves.copy_(out[0], non_blocking=True)
+        dev_buf.copy_(host_states, non_blocking=True)
+        stream.wait_stream(side)
+
+    h2d_gbs = link_gbs(lambda: dev_buf.copy_(host_states, non_blocking=True), P * STATE_BYTES)
+    d2h_gbs = link_gbs(lambda: host_states.copy_(dev_buf, non_blocking=True), P * STATE_BYTES)
+    bidir_gbs = link_gbs(both_ways, P * (STATE_BYTES + MAX_MOVES * MOVE_BYTES))
     del dev_buf
     e2e_step_s = float(t2.item()) / 1e3 / e2e_steps
-    link = {"h2d_gbs_measured": h2d_gbs, "d2h_gbs_measured": d2h_gbs,
+    # the step moves bytes both ways at once: its bound is the link's combined rate
+    link = {"h2d_gbs_measured": h2d_gbs, "d2h_gbs_measured": d2h_gbs, "bidir_gbs_measured": bidir_gbs,
             "h2d_gbs_achieved": h2d / e2e_step_s / 1e9, "d2h_gbs_achieved": d2h / e2e_step_s / 1e9,
-            "frac": (h2d / e2e_step_s / 1e9) / h2d_gbs}
+            "frac": (h2d + d2h) / e2e_step_s / 1e9 / bidir_gbs}
 
     # ---- roofline of the dominant kernel: the move generator k_root<gen>
     # (one of the step's two launches), timed alone with CUDA events on the
@@ -373,6 +405,8 @@ def run_gpu(args) -> None:
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
+                            f"staged upload (hv_stage_host_states: stack levels over occupied rows; "
+                            f"{n_tall} states with a 3-high stack), "
                             f"{args.e2e_chunk}-position chunks over 3 streams",
                     "link": link},
             "roofline": roofline,

@@ -1488,6 +1488,39 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
     return launch_status();
 }
 
+// Stack levels of a chunk of states, read from mapped host memory after the
+// heights are on the device.  Level L of a cell is read by the kernels only
+// when the cell's height exceeds L, so level L is fetched over the board rows
+// r0..r1 that hold such a cell: bytes L*529 + 23*r0 up to L*529 + 23*(r1+1),
+// widened to 16-byte words (the widening rewrites neighbouring bytes with the
+// host's own values).  Other level bytes of dev are left as they were.
+__global__ void __launch_bounds__(kThreads) k_stage_levels(const uint8_t* __restrict__ host, int64_t count,
+                                                           uint8_t* __restrict__ dev) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < count; p += nwarps) {
+        const uint8_t* h = dev + p * kStateBytes + kOffHeight;
+        unsigned lo[5], hi[5];
+#pragma unroll
+        for (int t = 0; t < 5; t++) lo[t] = kBoard, hi[t] = 0;
+        for (int c = l; c < kCells; c += 32) {
+            const unsigned ht = h[c], r = c / kBoard;
+#pragma unroll
+            for (int t = 0; t < 5; t++)
+                if (ht > (unsigned)t) lo[t] = min(lo[t], r), hi[t] = max(hi[t], r + 1);
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(host + p * kStateBytes);
+        uint4* dst = reinterpret_cast<uint4*>(dev + p * kStateBytes);
+#pragma unroll
+        for (int t = 0; t < 5; t++) {
+            const unsigned r0 = __reduce_min_sync(kFull, lo[t]), r1 = __reduce_max_sync(kFull, hi[t]);
+            if (r0 >= r1) break;  // no cell above level t, none above t + 1 either
+            const int w0 = (t * kCells + (int)r0 * kBoard) >> 4, w1 = (t * kCells + (int)r1 * kBoard + 15) >> 4;
+            for (int i = w0 + l; i < w1; i += 32) dst[i] = src[i];
+        }
+    }
+}
+
 }  // namespace hv
 
 using namespace hv;
@@ -1548,6 +1581,37 @@ int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batc
     int rc = launch_root<true, true, false>(states, nullptr, nullptr, batch, moves, num_legal, nullptr, stream);
     if (rc) return rc;
     return launch_root<false, false, true>(states, moves, num_legal, batch, nullptr, nullptr, features, stream);
+}
+
+int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev_states, void* stream) {
+    if (count < 0) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!host_states || !dev_states) return HV_EINVAL;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaPointerAttributes attr;
+    const void* mapped = nullptr;
+    // the level kernel moves 16-byte words: other alignments take the full copy
+    if (aligned16(host_states) && aligned16(dev_states)) {
+        if (cudaPointerGetAttributes(&attr, host_states) == cudaSuccess && attr.type == cudaMemoryTypeHost)
+            mapped = attr.devicePointer;
+        else
+            cudaGetLastError();  // a pageable pointer is not an error here
+    }
+    if (!mapped) {
+        if (cudaMemcpyAsync(dev_states, host_states, (size_t)count * kStateBytes, cudaMemcpyHostToDevice, s) !=
+            cudaSuccess)
+            return HV_ECUDA;
+        return HV_OK;
+    }
+    // heights, bitboards and fields (bytes 2645..3423) of every state
+    if (cudaMemcpy2DAsync(dev_states + kOffHeight, kStateBytes, host_states + kOffHeight, kStateBytes,
+                          kStateBytes - kOffHeight, (size_t)count, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return HV_ECUDA;
+    int grid = 0;
+    int rc = grid_for(k_stage_levels, count, 0, &grid);
+    if (rc) return rc;
+    k_stage_levels<<<grid, kThreads, 0, s>>>(static_cast<const uint8_t*>(mapped), count, dev_states);
+    return launch_status();
 }
 
 int hv_extract_fnn_features(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,

@@ -184,7 +184,10 @@ class HiveGPUExtension:
                 d_st, d_mv, d_nl, d_ft = slots[i % 3]
                 s = streams[i % 3]
                 with torch.cuda.stream(s):
-                    d_st[:n].copy_(states[lo:lo + n], non_blocking=True)
+                    # stack levels 2-4 only where some cell is 3 high (hv_stage_host_states)
+                    _lib.check(self._lib.hv_stage_host_states(states.data_ptr() + lo * SIZEOF_HIVE_STATE, n,
+                                                              _ptr(d_st), s.cuda_stream),
+                               "generate_legal_moves_and_fnn_features_host")
                     _lib.check(self._lib.hv_generate_legal_moves_and_fnn_features(
                         _ptr(d_st), n, _ptr(d_mv), _ptr(d_nl), _ptr(d_ft), s.cuda_stream),
                         "generate_legal_moves_and_fnn_features_host")

@@ -63,6 +63,21 @@ int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves
 int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
                                              int32_t* num_legal, float* features, void* stream);
 
+/* Host -> device staging of `count` 3424-byte states for the host-buffer
+ * pipeline (the reference's callers pass host tensors through .cuda() before
+ * generate_legal_moves_and_fnn_features_batch, game_logic.cu:1440-1464).
+ * Move generation and feature extraction read stack level L of a cell only
+ * when the cell's height exceeds L, so from pinned (device-mapped) host
+ * memory this copies each state's heights, bitboards and fields (bytes
+ * 2645..3423) with one strided copy, then a kernel reads level L from host
+ * memory over the board rows holding a cell higher than L, in 16-byte words.
+ * The remaining level bytes of dev_states are left as they were: the staged
+ * states are inputs for the read-only kernels, not a byte copy to hand back.
+ * Pageable memory, or either pointer off a 16-byte boundary: one full copy.
+ * Asynchronous on `stream`; the host buffer must stay valid until the stream
+ * reaches it. */
+int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev_states, void* stream);
+
 /* extract_fnn_features_batch(states, legal_moves, num_legal, batch_size)
  * replaces bindings.cpp:330-333 / game_logic.cu:1409-1431. */
 int hv_extract_fnn_features(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,

@@ -164,13 +164,23 @@ def test_queen_escape_and_child_probe(ext, orc):
 def test_host_buffer_pipeline_matches_device_call(ext, orc):
     """The chunked host-buffer form gives the same bytes as the device call (ragged last chunk)."""
     st = orc.generate_positions(4711, 0, 5000, 120, 7)
-    host = torch.from_numpy(st).pin_memory()
-    mh, nh, fh = ext.generate_legal_moves_and_fnn_features_host(host, 5000, chunk=1024)
-    torch.cuda.current_stream().synchronize()
-    mg, ng, fg = ext.generate_legal_moves_and_fnn_features_batch(_cuda(st), 5000)
-    assert np.array_equal(mh.numpy(), mg.cpu().numpy())
-    assert np.array_equal(nh.numpy(), ng.cpu().numpy())
-    assert np.array_equal(_bits(fh.numpy()), _bits(fg.cpu().numpy()))
+    tall = st[:, 2645:2645 + 529].max(1) >= 3
+    assert 0 < tall.sum() < len(st)  # both sides of the staged upload's level test
+    # the staged upload leaves level bytes above each cell's height as they
+    # were: poison the staging slots so that a byte it should have sent shows
+    slots, _ = ext._staging(torch.device("cuda", torch.cuda.current_device()), 1024)
+    for slot in slots:
+        slot[0].fill_(0xA7)
+    mg, ng, fg = (x.cpu().numpy() for x in ext.generate_legal_moves_and_fnn_features_batch(_cuda(st), 5000))
+    raw = torch.empty(5000 * 3424 + 8, dtype=torch.uint8).pin_memory()
+    odd = raw[8:].view(5000, 3424)  # pinned but off a 16-byte boundary: full copy
+    odd.copy_(torch.from_numpy(st))
+    for host in (torch.from_numpy(st).pin_memory(), torch.from_numpy(st), odd):
+        mh, nh, fh = ext.generate_legal_moves_and_fnn_features_host(host, 5000, chunk=1024)
+        torch.cuda.current_stream().synchronize()
+        assert np.array_equal(mh.numpy(), mg)
+        assert np.array_equal(nh.numpy(), ng)
+        assert np.array_equal(_bits(fh.numpy()), _bits(fg))
 
 
 @pytest.mark.parametrize("mask,max_ply", [(0, 60), (7, 120), (7, 200)])
