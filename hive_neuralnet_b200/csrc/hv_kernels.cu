@@ -44,10 +44,19 @@ __device__ __forceinline__ WarpSmem* warp_slot() {
     return reinterpret_cast<WarpSmem*>(smem_raw) + (threadIdx.x >> 5);
 }
 
+// The state into the warp's shared slot with asynchronous 16-byte copies:
+// all seven of a lane's copies are in flight together (a load/store loop
+// waits one memory latency per iteration).
 __device__ __forceinline__ void stage_state(WarpSmem* w, const uint8_t* src) {
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4* d4 = reinterpret_cast<uint4*>(w->st);
-    for (int i = lane_id(); i < kStateBytes / 16; i += 32) d4[i] = __ldg(s4 + i);
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(w->st));
+#pragma unroll
+    for (int k = 0; k < (kStateBytes / 16 + 31) / 32; k++) {
+        const int i = lane_id() + 32 * k;
+        if (i < kStateBytes / 16)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 16 * i), "l"(src + 16 * i)
+                         : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
 }
 
