@@ -69,7 +69,7 @@ struct __align__(16) WarpSmem {
     uint16_t pcell[32];          // cell of piece i
     uint16_t pref[24];           // piece index of the first occupied cell of row r
     uint16_t ppref[24];          // placement index of the first placement cell of row r
-    uint8_t pflag[32];           // bit0: pinned
+    uint8_t pflag[32];           // bit0: pinned (articulation point at height 1), bit1: articulation point
     uint32_t pl[24];             // mosquito union set (generators) / placement-cell set (features)
     // Generator scratch and feature accumulators are never live together
     // (features run on a finished move list), so they share storage: 1.3 KB
@@ -421,8 +421,29 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
     S.my_top = P.top(S.my_cell);
 
     S.my_ap = ARC ? articulation_arc(w, S) : articulation_flood(w, S);
-    w->pflag[l] = (S.my_ap && S.my_h == 1) ? 1 : 0;
+    w->pflag[l] = ((S.my_ap && S.my_h == 1) ? 1 : 0) | (S.my_ap ? 2 : 0);
     __syncwarp();
+    return S;
+}
+
+// The Setup of the staged position, re-read from the warp's shared slot
+// after setup_position.  Functions that are not inlined start from this
+// instead of a Setup passed by reference: such a Setup lives in local
+// memory, and local memory misses the small L1 left beside the shared
+// memory these kernels take (a round trip to L2 per field).
+__device__ __forceinline__ Setup reload_setup(WarpSmem* w) {
+    Setup S;
+    Pos P{w};
+    const int l = lane_id();
+    S.occ = l < 24 ? w->occ[l] : 0u;
+    S.own = l < 24 ? w->own[l] : 0u;
+    S.color = P.turn() & 1;
+    S.opp = load_row(w->st, S.color ? kOffWTop : kOffBTop, l);
+    S.n = min(28, (int)w->pref[23]);
+    S.my_cell = l < S.n ? (int)w->pcell[l] : -1;
+    S.my_h = P.height(S.my_cell);
+    S.my_top = P.top(S.my_cell);
+    S.my_ap = (w->pflag[l] >> 1) & 1;
     return S;
 }
 

@@ -49,8 +49,9 @@ __device__ __forceinline__ void hybrid_global(const uint8_t* st, float* gf) {
 // Token rows of the staged position (after setup_position).  Writes every
 // row of tf [28][27], tq/tr/tz/tm [28] (zero past the token count) and gf;
 // returns the token count (warp-uniform).
-__device__ __noinline__ int hybrid_tokens(WarpSmem* w, const Setup& S, float* tf, int32_t* tq, int32_t* tr,
-                                          int32_t* tz, uint8_t* tm, float* gf) {
+__device__ __noinline__ int hybrid_tokens(WarpSmem* w, float* tf, int32_t* tq, int32_t* tr, int32_t* tz, uint8_t* tm,
+                                          float* gf) {
+    const Setup S = reload_setup(w);
     Pos P{w};
     const int l = lane_id();
     // queen surround by colour as the token encoder reads it: queen_cell

@@ -44,20 +44,39 @@ __device__ __forceinline__ WarpSmem* warp_slot() {
     return reinterpret_cast<WarpSmem*>(smem_raw) + (threadIdx.x >> 5);
 }
 
-// The state into the warp's shared slot with asynchronous 16-byte copies:
-// all seven of a lane's copies are in flight together (a load/store loop
-// waits one memory latency per iteration).
-__device__ __forceinline__ void stage_state(WarpSmem* w, const uint8_t* src) {
-    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(w->st));
+// N16 16-byte words from global into shared memory by asynchronous copies:
+// all of a lane's copies are in flight together (a load/store loop waits one
+// memory latency per iteration).  Both addresses 16-byte aligned; the data
+// is there after stage_wait().
+template <int N16>
+__device__ __forceinline__ void stage_async(void* smem_dst, const void* src) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    const char* g = static_cast<const char*>(src);
 #pragma unroll
-    for (int k = 0; k < (kStateBytes / 16 + 31) / 32; k++) {
+    for (int k = 0; k < (N16 + 31) / 32; k++) {
         const int i = lane_id() + 32 * k;
-        if (i < kStateBytes / 16)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 16 * i), "l"(src + 16 * i)
-                         : "memory");
+        if (i < N16)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 16 * i), "l"(g + 16 * i) : "memory");
     }
+}
+
+__device__ __forceinline__ void stage_wait() {
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
+}
+
+constexpr int kState16 = kStateBytes / 16, kMoves16 = kMaxMoves * kMoveBytes / 16;
+
+__device__ __forceinline__ void stage_state(WarpSmem* w, const uint8_t* src) {
+    stage_async<kState16>(w->st, src);
+    stage_wait();
+}
+
+// state and stored move list of one position
+__device__ __forceinline__ void stage_state_moves(WarpSmem* w, const uint8_t* st, const uint8_t* mv) {
+    stage_async<kState16>(w->st, st);
+    stage_async<kMoves16>(w->mv, mv);
+    stage_wait();
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
@@ -93,7 +112,10 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
     for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
          p += nwarps) {
-        stage_state(w, states + p * kStateBytes);
+        if (GEN)
+            stage_state(w, states + p * kStateBytes);
+        else
+            stage_state_moves(w, states + p * kStateBytes, moves_in + p * (kMaxMoves * kMoveBytes));
         {
             // the warp's next position into L2 while this one is computed
             // (the feature launch waits on these loads otherwise)
@@ -110,21 +132,17 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
         if (GEN) {
             zero_moves(w);
             Setup S = setup_position(w);
-            n = gen_legal(w, S, &g_error);
+            n = gen_legal(w, &g_error);
             if (WRITE_MOVES) {
                 store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes));
                 if (lane_id() == 0) nl_out[p] = n;
             }
-            if (FEATS) features(w, S, n, feats_out + p * kFeat);
+            if (FEATS) features(w, n, feats_out + p * kFeat);
         } else {
-            const uint4* s4 = reinterpret_cast<const uint4*>(moves_in + p * (kMaxMoves * kMoveBytes));
-            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
-            for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
             n = nl_in[p];
             n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
-            __syncwarp();
             Setup S = setup_position<false, true>(w);  // no moves generated here
-            features(w, S, n, feats_out + p * kFeat);
+            features(w, n, feats_out + p * kFeat);
         }
         __syncwarp();
     }
@@ -182,14 +200,14 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             }
             __syncwarp();
             S = setup_position(w);
-            n = gen_compact(w, S, &g_error);
+            n = gen_compact(w, &g_error);
         }
         __syncthreads();
         if (ok) {
             if (SLAB) {
                 // the move list is consumed once the features are written: stage them there
                 float* f = reinterpret_cast<float*>(w->mv);
-                features(w, S, n, f);
+                features(w, n, f);
                 __syncwarp();
                 const int c = lane_id();
                 if (c < 16) {
@@ -204,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                     *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + c) * 128 + (a & 127)) * 8) = u;
                 }
             } else {
-                features(w, S, n, feats_out + a * kFeat);
+                features(w, n, feats_out + a * kFeat);
             }
         }
         __syncwarp();
@@ -242,13 +260,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
             for (int k = l; k < kFeat; k += 32) f->xs[0][k] = root_feats[p * kFeat + k];
             __syncwarp();
         } else {
-            stage_state(w, st_g);
-            const uint4* s4 = reinterpret_cast<const uint4*>(mv_g);
-            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
-            for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
-            __syncwarp();
+            stage_state_moves(w, st_g, mv_g);
             Setup S = setup_position(w);
-            features(w, S, n, f->xs[0]);
+            features(w, n, f->xs[0]);
         }
         float val[kFnnChunk], lg[kFnnChunk];
         fnn_encode_chunk(wts, dims, off, f, 1, val);
@@ -267,8 +281,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
                 }
                 __syncwarp();
                 Setup S = setup_position(w);
-                int cn = gen_compact(w, S, &g_error);
-                features(w, S, cn, f->xs[s]);
+                int cn = gen_compact(w, &g_error);
+                features(w, cn, f->xs[s]);
             }
             fnn_encode_chunk(wts, dims, off, f, ns, val);
             fnn_score_chunk(wts, dims, off, f, ns, lg);
@@ -416,13 +430,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
             for (int k = l; k < kFeat; k += 32) f->xs[0][k] = root_feats[p * kFeat + k];
             __syncwarp();
         } else {
-            stage_state(w, st_g);
-            const uint4* s4 = reinterpret_cast<const uint4*>(mv_g);
-            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
-            for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
-            __syncwarp();
+            stage_state_moves(w, st_g, mv_g);
             Setup S = setup_position(w);
-            features(w, S, n, f->xs[0]);
+            features(w, n, f->xs[0]);
         }
         float val[kFnnChunk], lg[kFnnChunk];
         const float root_value = hybrid_root(f, p, graph, glob, fw, fd, hw, hd);
@@ -453,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
                 }
                 __syncwarp();
                 Setup S = setup_position(w);
-                int cn = gen_compact(w, S, &g_error);
-                features(w, S, cn, f->xs[s]);
+                int cn = gen_compact(w, &g_error);
+                features(w, cn, f->xs[s]);
             }
             fnn_encode_chunk(fw, fd, fo, f, ns, val);
             // z = root_pre + W[:, 2E:3E] e_succ + C m
@@ -631,13 +641,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_leaf_root(
             __syncwarp();
         } else {
             int n = (int)clamp_rows(num_legal[p]);
-            stage_state(w, states + p * kStateBytes);
-            const uint4* s4 = reinterpret_cast<const uint4*>(legal_moves + p * (kMaxMoves * kMoveBytes));
-            uint4* m4 = reinterpret_cast<uint4*>(w->mv);
-            for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
-            __syncwarp();
+            stage_state_moves(w, states + p * kStateBytes, legal_moves + p * (kMaxMoves * kMoveBytes));
             Setup S = setup_position(w);
-            features(w, S, n, f->xs[0]);
+            features(w, n, f->xs[0]);
         }
         float v;
         if (HYB) {
@@ -818,13 +824,13 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_hybrid(const uint8_
         if (GEN) {
             zero_moves(w);
             Setup S = setup_position(w);
-            n = gen_legal(w, S, &g_error);
+            n = gen_legal(w, &g_error);
             store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes));
             if (l == 0) nl_out[p] = n;
-            features(w, S, n, feats_out + p * kFeat);
+            features(w, n, feats_out + p * kFeat);
             if (TOKENS) {
                 // reads only the staged state and S, which features() leaves intact
-                int t = hybrid_tokens(w, S, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,
+                int t = hybrid_tokens(w, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,
                                       o.tr + p * kTokens, o.tz + p * kTokens, o.tm + p * kTokens,
                                       o.gf + p * kGlobFeat);
                 if (l == 0) o.ntok[p] = t;
@@ -832,18 +838,16 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_hybrid(const uint8_
         } else {
             if (TOKENS) {
                 Setup S = setup_position(w);
-                int t = hybrid_tokens(w, S, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,
+                int t = hybrid_tokens(w, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,
                                       o.tr + p * kTokens, o.tz + p * kTokens, o.tm + p * kTokens,
                                       o.gf + p * kGlobFeat);
                 if (l == 0) o.ntok[p] = t;
             }
             if (MOVEF) {
-                const uint4* s4 = reinterpret_cast<const uint4*>(moves_in + p * (kMaxMoves * kMoveBytes));
-                uint4* m4 = reinterpret_cast<uint4*>(w->mv);
-                for (int i = l; i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = __ldg(s4 + i);
+                stage_async<kMoves16>(w->mv, moves_in + p * (kMaxMoves * kMoveBytes));
                 n = nl_in[p];
                 n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
-                __syncwarp();
+                stage_wait();
             }
         }
         if (MOVEF) {
@@ -1005,7 +1009,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_tac_win2(const uint8_t* __restr
         if (opp_s == 4 && cs <= opp_s) continue;
         if (opp_s == 5 && cs < opp_s) continue;
         Setup S = setup_position(w);
-        const int nr = gen_legal(w, S, &g_error);
+        const int nr = gen_legal(w, &g_error);
         for (int k = lane_id(); k < 3 * nr; k += 32) x->rep[k] = w->mv[k];
         __syncwarp();
         int r = 0;
@@ -1096,10 +1100,8 @@ __global__ void __launch_bounds__(kThreads) k_mcts_replay(const uint8_t* __restr
     const int nwarps = gridDim.x * kWarpsPerBlock;
     for (int s = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); s < total; s += nwarps) {
         if (leaf[s] < 0) continue;
-        const uint4* s4 = reinterpret_cast<const uint4*>(roots + (int64_t)(s % B) * kStateBytes);
-        uint4* d4 = reinterpret_cast<uint4*>(st);
-        for (int i = lane_id(); i < kStateBytes / 16; i += 32) d4[i] = __ldg(s4 + i);
-        __syncwarp();
+        stage_async<kState16>(st, roots + (int64_t)(s % B) * kStateBytes);
+        stage_wait();
         if (lane_id() == 0) {
             int n = plen[s];
             n = n < 0 ? 0 : (n > kTreeDepth ? kTreeDepth : n);
@@ -1110,6 +1112,7 @@ __global__ void __launch_bounds__(kThreads) k_mcts_replay(const uint8_t* __restr
         }
         __syncwarp();
         uint4* o4 = reinterpret_cast<uint4*>(leaves + (int64_t)s * kStateBytes);
+        const uint4* d4 = reinterpret_cast<const uint4*>(st);
         for (int i = lane_id(); i < kStateBytes / 16; i += 32) o4[i] = d4[i];
         __syncwarp();
     }
@@ -1240,7 +1243,7 @@ __global__ void __launch_bounds__(kThreads) k_playouts(uint64_t seed, int64_t fi
         for (int p = 1; p <= stop; p++) {
             if (w->st[kOffResult] != 0) break;
             Setup S = setup_position(w);
-            int n = gen_legal(w, S, &g_error);
+            int n = gen_legal(w, &g_error);
             int k = (int)(game_rng(seed, g, (uint64_t)p) % (uint64_t)n);
             if (lane_id() == 0) {
                 const uint16_t* m = w->mv + 3 * k;

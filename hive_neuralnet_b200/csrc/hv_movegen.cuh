@@ -374,7 +374,8 @@ __device__ __forceinline__ uint32_t placeable_types(const Pos& P, int color, boo
 // ---------------------------------------------------------------------------
 // full legal move list -> w->mv, returns the count
 // ---------------------------------------------------------------------------
-__device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err) {
+__device__ __noinline__ int gen_legal(WarpSmem* w, uint32_t* err) {
+    const Setup S = reload_setup(w);
     Pos P{w};
     int l = lane_id();
     if (P.result() != 0) return 0;
@@ -421,8 +422,11 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err
             __syncwarp();
         }
         // throws by own pillbugs and pillbug-adjacent ground mosquitoes
-        int mt = S.my_top & 15;
-        bool thr = mine && (mt == 8 || (mt == 6 && S.my_h == 1 && next_to_pillbug(w, S.my_cell)));
+        // (the piece lane's fields read again: nothing held across the calls)
+        const Setup T = reload_setup(w);
+        const int mt = T.my_top & 15;
+        const bool thr = T.my_cell >= 0 && rowbit(w->own, T.my_cell) &&
+                         (mt == 8 || (mt == 6 && T.my_h == 1 && next_to_pillbug(w, T.my_cell)));
         uint32_t throwers = __ballot_sync(kFull, thr);
 #pragma unroll 1
         while (throwers) {
@@ -455,7 +459,8 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err
 // ---------------------------------------------------------------------------
 // compact list for successor features (move_gen.cuh:1362-1563)
 // ---------------------------------------------------------------------------
-__device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* err) {
+__device__ __noinline__ int gen_compact(WarpSmem* w, uint32_t* err) {
+    const Setup S = reload_setup(w);
     Pos P{w};
     int l = lane_id();
     if (P.result() != 0) return 0;
@@ -506,8 +511,10 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, const Setup& S, uint32_t* e
         }
         __syncwarp();
     }
-    int mt = S.my_top & 15;
-    bool thr = mine && (mt == 8 || (mt == 6 && S.my_h == 1 && next_to_pillbug(w, S.my_cell)));
+    const Setup T = reload_setup(w);
+    const int mt = T.my_top & 15;
+    const bool thr = T.my_cell >= 0 && rowbit(w->own, T.my_cell) &&
+                     (mt == 8 || (mt == 6 && T.my_h == 1 && next_to_pillbug(w, T.my_cell)));
     uint32_t throwers = __ballot_sync(kFull, thr);
 #pragma unroll 1
     while (throwers && count < kMaxMoves) {
@@ -556,7 +563,8 @@ __device__ __forceinline__ int top_c(const WarpSmem* w, int c) {
     return h ? w->st[(h - 1) * kCells + c] : 0;
 }
 
-__device__ __noinline__ void features(WarpSmem* w, const Setup& S, int nmoves, float* out) {
+__device__ __noinline__ void features(WarpSmem* w, int nmoves, float* out) {
+    const Setup S = reload_setup(w);
     Pos P{w};
     int l = lane_id();
 #pragma unroll 1

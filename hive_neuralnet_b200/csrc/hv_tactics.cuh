@@ -93,7 +93,7 @@ __device__ bool immediate_win_staged(WarpSmem* w, Rebuild rebuild, uint32_t* err
     const int cell = lone_empty(w->st, player ^ 1);
     if (cell < 0) return false;
     Setup S = setup_position(w);
-    const int n = gen_legal(w, S, err);
+    const int n = gen_legal(w, err);
     for (int base = 0; base < n; base += 32) {
         const int m = base + lane_id();
         uint32_t hits = __ballot_sync(kFull, m < n && w->mv[3 * m + 2] == cell);
