@@ -383,8 +383,11 @@ __device__ __forceinline__ bool articulation_arc(WarpSmem* w, const Setup& S) {
 // articulation test that floods only from vertices whose neighbours form
 // two or more arcs of their ring (shorter, faster where the kernel is not
 // bound by branch issue; the result is the same).
-template <bool SLIDES = true, bool ARC = false>
-__device__ __forceinline__ Setup setup_position(WarpSmem* w) {
+// GIVEN_AP: the articulation flags come in as ap_mask (bit i: piece i, in
+// the piece-list order built here), from a generator launch on the same
+// position.
+template <bool SLIDES = true, bool ARC = false, bool GIVEN_AP = false>
+__device__ __forceinline__ Setup setup_position(WarpSmem* w, uint32_t ap_mask = 0u) {
     Setup S;
     Pos P{w};
     int l = lane_id();
@@ -420,7 +423,10 @@ __device__ __forceinline__ Setup setup_position(WarpSmem* w) {
     S.my_h = P.height(S.my_cell);
     S.my_top = P.top(S.my_cell);
 
-    S.my_ap = ARC ? articulation_arc(w, S) : articulation_flood(w, S);
+    if (GIVEN_AP)
+        S.my_ap = l < S.n && ((ap_mask >> l) & 1u);
+    else
+        S.my_ap = ARC ? articulation_arc(w, S) : articulation_flood(w, S);
     w->pflag[l] = ((S.my_ap && S.my_h == 1) ? 1 : 0) | (S.my_ap ? 2 : 0);
     __syncwarp();
     return S;

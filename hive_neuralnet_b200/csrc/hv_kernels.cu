@@ -84,16 +84,28 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-__device__ __forceinline__ void zero_moves(WarpSmem* w) {
-    uint4* m4 = reinterpret_cast<uint4*>(w->mv);
-    for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) m4[i] = make_uint4(0, 0, 0, 0);
-    __syncwarp();
-}
-
-__device__ __forceinline__ void store_moves(const WarpSmem* w, uint8_t* dst) {
+// The first n moves of the shared list out to a zero-padded global row; the
+// shared list past n is never read (no zeroing pass over it).
+__device__ __forceinline__ void store_moves(const WarpSmem* w, uint8_t* dst, int n) {
     const uint4* m4 = reinterpret_cast<const uint4*>(w->mv);
     uint4* d4 = reinterpret_cast<uint4*>(dst);
-    for (int i = lane_id(); i < kMaxMoves * kMoveBytes / 16; i += 32) d4[i] = m4[i];
+    const int bytes = n * kMoveBytes;
+    for (int i = lane_id(); i < kMoves16; i += 32) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        const int valid = bytes - 16 * i;
+        if (valid > 0) {
+            v = m4[i];
+            if (valid < 16) {
+                uint32_t* u = &v.x;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int keep = valid - 4 * j;  // bytes of word j inside the list
+                    u[j] = keep >= 4 ? u[j] : (keep <= 0 ? 0u : (u[j] & ((1u << (8 * keep)) - 1u)));
+                }
+            }
+        }
+        d4[i] = v;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -101,7 +113,11 @@ __device__ __forceinline__ void store_moves(const WarpSmem* w, uint8_t* dst) {
 // (game_logic.cu:63-91 generate_legal_moves[_and_fnn_features]_kernel,
 //  fnn_features.cuh:334-350 extract_fnn_features_kernel)
 // ---------------------------------------------------------------------------
-template <bool GEN, bool WRITE_MOVES, bool FEATS>
+// AP_LINK (the two launches of hv_generate_legal_moves_and_fnn_features):
+// the generator leaves each position's articulation mask in the first word
+// of its feature row, and the feature launch takes it from there before it
+// writes the row, instead of computing the articulation points again.
+template <bool GEN, bool WRITE_MOVES, bool FEATS, bool AP_LINK = false>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t* __restrict__ states,
                                                    const uint8_t* __restrict__ moves_in,
                                                    const int32_t* __restrict__ nl_in, int64_t batch,
@@ -130,18 +146,25 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
         }
         int n;
         if (GEN) {
-            zero_moves(w);
             Setup S = setup_position(w);
+            if (AP_LINK) {
+                const uint32_t apm = __ballot_sync(kFull, S.my_ap);
+                if (lane_id() == 0) reinterpret_cast<uint32_t*>(feats_out)[p * kFeat] = apm;
+            }
             n = gen_legal(w, &g_error);
             if (WRITE_MOVES) {
-                store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes));
+                store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes), n);
                 if (lane_id() == 0) nl_out[p] = n;
             }
             if (FEATS) features(w, n, feats_out + p * kFeat);
         } else {
             n = nl_in[p];
             n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
-            Setup S = setup_position<false, true>(w);  // no moves generated here
+            // no moves generated here
+            if (AP_LINK)
+                setup_position<false, true, true>(w, reinterpret_cast<const uint32_t*>(feats_out)[p * kFeat]);
+            else
+                setup_position<false, true>(w);
             features(w, n, feats_out + p * kFeat);
         }
         __syncwarp();
@@ -822,10 +845,9 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_hybrid(const uint8_
         stage_state(w, states + p * kStateBytes);
         int n = 0;
         if (GEN) {
-            zero_moves(w);
             Setup S = setup_position(w);
             n = gen_legal(w, &g_error);
-            store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes));
+            store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes), n);
             if (l == 0) nl_out[p] = n;
             features(w, n, feats_out + p * kFeat);
             if (TOKENS) {
@@ -1375,21 +1397,21 @@ static inline int launch_status() {
     return e == cudaSuccess ? HV_OK : HV_ECUDA;
 }
 
-template <bool GEN, bool WM, bool FE>
+template <bool GEN, bool WM, bool FE, bool AP_LINK = false>
 static int launch_root(const uint8_t* states, const uint8_t* mi, const int32_t* nli, int64_t batch,
                        uint8_t* mo, int32_t* nlo, float* fo, void* stream) {
     if (batch < 0) return HV_EINVAL;
     if (batch == 0) return HV_OK;
     if (!states || !aligned16(states)) return HV_EINVAL;
     if (WM && (!mo || !nlo || !aligned16(mo))) return HV_EINVAL;
-    if (FE && !fo) return HV_EINVAL;
+    if ((FE || AP_LINK) && !fo) return HV_EINVAL;
     if (!GEN && (!mi || !nli || !aligned16(mi))) return HV_EINVAL;
     size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
     int grid = 0;
-    int rc = grid_for(k_root<GEN, WM, FE>, batch, smem, &grid);
+    int rc = grid_for(k_root<GEN, WM, FE, AP_LINK>, batch, smem, &grid);
     if (rc) return rc;
-    k_root<GEN, WM, FE><<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, mi, nli, batch, mo,
-                                                                        nlo, fo);
+    k_root<GEN, WM, FE, AP_LINK><<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, mi, nli, batch, mo,
+                                                                                 nlo, fo);
     return launch_status();
 }
 
@@ -1590,9 +1612,12 @@ int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves
 int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
                                              int32_t* num_legal, float* features, void* stream) {
     if (batch > 0 && !features) return HV_EINVAL;
-    int rc = launch_root<true, true, false>(states, nullptr, nullptr, batch, moves, num_legal, nullptr, stream);
+    // the feature rows carry the generator's articulation masks between the launches
+    int rc = launch_root<true, true, false, true>(states, nullptr, nullptr, batch, moves, num_legal, features,
+                                                  stream);
     if (rc) return rc;
-    return launch_root<false, false, true>(states, moves, num_legal, batch, nullptr, nullptr, features, stream);
+    return launch_root<false, false, true, true>(states, moves, num_legal, batch, nullptr, nullptr, features,
+                                                 stream);
 }
 
 int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev_states, void* stream) {
