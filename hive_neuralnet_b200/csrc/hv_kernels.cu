@@ -216,11 +216,15 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
         Setup S;
         int n = 0;
         if (ok) {
-            stage_state(w, states + root * kStateBytes);
+            stage_async<kState16>(w->st, states + root * kStateBytes);
+            // the move's three 16-bit words load while the state copies are in flight
+            uint32_t m0 = 0, m1 = 0, m2 = 0;
             if (lane_id() == 0) {
-                const uint8_t* m = legal_moves + (root * kMaxMoves + mi) * kMoveBytes;
-                st_apply(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+                const uint16_t* m = reinterpret_cast<const uint16_t*>(legal_moves + (root * kMaxMoves + mi) * kMoveBytes);
+                m0 = __ldg(m), m1 = __ldg(m + 1), m2 = __ldg(m + 2);
             }
+            stage_wait();
+            if (lane_id() == 0) st_apply(w->st, m0 & 255, m0 >> 8, m1, m2);
             __syncwarp();
             S = setup_position(w);
             n = gen_compact(w, &g_error);
