@@ -22,6 +22,7 @@
 //     reference (move_gen.cuh:82-131) becomes one shared-memory bit test.
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 
 namespace hv {
@@ -88,6 +89,7 @@ struct __align__(16) WarpSmem {
         };
     };
 };
+static_assert(offsetof(WarpSmem, acc) % 16 == 0, "feature accumulators are cleared with 16-byte stores");
 
 // ---------------------------------------------------------------------------
 // small helpers

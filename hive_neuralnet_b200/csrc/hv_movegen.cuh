@@ -524,19 +524,23 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, uint32_t* err) {
         uint32_t tm, dm;
         throw_sets(w, pb, tm, dm);
         if (dm == 0u) continue;
-#pragma unroll 1
-        while (tm) {  // summarize_pillbug_throws_for_fnn, move_gen.cuh:1379-1410
-            int dt = __ffs(tm) - 1;
-            tm &= tm - 1;
-            int target = nbr(pb, dt);
-            int tt = P.top(target);
-            uint32_t bit = 1u << (((tt & 15) - 1) * 2 + ((tt >> 4) & 1));
-            if (P.height(target) > 0 && !(seen & bit) && count < kMaxMoves) {
-                seen |= bit;
-                if (l == 0) put_move(w, count, 1, tt & 15, p_to_c(target), 0);
-                count++;
-            }
-        }
+        // summarize_pillbug_throws_for_fnn, move_gen.cuh:1379-1410: targets in
+        // direction order, one entry per (type, owner) not seen yet.  Lane d
+        // takes target d; of the targets sharing a new (type, owner) the
+        // lowest direction is kept, as the sequential scan keeps the first.
+        const int target = (l < 6 && ((tm >> l) & 1u)) ? nbr(pb, l) : -1;
+        const int tt = target >= 0 ? P.top(target) : 0;
+        const bool live = target >= 0 && P.height(target) > 0;
+        const uint32_t bit = live ? 1u << (((tt & 15) - 1) * 2 + ((tt >> 4) & 1)) : 0u;
+        const bool fresh = live && !(seen & bit);
+        const uint32_t grp = __match_any_sync(kFull, fresh ? (int)bit : -1);
+        const bool keep = fresh && (grp & lanemask_lt()) == 0u;
+        const uint32_t kb = __ballot_sync(kFull, keep);
+        const int pos = count + __popc(kb & lanemask_lt());
+        if (keep && pos < kMaxMoves) put_move(w, pos, 1, tt & 15, p_to_c(target), 0);
+        // entries past the list's end are dropped, and so are their flags
+        seen |= __reduce_or_sync(kFull, (keep && pos < kMaxMoves) ? bit : 0u);
+        count = min(kMaxMoves, count + __popc(kb));
         __syncwarp();
     }
     if (count == 0) {
@@ -567,11 +571,14 @@ __device__ __noinline__ void features(WarpSmem* w, int nmoves, float* out) {
     const Setup S = reload_setup(w);
     Pos P{w};
     int l = lane_id();
-#pragma unroll 1
-    for (int i = l; i < A_N; i += 32) w->acc[i] = 0;
-#pragma unroll 1
-    for (int i = l; i < 16 * 17; i += 32) w->bm[i] = 0u;
-    if (l < 17) w->pl[l] = 0u;
+    {
+        // accumulators and source-cell sets are contiguous: 16-byte stores
+        static_assert(sizeof(w->acc) % 16 == 0 && (sizeof(w->acc) + sizeof(w->bm)) % 16 == 0, "acc/bm layout");
+        uint4* z = reinterpret_cast<uint4*>(w->acc);
+#pragma unroll
+        for (int i = l; i < (int)(sizeof(w->acc) + sizeof(w->bm)) / 16; i += 32) z[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (l < 17) w->pl[l] = 0u;
+    }
     __syncwarp();
     const int turn = P.turn(), cur = turn & 1, stun = P.stunned();
     const int q0 = P.queen_cell(0), q1 = P.queen_cell(1);
@@ -645,10 +652,14 @@ __device__ __noinline__ void features(WarpSmem* w, int nmoves, float* out) {
         }
     }
     __syncwarp();
-#pragma unroll 1
-    for (int i = l; i < 16 * 17 + 17; i += 32) {
-        int c = __popc(i < 16 * 17 ? w->bm[i] : w->pl[i - 16 * 17]);
-        if (c) atomicAdd(&w->acc[i < 16 * 17 ? A_SRC + i / 17 : A_PLACE], c);
+    // lane t < 16 counts the source cells of (type, owner) t, lane 16 the
+    // placement cells: 17 words each (stride 17: no bank conflicts)
+    if (l <= 16) {
+        const uint32_t* set = l < 16 ? &w->bm[l * 17] : w->pl;
+        int c = 0;
+#pragma unroll
+        for (int k = 0; k < 17; k++) c += __popc(set[k]);
+        w->acc[l < 16 ? A_SRC + l : A_PLACE] = c;
     }
     if (l == 0) {
         w->acc[A_SURR] = __popc(s0);
