@@ -218,14 +218,10 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
         if (ok) {
             stage_async<kState16>(w->st, states + root * kStateBytes);
             // the move's three 16-bit words load while the state copies are in flight
-            uint32_t m0 = 0, m1 = 0, m2 = 0;
-            if (lane_id() == 0) {
-                const uint16_t* m = reinterpret_cast<const uint16_t*>(legal_moves + (root * kMaxMoves + mi) * kMoveBytes);
-                m0 = __ldg(m), m1 = __ldg(m + 1), m2 = __ldg(m + 2);
-            }
+            const uint16_t* m = reinterpret_cast<const uint16_t*>(legal_moves + (root * kMaxMoves + mi) * kMoveBytes);
+            const uint32_t m0 = __ldg(m), m1 = __ldg(m + 1), m2 = __ldg(m + 2);
             stage_wait();
-            if (lane_id() == 0) st_apply(w->st, m0 & 255, m0 >> 8, m1, m2);
-            __syncwarp();
+            st_apply_warp(w->st, m0 & 255, m0 >> 8, m1, m2);
             S = setup_position(w);
             n = gen_compact(w, &g_error);
         }
@@ -302,11 +298,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
 #pragma unroll 1
             for (int s = 0; s < ns; s++) {
                 stage_state(w, st_g);
-                if (l == 0) {
+                {
                     const uint8_t* m = mv_g + (base + s) * kMoveBytes;
-                    st_apply(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+                    st_apply_warp(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
                 }
-                __syncwarp();
                 Setup S = setup_position(w);
                 int cn = gen_compact(w, &g_error);
                 features(w, cn, f->xs[s]);
@@ -484,11 +479,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
 #pragma unroll 1
             for (int s = 0; s < ns; s++) {
                 stage_state(w, st_g);
-                if (l == 0) {
+                {
                     const uint8_t* m = mv_g + (base + s) * kMoveBytes;
-                    st_apply(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
+                    st_apply_warp(w->st, m[0], m[1], m[2] | (m[3] << 8), m[4] | (m[5] << 8));
                 }
-                __syncwarp();
                 Setup S = setup_position(w);
                 int cn = gen_compact(w, &g_error);
                 features(w, cn, f->xs[s]);
@@ -778,11 +772,10 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_child_probe(
         }
         for (int m = 0; m < n; m++) {
             stage_state(w, states + p * kStateBytes);
-            if (l == 0) {
+            {
                 const uint8_t* x = legal + (p * kMaxMoves + m) * kMoveBytes;
-                st_apply(w->st, x[0], x[1], x[2] | (x[3] << 8), x[4] | (x[5] << 8));
+                st_apply_warp(w->st, x[0], x[1], x[2] | (x[3] << 8), x[4] | (x[5] << 8));
             }
-            __syncwarp();
             Pos P{w};
             const int color = P.turn() & 1;
             // occupied (height > 0) neighbours of the queen cell field, as
@@ -1271,11 +1264,10 @@ __global__ void __launch_bounds__(kThreads) k_playouts(uint64_t seed, int64_t fi
             Setup S = setup_position(w);
             int n = gen_legal(w, &g_error);
             int k = (int)(game_rng(seed, g, (uint64_t)p) % (uint64_t)n);
-            if (lane_id() == 0) {
+            {
                 const uint16_t* m = w->mv + 3 * k;
-                st_apply(w->st, m[0] & 255, m[0] >> 8, m[1], m[2]);
+                st_apply_warp(w->st, m[0] & 255, m[0] >> 8, m[1], m[2]);
             }
-            __syncwarp();
         }
         uint4* o4 = reinterpret_cast<uint4*>(out + i * kStateBytes);
         for (int k = lane_id(); k < kStateBytes / 16; k += 32) o4[k] = d4[k];

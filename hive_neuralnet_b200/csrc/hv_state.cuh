@@ -46,7 +46,8 @@ __device__ __forceinline__ bool st_queen_surrounded(const uint8_t* st, int color
 
 // apply_move (hive_state.cuh:497-517) including its silent refusals: a full
 // destination stack leaves the board unchanged but still advances the turn.
-__device__ inline void st_apply(uint8_t* st, int type, int pt, int from, int to) {
+// This part moves the piece and advances turn and stun; the result follows.
+__device__ inline void st_apply_board(uint8_t* st, int type, int pt, int from, int to) {
     int turn = st_u16(st, kOffTurn);
     int color = turn & 1;
     int stun = st_u16(st, kOffStun);
@@ -95,10 +96,38 @@ __device__ inline void st_apply(uint8_t* st, int type, int pt, int from, int to)
     }
     st_put_u16(st, kOffStun, stun);
     st_put_u16(st, kOffTurn, turn + 1);
-    bool w = st_queen_surrounded(st, 0), b = st_queen_surrounded(st, 1);
+}
+
+__device__ __forceinline__ void st_set_result(uint8_t* st, bool w, bool b) {
     if (w && b) st[kOffResult] = 3;
     else if (w) st[kOffResult] = 2;
     else if (b) st[kOffResult] = 1;
+}
+
+// one thread
+__device__ inline void st_apply(uint8_t* st, int type, int pt, int from, int to) {
+    st_apply_board(st, type, pt, from, to);
+    st_set_result(st, st_queen_surrounded(st, 0), st_queen_surrounded(st, 1));
+}
+
+// one warp (all lanes, same arguments): lane 0 moves the piece, then lanes
+// 0..11 test the six neighbours of both queens at once
+__device__ inline void st_apply_warp(uint8_t* st, int type, int pt, int from, int to) {
+    const int l = threadIdx.x & 31;
+    if (l == 0) st_apply_board(st, type, pt, from, to);
+    __syncwarp();
+    bool occ = false;
+    if (l < 12) {
+        const int color = l >= 6, d = l - 6 * color;
+        const int q = st_u16(st, kOffQCell + 2 * color);
+        if (((st[kOffQPlaced] >> color) & 1) && q < kCells) {
+            const int nb = nbr(c_to_p(q), d);
+            occ = nb >= 0 && st_bb_get(st, kOffOcc, p_to_c(nb));
+        }
+    }
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, occ);
+    if (l == 0) st_set_result(st, (m & 63u) == 63u, ((m >> 6) & 63u) == 63u);
+    __syncwarp();
 }
 
 // initial state (hive_state.cuh:454-492) into a zeroed buffer; one thread
