@@ -23,6 +23,7 @@
 #include "hv_trunk.cuh"
 #include "hv_mlp.cuh"
 #include "hv_mlp_tc.cuh"
+#include "hv_mlp32.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -175,17 +176,22 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
 // successor features: apply one root move, compact list, features
 // (game_logic.cu:182-229 fnn_successor_features_kernel)
 // ---------------------------------------------------------------------------
-// SLAB: rows go out as fp16 in the K-major slab layout of 128-row tiles that
-// the hybrid's tensor-core row network copies straight into its A operand
-// (row r: tile r / 128, chunk c of 8 features at ((tile * 16 + c) * 128 +
-// r % 128) * 8 halves, features 122..127 zero); otherwise fp32 [rows][122].
-template <bool SLAB>
+// OUT selects the row format: kRowsF32 = fp32 [rows][122]; kSlabF16 = fp16
+// in the K-major slab layout of 128-row tiles that the hybrid's tensor-core
+// row network copies straight into its A operand (row r: tile r / 128, chunk
+// c of 8 features at ((tile * 16 + c) * 128 + r % 128) * 8 halves, features
+// 122..127 zero); kSlabF32 = fp32 tiles of 128 rows in 4-feature chunks
+// (chunk c of row r at ((tile * 32 + c) * 128 + r % 128) * 4 floats, features
+// 122..127 zero) for the FNN row network.
+enum : int { kRowsF32 = 0, kSlabF16 = 1, kSlabF32 = 2 };
+template <int OUT>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
     const int64_t* __restrict__ action_to_root, const int64_t* __restrict__ move_indices,
     int64_t num_actions, void* __restrict__ out, const int64_t* __restrict__ n_actual) {
     float* feats_out = static_cast<float*>(out);
     __half* slab = static_cast<__half*>(out);
+    constexpr bool SLAB = OUT != kRowsF32;
     WarpSmem* w = warp_slot();
     if (n_actual) num_actions = min(num_actions, *n_actual);  // row pipeline: rows actually filled
     // The block's warps take consecutive rows and cross one block barrier
@@ -202,10 +208,13 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             mi = move_indices[a];
             if (root < 0 || root >= num_states || mi < 0 || mi >= kMaxMoves) {
                 // out-of-range request: zero row, flag it, touch nothing else
-                if (SLAB) {
+                if (OUT == kSlabF16) {
                     if (lane_id() < 16)
                         *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + lane_id()) * 128 + (a & 127)) * 8) =
                             make_uint4(0, 0, 0, 0);
+                } else if (OUT == kSlabF32) {
+                    *reinterpret_cast<float4*>(feats_out + (((a >> 7) * 32 + lane_id()) * 128 + (a & 127)) * 4) =
+                        make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 } else {
                     for (int k = lane_id(); k < kFeat; k += 32) feats_out[a * kFeat + k] = 0.0f;
                 }
@@ -233,7 +242,13 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                 features(w, n, f);
                 __syncwarp();
                 const int c = lane_id();
-                if (c < 16) {
+                if (OUT == kSlabF32) {
+                    float v[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) v[i] = 4 * c + i < kFeat ? f[4 * c + i] : 0.0f;
+                    *reinterpret_cast<float4*>(feats_out + (((a >> 7) * 32 + c) * 128 + (a & 127)) * 4) =
+                        make_float4(v[0], v[1], v[2], v[3]);
+                } else if (c < 16) {
                     float v[8];
 #pragma unroll
                     for (int i = 0; i < 8; i++) v[i] = 8 * c + i < kFeat ? f[8 * c + i] : 0.0f;
@@ -1434,7 +1449,7 @@ struct RowWorkspace {
     int64_t* row_start;  // [count + 1]
     int64_t* atr;        // [rows]
     int64_t* mi;         // [rows]
-    float* x;            // [rows][122] (FNN)
+    float* x;            // FNN: fp32 slab tiles of the successor features, 512 bytes per row
     __half* xh;          // hybrid: fp16 slab tiles of the successor features, 256 bytes per row
     __half* mfh;         // hybrid: fp16 slab tiles of the move features, 64 bytes per row
     float* root_pre;     // [count][64]
@@ -1454,9 +1469,10 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
     k_row_index<<<grid, kThreads, 0, s>>>(num_legal, count, w.row_start, rows, w.atr, w.mi);
     if (rows > 0) {
         size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
-        rc = grid_for(k_successor_features<HYB>, rows, smem, &grid);
+        constexpr int OUT = HYB ? kSlabF16 : kSlabF32;
+        rc = grid_for(k_successor_features<OUT>, rows, smem, &grid);
         if (rc) return rc;
-        k_successor_features<HYB><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows,
+        k_successor_features<OUT><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows,
                                                               HYB ? static_cast<void*>(w.xh) : static_cast<void*>(w.x),
                                                               w.row_start + count);
         if (HYB) {
@@ -1505,12 +1521,15 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
                                                      w.row_start + count, err);
       }
     } else if (rows > 0) {
-        const size_t smem = sizeof(MlpSmem<HYB>);
-        const int64_t tiles = (rows + kMlpRows - 1) / kMlpRows;
-        rc = grid_for(k_mlp_rows<HYB>, tiles * kWarpsPerBlock, smem, &grid);
+        // the FNN network over the fp32 slab tiles, one CTA per SM (shared memory)
+        uint32_t* err = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
+        const size_t smem = sizeof(F32Smem);
+        const int64_t tiles = (rows + kF32Rows - 1) / kF32Rows;
+        rc = grid_for(k_fnn_rows, tiles * kWarpsPerBlock, smem, &grid);
         if (rc) return rc;
-        k_mlp_rows<HYB><<<grid, kMlpThreads, smem, s>>>(w.x, nullptr, w.atr, w.mi, rows, w.root_pre, fw, fd, hw, hd,
-                                                        lg, child_q, w.row_start + count);
+        k_fnn_rows<<<grid, kF32Threads, smem, s>>>(w.x, w.atr, w.mi, rows, w.root_pre, fw, fd, lg, child_q,
+                                                   w.row_start + count, err);
     }
     rc = grid_for(k_leaf_softmax<HYB>, count, 0, &grid);
     if (rc) return rc;
@@ -1663,9 +1682,9 @@ int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const u
         return HV_EINVAL;
     size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
     int grid = 0;
-    int rc = grid_for(k_successor_features<false>, num_actions, smem, &grid);
+    int rc = grid_for(k_successor_features<kRowsF32>, num_actions, smem, &grid);
     if (rc) return rc;
-    k_successor_features<false><<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+    k_successor_features<kRowsF32><<<grid, kThreads, smem, (cudaStream_t)stream>>>(
         states, num_states, legal_moves, action_to_root, move_indices, num_actions, features, nullptr);
     return launch_status();
 }
@@ -1869,7 +1888,7 @@ static size_t row_workspace_layout(int64_t count, int64_t rows, bool hybrid, boo
     uint8_t* at = take(r * sizeof(int64_t));
     uint8_t* mi = take(r * sizeof(int64_t));
     const size_t rt = (r + 127) / 128 * 128;  // whole 128-row tiles
-    uint8_t* x = hybrid ? nullptr : take(r * kFeat * sizeof(float));
+    uint8_t* x = hybrid ? nullptr : take(rt * 128 * sizeof(float));  // fp32 slab tiles
     uint8_t* xh = hybrid ? take(rt * 128 * 2) : nullptr;
     uint8_t* mf = hybrid ? take(rt * 32 * 2) : nullptr;
     uint8_t* rp = take(n * 64 * sizeof(float));
