@@ -180,9 +180,9 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
 // in the K-major slab layout of 128-row tiles that the hybrid's tensor-core
 // row network copies straight into its A operand (row r: tile r / 128, chunk
 // c of 8 features at ((tile * 16 + c) * 128 + r % 128) * 8 halves, features
-// 122..127 zero); kSlabF32 = fp32 tiles of 128 rows in 4-feature chunks
-// (chunk c of row r at ((tile * 32 + c) * 128 + r % 128) * 4 floats, features
-// 122..127 zero) for the FNN row network.
+// 122..127 zero); kSlabF32 = fp32 tiles of kF32Rows (64) rows in 4-feature
+// chunks (chunk c of row r at ((tile * 32 + c) * 64 + r % 64) * 4 floats,
+// features 122..127 zero) for the FNN row network.
 enum : int { kRowsF32 = 0, kSlabF16 = 1, kSlabF32 = 2 };
 template <int OUT>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
@@ -213,8 +213,8 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                         *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + lane_id()) * 128 + (a & 127)) * 8) =
                             make_uint4(0, 0, 0, 0);
                 } else if (OUT == kSlabF32) {
-                    *reinterpret_cast<float4*>(feats_out + (((a >> 7) * 32 + lane_id()) * 128 + (a & 127)) * 4) =
-                        make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    *reinterpret_cast<float4*>(feats_out + (((a / kF32Rows) * 32 + lane_id()) * kF32Rows +
+                                                            a % kF32Rows) * 4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 } else {
                     for (int k = lane_id(); k < kFeat; k += 32) feats_out[a * kFeat + k] = 0.0f;
                 }
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                     float v[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) v[i] = 4 * c + i < kFeat ? f[4 * c + i] : 0.0f;
-                    *reinterpret_cast<float4*>(feats_out + (((a >> 7) * 32 + c) * 128 + (a & 127)) * 4) =
+                    *reinterpret_cast<float4*>(feats_out + (((a / kF32Rows) * 32 + c) * kF32Rows + a % kF32Rows) * 4) =
                         make_float4(v[0], v[1], v[2], v[3]);
                 } else if (c < 16) {
                     float v[8];
@@ -1525,8 +1525,8 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         uint32_t* err = nullptr;
         if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
         const size_t smem = sizeof(F32Smem);
-        const int64_t tiles = (rows + kF32Rows - 1) / kF32Rows;
-        rc = grid_for(k_fnn_rows, tiles * kWarpsPerBlock, smem, &grid);
+        const int64_t tiles = (rows + kF32Rows - 1) / kF32Rows, ctas = (tiles + kF32Groups - 1) / kF32Groups;
+        rc = grid_for(k_fnn_rows, ctas * kWarpsPerBlock, smem, &grid);
         if (rc) return rc;
         k_fnn_rows<<<grid, kF32Threads, smem, s>>>(w.x, w.atr, w.mi, rows, w.root_pre, fw, fd, lg, child_q,
                                                    w.row_start + count, err);

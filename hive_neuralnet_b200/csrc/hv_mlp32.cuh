@@ -4,15 +4,17 @@
 //   h = LayerNorm(sigmoid(X W1 + b1)),  e = h W2 + b2,
 //   child_q = -tanh(wv . e + bv),
 //   logit   = a2 . sigmoid(root_pre[leaf] + A1s e) + a2b
-// The rows arrive as fp32 tiles of 128 rows in 4-feature chunks (written so
-// by k_successor_features<kSlabF32>): tile t is [32 chunks][128 rows][4]
-// floats, 64 KB, copied whole into shared memory by one bulk copy while the
-// CTA computes the previous tile.  A CTA of 512 threads computes 128 rows x
-// 64 neurons per layer; a thread holds 4 rows (ty + 32 i) x 4 neurons (4 tx):
+// The rows arrive as fp32 tiles of 64 rows in 4-feature chunks (written so
+// by k_successor_features<kSlabF32>): tile t is [32 chunks][64 rows][4]
+// floats, 32 KB, copied whole into shared memory by one bulk copy while the
+// previous tile computes.  A CTA (one per SM, the weights resident in shared
+// memory) holds two independent groups of 8 warps with their own tiles,
+// copy barriers and named barrier, so one group's epilogues (sigmoid,
+// LayerNorm, tanh) overlap the other's FMAs.  A group computes 64 rows x 64
+// neurons per layer; a thread holds 4 rows (ty + 16 i) x 4 neurons (4 tx):
 // per 4-feature chunk it loads 4 row vectors and 4 weight vectors for 64
 // FMAs (the row-major kernel, k_mlp_rows, loads 5 values per 16 FMAs and is
-// bound by shared-memory bandwidth).  Sixteen warps per SM: with eight, the
-// FMA pipe waited on shared-memory and barrier latencies.  Every output is the same fmaf chain as
+// bound by shared-memory bandwidth).  Every output is the same fmaf chain as
 // in k_mlp_rows: from the bias, k ascending; the features past 122 and the
 // neurons past H are zero and add exact zeros.  fp32 throughout (checked at
 // 1e-5 relative).
@@ -25,20 +27,28 @@
 
 namespace hv {
 
-constexpr int kF32Rows = 128, kF32Threads = 512, kF32Chunks = 32;
-constexpr int kF32Ty = kF32Threads / 16, kF32Rpt = kF32Rows / kF32Ty;  // row groups; rows per thread
-constexpr uint32_t kF32TileBytes = kF32Chunks * kF32Rows * 4 * sizeof(float);  // 64 KB
+constexpr int kF32Rows = 64, kF32Groups = 2, kF32GroupThreads = 256, kF32Chunks = 32;
+constexpr int kF32Threads = kF32Groups * kF32GroupThreads;
+constexpr int kF32Ty = kF32GroupThreads / 16, kF32Rpt = kF32Rows / kF32Ty;  // row groups; rows per thread
+constexpr uint32_t kF32TileBytes = kF32Chunks * kF32Rows * 4 * sizeof(float);  // 32 KB
 constexpr uint32_t kErrF32Wait = 8u;
 
 struct __align__(128) F32Smem {
-    float x[2][kF32Chunks][kF32Rows][4];  // feature tiles (double-buffered); h, then e, overwrite the current one
+    float x[kF32Groups][2][kF32Chunks][kF32Rows][4];  // per group: feature tiles (double-buffered); h, then e,
+                                                      // overwrite the current one
     float w1[4 * 31][64];                 // W1^T over features 0..123 (122, 123 and neurons >= H zero)
     float w2[64][64];                     // W2^T, rows >= H and columns >= E zero
     float a1[64][64];                     // successor block of the action layer, rows >= E and columns >= A zero
     float b1[64], g1[64], be1[64], b2[64], wv[64], a2[64];
     float bv, a2b;
-    uint64_t bar[2];
+    uint64_t bar[kF32Groups][2];
+    int fail[kF32Groups];
 };
+
+// barrier of one group's 256 threads (named barrier 1 + g)
+__device__ __forceinline__ void f32_group_sync(int g) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kF32GroupThreads) : "memory");
+}
 
 // 16 lanes (tx) share a row
 __device__ __forceinline__ float f32_row_sum16(float v) {
@@ -88,21 +98,28 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
                                                              uint32_t* __restrict__ err_word) {
     extern __shared__ __align__(128) uint8_t f32_raw[];
     F32Smem* s = reinterpret_cast<F32Smem*>(f32_raw);
-    const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+    const int t = threadIdx.x, g = t / kF32GroupThreads, gt = t - g * kF32GroupThreads;
+    const int tx = gt & 15, ty = gt >> 4;
     const int H = fd.H, E = fd.E, A = fd.A;
     const float invH = 1.0f / (float)H;
     const FnnOffsets fo = fnn_offsets(fd);
     if (n_actual) N = min(N, *n_actual);  // rows actually filled
     const int64_t tiles = (N + kF32Rows - 1) / kF32Rows;
 
+    // group g takes tiles first, first + stride, ...
+    const int64_t first = (int64_t)blockIdx.x * kF32Groups + g, stride = (int64_t)gridDim.x * kF32Groups;
     if (t == 0) {
-        mbar_init(&s->bar[0], 1);
-        mbar_init(&s->bar[1], 1);
-        fence_mbar_init();
-        if ((int64_t)blockIdx.x < tiles) {
-            mbar_expect_tx(&s->bar[0], kF32TileBytes);
-            bulk_g2s(&s->x[0][0][0][0], X + (int64_t)blockIdx.x * (kF32TileBytes / 4), kF32TileBytes, &s->bar[0]);
+        for (int i = 0; i < kF32Groups; i++) {
+            mbar_init(&s->bar[i][0], 1);
+            mbar_init(&s->bar[i][1], 1);
+            s->fail[i] = 0;
         }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (gt == 0 && first < tiles) {
+        mbar_expect_tx(&s->bar[g][0], kF32TileBytes);
+        bulk_g2s(&s->x[g][0][0][0][0], X + first * (kF32TileBytes / 4), kF32TileBytes, &s->bar[g][0]);
     }
     for (int i = t; i < 4 * 31 * 64; i += kF32Threads) {
         const int k = i >> 6, o = i & 63;
@@ -127,28 +144,31 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
     }
     __syncthreads();
 
-    // bit b: wait parity of buffer b; copies in flight per buffer (thread 0's view)
-    uint32_t phases = 0u, pend = (int64_t)blockIdx.x < tiles ? 1u : 0u;
+    // bit b: wait parity of the group's buffer b; copies in flight per buffer
+    // (the group's thread 0's view)
+    uint32_t phases = 0u, pend = first < tiles ? 1u : 0u;
     bool failed = false;
     int buf = 0;
-    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, buf ^= 1) {
+    for (int64_t tile = first; tile < tiles; tile += stride, buf ^= 1) {
         // the next tile into the other buffer (its last reader finished at
-        // the barrier that ended the previous tile)
-        const int64_t nt = tile + gridDim.x;
-        if (t == 0 && nt < tiles) {
+        // the group barrier that ended the previous tile)
+        const int64_t nt = tile + stride;
+        if (gt == 0 && nt < tiles) {
             fence_proxy_async();
-            mbar_expect_tx(&s->bar[buf ^ 1], kF32TileBytes);
-            bulk_g2s(&s->x[buf ^ 1][0][0][0], X + nt * (kF32TileBytes / 4), kF32TileBytes, &s->bar[buf ^ 1]);
+            mbar_expect_tx(&s->bar[g][buf ^ 1], kF32TileBytes);
+            bulk_g2s(&s->x[g][buf ^ 1][0][0][0], X + nt * (kF32TileBytes / 4), kF32TileBytes, &s->bar[g][buf ^ 1]);
             pend |= 2u >> buf;
         }
-        const bool ok = mbar_wait(&s->bar[buf], (phases >> buf) & 1u);  // every thread, bounded
-        if (__syncthreads_or(!ok)) {
+        const bool ok = mbar_wait(&s->bar[g][buf], (phases >> buf) & 1u);  // every thread, bounded
+        if (!ok) s->fail[g] = 1;
+        f32_group_sync(g);
+        if (s->fail[g]) {
             failed = true;
             break;
         }
         phases ^= 1u << buf;
         pend &= ~(1u << buf);
-        float (*xb)[kF32Rows][4] = s->x[buf];
+        float (*xb)[kF32Rows][4] = s->x[g][buf];
         const int64_t r0 = tile * kF32Rows;
         const int nrows = (int)min((int64_t)kF32Rows, N - r0);
         float acc[kF32Rpt][4];
@@ -170,7 +190,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[i][j] = s->b1[4 * tx + j];
         f32_chunks<31, false>(xb, s->w1, tx, ty, acc);
-        __syncthreads();  // the feature tile is consumed: h overwrites it
+        f32_group_sync(g);  // the feature tile is consumed: h overwrites it
 #pragma unroll
         for (int i = 0; i < kF32Rpt; i++) {
             float a[4], sum = 0.0f;
@@ -194,7 +214,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
             *reinterpret_cast<float4*>(&xb[tx][(ty + kF32Ty * i) ^ (tx & 7)][0]) =
                 make_float4(hv4[0], hv4[1], hv4[2], hv4[3]);
         }
-        __syncthreads();
+        f32_group_sync(g);
 
         // ---- e = h W2 + b2, child_q = -tanh(wv . e + bv)
 #pragma unroll
@@ -202,7 +222,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[i][j] = s->b2[4 * tx + j];
         f32_chunks<16, true>(xb, s->w2, tx, ty, acc);
-        __syncthreads();  // the hidden rows are consumed: e overwrites them
+        f32_group_sync(g);  // the hidden rows are consumed: e overwrites them
 #pragma unroll
         for (int i = 0; i < kF32Rpt; i++) {
             const int r = ty + kF32Ty * i;
@@ -213,7 +233,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
             pv = f32_row_sum16(pv);
             if (tx == 0 && r < nrows) child_q[(int64_t)lf[i] * kMaxMoves + sl[i]] = -tanhf(pv + s->bv);
         }
-        __syncthreads();
+        f32_group_sync(g);
 
         // ---- logit = a2 . sigmoid(root_pre[leaf] + A1s e) + a2b
 #pragma unroll
@@ -234,15 +254,15 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
             p = f32_row_sum16(p);
             if (tx == 0 && r < nrows) logits[(int64_t)lf[i] * kMaxMoves + sl[i]] = p + s->a2b;
         }
-        __syncthreads();  // this buffer takes the tile after next
+        f32_group_sync(g);  // this buffer takes the tile after next
     }
     if (failed) {
         // a bounded wait gave up: record it, let the copies in flight land
         // (bounded again) and return
-        if (t == 0) {
+        if (gt == 0) {
             atomicOr(err_word, kErrF32Wait);
             for (int b = 0; b < 2; b++)
-                if ((pend >> b) & 1u) mbar_wait(&s->bar[b], (phases >> b) & 1u);
+                if ((pend >> b) & 1u) mbar_wait(&s->bar[g][b], (phases >> b) & 1u);
         }
     }
 }
