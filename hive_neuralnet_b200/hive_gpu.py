@@ -25,6 +25,8 @@ NUM_CELLS = 529
 MAX_LEGAL_MOVES = 256
 MAX_STACK = 5
 SIZEOF_HIVE_STATE = 3424
+# device staging slots (and streams) of the chunked host-buffer pipeline
+HOST_PIPELINE_STAGES = 3
 SIZEOF_GPU_MOVE = 6
 OFF_TURN = 3412
 OFF_QUEEN_PLACED = 3414
@@ -181,8 +183,8 @@ class HiveGPUExtension:
                 s.wait_event(ready)
             for i, lo in enumerate(range(0, batch_size, chunk)):
                 n = min(chunk, batch_size - lo)
-                d_st, d_mv, d_nl, d_ft = slots[i % 3]
-                s = streams[i % 3]
+                d_st, d_mv, d_nl, d_ft = slots[i % len(slots)]
+                s = streams[i % len(streams)]
                 with torch.cuda.stream(s):
                     # stack levels 2-4 only where some cell is 3 high (hv_stage_host_states)
                     _lib.check(self._lib.hv_stage_host_states(states.data_ptr() + lo * SIZEOF_HIVE_STATE, n,
@@ -208,8 +210,8 @@ class HiveGPUExtension:
                           torch.empty((chunk, MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE), dtype=torch.uint8, device=dev),
                           torch.empty((chunk,), dtype=torch.int32, device=dev),
                           torch.empty((chunk, FNN_FEAT_DIM), dtype=torch.float32, device=dev))
-                         for _ in range(3)]
-                streams = [torch.cuda.Stream(dev) for _ in range(3)]
+                         for _ in range(HOST_PIPELINE_STAGES)]
+                streams = [torch.cuda.Stream(dev) for _ in range(HOST_PIPELINE_STAGES)]
             cache[key] = (slots, streams)
         return cache[key]
 
