@@ -61,3 +61,25 @@ def test_terminal_and_empty_rows():
         assert (p == 0).all() and (c == 0).all() and torch.isfinite(v).all()
     p0, v0, c0 = ev.eval_states(st[:0], mv[:0], nl[:0], 0)
     assert p0.shape == (0, 256) and v0.shape == (0,)
+
+
+@pytest.mark.parametrize("count", [1, 2, 5, 17])
+def test_rows_small_batches(count):
+    """Ragged row counts: one partial 64-row tile (a CTA whose second group
+    has no tile), two tiles in one CTA, and a partial last tile."""
+    from hive_neuralnet_b200.fnn import FusedFNNEvaluator, HiveFNN
+    orc = O.oracle()
+    torch.manual_seed(2)
+    net = HiveFNN().eval()
+    st = orc.generate_positions(900 + count, 0, count, 90, 7)
+    mo, no, fo = orc.legal_moves_features(st)
+    roots = np.repeat(np.arange(len(st), dtype=np.int64), no)
+    idx = np.concatenate([np.arange(n, dtype=np.int64) for n in no])
+    sf = orc.successor_features(st, mo, roots, idx)
+    pr, vr, cr, lr = eval_states_reference(net, fo, sf, no)
+    ev = FusedFNNEvaluator(net)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    pg, vg, cg, lg = (x.cpu().numpy() for x in ev.eval_states(t(st), t(mo), t(no), count, t(fo), return_logits=True))
+    valid = np.arange(256)[None, :] < no[:, None]
+    assert _close(vg, vr).all() and _close(cg, cr).all() and _close(pg, pr).all()
+    assert _close(lg[valid], lr[valid]).all()
