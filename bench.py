@@ -362,8 +362,12 @@ def run_gpu(args) -> None:
 
     # ---- roofline of the dominant kernel: the move generator k_root<gen>
     # (one of the step's two launches), timed alone with CUDA events on the
-    # launching stream; algorithmic bytes per position = state read + move
-    # list (6 bytes per legal move) + num_legal written
+    # launching stream through the standalone entry (static position stride:
+    # the step's generator launch claims positions from a counter in the
+    # step's feature buffer, which a lone launch does not have, so this
+    # figure is an upper bound on the step's generator time); algorithmic
+    # bytes per position = state read + move list (6 bytes per legal move) +
+    # num_legal written
     peak, peak_kind = measured_peak_gbs()
     for _ in range(3):
         ext.generate_legal_moves_batch(states, P)
@@ -384,7 +388,9 @@ def run_gpu(args) -> None:
                 "frac": achieved / peak, "peak_source": peak_kind,
                 "traffic": (tpp * P) if tpp else None,
                 "algorithmic_bytes_per_launch": alg_bytes,
-                "kernel": f"k_root<1,1,0> move generator, {gen_s * 1e3:.3f} ms per launch",
+                "kernel": f"k_root<1,1,0> move generator (standalone entry, static position stride), "
+                          f"{gen_s * 1e3:.3f} ms per launch; the step's generator claims positions "
+                          f"dynamically and runs faster",
                 "step": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / ((ms / args.steps) / 1e3) / 1e9,
                          "launches": ["k_root<1,1,0> (legal moves)", "k_root<0,0,1> (FNN features)"]}}
 

@@ -127,16 +127,29 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
                                                    float* __restrict__ feats_out) {
     WarpSmem* w = warp_slot();
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
-    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < batch;
-         p += nwarps) {
+    // DYN (the generator launch of the fused entry): warps take positions
+    // from a counter in the second 8 bytes of feature row 0 (zeroed by the
+    // host before the launch; the generator writes only word 0 of a row), so
+    // a warp that drew cheap positions takes more: position costs vary
+    // widely (opening to late game) and a static stride left the slowest
+    // warps running alone at the end.
+    constexpr bool DYN = GEN && AP_LINK;
+    unsigned long long* ctr = DYN ? reinterpret_cast<unsigned long long*>(feats_out + 2) : nullptr;
+    auto claim = [&]() -> int64_t {
+        unsigned long long v = 0;
+        if (lane_id() == 0) v = atomicAdd(ctr, 1ull);
+        return (int64_t)__shfl_sync(kFull, v, 0);
+    };
+    int64_t p = DYN ? claim() : (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    while (p < batch) {
         if (GEN)
             stage_state(w, states + p * kStateBytes);
         else
             stage_state_moves(w, states + p * kStateBytes, moves_in + p * (kMaxMoves * kMoveBytes));
+        // the warp's next position, claimed now, into L2 while this one is
+        // computed (the feature launch waits on these loads otherwise)
+        const int64_t q = DYN ? claim() : p + nwarps;
         {
-            // the warp's next position into L2 while this one is computed
-            // (the feature launch waits on these loads otherwise)
-            const int64_t q = p + nwarps;
             const int l = lane_id();
             if (q < batch) {
                 if (l < kStateBytes / 128 + 1)
@@ -169,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
             features(w, n, feats_out + p * kFeat);
         }
         __syncwarp();
+        p = q;
     }
 }
 
@@ -1627,7 +1641,11 @@ int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves
 int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
                                              int32_t* num_legal, float* features, void* stream) {
     if (batch > 0 && !features) return HV_EINVAL;
-    // the feature rows carry the generator's articulation masks between the launches
+    // the feature rows carry the generator's articulation masks between the
+    // launches, and row 0 the generator's position counter (bytes 8..15)
+    if (batch > 0 && (reinterpret_cast<uintptr_t>(features) & 7) != 0) return HV_EINVAL;
+    if (batch > 0 && cudaMemsetAsync(features + 2, 0, sizeof(unsigned long long), (cudaStream_t)stream) != cudaSuccess)
+        return HV_ECUDA;
     int rc = launch_root<true, true, false, true>(states, nullptr, nullptr, batch, moves, num_legal, features,
                                                   stream);
     if (rc) return rc;
