@@ -46,6 +46,10 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     assert lib.hv_generate_legal_moves(None, -1, None, None, None) == 1
     misaligned = ctypes.c_void_p(8)
     assert lib.hv_generate_legal_moves_and_fnn_features(misaligned, 1, None, None, None, None) == 1
+    # the fused entry keeps 8-byte working data in its feature rows
+    aligned = ctypes.c_void_p(256)
+    assert lib.hv_generate_legal_moves_and_fnn_features(aligned, 1, aligned, aligned, ctypes.c_void_p(260),
+                                                        None) == 1
     assert lib.hv_apply_moves(None, None, 0, None) == 0  # empty batch is a no-op
 
 
