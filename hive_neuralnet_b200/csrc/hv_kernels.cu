@@ -202,7 +202,8 @@ template <int OUT>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
     const int64_t* __restrict__ action_to_root, const int64_t* __restrict__ move_indices,
-    int64_t num_actions, void* __restrict__ out, const int64_t* __restrict__ n_actual) {
+    int64_t num_actions, void* __restrict__ out, const int64_t* __restrict__ n_actual,
+    unsigned long long* __restrict__ ctr) {
     float* feats_out = static_cast<float*>(out);
     __half* slab = static_cast<__half*>(out);
     constexpr bool SLAB = OUT != kRowsF32;
@@ -212,8 +213,17 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     // between the compact list and the features: the warps of an SM then run
     // fewer distinct code regions at a time, and this kernel is bound by
     // instruction fetch (measured: 25 % faster than free-running warps).
-    for (int64_t base = (int64_t)blockIdx.x * kWarpsPerBlock; base < num_actions;
-         base += (int64_t)gridDim.x * kWarpsPerBlock) {
+    // With a counter (ctr, zeroed before the launch), blocks claim their next
+    // rows from it instead of a static stride, so a block that drew cheap rows
+    // takes more; the claim for the next round is made before the barrier and
+    // read after it (two slots: a slot is rewritten only two barriers later).
+    __shared__ int64_t next_base[2];
+    if (ctr) {
+        if (threadIdx.x == 0) next_base[1] = (int64_t)atomicAdd(ctr, (unsigned long long)kWarpsPerBlock);
+        __syncthreads();
+    }
+    int round = 0;
+    for (int64_t base = ctr ? next_base[1] : (int64_t)blockIdx.x * kWarpsPerBlock; base < num_actions; round ^= 1) {
         const int64_t a = base + (threadIdx.x >> 5);
         bool ok = a < num_actions;
         int64_t root = 0, mi = 0;
@@ -248,7 +258,9 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             S = setup_position(w);
             n = gen_compact(w, &g_error);
         }
+        if (ctr && threadIdx.x == 0) next_base[round] = (int64_t)atomicAdd(ctr, (unsigned long long)kWarpsPerBlock);
         __syncthreads();
+        const int64_t nb = ctr ? next_base[round] : base + (int64_t)gridDim.x * kWarpsPerBlock;
         if (ok) {
             if (SLAB) {
                 // the move list is consumed once the features are written: stage them there
@@ -278,6 +290,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             }
         }
         __syncwarp();
+        base = nb;
     }
 }
 
@@ -1486,9 +1499,12 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
         constexpr int OUT = HYB ? kSlabF16 : kSlabF32;
         rc = grid_for(k_successor_features<OUT>, rows, smem, &grid);
         if (rc) return rc;
+        // the row counter lives in root_pre, which the per-leaf kernel writes only later
+        unsigned long long* ctr = reinterpret_cast<unsigned long long*>(w.root_pre);
+        if (cudaMemsetAsync(ctr, 0, sizeof(unsigned long long), s) != cudaSuccess) return HV_ECUDA;
         k_successor_features<OUT><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows,
                                                               HYB ? static_cast<void*>(w.xh) : static_cast<void*>(w.x),
-                                                              w.row_start + count);
+                                                              w.row_start + count, ctr);
         if (HYB) {
             rc = grid_for(k_row_move_features, count, smem, &grid);
             if (rc) return rc;
@@ -1703,7 +1719,7 @@ int hv_fnn_successor_features(const uint8_t* states, int64_t num_states, const u
     int rc = grid_for(k_successor_features<kRowsF32>, num_actions, smem, &grid);
     if (rc) return rc;
     k_successor_features<kRowsF32><<<grid, kThreads, smem, (cudaStream_t)stream>>>(
-        states, num_states, legal_moves, action_to_root, move_indices, num_actions, features, nullptr);
+        states, num_states, legal_moves, action_to_root, move_indices, num_actions, features, nullptr, nullptr);
     return launch_status();
 }
 
