@@ -392,7 +392,8 @@ def run_gpu(args) -> None:
                           f"{gen_s * 1e3:.3f} ms per launch; the step's generator claims positions "
                           f"dynamically and runs faster",
                 "step": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / ((ms / args.steps) / 1e3) / 1e9,
-                         "launches": ["k_root<1,1,0> (legal moves)", "k_root<0,0,1> (FNN features)"]}}
+                         "launches": ["k_root<1,1,0,1> (legal moves)", "k_root<0,0,1,1,1> (FNN features, positions 1..)",
+                                      "k_root<0,0,1,1> (FNN features, position 0)"]}}
 
     line = None
     if rank == 0:
@@ -418,7 +419,7 @@ def run_gpu(args) -> None:
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,  # per step: generator, features, features of position 0
             "mean_legal_moves": mean_legal,
         }
     if dist is not None:

@@ -114,11 +114,14 @@ __device__ __forceinline__ void store_moves(const WarpSmem* w, uint8_t* dst, int
 // (game_logic.cu:63-91 generate_legal_moves[_and_fnn_features]_kernel,
 //  fnn_features.cuh:334-350 extract_fnn_features_kernel)
 // ---------------------------------------------------------------------------
-// AP_LINK (the two launches of hv_generate_legal_moves_and_fnn_features):
-// the generator leaves each position's articulation mask in the first word
-// of its feature row, and the feature launch takes it from there before it
+// AP_LINK (the launches of hv_generate_legal_moves_and_fnn_features): the
+// generator leaves each position's articulation mask in the first word of
+// its feature row, and the feature launch takes it from there before it
 // writes the row, instead of computing the articulation points again.
-template <bool GEN, bool WRITE_MOVES, bool FEATS, bool AP_LINK = false>
+// DYNF: a feature launch of that entry that claims positions 1.. from a
+// counter in bytes 16..23 of feature row 0; position 0 (whose row holds the
+// counters) is left to a one-warp launch that follows.
+template <bool GEN, bool WRITE_MOVES, bool FEATS, bool AP_LINK = false, bool DYNF = false>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t* __restrict__ states,
                                                    const uint8_t* __restrict__ moves_in,
                                                    const int32_t* __restrict__ nl_in, int64_t batch,
@@ -133,12 +136,12 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
     // a warp that drew cheap positions takes more: position costs vary
     // widely (opening to late game) and a static stride left the slowest
     // warps running alone at the end.
-    constexpr bool DYN = GEN && AP_LINK;
-    unsigned long long* ctr = DYN ? reinterpret_cast<unsigned long long*>(feats_out + 2) : nullptr;
+    constexpr bool DYN = (GEN && AP_LINK) || DYNF;
+    unsigned long long* ctr = DYN ? reinterpret_cast<unsigned long long*>(feats_out + (GEN ? 2 : 4)) : nullptr;
     auto claim = [&]() -> int64_t {
         unsigned long long v = 0;
         if (lane_id() == 0) v = atomicAdd(ctr, 1ull);
-        return (int64_t)__shfl_sync(kFull, v, 0);
+        return (int64_t)__shfl_sync(kFull, v, 0) + (DYNF ? 1 : 0);
     };
     int64_t p = DYN ? claim() : (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
     while (p < batch) {
@@ -1435,7 +1438,7 @@ static inline int launch_status() {
     return e == cudaSuccess ? HV_OK : HV_ECUDA;
 }
 
-template <bool GEN, bool WM, bool FE, bool AP_LINK = false>
+template <bool GEN, bool WM, bool FE, bool AP_LINK = false, bool DYNF = false>
 static int launch_root(const uint8_t* states, const uint8_t* mi, const int32_t* nli, int64_t batch,
                        uint8_t* mo, int32_t* nlo, float* fo, void* stream) {
     if (batch < 0) return HV_EINVAL;
@@ -1446,10 +1449,10 @@ static int launch_root(const uint8_t* states, const uint8_t* mi, const int32_t* 
     if (!GEN && (!mi || !nli || !aligned16(mi))) return HV_EINVAL;
     size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
     int grid = 0;
-    int rc = grid_for(k_root<GEN, WM, FE, AP_LINK>, batch, smem, &grid);
+    int rc = grid_for(k_root<GEN, WM, FE, AP_LINK, DYNF>, batch, smem, &grid);
     if (rc) return rc;
-    k_root<GEN, WM, FE, AP_LINK><<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, mi, nli, batch, mo,
-                                                                                 nlo, fo);
+    k_root<GEN, WM, FE, AP_LINK, DYNF><<<grid, kThreads, smem, (cudaStream_t)stream>>>(states, mi, nli, batch, mo,
+                                                                                       nlo, fo);
     return launch_status();
 }
 
@@ -1658,15 +1661,21 @@ int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batc
                                              int32_t* num_legal, float* features, void* stream) {
     if (batch > 0 && !features) return HV_EINVAL;
     // the feature rows carry the generator's articulation masks between the
-    // launches, and row 0 the generator's position counter (bytes 8..15)
+    // launches, and row 0 the position counters of the generator (bytes
+    // 8..15) and of the feature launch (16..23); position 0 goes last
     if (batch > 0 && (reinterpret_cast<uintptr_t>(features) & 7) != 0) return HV_EINVAL;
-    if (batch > 0 && cudaMemsetAsync(features + 2, 0, sizeof(unsigned long long), (cudaStream_t)stream) != cudaSuccess)
+    if (batch > 0 &&
+        cudaMemsetAsync(features + 2, 0, 2 * sizeof(unsigned long long), (cudaStream_t)stream) != cudaSuccess)
         return HV_ECUDA;
     int rc = launch_root<true, true, false, true>(states, nullptr, nullptr, batch, moves, num_legal, features,
                                                   stream);
     if (rc) return rc;
-    return launch_root<false, false, true, true>(states, moves, num_legal, batch, nullptr, nullptr, features,
-                                                 stream);
+    if (batch > 1) {
+        rc = launch_root<false, false, true, true, true>(states, moves, num_legal, batch, nullptr, nullptr, features,
+                                                         stream);
+        if (rc) return rc;
+    }
+    return launch_root<false, false, true, true>(states, moves, num_legal, 1, nullptr, nullptr, features, stream);
 }
 
 int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev_states, void* stream) {

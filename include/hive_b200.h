@@ -61,8 +61,8 @@ int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves
 /* generate_legal_moves_and_fnn_features_batch(states, batch_size)
  * replaces bindings.cpp:335-338 / game_logic.cu:1440-1464.  `features`
  * must be 8-byte aligned: until the call's second kernel writes them, the
- * feature rows carry working data between its two kernels (each row's
- * articulation mask, and a position counter in row 0). */
+ * feature rows carry working data between its kernels (each row's
+ * articulation mask, and position counters in row 0). */
 int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
                                              int32_t* num_legal, float* features, void* stream);
 
