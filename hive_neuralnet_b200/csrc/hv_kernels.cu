@@ -1657,25 +1657,38 @@ int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves
 // lead the fused kernel's profile), while each alone fits.  Measured on
 // 262,144 positions: fused 6.2 ms, generator 3.2 ms + features from the
 // stored list 1.7 ms; re-reading the states and lists costs ~0.2 ms of HBM.
-int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
-                                             int32_t* num_legal, float* features, void* stream) {
+int hv_generate_legal_moves_linked(const uint8_t* states, int64_t batch, uint8_t* moves, int32_t* num_legal,
+                                   float* features, void* stream) {
     if (batch > 0 && !features) return HV_EINVAL;
-    // the feature rows carry the generator's articulation masks between the
-    // launches, and row 0 the position counters of the generator (bytes
-    // 8..15) and of the feature launch (16..23); position 0 goes last
+    // the feature rows carry the generator's articulation masks to the
+    // feature launch, and row 0 the position counters of the generator
+    // (bytes 8..15) and of the feature launch (16..23)
     if (batch > 0 && (reinterpret_cast<uintptr_t>(features) & 7) != 0) return HV_EINVAL;
     if (batch > 0 &&
         cudaMemsetAsync(features + 2, 0, 2 * sizeof(unsigned long long), (cudaStream_t)stream) != cudaSuccess)
         return HV_ECUDA;
-    int rc = launch_root<true, true, false, true>(states, nullptr, nullptr, batch, moves, num_legal, features,
-                                                  stream);
-    if (rc) return rc;
+    return launch_root<true, true, false, true>(states, nullptr, nullptr, batch, moves, num_legal, features, stream);
+}
+
+int hv_fnn_features_linked(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t batch,
+                           float* features, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch > 0 && (!features || (reinterpret_cast<uintptr_t>(features) & 7) != 0)) return HV_EINVAL;
+    // positions 1.. claim from the counter in row 0; position 0 goes last
     if (batch > 1) {
-        rc = launch_root<false, false, true, true, true>(states, moves, num_legal, batch, nullptr, nullptr, features,
-                                                         stream);
+        const int rc = launch_root<false, false, true, true, true>(states, moves, num_legal, batch, nullptr, nullptr,
+                                                                   features, stream);
         if (rc) return rc;
     }
-    return launch_root<false, false, true, true>(states, moves, num_legal, 1, nullptr, nullptr, features, stream);
+    return launch_root<false, false, true, true>(states, moves, num_legal, batch > 0 ? 1 : 0, nullptr, nullptr,
+                                                 features, stream);
+}
+
+int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
+                                             int32_t* num_legal, float* features, void* stream) {
+    const int rc = hv_generate_legal_moves_linked(states, batch, moves, num_legal, features, stream);
+    if (rc) return rc;
+    return hv_fnn_features_linked(states, moves, num_legal, batch, features, stream);
 }
 
 int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev_states, void* stream) {

@@ -60,11 +60,23 @@ int hv_generate_legal_moves(const uint8_t* states, int64_t batch, uint8_t* moves
 
 /* generate_legal_moves_and_fnn_features_batch(states, batch_size)
  * replaces bindings.cpp:335-338 / game_logic.cu:1440-1464.  `features`
- * must be 8-byte aligned: until the call's second kernel writes them, the
+ * must be 8-byte aligned: until the call's feature kernels write them, the
  * feature rows carry working data between its kernels (each row's
- * articulation mask, and position counters in row 0). */
+ * articulation mask, and position counters in row 0).  The call is
+ * hv_generate_legal_moves_linked followed by hv_fnn_features_linked. */
 int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batch, uint8_t* moves,
                                              int32_t* num_legal, float* features, void* stream);
+
+/* The two halves of hv_generate_legal_moves_and_fnn_features, callable
+ * apart so that a caller (a profiler, the benchmark) can time each; no
+ * counterpart in the reference, whose fused kernel computes both in one.
+ * hv_generate_legal_moves_linked writes the move lists and num_legal and
+ * leaves working data in `features` (see above); hv_fnn_features_linked must
+ * follow it on the same buffers and stream and writes the features. */
+int hv_generate_legal_moves_linked(const uint8_t* states, int64_t batch, uint8_t* moves, int32_t* num_legal,
+                                   float* features, void* stream);
+int hv_fnn_features_linked(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t batch,
+                           float* features, void* stream);
 
 /* Host -> device staging of `count` 3424-byte states for the host-buffer
  * pipeline (the reference's callers pass host tensors through .cuda() before

@@ -222,3 +222,19 @@ def test_legal_mask_matches_action_indices(ext, orc):
     assert np.array_equal(nl.cpu().numpy(), no) and np.array_equal(nl2.cpu().numpy(), no)
     assert np.array_equal(mv2.cpu().numpy(), mo)
     assert np.array_equal(masks.cpu().numpy(), want) and np.array_equal(masks2.cpu().numpy(), want)
+
+
+def test_linked_halves_match_fused_entry(ext, orc):
+    """hv_generate_legal_moves_linked + hv_fnn_features_linked give the fused entry's bytes."""
+    st = _cuda(orc.generate_positions(5150, 0, 3000, 120, 7))
+    mg, ng, fg = ext.generate_legal_moves_and_fnn_features_batch(st, 3000)
+    lib = ext._lib
+    mv = torch.zeros_like(mg)
+    nl = torch.zeros_like(ng)
+    ft = torch.zeros_like(fg)
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.hv_generate_legal_moves_linked(st.data_ptr(), 3000, mv.data_ptr(), nl.data_ptr(), ft.data_ptr(), s) == 0
+    assert lib.hv_fnn_features_linked(st.data_ptr(), mv.data_ptr(), nl.data_ptr(), 3000, ft.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(mv, mg) and torch.equal(nl, ng)
+    assert np.array_equal(_bits(ft.cpu().numpy()), _bits(fg.cpu().numpy()))
