@@ -186,7 +186,8 @@ class HiveGPUExtension:
                 d_st, d_mv, d_nl, d_ft = slots[i % len(slots)]
                 s = streams[i % len(streams)]
                 with torch.cuda.stream(s):
-                    # stack levels 2-4 only where some cell is 3 high (hv_stage_host_states)
+                    # heights, bitboards and fields, and the stack levels over the
+                    # rows that hold pieces (hv_stage_host_states)
                     _lib.check(self._lib.hv_stage_host_states(states.data_ptr() + lo * SIZEOF_HIVE_STATE, n,
                                                               _ptr(d_st), s.cuda_stream),
                                "generate_legal_moves_and_fnn_features_host")
