@@ -58,18 +58,17 @@ constexpr uint32_t kRowBits = 0x7fffffu;
 constexpr uint32_t kErrBuffer = 1u;  // a generator list exceeded its buffer
 constexpr uint32_t kErrIndex = 2u;   // a root / move index was out of range
 
+// The fields up to and including the union are all that the feature launch
+// of the fused movegen + features entry touches (articulation masks given,
+// no slide masks): that launch gives each warp only that prefix
+// (kFeatSlotBytes) and fits one more block per SM.
 struct __align__(16) WarpSmem {
     uint8_t st[kStateBytes];     // staged HiveState
     uint16_t mv[kMaxMoves * 3];  // move list: (type | pt << 8, from, to) per move
     uint32_t occ[24];            // occupied row words
     uint32_t own[24];            // side-to-move top-piece row words
-    uint32_t sl[6][24];          // slide masks of the position
-    uint32_t seen[24];           // scratch cell set
-    uint32_t prow[24];           // placement row words
-    uint32_t adj[32];            // piece adjacency (piece-index space)
     uint16_t pcell[32];          // cell of piece i
     uint16_t pref[24];           // piece index of the first occupied cell of row r
-    uint16_t ppref[24];          // placement index of the first placement cell of row r
     uint8_t pflag[32];           // bit0: pinned (articulation point at height 1), bit1: articulation point
     uint32_t pl[24];             // mosquito union set (generators) / placement-cell set (features)
     // Generator scratch and feature accumulators are never live together
@@ -88,8 +87,16 @@ struct __align__(16) WarpSmem {
             uint32_t bm[16 * 17];  // per (type, owner) source-cell sets
         };
     };
+    // generator-only fields (past the feature launch's prefix)
+    uint32_t sl[6][24];          // slide masks of the position
+    uint32_t seen[24];           // scratch cell set
+    uint32_t prow[24];           // placement row words
+    uint32_t adj[32];            // piece adjacency (piece-index space)
+    uint16_t ppref[24];          // placement index of the first placement cell of row r
 };
 static_assert(offsetof(WarpSmem, acc) % 16 == 0, "feature accumulators are cleared with 16-byte stores");
+constexpr int kFeatSlotBytes = (int)offsetof(WarpSmem, sl);
+static_assert(kFeatSlotBytes % 16 == 0, "feature-launch warp slots stay 16-byte aligned");
 
 // ---------------------------------------------------------------------------
 // small helpers

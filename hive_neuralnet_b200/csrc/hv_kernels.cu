@@ -45,6 +45,12 @@ __device__ __forceinline__ WarpSmem* warp_slot() {
     return reinterpret_cast<WarpSmem*>(smem_raw) + (threadIdx.x >> 5);
 }
 
+// a slot of kFeatSlotBytes: only the fields before WarpSmem::sl exist
+__device__ __forceinline__ WarpSmem* feat_warp_slot() {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    return reinterpret_cast<WarpSmem*>(smem_raw + (threadIdx.x >> 5) * kFeatSlotBytes);
+}
+
 // N16 16-byte words from global into shared memory by asynchronous copies:
 // all of a lane's copies are in flight together (a load/store loop waits one
 // memory latency per iteration).  Both addresses 16-byte aligned; the data
@@ -128,7 +134,8 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
                                                    uint8_t* __restrict__ moves_out,
                                                    int32_t* __restrict__ nl_out,
                                                    float* __restrict__ feats_out) {
-    WarpSmem* w = warp_slot();
+    // the feature launch of the fused entry touches only the slot's prefix
+    WarpSmem* w = (!GEN && AP_LINK) ? feat_warp_slot() : warp_slot();
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
     // DYN (the generator launch of the fused entry): warps take positions
     // from a counter in the second 8 bytes of feature row 0 (zeroed by the
@@ -1447,7 +1454,7 @@ static int launch_root(const uint8_t* states, const uint8_t* mi, const int32_t* 
     if (WM && (!mo || !nlo || !aligned16(mo))) return HV_EINVAL;
     if ((FE || AP_LINK) && !fo) return HV_EINVAL;
     if (!GEN && (!mi || !nli || !aligned16(mi))) return HV_EINVAL;
-    size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
+    size_t smem = (size_t)((!GEN && AP_LINK) ? kFeatSlotBytes : (int)sizeof(WarpSmem)) * kWarpsPerBlock;
     int grid = 0;
     int rc = grid_for(k_root<GEN, WM, FE, AP_LINK, DYNF>, batch, smem, &grid);
     if (rc) return rc;
