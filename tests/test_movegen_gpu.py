@@ -238,3 +238,15 @@ def test_linked_halves_match_fused_entry(ext, orc):
     torch.cuda.synchronize()
     assert torch.equal(mv, mg) and torch.equal(nl, ng)
     assert np.array_equal(_bits(ft.cpu().numpy()), _bits(fg.cpu().numpy()))
+
+
+@pytest.mark.parametrize("count", [1, 2, 3, 33, 4145])
+def test_fused_entry_small_and_ragged_batches(ext, orc, count):
+    """The fused entry's position counters: one position (no claiming
+    launch), two (one claimed position plus position 0), and counts around
+    the number of resident warps."""
+    st = orc.generate_positions(7000 + count, 0, count, 120, 7)
+    mo, no, fo = orc.legal_moves_features(st)
+    mg, ng, fg = (x.cpu().numpy() for x in ext.generate_legal_moves_and_fnn_features_batch(_cuda(st), count))
+    assert np.array_equal(ng, no) and np.array_equal(mg, mo)
+    assert np.array_equal(_bits(fg), _bits(fo))
