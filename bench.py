@@ -78,8 +78,9 @@ def cpu_model() -> str:
 # --------------------------------------------------------------------------
 def _cpu_lib():
     from oracle import oracle as O
-    if not O.ref_available() and os.path.isdir("/root/reference/hive_gpu/csrc"):
-        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref"], check=False)
+    if not O.ref_available() and O.reference_available():
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref",
+                        f"HIVE_REFERENCE={O.reference_dir()}"], check=False)
     if O.ref_available():
         return O.ref(), "reference"
     if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
@@ -371,6 +372,9 @@ def run_gpu(args) -> None:
     lib = ext._lib
     mv_t, nl_t, ft_t = out[0], out[1], out[2]
 
+    # Only the generator half is timed on its own: the feature half
+    # (hv_fnn_features_linked) consumes the working data that its own
+    # generator half leaves in the feature rows, so it cannot run alone.
     def linked_gen():
         rc = lib.hv_generate_legal_moves_linked(states.data_ptr(), P, mv_t.data_ptr(), nl_t.data_ptr(),
                                                 ft_t.data_ptr(), stream.cuda_stream)

@@ -1905,10 +1905,31 @@ int hv_hybrid_evaluate(const uint8_t* states, const uint8_t* legal_moves, const 
 }
 
 // Fixed scratch of hv_hybrid_evaluate_noalloc: enough for 9137 positions in
-// the hybrid_workspace_layout arrays.  Its address is resolved once per device.
+// the hybrid_workspace_layout arrays.  Its address is resolved once per device
+// context: a context that was destroyed and re-created (cudaDeviceReset) loads
+// the module again, at a new address, so the cache is keyed on the context
+// handle as well as the device index.
 static __device__ __align__(256) uint8_t g_hybrid_scratch[32u << 20];
 static void* g_hybrid_scratch_ptr[64];
+static void* g_hybrid_scratch_ctx[64];
 static std::mutex g_hybrid_scratch_mu;
+
+// The current driver context (cuCtxGetCurrent through the runtime's entry-point
+// query, so the library needs no link against libcuda).  nullptr if unknown.
+static void* current_context() {
+    typedef int (*CtxGetCurrent)(void**);
+    static CtxGetCurrent fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<CtxGetCurrent>(f);
+    }();
+    void* ctx = nullptr;
+    if (!fn || fn(&ctx) != 0) return nullptr;
+    return ctx;
+}
 
 int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
                                const float* root_features, int64_t count, int node_feat_dim,
@@ -1924,10 +1945,14 @@ int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves
     void* scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_hybrid_scratch_mu);
-        if (!g_hybrid_scratch_ptr[dev]) {
+        void* ctx = current_context();
+        if (!g_hybrid_scratch_ptr[dev] || !ctx || ctx != g_hybrid_scratch_ctx[dev]) {
+            // resolving the symbol makes the device's primary context current
+            // when no context was, so the context is read again afterwards
             void* p = nullptr;
             if (cudaGetSymbolAddress(&p, g_hybrid_scratch) != cudaSuccess || !p) return HV_ECUDA;
             g_hybrid_scratch_ptr[dev] = p;
+            g_hybrid_scratch_ctx[dev] = current_context();
         }
         scratch = g_hybrid_scratch_ptr[dev];
     }

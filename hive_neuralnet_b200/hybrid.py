@@ -365,6 +365,18 @@ def _slabs_b(w: torch.Tensor, k_pad: int, split: int | None = None, rows: int = 
     return out.half().reshape(rows, k_pad // 8, 8).permute(1, 0, 2).contiguous().reshape(-1)
 
 
+
+def _check_leaf_inputs(states, legal_moves, num_legal, root_features) -> None:
+    """The library reads these buffers as packed arrays: reject any other
+    dtype, layout or device before a pointer is passed."""
+    for t, name, dt in ((states, "states", torch.uint8), (legal_moves, "legal_moves", torch.uint8),
+                        (num_legal, "num_legal", torch.int32)):
+        if t.dtype != dt or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"{name}: expected contiguous CUDA {dt}")
+    if root_features is not None and (root_features.dtype != torch.float32 or not root_features.is_cuda
+                                      or not root_features.is_contiguous()):
+        raise ValueError("root_features: expected contiguous CUDA float32")
+
 class HybridEvaluator:
     """Leaf evaluation of the hybrid network with the signature and outputs of the
     reference's ``HybridMCTSOrchestrator._eval_states``: (priors [T,256], values [T],
@@ -446,12 +458,7 @@ class HybridEvaluator:
         logits = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev) if return_logits else None
         if total == 0:
             return (priors, values, child_q, logits) if return_logits else (priors, values, child_q)
-        for t, name, dt in ((states, "states", torch.uint8), (legal_moves, "legal_moves", torch.uint8),
-                            (num_legal, "num_legal", torch.int32)):
-            if t.dtype != dt or not t.is_cuda or not t.is_contiguous():
-                raise ValueError(f"{name}: expected contiguous CUDA {dt}")
-        if root_features is not None and (root_features.dtype != torch.float32 or not root_features.is_contiguous()):
-            raise ValueError("root_features: expected contiguous float32")
+        _check_leaf_inputs(states, legal_moves, num_legal, root_features)
         ws = self._workspace(total, dev)
         with torch.cuda.device(dev):
             _lib.check(self.lib.hv_hybrid_evaluate(
@@ -475,6 +482,7 @@ class HybridEvaluator:
         child_q = torch.empty((total, MAX_LEGAL), dtype=torch.float32, device=dev)
         if total == 0:
             return priors, values, child_q
+        _check_leaf_inputs(states, legal_moves, num_legal, root_features)
         with torch.cuda.device(dev):
             _lib.check(self.lib.hv_hybrid_evaluate_noalloc(
                 states.data_ptr(), legal_moves.data_ptr(), num_legal.data_ptr(),

@@ -72,7 +72,15 @@ int hv_generate_legal_moves_and_fnn_features(const uint8_t* states, int64_t batc
  * counterpart in the reference, whose fused kernel computes both in one.
  * hv_generate_legal_moves_linked writes the move lists and num_legal and
  * leaves working data in `features` (see above); hv_fnn_features_linked must
- * follow it on the same buffers and stream and writes the features. */
+ * follow it on the same buffers and stream and writes the features.  Each
+ * hv_fnn_features_linked call needs its own hv_generate_legal_moves_linked
+ * call just before it: the feature half reads the position counters (bytes
+ * 16..23 of row 0) and each row's articulation mask (its first word) that
+ * only the generator half leaves behind, and overwrites them.  A second
+ * feature half on the same buffers, or one without the generator half
+ * first, reads feature values as counters and masks and writes wrong
+ * features without any error: the feature half cannot be repeated alone
+ * (for example to time it). */
 int hv_generate_legal_moves_linked(const uint8_t* states, int64_t batch, uint8_t* moves, int32_t* num_legal,
                                    float* features, void* stream);
 int hv_fnn_features_linked(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal, int64_t batch,
@@ -298,9 +306,11 @@ int hv_legal_mask(const uint8_t* states, const uint8_t* moves, const int32_t* nu
  * 32 MiB file-scope device array instead of a caller workspace, so a caller
  * that owns no device allocator can still run it.  At most 9137 positions per
  * call; larger requests return HV_ESCRATCH and launch nothing.  The scratch
- * address is looked up once per device on the first call, so make the first
- * call before any stream capture.  The scratch is shared by every call on a
- * device: calls that overlap (other streams, other host threads) race. */
+ * address is looked up on the first call in each device context (once per
+ * device, and again after the context was reset and re-created, e.g. by
+ * cudaDeviceReset), so make the first call before any stream capture.  The
+ * scratch is shared by every call on a device: calls that overlap (other
+ * streams, other host threads) race. */
 int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
                                const float* root_features, int64_t count, int node_feat_dim,
                                const uint16_t* trunk_image, const float* trunk_params, const float* fnn_weights,

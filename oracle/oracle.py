@@ -35,11 +35,26 @@ _i64 = C.c_int64
 _int = C.c_int
 
 
+def reference_dir() -> str:
+    """Root of the reference source tree (chrismejias/hive_neuralnet): the
+    ``HIVE_REFERENCE`` environment variable, else a directory named
+    ``reference`` beside this repository.  Only fixture generators and the
+    reference build of the oracle read it; GPU tests and the bench never do."""
+    env = os.environ.get("HIVE_REFERENCE")
+    if env:
+        return os.path.abspath(env)
+    return os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
+def reference_available() -> bool:
+    return os.path.isdir(os.path.join(reference_dir(), "hive_gpu", "csrc"))
+
+
 def build(ref: bool = True) -> None:
     """Compile liboracle.so (and the reference build when the tree exists)."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
-    if ref and os.path.isdir("/root/reference/hive_gpu/csrc"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    if ref and reference_available():
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"HIVE_REFERENCE={reference_dir()}"], check=True)
 
 
 class _Lib:

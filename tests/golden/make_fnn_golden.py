@@ -12,7 +12,11 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, "/root/reference")
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+from oracle.oracle import reference_dir  # noqa: E402
+
+sys.path.insert(0, reference_dir())
 
 from hive_fnn.fnn_network import FNNConfig, HiveFNN  # noqa: E402  (the reference module)
 

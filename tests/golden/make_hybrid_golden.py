@@ -17,7 +17,9 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-sys.path.insert(0, "/root/reference")
+from oracle.oracle import reference_dir  # noqa: E402
+
+sys.path.insert(0, reference_dir())
 
 from oracle import oracle as O  # noqa: E402
 from hive_fnn_transformer.fnn_transformer_net import HiveHybridGNN, HybridGNNConfig  # noqa: E402  (reference)
