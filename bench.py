@@ -1,24 +1,38 @@
-"""Benchmark: batched legal move generation + FNN feature encoding on B200.
+"""Benchmark of the self-play hot path on B200: the BASELINE configs' metrics.
 
-Workload: 262,144 positions per GPU from the seeded
-random-playout generator with all expansions (mosquito, ladybug, pillbug)
-and stop ply U[0, 120]; one step = one pass of
-``generate_legal_moves_and_fnn_features_batch`` over the whole batch
-(moves [P,256,6] u8, num_legal [P] i32, features [P,122] f32).  Inputs
-(898 MB per GPU) are larger than L2, so no flush is needed between steps.
+Default run (one JSON line):
+
+* headline: batched legal move generation + FNN feature
+  encoding of 262,144 positions per GPU from the seeded random-playout
+  generator (all expansions, stop ply U[0, 120]); one step = one pass of
+  ``generate_legal_moves_and_fnn_features_batch`` over the batch (moves
+  [P,256,6] u8, num_legal [P] i32, features [P,122] f32).  Inputs (898 MB per
+  GPU) are larger than L2, so no flush is needed between steps.  Beside the
+  K-step region, a second region of >= 2 s of the same steps, and each
+  rank's time and clocks;
+* ``mcts``: Gumbel-root MCTS, 512 games per GPU, 4,096
+  simulations per move, FNN large; one step = one searched move of every
+  game through ``FNNMCTSOrchestrator.self_play_batch`` (host states in,
+  training examples out); simulations/s, an FP32 roofline, the reference's
+  CPU player beside it, and at N > 1 the replay-sample all-gather over NCCL;
+* ``hybrid``: PUCT with the FNN-transformer evaluator,
+  256 games per GPU, 1,024 simulations per move; simulations/s and a tensor
+  roofline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--workload all|movegen|mcts|hybrid|fnn]
 
 N > 1 runs one process per GPU under torch.distributed (weak scaling: every
-rank owns its own 262,144 games, no data-path collective); timing is the
-max over ranks of CUDA-event time.  ``--impl reference`` times the
-reference's own CPU implementation (its hive_gpu/csrc headers compiled on
-the host, oracle/_ref) on all host cores for the same metric.
+rank owns its own games, no data-path collective); timing is the max over
+ranks of CUDA-event time.  ``--impl reference`` times the reference's own
+CPU implementation (its hive_gpu/csrc headers compiled on the host,
+oracle/_ref) on all host cores for the same metric.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -235,28 +249,89 @@ def run_reference(args) -> None:
                          "sample": f"{sample_n} positions of the workload per step, {cpu_model()}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.workload in ("all", "mcts"):
+        # the reference's CPU player on config 4's kind of roots (base game, ply U[0, 30])
+        roots = lib.generate_positions(SEED + 97, 0, 4 * cores, 30, 0, cores)
+        roots = roots[roots[:, 3415] == 0]
+        rec = mcts_cpu_player_baseline(roots, args.sims)
+        line["mcts"] = {"impl": "reference", "metric": "MCTS simulations/sec", "value": rec["value"],
+                        "unit": "simulations/s", "cpu_baseline": rec,
+                        "e2e": {"value": rec["value"], "unit": "simulations/s", "h2d_bytes_per_step": 0,
+                                "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------------------
 # B200 arm
 # --------------------------------------------------------------------------
-def run_gpu(args) -> None:
-    import numpy as np
+class Ranks:
+    """One process per GPU: the rank's device and the process group (None at N = 1)."""
+
+    def __init__(self, timeout_s: int = 300):
+        import torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=self.dev)
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier(device_ids=[self.local])
+
+    def gather(self, x: float) -> list[float]:
+        """x of every rank, in rank order."""
+        import torch
+        t = torch.tensor([float(x)], device=self.dev, dtype=torch.float64)
+        if self.dist is None:
+            return [float(x)]
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+    def gather_obj(self, obj) -> list:
+        if self.dist is None:
+            return [obj]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier(device_ids=[self.local])
+            self.dist.destroy_process_group()
+
+
+def timed_region(ranks: Ranks, fn, steps: int) -> tuple[float, list[float]]:
+    """CUDA-event time (ms) of `steps` calls of fn on the current stream,
+    bracketed by a barrier and a synchronize on both sides: (max over ranks,
+    every rank's time)."""
     import torch
+    stream = torch.cuda.current_stream(ranks.dev)
+    ranks.barrier()
+    torch.cuda.synchronize(ranks.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(ranks.dev)
+    ranks.barrier()
+    per_rank = ranks.gather(e0.elapsed_time(e1))
+    return max(per_rank), per_rank
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
 
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+def bench_movegen(args, ranks: Ranks) -> dict:
+    """BASELINE config 2, the headline line."""
+    import torch
+    dev, rank, world = ranks.dev, ranks.rank, ranks.world
 
     from hive_neuralnet_b200.hive_gpu import load_extension
     ext = load_extension()
@@ -264,35 +339,25 @@ def run_gpu(args) -> None:
     states = ext.generate_positions(SEED, rank * P, P, MAX_PLY, EXPANSIONS, device=dev)
     stream = torch.cuda.current_stream(dev)
     torch.cuda.synchronize(dev)
+    box = {}
 
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local])
+    def step():
+        box["out"] = ext.generate_legal_moves_and_fnn_features_batch(states, P)
 
-    # ---- device-resident throughput ----
+    # ---- device-resident throughput: exactly K timed steps ----
     for _ in range(args.warmup):
-        out = ext.generate_legal_moves_and_fnn_features_batch(states, P)
+        step()
     torch.cuda.synchronize(dev)
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(ranks.local)
     sampler.start()
     time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        out = ext.generate_legal_moves_and_fnn_features_batch(states, P)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max, per_rank_ms = timed_region(ranks, step, args.steps)
     value = world * P * args.steps / (ms_max / 1e3)
+    # ---- the same steps over a region of >= 2 s (every rank the same count) ----
+    long_steps = max(args.steps, int(math.ceil(2000.0 / (ms_max / args.steps))))
+    long_max, long_per_rank = timed_region(ranks, step, long_steps)
+    clocks = sampler.stop()
+    out = box["out"]
     mean_legal = float(out[1].float().mean().item())
 
     # ---- end to end through the public API with host buffers ----
@@ -311,17 +376,8 @@ def run_gpu(args) -> None:
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize(dev)
-    barrier()
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    t2 = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-    e2e_value = world * P * e2e_steps / (float(t2.item()) / 1e3)
+    e2e_ms, e2e_per_rank = timed_region(ranks, e2e_step, e2e_steps)
+    e2e_value = world * P * e2e_steps / (e2e_ms / 1e3)
     h2d = staged_upload_bytes(states)
     n_tall = int((states[:, 2645:2645 + 529].amax(1) >= 3).sum().item())
     d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
@@ -329,6 +385,7 @@ def run_gpu(args) -> None:
     # ---- the host link the e2e leg runs against: plain pinned copies of the
     # step's state bytes, each direction alone, CUDA events on this stream
     dev_buf = torch.empty_like(states)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     def link_gbs(copy, nbytes):
         for _ in range(2):
@@ -355,7 +412,7 @@ def run_gpu(args) -> None:
     d2h_gbs = link_gbs(lambda: host_states.copy_(dev_buf, non_blocking=True), P * STATE_BYTES)
     bidir_gbs = link_gbs(both_ways, P * (STATE_BYTES + MAX_MOVES * MOVE_BYTES))
     del dev_buf
-    e2e_step_s = float(t2.item()) / 1e3 / e2e_steps
+    e2e_step_s = e2e_ms / 1e3 / e2e_steps
     # the step moves bytes both ways at once: its bound is the link's combined rate
     link = {"h2d_gbs_measured": h2d_gbs, "d2h_gbs_measured": d2h_gbs, "bidir_gbs_measured": bidir_gbs,
             "h2d_gbs_achieved": h2d / e2e_step_s / 1e9, "d2h_gbs_achieved": d2h / e2e_step_s / 1e9,
@@ -407,49 +464,81 @@ def run_gpu(args) -> None:
                 "kernel": f"k_root<1,1,0,1,0> move generator (the step's first launch, positions claimed "
                           f"from a counter), {gen_s * 1e3:.3f} ms per launch",
                 "standalone_generator_ms": static_s * 1e3,
-                "step": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / ((ms / args.steps) / 1e3) / 1e9,
+                "step": {"algorithmic_bytes": step_bytes,
+                         "achieved_gbs": step_bytes / ((ms_max / args.steps) / 1e3) / 1e9,
                          "launches": ["k_root<1,1,0,1> (legal moves)", "k_root<0,0,1,1,1> (FNN features, positions 1..)",
                                       "k_root<0,0,1,1> (FNN features, position 0)"]}}
-
-    line = None
-    if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu:
-            sample = states[:65536].cpu().numpy()
-            cores = host_cores()
-            rate, kind, n, dt = cpu_rate(sample, cores)
-            cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": kind,
-                   "sample": f"first {n} positions of the workload ({dt:.1f} s), {cpu_model()}"}
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-            "config": workload_config(world),
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
-                            f"staged upload (hv_stage_host_states: stack levels over occupied rows; "
-                            f"{n_tall} states with a 3-high stack), "
-                            f"{args.e2e_chunk}-position chunks over 3 streams",
-                    "link": link},
-            "roofline": roofline,
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-            "gpu_launches": 3 * args.steps,  # per step: generator, features, features of position 0
-            "mean_legal_moves": mean_legal,
-        }
-    if dist is not None:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
-    if line is not None:
-        print(json.dumps(line), flush=True)
+    rank_clocks = ranks.gather_obj(clocks)
+    cpu_sample = states[:65536].cpu().numpy() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    del states, host_states, h_moves, h_nl, h_feat, box, out, mv_t, nl_t, ft_t
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return {}
+    cpu = None
+    if cpu_sample is not None:
+        cores = host_cores()
+        rate, kind, n, dt = cpu_rate(cpu_sample, cores)
+        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": kind,
+               "sample": f"first {n} positions of the workload ({dt:.1f} s), {cpu_model()}"}
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": workload_config(world),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "per_rank_ms_per_step": [t / e2e_steps for t in e2e_per_rank],
+                "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
+                        f"staged upload (hv_stage_host_states: stack levels over occupied rows; "
+                        f"{n_tall} states with a 3-high stack), "
+                        f"{args.e2e_chunk}-position chunks over 3 streams",
+                "link": link},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "per_rank": {"ms_per_step": [t / args.steps for t in per_rank_ms],
+                     "clocks": [{"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons"),
+                                 "samples": c.get("samples")} for c in rank_clocks]},
+        "long_run": {"steps": long_steps, "ms_per_step": long_max / long_steps,
+                     "value": world * P * long_steps / (long_max / 1e3),
+                     "per_rank_ms_per_step": [t / long_steps for t in long_per_rank],
+                     "timed_s": long_max / 1e3},
+        "gpu_launches": 3 * args.steps,  # per step: generator, features, features of position 0
+        "mean_legal_moves": mean_legal,
+    }
 
 
 # --------------------------------------------------------------------------
-# secondary workloads (--workload mcts / fnn): BASELINE configs 4 and 3
+# BASELINE configs 4 (Gumbel MCTS + FNN) and 5 (PUCT + FNN-transformer)
 # --------------------------------------------------------------------------
 MCTS_GAMES = 512
 MCTS_SIMS = 4096
+# FLOPs of the FNN large evaluation (multiply-add = 2): per evaluated position
+# encode 2*(122*64 + 64*64) + value head 2*64; per successor row the same
+# encode and value head (child Q) + the action tower 2*(128*64) + 2*64
+FNN_FLOP_PER_LEAF = 2 * (122 * 64 + 64 * 64) + 2 * 64
+FNN_FLOP_PER_ROW = 2 * (122 * 64 + 64 * 64) + 2 * 64 + 2 * (128 * 64) + 2 * 64
+SMS = 148
+FP32_LANES_PER_SM = 128
+
+
+def fp32_peak_tflops() -> tuple[float, str]:
+    """FP32 FMA peak: 148 SMs x 128 lanes x 2 FLOP x the max SM clock (MEASURED_PEAKS.json's)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f)["sm_max_mhz"])
+    except Exception:
+        mhz = 1965.0
+    return SMS * FP32_LANES_PER_SM * 2 * mhz * 1e6 / 1e12, f"computed: {SMS} SMs x {FP32_LANES_PER_SM} lanes x 2 x {mhz:.0f} MHz"
+
+
+def bf16_peak_tflops(sustained: bool) -> tuple[float, str]:
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)[key]), f"measured ({key})"
+    except Exception:
+        return (1400.0 if sustained else 1590.0), "fallback"
 
 
 def _mcts_start_states(ext, n, seed, device, no_immediate_end=False):
@@ -475,28 +564,70 @@ def torch_nonzero(mask):
     return torch.nonzero(mask, as_tuple=False).squeeze(1)
 
 
-def run_mcts(args) -> None:
-    """Config 4: Gumbel-root MCTS, 512 games/GPU, 4096 simulations per move,
-    16 considered actions, wave schedule (2, 4, 8, 16), FNN large random
-    init (seed 0), seeded Philox Gumbel noise, Dirichlet off, root tactical
-    probe on (the trainer's default).  One step =
-    one searched move of every game; metric = simulations per second."""
+def _search_steps(ranks: Ranks, orch, starts, warmup: int, steps: int):
+    """Warm-up and timed searched moves: (ms max over ranks, per-rank ms,
+    simulations of all ranks, evaluated positions and rows of all ranks,
+    clocks, the last step's examples)."""
+    import torch
+    for i in range(warmup):
+        orch.self_play_batch(starts[i])
+    torch.cuda.synchronize(ranks.dev)
+    sampler = ClockSampler(ranks.local)
+    sampler.start()
+    orch.sims_done.zero_()
+    orch.rows_evaluated.zero_()
+    orch.leaves_evaluated = 0
+    box = {}
+
+    it = iter(range(warmup, warmup + steps))
+
+    def step():
+        box["ex"] = orch.self_play_batch(starts[next(it)])  # host states in, training examples out
+
+    ms, per_rank = timed_region(ranks, step, steps)
+    clocks = sampler.stop()
+    sims = sum(ranks.gather(float(orch.sims_done.item())))
+    rows = sum(ranks.gather(float(orch.rows_evaluated.item())))
+    leaves = sum(ranks.gather(float(orch.leaves_evaluated)))
+    return ms, per_rank, sims, leaves, rows, clocks, box["ex"]
+
+
+def _replay_gather(ranks: Ranks, examples) -> dict | None:
+    """The once-per-iteration replay exchange at N > 1: every rank's examples
+    of the last searched move all-gathered over NCCL (replay.gather_examples)."""
+    if ranks.dist is None:
+        return None
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
+    from hive_neuralnet_b200.replay import gather_examples, pack_examples
+    flat = [e for games in examples for e in games]
+    nbytes = int(pack_examples(flat).size)
+    ranks.barrier()
+    torch.cuda.synchronize(ranks.dev)
+    t0 = time.perf_counter()
+    got = gather_examples(flat)
+    torch.cuda.synchronize(ranks.dev)
+    ms = (time.perf_counter() - t0) * 1e3
+    per_rank_ms = ranks.gather(ms)
+    total = sum(ranks.gather(float(nbytes)))
+    return {"examples_per_rank": len(flat), "examples_gathered": len(got), "bytes_per_rank": nbytes,
+            "bytes_total": int(total), "ms": max(per_rank_ms), "per_rank_ms": per_rank_ms,
+            "path": "replay.gather_examples: sizes then padded byte buffers, two NCCL all_gathers, "
+                    "host pack / unpack included"}
 
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+def bench_mcts(args, ranks: Ranks) -> dict:
+    """Gumbel-root MCTS, 512 games/GPU, 4,096 simulations
+    per move, 16 considered actions, wave schedule (2, 4, 8, 16), FNN large
+    random init (seed 0), seeded Philox Gumbel noise, Dirichlet off, root
+    tactical probe on (the trainer's default).  One step = one searched move
+    of every game; metric = simulations per second."""
+    import torch
+
     from hive_neuralnet_b200.fnn import HiveFNN
     from hive_neuralnet_b200.hive_gpu import load_extension
     from hive_neuralnet_b200.orchestrator import FNNMCTSConfig, FNNMCTSOrchestrator
+    dev, rank, world = ranks.dev, ranks.rank, ranks.world
     ext = load_extension()
     torch.manual_seed(0)
     net = HiveFNN()
@@ -505,55 +636,63 @@ def run_mcts(args) -> None:
                         seed=1234 + rank, max_tree_nodes=65536, expansion_mask=0,
                         short_forced_win_probe=True)
     orch = FNNMCTSOrchestrator(net, cfg, device=dev)
-    starts = [_mcts_start_states(ext, games, SEED + 97 * (rank * 1000 + i), dev) for i in range(args.warmup + args.steps)]
-    host_starts = [s.cpu() for s in starts]
-    torch.cuda.synchronize(dev)
-    for i in range(args.warmup):
-        orch.self_play_batch(host_starts[i])
-    torch.cuda.synchronize(dev)
-    sampler = ClockSampler(local)
-    sampler.start()
-    if dist is not None:
-        dist.barrier(device_ids=[local])
-    orch.sims_done.zero_()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.warmup, args.warmup + args.steps):
-        orch.self_play_batch(host_starts[i])  # host states in, training examples out
-    e1.record()
-    torch.cuda.synchronize(dev)
-    clocks = sampler.stop()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    sims = orch.sims_done.to(torch.float64).reshape(1)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(sims, op=dist.ReduceOp.SUM)
-    ms = float(t.item())
-    value = float(sims.item()) / (ms / 1e3)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = mcts_cpu_baseline(net, host_starts[0][:64].numpy(), sims=256, wave=16, c_puct=cfg.c_puct,
-                                hybrid=False)
-    if rank == 0:
-        line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic",
-                "config": {"workload": f"config4: Gumbel MCTS {games} games/GPU x {args.sims} sims/move, k=16, "
-                                       "waves (2,4,8,16), FNN large random init",
-                           "simulations": float(sims.item()), "games_per_gpu": games,
-                           "parallelism": f"games sharded dp{world}" if world > 1 else "single GPU",
-                           "l2": "tree arrays (1.6 GB/GPU) larger than L2"},
-                "e2e": {"value": value, "unit": "simulations/s",
-                        "h2d_bytes_per_step": games * STATE_BYTES, "d2h_bytes_per_step": None,
-                        "note": "start states come from host memory and training examples return to it "
-                                "inside every timed step"},
-                "cpu_baseline": cpu,
-                "clocks": clocks}
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
+    W, K = args.mcts_warmup, args.mcts_steps
+    starts = [_mcts_start_states(ext, games, SEED + 97 * (rank * 1000 + i), dev).cpu() for i in range(W + K)]
+    ms, per_rank, sims, leaves, rows, clocks, examples = _search_steps(ranks, orch, starts, W, K)
+    value = sims / (ms / 1e3)
+    flops = leaves * FNN_FLOP_PER_LEAF + rows * FNN_FLOP_PER_ROW
+    peak, peak_src = fp32_peak_tflops()
+    achieved = flops / world / (ms / 1e3) / 1e12
+    gather = _replay_gather(ranks, examples)
+    rank_clocks = ranks.gather_obj(clocks)
+    cpu_states = starts[0].numpy() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    del orch, starts
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return {}
+    cpu = mcts_cpu_player_baseline(cpu_states, args.sims) if cpu_states is not None else None
+    return {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config4: Gumbel MCTS {games} games/GPU x {args.sims} sims/move, k=16, "
+                                   "waves (2,4,8,16), FNN large random init",
+                       "simulations": sims, "games_per_gpu": games,
+                       "parallelism": f"games sharded dp{world}" if world > 1 else "single GPU",
+                       "l2": "tree arrays (1.6 GB/GPU) larger than L2"},
+            "e2e": {"value": value, "unit": "simulations/s", "h2d_bytes_per_step": games * STATE_BYTES,
+                    "d2h_bytes_per_step": games * (STATE_BYTES + MAX_MOVES * 4 + 4 + 1 + 1),
+                    "note": "the timed steps are end to end: start states come from pinned-less host memory and "
+                            "the move's states, policy targets, move counts and flags return to the host in every "
+                            "step (self_play_batch's public API)"},
+            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": peak_src, "traffic": None,
+                         "algorithmic_flop": flops / world,
+                         "formula": f"{FNN_FLOP_PER_LEAF} FLOP per evaluated position + {FNN_FLOP_PER_ROW} per "
+                                    f"successor row (FNN large), per GPU per step time",
+                         "evaluated_positions": leaves, "successor_rows": rows},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "per_rank": {"ms_per_step": [t / K for t in per_rank],
+                         "clocks": [{"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons")} for c in rank_clocks]},
+            "replay_gather": gather}
+
+
+def mcts_cpu_player_baseline(roots_np, sims: int, seconds: float = 15.0) -> dict:
+    """The reference's CPU player for the Gumbel search (FNNNativeCPUPlayer,
+    hive_fnn/fnn_native_cpu_player.py:211-281), restated in oracle/cpu_player.py
+    over the reference's own cpu_native backend built into oracle/_ref: one
+    game per process on every host core, torch on one thread per process."""
+    from oracle import cpu_player as CP
+    if CP.backend_path() is None:
+        return {"value": None, "unit": "simulations/s", "cores": 0, "kind": "port",
+                "sample": "oracle/_ref cpu_native backend not built"}
+    cores = host_cores()
+    rate, done, wall, moves = CP.timed_rate(roots_np, sims, cores, seconds)
+    return {"value": rate, "unit": "simulations/s", "cores": cores, "kind": "port",
+            "sample": f"FNNNativeCPUPlayer's Gumbel search (restated in oracle/cpu_player.py, pinned to the "
+                      f"reference player by tests/test_cpu_player.py) over the reference's compiled cpu_native "
+                      f"backend, {sims} simulations per move, one game per process x {cores} processes for "
+                      f"{wall:.1f} s ({done} simulations, {moves} moves finished), {cpu_model()}"}
 
 
 def mcts_cpu_baseline(net, roots_np, sims, wave, c_puct, hybrid):
@@ -577,7 +716,7 @@ def mcts_cpu_baseline(net, roots_np, sims, wave, c_puct, hybrid):
 
 
 def run_fnn(args) -> None:
-    """Config 3: fused leaf evaluation of 65,536 roots (all legal successors)
+    """Config 3: leaf evaluation of 65,536 roots (all legal successors)
     with FNN large (fp32, random init seed 0)."""
     import torch
 
@@ -601,7 +740,8 @@ def run_fnn(args) -> None:
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     succ = int(nl.sum().item())
-    flops = P * 2 * (122 * 64 + 64 * 64 + 64 + 64 * 64) + succ * 2 * (122 * 64 + 64 * 64 + 64 + 64 * 64 + 64)
+    flops = P * FNN_FLOP_PER_LEAF + succ * FNN_FLOP_PER_ROW
+    peak, peak_src = fp32_peak_tflops()
     cpu = None
     if not args.no_cpu:
         from oracle import cpu_search as CS
@@ -625,16 +765,24 @@ def run_fnn(args) -> None:
                       "warmup": args.warmup, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
                       "config": {"workload": f"config3: {P} roots x all legal successors, FNN large fp32",
                                  "successors": succ},
-                      "mlp_tflops": flops / (ms / 1e3) / 1e12, "cpu_baseline": cpu}), flush=True)
+                      "roofline": {"bound": "fp32", "achieved": flops / (ms / 1e3) / 1e12, "peak": peak,
+                                   "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / peak,
+                                   "peak_source": peak_src, "traffic": None},
+                      "cpu_baseline": cpu}), flush=True)
 
 
 HYBRID_GAMES = 256
 HYBRID_SIMS = 1024
 HYBRID_WAVE = 32  # 256 games x 32 = 8,192 leaves per wave
 TRUNK_FLOP_PER_LEAF = 7.61e6  # algorithmic trunk FLOPs per position (29 tokens, 4 blocks)
+# tensor FLOPs of the hybrid evaluation: per position the trunk, the value
+# head and the root FNN encode (~7.65 MFLOP); per legal action the FNN
+# successor encode, graph and move projections and the action layer (68.9 KFLOP)
+HYBRID_FLOP_PER_LEAF = 7.65e6
+HYBRID_FLOP_PER_ROW = 68.9e3
 
 
-def run_hybrid(args) -> None:
+def bench_hybrid(args, ranks: Ranks) -> dict:
     """Config 5: PUCT MCTS with the hybrid FNN-transformer evaluator, 256
     games/GPU, 1,024 simulations per move, c_puct 1.5, 8,192 leaves per wave,
     HybridGNNConfig() random init (seed 0), fp16-operand tensor-core trunk
@@ -642,20 +790,10 @@ def run_hybrid(args) -> None:
     = one searched move of every game; metric = simulations per second."""
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     from hive_neuralnet_b200.hive_gpu import load_extension
     from hive_neuralnet_b200.hybrid import HiveHybridGNN, HybridPieceTensorBatch
     from hive_neuralnet_b200.orchestrator import HybridPUCTConfig, HybridPUCTOrchestrator
+    dev, rank, world = ranks.dev, ranks.rank, ranks.world
     ext = load_extension()
     torch.manual_seed(0)
     net = HiveHybridGNN().eval()
@@ -664,30 +802,14 @@ def run_hybrid(args) -> None:
     cfg = HybridPUCTConfig(num_simulations=sims, batch_size=games, max_game_length=1, dirichlet_epsilon=0.0,
                            seed=4321 + rank, max_tree_nodes=65536, wave_size=HYBRID_WAVE, c_puct=1.5)
     orch = HybridPUCTOrchestrator(net, cfg, device=dev)
+    W, K = args.hybrid_warmup, args.hybrid_steps
     starts = [_mcts_start_states(ext, games, SEED + 131 * (rank * 1000 + i), dev, no_immediate_end=True).cpu()
-              for i in range(args.warmup + args.steps)]
-    for i in range(args.warmup):
-        orch.self_play_batch(starts[i])
-    torch.cuda.synchronize(dev)
-    sampler = ClockSampler(local)
-    sampler.start()
-    if dist is not None:
-        dist.barrier(device_ids=[local])
-    orch.sims_done.zero_()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.warmup, args.warmup + args.steps):
-        orch.self_play_batch(starts[i])
-    e1.record()
-    torch.cuda.synchronize(dev)
-    clocks = sampler.stop()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    done = orch.sims_done.to(torch.float64).reshape(1)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(done, op=dist.ReduceOp.SUM)
-    ms = float(t.item())
-    value = float(done.item()) / (ms / 1e3)
+              for i in range(W + K)]
+    ms, per_rank, done, leaves, rows, clocks, _ = _search_steps(ranks, orch, starts, W, K)
+    value = done / (ms / 1e3)
+    flops = leaves * HYBRID_FLOP_PER_LEAF + rows * HYBRID_FLOP_PER_ROW
+    peak_s, peak_s_src = bf16_peak_tflops(sustained=True)
+    achieved = flops / world / (ms / 1e3) / 1e12
 
     # trunk kernel alone on one wave's worth of leaves (8,192 positions)
     L = games * HYBRID_WAVE
@@ -707,67 +829,90 @@ def run_hybrid(args) -> None:
     t1.record(stream)
     torch.cuda.synchronize(dev)
     trunk_ms = t0.elapsed_time(t1) / reps
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peak, peak_kind = float(json.load(f)["bf16_tflops"]), "measured"
-    except Exception:
-        peak, peak_kind = 1590.0, "fallback"
-    achieved = L * TRUNK_FLOP_PER_LEAF / (trunk_ms / 1e3) / 1e12
+    peak_b, peak_b_src = bf16_peak_tflops(sustained=False)
+    trunk_tf = L * TRUNK_FLOP_PER_LEAF / (trunk_ms / 1e3) / 1e12
+    rank_clocks = ranks.gather_obj(clocks)
+    cpu_roots = starts[0][:32].numpy() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    del orch, starts, st, mv, nl, pb
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return {}
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = mcts_cpu_baseline(net, starts[0][:32].numpy(), sims=128, wave=HYBRID_WAVE, c_puct=1.5, hybrid=True)
-    if rank == 0:
-        line = {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-                "data": "synthetic",
-                "config": {"workload": f"config5: PUCT {games} games/GPU x {sims} sims/move, c_puct 1.5, "
-                                       f"{games * HYBRID_WAVE} leaves/wave, HybridGNNConfig() random init "
-                                       f"({net.count_parameters()} params)",
-                           "simulations": float(done.item()), "games_per_gpu": games,
-                           "parallelism": f"games sharded dp{world}" if world > 1 else "single GPU"},
-                "e2e": {"value": value, "unit": "simulations/s",
-                        "h2d_bytes_per_step": games * STATE_BYTES, "d2h_bytes_per_step": None,
-                        "note": "start states come from host memory and training examples return to it "
-                                "inside every timed step"},
-                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
-                             "kernel": f"k_hybrid_trunk on {L} positions ({trunk_ms:.3f} ms)",
-                             "algorithmic_flop_per_position": TRUNK_FLOP_PER_LEAF},
-                "cpu_baseline": cpu,
-                "clocks": clocks}
+    if cpu_roots is not None:
+        cpu = mcts_cpu_baseline(net, cpu_roots, sims=128, wave=HYBRID_WAVE, c_puct=1.5, hybrid=True)
+    return {"metric": "MCTS simulations/sec", "value": value, "unit": "simulations/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"config5: PUCT {games} games/GPU x {sims} sims/move, c_puct 1.5, "
+                                   f"{games * HYBRID_WAVE} leaves/wave, HybridGNNConfig() random init "
+                                   f"({net.count_parameters()} params)",
+                       "simulations": done, "games_per_gpu": games,
+                       "parallelism": f"games sharded dp{world}" if world > 1 else "single GPU"},
+            "e2e": {"value": value, "unit": "simulations/s", "h2d_bytes_per_step": games * STATE_BYTES,
+                    "d2h_bytes_per_step": games * (STATE_BYTES + MAX_MOVES * 4 + 4 + 1),
+                    "note": "the timed steps are end to end: start states come from host memory and training "
+                            "examples return to it inside every step (self_play_batch's public API)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_s, "unit": "TFLOP/s",
+                         "frac": achieved / peak_s, "peak_source": peak_s_src, "traffic": None,
+                         "formula": f"{HYBRID_FLOP_PER_LEAF:.3g} FLOP per evaluated position + "
+                                    f"{HYBRID_FLOP_PER_ROW:.3g} per legal action, per GPU per step time",
+                         "evaluated_positions": leaves, "successor_rows": rows,
+                         "trunk_kernel": {"kernel": f"k_hybrid_trunk on {L} positions ({trunk_ms:.3f} ms, alone)",
+                                          "achieved": trunk_tf, "peak": peak_b, "peak_source": peak_b_src,
+                                          "frac": trunk_tf / peak_b,
+                                          "algorithmic_flop_per_position": TRUNK_FLOP_PER_LEAF}},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "per_rank": {"ms_per_step": [t / K for t in per_rank],
+                         "clocks": [{"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons")} for c in rank_clocks]}}
+
+
+def run_gpu(args) -> None:
+    import torch
+    ranks = Ranks()
+    line = {}
+    if args.workload in ("all", "movegen"):
+        line = bench_movegen(args, ranks)
+    if args.workload in ("all", "mcts"):
+        rec = bench_mcts(args, ranks)
+        line = rec if args.workload == "mcts" else {**line, "mcts": rec}
+    if args.workload in ("all", "hybrid"):
+        rec = bench_hybrid(args, ranks)
+        line = rec if args.workload == "hybrid" else {**line, "hybrid": rec}
+    torch.cuda.synchronize(ranks.dev)
+    ranks.close()
+    if ranks.rank == 0:
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
 
 
 def main() -> None:
     global POSITIONS
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["movegen", "mcts", "fnn", "hybrid"], default="movegen")
+    ap.add_argument("--workload", choices=["all", "movegen", "mcts", "fnn", "hybrid"], default="all",
+                    help="all: the headline (config 2) line with the config-4 and config-5 records in it")
     ap.add_argument("--games", type=int, default=MCTS_GAMES)
     ap.add_argument("--sims", type=int, default=MCTS_SIMS)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--mcts-steps", type=int, default=5, help="timed searched moves of the config-4 record")
+    ap.add_argument("--mcts-warmup", type=int, default=3)
+    ap.add_argument("--hybrid-steps", type=int, default=10, help="timed searched moves of the config-5 record")
+    ap.add_argument("--hybrid-warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline legs")
     ap.add_argument("--e2e-chunk", type=int, default=16384, help="positions per pipelined chunk of the e2e leg")
     ap.add_argument("--positions", type=int, default=POSITIONS,
                     help="positions per GPU (profiling runs use a smaller case)")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3)
+    args.mcts_warmup = max(args.mcts_warmup, 3)
+    args.hybrid_warmup = max(args.hybrid_warmup, 3)
     POSITIONS = args.positions
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "mcts":
-        run_mcts(args)
     elif args.workload == "fnn":
         run_fnn(args)
-    elif args.workload == "hybrid":
-        run_hybrid(args)
     else:
         run_gpu(args)
 

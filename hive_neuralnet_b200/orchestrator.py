@@ -164,6 +164,16 @@ class _SearchBase:
         self.trace: list | None = None  # set to a list to record per-wave evaluator outputs
         # simulations executed (leaves with a node), accumulated on the device
         self.sims_done = torch.zeros((), dtype=torch.int64, device=self.device)
+        # positions and successor rows the evaluator ran (the work behind the
+        # FLOP count of a step): a host count and a device count, no sync
+        self.leaves_evaluated = 0
+        self.rows_evaluated = torch.zeros((), dtype=torch.int64, device=self.device)
+
+    def _uniform(self, *shape: int) -> torch.Tensor:
+        """U[0, 1) float32 draws of the search (the reference's torch.rand
+        calls), from the driver's seeded generator; the single place a test
+        substitutes recorded draws."""
+        return torch.rand(shape, device=self.device, generator=self.gen)
 
     # -- tree ---------------------------------------------------------------
     def _alloc_tree(self, B: int) -> dict[str, torch.Tensor]:
@@ -321,6 +331,9 @@ class _SearchBase:
         return torch.where(valid_queen, surround, torch.zeros_like(surround)), qcell
 
     def _eval_states(self, states, legal_moves, num_legal, total, root_features=None):
+        self.leaves_evaluated += int(total)
+        if total:
+            self.rows_evaluated += num_legal[:total].to(torch.int64).clamp(0, self._max_legal).sum()
         return self.evaluator.eval_states(states, legal_moves, num_legal, total, root_features)
 
 
@@ -384,7 +397,7 @@ class FNNMCTSOrchestrator(_SearchBase):
             valid = valid & allowed_slot_mask
         reserve = min(int(cfg.queen_surround_reserve_slots), k)
         if reserve <= 0:
-            u = torch.rand(total, self._max_legal, device=self.device, generator=self.gen).clamp(1e-4, 1 - 1e-4)
+            u = self._uniform(total, self._max_legal).clamp(1e-4, 1 - 1e-4)
             g = torch.where(valid, -torch.log(-torch.log(u)), torch.full_like(u, -1e30))
             return torch.topk(g + legal_logits, k, dim=1).indices.to(torch.int32)
         qual = self._queen_surround_qualifying_mask(states, legal_moves, num_legal, total)
@@ -468,7 +481,7 @@ class FNNMCTSOrchestrator(_SearchBase):
                 child_q.zero_()
             search_rows = has_actions & ~has_win & ~forced
             legal_logits = torch.where(allowed, priors.clamp(min=1e-20).log(), torch.full_like(priors, -1e30))
-            u = torch.rand(B, L, device=dev, generator=self.gen).clamp(1e-4, 1 - 1e-4)
+            u = self._uniform(B, L).clamp(1e-4, 1 - 1e-4)
             gumbel = torch.where(allowed, -torch.log(-torch.log(u)), torch.full_like(u, -1e30))
             topk_slots = self._root_candidate_slots(states, legal, nl, priors, legal_logits, B, allowed)
             game_active = search_rows.to(torch.int8)
@@ -535,7 +548,7 @@ class FNNMCTSOrchestrator(_SearchBase):
                 probs[rows_w, wins[rows_w]] = 1.0
                 chosen = torch.where(has_win, wins, chosen)
             if bool(forced.any().item()):
-                rnd = (torch.rand((B,), device=dev, generator=self.gen) * n64.clamp(min=1).float()).to(torch.int64)
+                rnd = (self._uniform(B) * n64.clamp(min=1).float()).to(torch.int64)
                 chosen = torch.where(forced, rnd, chosen)
                 probs = torch.where(forced.unsqueeze(1), torch.zeros_like(probs), probs)
             records.append((states.cpu().numpy(), probs.cpu().numpy(), nl.cpu().numpy(),

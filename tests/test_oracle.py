@@ -140,3 +140,37 @@ def test_action_indices_give_the_reference_legal_mask(orc):
         a = act[i, :no[i]]
         want[i, a[a >= 0]] = 1.0
     assert np.array_equal(O.ref().legal_mask(st, mo, no), want)
+
+
+def test_oracle_matches_reference_edge_fixtures(orc):
+    """The C oracle on the reference's edge-case fixtures (move lists cut at
+    256, 5-high stacks, grid edge, pillbug / mosquito rule scenarios;
+    tests/golden/make_edge_golden.py), every output bit-exact."""
+    g = dict(np.load(os.path.join(GOLD, "golden_edge.npz")))
+    with open(os.path.join(GOLD, "golden_edge.json")) as f:
+        d = json.load(f)
+    st = g["states"]
+    o = _outputs(orc, st)
+    for k in ("moves", "num_legal", "compact_moves", "compact_num", "articulation", "actions", "centroids"):
+        assert np.array_equal(o[k], g[k]), k
+    assert np.array_equal(o["features"].view(np.uint32), g["features"].view(np.uint32))
+    offs = np.concatenate([[0], np.cumsum(o["num_legal"])])
+    hyb = orc.hybrid_encode(st, o["moves"], o["num_legal"])
+    for i in range(len(st)):
+        n = int(o["num_legal"][i])
+        assert _digest(o["succ_features"][offs[i]:offs[i + 1]]) == d["successor_features"][i], g["case"][i]
+        kids = orc.apply_moves(np.repeat(st[i:i + 1], n, 0), o["moves"][i, :n])
+        assert _digest(kids) == d["successor_states"][i], g["case"][i]
+        assert _digest(*(a[i:i + 1] for a in hyb[:7])) == d["hybrid_tokens"][i], g["case"][i]
+        assert _digest(hyb[7][i, :n]) == d["hybrid_move_features"][i], g["case"][i]
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference build not present")
+def test_oracle_tactical_probe_matches_reference_on_edge_fixtures(orc):
+    g = dict(np.load(os.path.join(GOLD, "golden_edge.npz")))
+    st, mv, nl = g["states"], g["moves"], g["num_legal"]
+    rng = np.random.default_rng(17)
+    pri = rng.uniform(0.01, 1, (len(st), 256)).astype(np.float32)
+    pri = np.where(np.arange(256)[None, :] < nl[:, None], pri, 0).astype(np.float32)
+    for a, b in zip(orc.tactical_probe(st, mv, nl, pri), O.ref().tactical_probe(st, mv, nl, pri)):
+        assert np.array_equal(a, b)
