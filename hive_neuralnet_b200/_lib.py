@@ -72,6 +72,7 @@ _SIGNATURES = {
     "hv_version": ([], _int),
     "hv_status_string": ([_int], C.c_char_p),
     "hv_get_error": ([_vp, _int], _int),
+    "hv_set_wait_limit_ns": ([C.c_uint64], _int),
     "hv_create_initial_states": ([_vp, _i64, _int, _vp], _int),
     "hv_generate_legal_moves": ([_vp, _i64, _vp, _vp, _vp], _int),
     "hv_generate_legal_moves_and_fnn_features": ([_vp, _i64, _vp, _vp, _vp, _vp], _int),

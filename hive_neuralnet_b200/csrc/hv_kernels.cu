@@ -1170,7 +1170,14 @@ __global__ void __launch_bounds__(kThreads) k_mcts_replay(const uint8_t* __restr
     uint8_t* st = smem_raw + (threadIdx.x >> 5) * kStateBytes;
     const int nwarps = gridDim.x * kWarpsPerBlock;
     for (int s = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); s < total; s += nwarps) {
-        if (leaf[s] < 0) continue;
+        if (leaf[s] < 0) {
+            // no simulation in this slot: an all-zero state, as the
+            // reference's zero-filled leaf buffer holds there (so the caller
+            // needs no zero-fill of the whole buffer first)
+            uint4* o4 = reinterpret_cast<uint4*>(leaves + (int64_t)s * kStateBytes);
+            for (int i = lane_id(); i < kStateBytes / 16; i += 32) o4[i] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+        }
         stage_async<kState16>(st, roots + (int64_t)(s % B) * kStateBytes);
         stage_wait();
         if (lane_id() == 0) {
@@ -1640,6 +1647,11 @@ int hv_get_error(uint32_t* out, int clear) {
         uint32_t z = 0;
         if (cudaMemcpyToSymbol(g_error, &z, sizeof(z)) != cudaSuccess) return HV_ECUDA;
     }
+    return HV_OK;
+}
+
+int hv_set_wait_limit_ns(uint64_t ns) {
+    if (cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)) != cudaSuccess) return HV_ECUDA;
     return HV_OK;
 }
 

@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) k_fnn_rows(const float* __rest
         if (gt == 0) {
             atomicOr(err_word, kErrF32Wait);
             for (int b = 0; b < 2; b++)
-                if ((pend >> b) & 1u) mbar_wait(&s->bar[g][b], (phases >> b) & 1u);
+                if ((pend >> b) & 1u) mbar_drain(&s->bar[g][b], (phases >> b) & 1u);
         }
     }
 }

@@ -279,9 +279,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_mlp_rows_tc(const __half* __r
         // a bounded wait gave up: record it, let the group's MMAs and the
         // weight copy finish (bounded again), free TMEM and return
         if (gt == 0) atomicOr(err_word, kErrMlpWait);
-        if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
-        if (gt == 0 && xpend) mbar_wait(&s->bar_x[g], xphase);
-        if (t == 0 && live) mbar_wait(&s->bar_w, 0);
+        if (pending) mbar_drain(&s->bar[g], phase ^ 1u);
+        if (gt == 0 && xpend) mbar_drain(&s->bar_x[g], xphase);
+        if (t == 0 && live) mbar_drain(&s->bar_w, 0);
     }
     tc_fence_before();
     __syncthreads();
@@ -562,8 +562,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) k_leaf_root_tc(const float* __r
     if (failed) {
         // as in k_mlp_rows_tc: record, drain this group's MMAs and the weight copy (bounded)
         if (gt == 0) atomicOr(err_word, kErrMlpWait);
-        if (pending) mbar_wait(&s->bar[g], phase ^ 1u);
-        if (t == 0 && live) mbar_wait(&s->bar_w, 0);
+        if (pending) mbar_drain(&s->bar[g], phase ^ 1u);
+        if (t == 0 && live) mbar_drain(&s->bar_w, 0);
     }
     tc_fence_before();
     __syncthreads();

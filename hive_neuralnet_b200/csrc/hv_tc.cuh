@@ -47,13 +47,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// wait for the phase with the given parity to complete; false after ~1 s
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wall-time limit of the waits after which a kernel gives up on its work
+// (mbar_wait).  Only a test changes it (hv_set_wait_limit_ns): 0 makes every
+// such wait give up at once, while the copy or MMA it waits for is still in
+// flight, so that the exit path runs on a real case.
+__device__ uint64_t g_wait_limit_ns = kWaitNs;
+
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 0;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 63 && globaltimer() - t0 > kWaitNs) return false;
+        if ((i & 63) == 63 && globaltimer() - t0 > limit_ns) return false;
     }
+}
+
+// wait for the phase with the given parity to complete; false after the
+// wait limit (~1 s)
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t limit = g_wait_limit_ns;
+    if (limit == 0) return false;
+    return mbar_wait_for(bar, parity, limit);
+}
+
+// the exit path's wait for a copy or MMA this CTA started: always the full
+// ~1 s, whatever the give-up limit, so no work of the CTA outlives it
+__device__ __noinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, kWaitNs);
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {

@@ -470,9 +470,9 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
         // MMAs in flight finish (bounded again), free TMEM and return
         if (t == 0) {
             atomicOr(err_word, 4u);
-            if (wpend) mbar_wait(&s->bar_w, wphase);
+            if (wpend) mbar_drain(&s->bar_w, wphase);
         }
-        if (mpend) mbar_wait(&s->bar_mma, mphase ^ 1u);
+        if (mpend) mbar_drain(&s->bar_mma, mphase ^ 1u);
     }
     tc_fence_before();
     __syncthreads();

@@ -117,8 +117,19 @@ def pack_weights(net: HiveFNN, device: torch.device | str = "cuda") -> torch.Ten
     return flat.to(device).contiguous()
 
 
+# Batches up to this many leaves size the row workspace for 256 rows per leaf
+# (about 2 GB at 16,384 leaves) instead of counting the rows: the count would
+# be a device -> host read, one synchronisation per search wave.  The row
+# kernels read the actual count from the device.
+ROWS_BOUND_MAX_LEAVES = 16384
+
+
 def _rows(num_legal: torch.Tensor, total: int) -> int:
-    """Successor rows of a batch: sum of min(max(num_legal, 0), 256) (one device sync)."""
+    """Rows to size the row pipeline for: an upper bound (256 per leaf, no
+    synchronisation) for batches up to ROWS_BOUND_MAX_LEAVES, else the exact
+    sum of min(max(num_legal, 0), 256) (one device sync)."""
+    if total <= ROWS_BOUND_MAX_LEAVES:
+        return total * MAX_LEGAL
     return int(num_legal[:total].clamp(0, MAX_LEGAL).sum().item())
 
 

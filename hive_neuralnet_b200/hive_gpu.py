@@ -602,7 +602,8 @@ class HiveGPUExtension:
             num_candidates, max_root_children, c_puct, B, W, max_nodes, deterministic_non_root, non_root_sigma,
             q_penalty)
         total = leaf.shape[0]
-        leaf_states = torch.zeros((total, SIZEOF_HIVE_STATE), dtype=torch.uint8, device=leaf.device)
+        # every row is written by the replay (zeros where a slot holds no simulation)
+        leaf_states = torch.empty((total, SIZEOF_HIVE_STATE), dtype=torch.uint8, device=leaf.device)
         self.mcts_replay_batch(root_states, leaf_states, paths, plen, leaf, B, total)
         results = self.check_results_batch(leaf_states, total)
         legal, num_legal, feats = self.generate_legal_moves_and_fnn_features_batch(leaf_states, total)

@@ -406,8 +406,12 @@ class FNNMCTSOrchestrator(_SearchBase):
         r_order = torch.topk(rs, reserve, dim=1).indices
         r_valid = torch.arange(reserve, device=self.device).unsqueeze(0) < per_game.unsqueeze(1)
         r_cand = torch.where(r_valid, r_order.to(torch.int32), torch.full_like(r_order, -1, dtype=torch.int32))
-        chosen = torch.zeros_like(valid)
-        chosen.scatter_(1, torch.where(r_valid, r_order, torch.zeros_like(r_order)), r_valid)
+        # reserved slots marked in an extra column's worth of room: entries past
+        # a game's reserve count land in the spare column, never on a real slot
+        chosen = torch.zeros((total, self._max_legal + 1), dtype=torch.bool, device=valid.device)
+        chosen.scatter_(1, torch.where(r_valid, r_order, torch.full_like(r_order, self._max_legal)),
+                        torch.ones_like(r_valid))
+        chosen = chosen[:, :self._max_legal]
         fs = torch.where(valid & ~chosen, priors, torch.full_like(priors, -1e30))
         f_order = torch.topk(fs, k, dim=1).indices
         f_keep = (k - per_game).clamp(min=0)

@@ -48,6 +48,15 @@ const char* hv_status_string(int status);
  * device.  Synchronous: call it between steps, not inside a hot loop. */
 int hv_get_error(uint32_t* out, int clear);
 
+/* Test hook, no counterpart in the reference: set the current device's limit
+ * on the tensor-core kernels' bounded waits (mbarrier waits for bulk copies
+ * and MMAs; default 1e9 ns).  0 makes every such wait give up at once, with
+ * its copy or MMA still in flight: the kernel sets its error bit (4: the
+ * hybrid trunk, 8: the row and leaf networks), waits up to 1 s for the work
+ * it started, frees its tensor memory and returns, and the call's outputs are
+ * undefined.  Synchronous; not for use inside a step. */
+int hv_set_wait_limit_ns(uint64_t ns);
+
 /* create_initial_states(batch_size, expansion_mask)
  * replaces bindings.cpp:264-266 / game_logic.cu:413-428.
  * states: [batch, 3424] uint8 (written). */
@@ -174,7 +183,10 @@ int hv_mcts_select(const hv_tree* tree, int mode, const float* child_init_q, con
                    void* stream);
 
 /* mcts_replay_batch (bindings.cpp:118-121, mcts_tree.cuh:298-320):
- * leaf_states[s] = root_states[s % B] + move path s. */
+ * leaf_states[s] = root_states[s % B] + move path s; a slot with leaf[s] < 0
+ * (no simulation) is written as an all-zero state, where the reference
+ * leaves its buffer as it was (its callers zero-fill it, the rows are
+ * unused), so a caller needs no zero-fill before the call. */
 int hv_mcts_replay(const uint8_t* root_states, uint8_t* leaf_states, const uint8_t* move_paths,
                    const int32_t* path_len, const int32_t* leaf, int B, int total, void* stream);
 

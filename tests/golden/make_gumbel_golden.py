@@ -16,6 +16,10 @@ tests/test_gpu_training_logic.py builds its orchestrators) and given
   (exact on any device, so the network cannot blur a decision);
 * ``torch`` factory calls and ``.cuda()`` mapped to the CPU while it runs.
 
+Each case uses the first seed whose search meets no immediate win: a win
+anywhere in the batch zeroes every game's priors (:621-625), after which the
+candidate top-k breaks ties, in an order that differs between CPU and CUDA.
+
 Every ``torch.rand`` draw of the search (Gumbel uniforms, forced-random
 moves) is recorded, so the B200 run can replay the same noise.  Recorded per
 searched move: the candidate slots of every halving round and of the final
@@ -38,7 +42,6 @@ flags).  Cases:
 """
 from __future__ import annotations
 
-import contextlib
 import os
 import sys
 
@@ -48,13 +51,12 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-sys.path.insert(0, os.path.dirname(HERE))
 
 from oracle import oracle as O  # noqa: E402
-from hash_eval import hash_eval  # noqa: E402
+from tests.hash_eval import hash_eval  # noqa: E402
+from tests.reference_cpu import reference_module, torch_on_cpu  # noqa: E402
 
-sys.path.insert(0, O.reference_dir())
-import hive_fnn.fnn_mcts_orchestrator as R  # noqa: E402  (the reference module)
+R = reference_module("hive_fnn.fnn_mcts_orchestrator")  # the reference module
 
 TREE_NAMES = [n for n, _, _ in O.TREE_FIELDS]
 
@@ -157,34 +159,6 @@ class RefHostExt:
         O.mcts_root_noise("ref", tree, _np(noise), _np(root_nodes), float(eps), float(temp))
 
 
-@contextlib.contextmanager
-def torch_on_cpu(draws: list):
-    """Map the module's device="cuda" factory calls and .cuda() to the CPU,
-    and record every torch.rand draw."""
-    saved = {k: getattr(torch, k) for k in ("zeros", "ones", "full", "arange", "rand")}
-    saved_cuda = torch.Tensor.cuda
-
-    def strip(fn, record=False):
-        def f(*a, **k):
-            if k.get("device") is not None and str(k["device"]).startswith("cuda"):
-                k["device"] = "cpu"
-            out = fn(*a, **k)
-            if record:
-                draws.append(out.numpy().copy())
-            return out
-        return f
-
-    for k, fn in saved.items():
-        setattr(torch, k, strip(fn, record=(k == "rand")))
-    torch.Tensor.cuda = lambda self, *a, **k: self
-    try:
-        yield
-    finally:
-        for k, fn in saved.items():
-            setattr(torch, k, fn)
-        torch.Tensor.cuda = saved_cuda
-
-
 def run_reference(case: dict, start: np.ndarray, seed: int):
     cfg = R.FNNMCTSConfig(**case["cfg"])
     orch = R.FNNMCTSOrchestrator.__new__(R.FNNMCTSOrchestrator)
@@ -222,6 +196,25 @@ def run_reference(case: dict, start: np.ndarray, seed: int):
     orch._gather_root_candidate_stats = cand_stats
     orch._gather_root_child_stats = child_stats
     orch._build_policy_target = target
+    # an immediate win anywhere in the batch zeroes every game's priors
+    # (fnn_mcts_orchestrator.py:621-625): the candidate top-k then breaks ties
+    # among equal priors, and CPU and CUDA top-k break ties differently, so a
+    # case is kept only if its search never meets one
+    wins_seen = []
+    imm_fn, tac_fn = orch._find_immediate_wins, orch._analyze_short_tactics
+
+    def find_wins(*a, **k):
+        w = imm_fn(*a, **k)
+        wins_seen.append(bool((w >= 0).any()))
+        return w
+
+    def tactics(*a, **k):
+        t = tac_fn(*a, **k)
+        wins_seen.append(bool((t.winning_moves >= 0).any()))
+        return t
+
+    orch._find_immediate_wins = find_wins
+    orch._analyze_short_tactics = tactics
     torch.manual_seed(seed)
     with torch_on_cpu(draws):
         examples = orch.self_play_batch(torch.from_numpy(start.copy()))
@@ -236,7 +229,7 @@ def run_reference(case: dict, start: np.ndarray, seed: int):
             ex_n.append(len(e.policy_target))
             ex_val.append([e.value_target, e.value_weight])
             ex_flags.append([int(e.use_for_policy), int(e.use_for_value)])
-    return dict(draws=draws, candidates=cands, visits=np.array(visits), probs=np.array(probs),
+    return dict(any_win=any(wins_seen), draws=draws, candidates=cands, visits=np.array(visits), probs=np.array(probs),
                 ex_game=np.array(ex_game, np.int32), ex_state=np.array(ex_state, np.uint8),
                 ex_policy=np.array(ex_pi, np.float32), ex_len=np.array(ex_n, np.int32),
                 ex_value=np.array(ex_val, np.float32), ex_flags=np.array(ex_flags, np.int8))
@@ -248,8 +241,14 @@ def main() -> None:
         raise SystemExit("reference build unavailable: the reference tree is needed to make goldens")
     out = {}
     for name, case in CASES.items():
-        start = start_states(O.ref(), case["games"], case["seed"], case["max_ply"], case["mask"])
-        rec = run_reference(case, start, 1000 + case["seed"])
+        for attempt in range(60):
+            seed = case["seed"] + 1000 * attempt
+            start = start_states(O.ref(), case["games"], seed, case["max_ply"], case["mask"])
+            rec = run_reference(case, start, 1000 + seed)
+            if not rec["any_win"]:
+                break
+        else:
+            raise SystemExit(f"{name}: every seed met an immediate win")
         out[f"{name}/start"] = start
         out[f"{name}/cfg"] = np.array(repr(case["cfg"]))
         out[f"{name}/n_draws"] = np.array(len(rec["draws"]), np.int32)
