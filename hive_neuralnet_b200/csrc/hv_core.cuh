@@ -237,18 +237,6 @@ __device__ __forceinline__ int warp_excl_scan(int v) {
     return x - v;
 }
 
-// k-th set cell (k < total) of a row-bitboard stored in smem with row prefix
-__device__ __forceinline__ int kth_cell(const uint32_t* rows, const uint16_t* pre, int k) {
-    int lo = 0, hi = kBoard - 1;  // largest r with pre[r] <= k
-#pragma unroll 1
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (pre[mid] <= k) lo = mid;
-        else hi = mid - 1;
-    }
-    return (lo << 5) + __fns(rows[lo], 0, k - pre[lo] + 1);
-}
-
 // ---------------------------------------------------------------------------
 // per-position setup
 // ---------------------------------------------------------------------------

@@ -239,6 +239,50 @@ __device__ __forceinline__ uint32_t neighbour_types(WarpSmem* w, int cell) {
     return __reduce_or_sync(kFull, t);
 }
 
+// ---------------------------------------------------------------------------
+// existence of a move (the compact list's has_*_move predicates,
+// move_gen.cuh:1416-1563): lane d tests direction d, one ballot.  Same tests
+// as the walk engine's first round for these modes.
+// ---------------------------------------------------------------------------
+// queen / ant / pillbug: a slide out of the cell (lifting the piece does not
+// change the slides out of its own cell, so the position's masks serve)
+__device__ __forceinline__ bool slide_out(WarpSmem* w, int cell) {
+    const int l = lane_id();
+    return __ballot_sync(kFull, l < 6 && rowbit(w->sl[l < 6 ? l : 0], cell)) != 0u;
+}
+
+// beetle (or a stacked mosquito): elevated gate or slide (WM_BEETLE)
+__device__ __forceinline__ bool beetle_out(WarpSmem* w, int cell) {
+    Pos P{w};
+    const int l = lane_id();
+    bool ok = false;
+    if (l < 6) {
+        const int nb = nbr(cell, l);
+        if (nb >= 0) {
+            const int hc = P.height(cell), hd = P.height(nb), mh = hd > hc - 1 ? hd : hc - 1;
+            ok = mh > 0 ? !P.gate_blocked(cell, l, mh) : (bool)rowbit(w->sl[l], cell);
+        }
+    }
+    return __ballot_sync(kFull, ok) != 0u;
+}
+
+// grasshopper: over a line of pieces onto the first empty cell on the grid (WM_HOP)
+__device__ __forceinline__ bool hop_out(WarpSmem* w, int cell) {
+    Pos P{w};
+    const int l = lane_id();
+    bool ok = false;
+    if (l < 6) {
+        const int nb = nbr(cell, l);
+        if (nb >= 0 && P.occupied(nb)) {
+            int p = nb;
+#pragma unroll 1
+            while (p >= 0 && P.occupied(p)) p = nbr(p, l);
+            ok = p >= 0;
+        }
+    }
+    return __ballot_sync(kFull, ok) != 0u;
+}
+
 // walk mode of a piece type (1..8), pillbug moves like the queen
 __device__ __forceinline__ int mode_of(int pt) {
     // Q A G S B M L P -> STEP ANT HOP SPIDER BEETLE (mosquito) LADY STEP
@@ -288,6 +332,25 @@ __device__ __noinline__ int gen_mosquito(WarpSmem* w, int cell, bool first_only,
         }
     }
     return cnt;
+}
+
+// Does a mosquito have a move (gen_mosquito's first_only answer)?  Stacked:
+// as a beetle.  On the ground: any copied movement has one; the cheap
+// lane-per-direction tests go first, and the slide masks are rebuilt with
+// the mosquito lifted only if a spider part is still to test.
+__device__ __noinline__ bool mosquito_out(WarpSmem* w, uint32_t occ_row, int cell) {
+    Pos P{w};
+    if (P.height(cell) > 1) return beetle_out(w, cell);
+    const uint32_t t = neighbour_types(w, cell);
+    if ((t & 0x106u) && slide_out(w, cell)) return true;  // queen, pillbug, ant
+    if ((t & 0x8u) && hop_out(w, cell)) return true;      // grasshopper
+    if ((t & 0x20u) && beetle_out(w, cell)) return true;  // beetle
+    if ((t & 0x80u) && walk(w, cell, WM_LADY, w->dst, 32, true)) return true;
+    if (t & 0x10u) {                                      // spider
+        lift_mover(w, occ_row, cell);
+        return walk(w, cell, WM_SPIDER, w->dst, 32, true) != 0;
+    }
+    return false;
 }
 
 // Destinations of one own piece; returns the list (w->dst or w->tmp) and count.
@@ -362,6 +425,27 @@ __device__ __noinline__ int placement_cells(WarpSmem* w, uint32_t occ, uint32_t 
     return __shfl_sync(kFull, pre + c, 31);
 }
 
+// The placement cells of w->prow in ascending order, as reference cell
+// indices, into w->dst (free until the first mover's walk): lane r lists the
+// cells of row r from the row's prefix count, so that a placement move
+// finds its cell by one load instead of a search over the rows.  At most
+// 6 x 14 cells border the side's pieces, inside dst's 128 entries.
+__device__ __forceinline__ void placement_list(WarpSmem* w) {
+    const int l = lane_id();
+    if (l < kBoard) {
+        uint32_t bits = w->prow[l];
+        int k = w->ppref[l];
+#pragma unroll 1
+        while (bits) {
+            const int q = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (k < 128) w->dst[k] = (uint16_t)p_to_c((l << 5) + q);
+            k++;
+        }
+    }
+    __syncwarp();
+}
+
 // placeable piece-type mask of the side to move (move_gen.cuh:1161-1174)
 __device__ __forceinline__ uint32_t placeable_types(const Pos& P, int color, bool forced) {
     uint32_t m = 0;
@@ -389,11 +473,18 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, uint32_t* err) {
         int nt = __popc(types);
         int total = np * nt;
         if (total > kMaxMoves) total = kMaxMoves;
+        placement_list(w);
+        // cell-major, type-minor (move k * nt + j): a lane per cell writes its
+        // cell's types in ascending order
 #pragma unroll 1
-        for (int m = l; m < total; m += 32) {
-            int k = m / nt, j = m - (m / nt) * nt;
-            int cell = kth_cell(w->prow, w->ppref, k);
-            put_move(w, m, 0, __fns(types, 0, j + 1) + 1, 0, p_to_c(cell));
+        for (int k = l; k < np && k * nt < total; k += 32) {
+            const int c = w->dst[k < 128 ? k : 127];
+            uint32_t t = types;
+#pragma unroll 1
+            for (int m = k * nt; t && m < total; m++) {
+                put_move(w, m, 0, __ffs(t), 0, c);
+                t &= t - 1;
+            }
         }
         count = total;
     }
@@ -436,9 +527,12 @@ __device__ __noinline__ int gen_legal(WarpSmem* w, uint32_t* err) {
             uint32_t tm, dm;
             throw_sets(w, pb, tm, dm);
             int nt = __popc(tm), nd = __popc(dm), total = nt * nd;
+            // m / nd for m < 64 and nd <= 6 as a multiply by 2^16 / nd + 1
+            // (exact over that range), no integer division per move
+            const uint32_t inv = nd ? 0x10000u / (uint32_t)nd + 1u : 0u;
 #pragma unroll 1
             for (int m = l; m < total; m += 32) {
-                int kt = m / nd, kd = m - (m / nd) * nd;
+                int kt = (int)(((uint32_t)m * inv) >> 16), kd = m - kt * nd;
                 int target = nbr(pb, __fns(tm, 0, kt + 1));
                 int dest = nbr(pb, __fns(dm, 0, kd + 1));
                 if (count + m < kMaxMoves)
@@ -471,9 +565,9 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, uint32_t* err) {
     if (any) {
         int np = placement_cells(w, S.occ, S.own, S.opp, turn);
         int total = np < kMaxMoves ? np : kMaxMoves;
+        placement_list(w);
 #pragma unroll 1
-        for (int m = l; m < total; m += 32)
-            put_move(w, m, 0, 0, 0, p_to_c(kth_cell(w->prow, w->ppref, m)));
+        for (int m = l; m < total; m += 32) put_move(w, m, 0, 0, 0, w->dst[m < 128 ? m : 127]);
         count = total;
     }
     if (!queen_down || count >= kMaxMoves) {
@@ -501,9 +595,12 @@ __device__ __noinline__ int gen_compact(WarpSmem* w, uint32_t* err) {
         // queen, ant, pillbug: a move exists iff one slide out of the cell is
         // legal (the first step of each; lifting the piece does not change
         // slides out of its own cell), read from the position's slide masks
-        const bool slider = pt == 1 || pt == 2 || pt == 8;
-        const bool has = slider ? __ballot_sync(kFull, l < 6 && rowbit(w->sl[l < 6 ? l : 0], cell)) != 0u
-                                : piece_moves(w, S.occ, cell, pt, 128, true, err, &list) != 0;
+        bool has;
+        if (pt == 1 || pt == 2 || pt == 8) has = slide_out(w, cell);
+        else if (pt == 3) has = hop_out(w, cell);
+        else if (pt == 5) has = beetle_out(w, cell);
+        else if (pt == 6) has = mosquito_out(w, S.occ, cell);
+        else has = piece_moves(w, S.occ, cell, pt, 128, true, err, &list) != 0;  // spider, ladybug
         if (has) {
             seen |= bit;
             if (l == 0) put_move(w, count, 1, pt, p_to_c(cell), 0);
