@@ -345,12 +345,14 @@ def bench_movegen(args, ranks: Ranks) -> dict:
         box["out"] = ext.generate_legal_moves_and_fnn_features_batch(states, P)
 
     # ---- device-resident throughput: exactly K timed steps ----
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
+    # the clock sampler starts first; the warm-up steps then run right before
+    # the timed region, so the GPU does not enter it from an idle spell (a
+    # GPU idle for a fraction of a second runs its first steps slower)
     sampler = ClockSampler(ranks.local)
     sampler.start()
     time.sleep(0.3)
+    for _ in range(args.warmup):
+        step()
     ms_max, per_rank_ms = timed_region(ranks, step, args.steps)
     value = world * P * args.steps / (ms_max / 1e3)
     # ---- the same steps over a region of >= 2 s (every rank the same count) ----
@@ -569,11 +571,11 @@ def _search_steps(ranks: Ranks, orch, starts, warmup: int, steps: int):
     simulations of all ranks, evaluated positions and rows of all ranks,
     clocks, the last step's examples)."""
     import torch
+    sampler = ClockSampler(ranks.local)
+    sampler.start()
     for i in range(warmup):
         orch.self_play_batch(starts[i])
     torch.cuda.synchronize(ranks.dev)
-    sampler = ClockSampler(ranks.local)
-    sampler.start()
     orch.sims_done.zero_()
     orch.rows_evaluated.zero_()
     orch.leaves_evaluated = 0

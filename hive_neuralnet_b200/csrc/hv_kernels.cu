@@ -24,6 +24,7 @@
 #include "hv_mlp.cuh"
 #include "hv_mlp_tc.cuh"
 #include "hv_mlp32.cuh"
+#include "hv_fnn_tc.cuh"
 #include "../../include/hive_b200.h"
 
 namespace hv {
@@ -207,7 +208,15 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
 // 122..127 zero); kSlabF32 = fp32 tiles of kF32Rows (64) rows in 4-feature
 // chunks (chunk c of row r at ((tile * 32 + c) * 64 + r % 64) * 4 floats,
 // features 122..127 zero) for the FNN row network.
-enum : int { kRowsF32 = 0, kSlabF16 = 1, kSlabF32 = 2 };
+// kSlabF16x2 = 128-row tiles of the features split into fp16 high and low
+// parts (x = hi + lo to ~2^-22) for the FNN's tensor-core row network: tile t
+// holds the hi slab [16 chunks][128 rows][8] then the lo slab, 64 KB.
+enum : int { kRowsF32 = 0, kSlabF16 = 1, kSlabF32 = 2, kSlabF16x2 = 3 };
+
+// row a's chunk c (8 halves) of a kSlabF16x2 tile buffer: hi part; the lo part follows 16 x 128 x 8 halves later
+__device__ __forceinline__ int64_t f16x2_at(int64_t a, int c) {
+    return (a >> 7) * (2 * 16 * 128 * 8) + ((int64_t)c * 128 + (a & 127)) * 8;
+}
 template <int OUT>
 __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
     const uint8_t* __restrict__ states, int64_t num_states, const uint8_t* __restrict__ legal_moves,
@@ -246,6 +255,12 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                     if (lane_id() < 16)
                         *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + lane_id()) * 128 + (a & 127)) * 8) =
                             make_uint4(0, 0, 0, 0);
+                } else if (OUT == kSlabF16x2) {
+                    if (lane_id() < 16) {
+                        __half* q = slab + f16x2_at(a, lane_id());
+                        *reinterpret_cast<uint4*>(q) = make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(q + 16 * 128 * 8) = make_uint4(0, 0, 0, 0);
+                    }
                 } else if (OUT == kSlabF32) {
                     *reinterpret_cast<float4*>(feats_out + (((a / kF32Rows) * 32 + lane_id()) * kF32Rows +
                                                             a % kF32Rows) * 4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -278,7 +293,20 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                 features(w, n, f);
                 __syncwarp();
                 const int c = lane_id();
-                if (OUT == kSlabF32) {
+                if (OUT == kSlabF16x2) {
+                    if (c < 16) {
+                        __align__(16) __half hi[8], lo[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float x = 8 * c + i < kFeat ? f[8 * c + i] : 0.0f;
+                            hi[i] = __float2half_rn(x);
+                            lo[i] = __float2half_rn(x - __half2float(hi[i]));
+                        }
+                        __half* q = slab + f16x2_at(a, c);
+                        *reinterpret_cast<uint4*>(q) = *reinterpret_cast<const uint4*>(hi);
+                        *reinterpret_cast<uint4*>(q + 16 * 128 * 8) = *reinterpret_cast<const uint4*>(lo);
+                    }
+                } else if (OUT == kSlabF32) {
                     float v[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) v[i] = 4 * c + i < kFeat ? f[4 * c + i] : 0.0f;
@@ -1500,6 +1528,13 @@ struct RowWorkspace {
     float* logits;       // [count][256] (when the caller passes none)
 };
 
+// The FNN row network of widths 32 and up (the medium and large presets)
+// runs on the tensor cores with split fp16 products; the 8-wide small
+// preset keeps the fp32 CUDA-core kernel: LayerNorm over 8 neurons amplifies
+// rounding differences to the edge of the 1e-5 check even with exact
+// products, and the split adds its own ~2^-22 on top.
+static inline bool fnn_rows_on_tensor_cores(FnnDims fd) { return fd.H >= 32; }
+
 template <bool HYB>
 static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, const int32_t* num_legal,
                             const float* root_features, const float* graph, const float* glob, int64_t count,
@@ -1513,15 +1548,25 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
     k_row_index<<<grid, kThreads, 0, s>>>(num_legal, count, w.row_start, rows, w.atr, w.mi);
     if (rows > 0) {
         size_t smem = sizeof(WarpSmem) * kWarpsPerBlock;
-        constexpr int OUT = HYB ? kSlabF16 : kSlabF32;
-        rc = grid_for(k_successor_features<OUT>, rows, smem, &grid);
-        if (rc) return rc;
         // the row counter lives in root_pre, which the per-leaf kernel writes only later
         unsigned long long* ctr = reinterpret_cast<unsigned long long*>(w.root_pre);
         if (cudaMemsetAsync(ctr, 0, sizeof(unsigned long long), s) != cudaSuccess) return HV_ECUDA;
-        k_successor_features<OUT><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi, rows,
-                                                              HYB ? static_cast<void*>(w.xh) : static_cast<void*>(w.x),
-                                                              w.row_start + count, ctr);
+        if (HYB) {
+            rc = grid_for(k_successor_features<kSlabF16>, rows, smem, &grid);
+            if (rc) return rc;
+            k_successor_features<kSlabF16><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi,
+                                                                        rows, w.xh, w.row_start + count, ctr);
+        } else if (fnn_rows_on_tensor_cores(fd)) {
+            rc = grid_for(k_successor_features<kSlabF16x2>, rows, smem, &grid);
+            if (rc) return rc;
+            k_successor_features<kSlabF16x2><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi,
+                                                                          rows, w.x, w.row_start + count, ctr);
+        } else {
+            rc = grid_for(k_successor_features<kSlabF32>, rows, smem, &grid);
+            if (rc) return rc;
+            k_successor_features<kSlabF32><<<grid, kThreads, smem, s>>>(states, count, legal_moves, w.atr, w.mi,
+                                                                        rows, w.x, w.row_start + count, ctr);
+        }
         if (HYB) {
             rc = grid_for(k_row_move_features, count, smem, &grid);
             if (rc) return rc;
@@ -1568,15 +1613,26 @@ static int run_row_pipeline(const uint8_t* states, const uint8_t* legal_moves, c
                                                      w.row_start + count, err);
       }
     } else if (rows > 0) {
-        // the FNN network over the fp32 slab tiles, one CTA per SM (shared memory)
         uint32_t* err = nullptr;
         if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
-        const size_t smem = sizeof(F32Smem);
-        const int64_t tiles = (rows + kF32Rows - 1) / kF32Rows, ctas = (tiles + kF32Groups - 1) / kF32Groups;
-        rc = grid_for(k_fnn_rows, ctas * kWarpsPerBlock, smem, &grid);
-        if (rc) return rc;
-        k_fnn_rows<<<grid, kF32Threads, smem, s>>>(w.x, w.atr, w.mi, rows, w.root_pre, fw, fd, lg, child_q,
-                                                   w.row_start + count, err);
+        if (fnn_rows_on_tensor_cores(fd)) {
+            // the network on the tensor cores over the hi / lo fp16 slab
+            // tiles (fp32-accurate), one CTA per SM (shared memory)
+            const size_t smem = sizeof(FxSmem);
+            const int64_t tiles = (rows + kFxRows - 1) / kFxRows, ctas = (tiles + kFxGroups - 1) / kFxGroups;
+            rc = grid_for(k_fnn_rows_tc, ctas * kWarpsPerBlock, smem, &grid);
+            if (rc) return rc;
+            k_fnn_rows_tc<<<grid, kFxThreads, smem, s>>>(reinterpret_cast<const __half*>(w.x), w.atr, w.mi, rows,
+                                                         w.root_pre, fw, fd, lg, child_q, w.row_start + count, err);
+        } else {
+            // the network over the fp32 slab tiles on the CUDA cores, one CTA per SM (shared memory)
+            const size_t smem = sizeof(F32Smem);
+            const int64_t tiles = (rows + kF32Rows - 1) / kF32Rows, ctas = (tiles + kF32Groups - 1) / kF32Groups;
+            rc = grid_for(k_fnn_rows, ctas * kWarpsPerBlock, smem, &grid);
+            if (rc) return rc;
+            k_fnn_rows<<<grid, kF32Threads, smem, s>>>(w.x, w.atr, w.mi, rows, w.root_pre, fw, fd, lg, child_q,
+                                                       w.row_start + count, err);
+        }
     }
     rc = grid_for(k_leaf_softmax<HYB>, count, 0, &grid);
     if (rc) return rc;
