@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             stage_wait();
             st_apply_warp(w->st, m0 & 255, m0 >> 8, m1, m2);
             S = setup_position(w);
-            n = gen_compact(w, &g_error);
+            n = gen_compact_body(w, &g_error);
         }
         if (ctr && threadIdx.x == 0) next_base[round] = (int64_t)atomicAdd(ctr, (unsigned long long)kWarpsPerBlock);
         __syncthreads();
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
             if (SLAB) {
                 // the move list is consumed once the features are written: stage them there
                 float* f = reinterpret_cast<float*>(w->mv);
-                features(w, n, f);
+                features_body(w, n, f);
                 __syncwarp();
                 const int c = lane_id();
                 if (OUT == kSlabF16x2) {
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_successor_features(
                     *reinterpret_cast<uint4*>(slab + (((a >> 7) * 16 + c) * 128 + (a & 127)) * 8) = u;
                 }
             } else {
-                features(w, n, feats_out + a * kFeat);
+                features_body(w, n, feats_out + a * kFeat);
             }
         }
         __syncwarp();
