@@ -62,8 +62,8 @@ enum WalkMode : int {
 // lane, which reproduces the reference's sequential first-seen order.
 // first_only: return 1 as soon as one destination exists (has_*_move).
 // Ant and spider need slx built for this cell.
-__device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out, int cap,
-                                 bool first_only) {
+__device__ __forceinline__ int walk_body(WarpSmem* w, int cell, int mode, uint16_t* out, int cap,
+                                        bool first_only) {
     Pos P{w};
     const int l = lane_id();
     const uint32_t lt = lanemask_lt();
@@ -175,6 +175,13 @@ __device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out,
         if (!first_only && cnt >= cap) break;
     }
     return first_only ? 0 : cnt;
+}
+
+// The walk engine out of line: one copy of its code serves every piece of
+// the move generator.  (The compact list's existence tests inline
+// walk_body instead: specialised to first_only, it is short.)
+__device__ __noinline__ int walk(WarpSmem* w, int cell, int mode, uint16_t* out, int cap, bool first_only) {
+    return walk_body(w, cell, mode, out, cap, first_only);
 }
 
 // The ant's breadth-first search (move_gen.cuh:267-388), the hottest walk:
@@ -338,17 +345,17 @@ __device__ __forceinline__ int gen_mosquito(WarpSmem* w, int cell, bool first_on
 // as a beetle.  On the ground: any copied movement has one; the cheap
 // lane-per-direction tests go first, and the slide masks are rebuilt with
 // the mosquito lifted only if a spider part is still to test.
-__device__ __noinline__ bool mosquito_out(WarpSmem* w, uint32_t occ_row, int cell) {
+__device__ __forceinline__ bool mosquito_out(WarpSmem* w, uint32_t occ_row, int cell) {
     Pos P{w};
     if (P.height(cell) > 1) return beetle_out(w, cell);
     const uint32_t t = neighbour_types(w, cell);
     if ((t & 0x106u) && slide_out(w, cell)) return true;  // queen, pillbug, ant
     if ((t & 0x8u) && hop_out(w, cell)) return true;      // grasshopper
     if ((t & 0x20u) && beetle_out(w, cell)) return true;  // beetle
-    if ((t & 0x80u) && walk(w, cell, WM_LADY, w->dst, 32, true)) return true;
+    if ((t & 0x80u) && walk_body(w, cell, WM_LADY, w->dst, 32, true)) return true;
     if (t & 0x10u) {                                      // spider
         lift_mover(w, occ_row, cell);
-        return walk(w, cell, WM_SPIDER, w->dst, 32, true) != 0;
+        return walk_body(w, cell, WM_SPIDER, w->dst, 32, true) != 0;
     }
     return false;
 }
@@ -598,7 +605,6 @@ __device__ __forceinline__ int gen_compact_body(WarpSmem* w, uint32_t* err) {
         int pt = P.top(cell) & 15;
         uint32_t bit = 1u << ((pt - 1) * 2 + color);
         if (seen & bit) continue;
-        const uint16_t* list;
         // queen, ant, pillbug: a move exists iff one slide out of the cell is
         // legal (the first step of each; lifting the piece does not change
         // slides out of its own cell), read from the position's slide masks
@@ -607,7 +613,14 @@ __device__ __forceinline__ int gen_compact_body(WarpSmem* w, uint32_t* err) {
         else if (pt == 3) has = hop_out(w, cell);
         else if (pt == 5) has = beetle_out(w, cell);
         else if (pt == 6) has = mosquito_out(w, S.occ, cell);
-        else has = piece_moves(w, S.occ, cell, pt, 128, true, err, &list) != 0;  // spider, ladybug
+        else if (pt == 4) {  // spider: three slides with the spider lifted
+            lift_mover(w, S.occ, cell);
+            has = walk_body(w, cell, WM_SPIDER, w->dst, 32, true) != 0;
+        } else if (pt == 7) {  // ladybug
+            has = walk_body(w, cell, WM_LADY, w->dst, 32, true) != 0;
+        } else {
+            has = false;
+        }
         if (has) {
             seen |= bit;
             if (l == 0) put_move(w, count, 1, pt, p_to_c(cell), 0);
