@@ -355,9 +355,9 @@ def bench_movegen(args, ranks: Ranks) -> dict:
         step()
     ms_max, per_rank_ms = timed_region(ranks, step, args.steps)
     value = world * P * args.steps / (ms_max / 1e3)
-    # ---- the same steps over a region of >= 2 s (every rank the same count) ----
-    long_steps = max(args.steps, int(math.ceil(2000.0 / (ms_max / args.steps))))
-    long_max, long_per_rank = timed_region(ranks, step, long_steps)
+    # ---- the same steps over a region of >= --long-s seconds (every rank the same count) ----
+    long_steps = max(args.steps, int(math.ceil(1000.0 * args.long_s / (ms_max / args.steps))))
+    long_max, long_per_rank = timed_region(ranks, step, long_steps) if args.long_s > 0 else (None, None)
     clocks = sampler.stop()
     out = box["out"]
     mean_legal = float(out[1].float().mean().item())
@@ -504,7 +504,7 @@ def bench_movegen(args, ranks: Ranks) -> dict:
         "long_run": {"steps": long_steps, "ms_per_step": long_max / long_steps,
                      "value": world * P * long_steps / (long_max / 1e3),
                      "per_rank_ms_per_step": [t / long_steps for t in long_per_rank],
-                     "timed_s": long_max / 1e3},
+                     "timed_s": long_max / 1e3} if long_max is not None else None,
         "gpu_launches": 3 * args.steps,  # per step: generator, features, features of position 0
         "mean_legal_moves": mean_legal,
     }
@@ -904,6 +904,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline legs")
     ap.add_argument("--e2e-chunk", type=int, default=16384, help="positions per pipelined chunk of the e2e leg")
+    ap.add_argument("--long-s", type=float, default=2.0,
+                    help="seconds of the config-2 steps' second, long timed region (0: none; profiling runs)")
     ap.add_argument("--positions", type=int, default=POSITIONS,
                     help="positions per GPU (profiling runs use a smaller case)")
     args = ap.parse_args()
