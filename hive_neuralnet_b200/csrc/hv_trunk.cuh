@@ -41,6 +41,9 @@ constexpr uint32_t kImgLayerBytes = kImgLayer * 2;           // 57344
 constexpr int kParTpB = 0, kParCls = 64, kParFnG = 128, kParFnB = 192, kParLayer0 = 256;
 constexpr int kLLn1G = 0, kLLn1B = 64, kLBqkv = 128, kLBo = 320, kLLn2G = 384, kLLn2B = 448, kLB1 = 512,
               kLB2 = 608, kLDq = 672, kLDr = 808, kLDz = 944, kLEnd = 984;
+// relative-bias classes: (dq, dr, dz) clipped offsets, 17 x 17 x 5, then one
+// entry for a masked key (fp16 lowest: its softmax weight is exactly 0)
+constexpr int kRbClasses = 17 * 17 * 5, kRbStride = kRbClasses + 1;
 
 struct __align__(16) TrunkSmem {
     __half w[kImgLayer];                           // this block's weights
@@ -50,6 +53,7 @@ struct __align__(16) TrunkSmem {
     __half vt[kTrWarps][kTrH * kTrVtStride];       // values, transposed per position [dim][key]
     int32_t cq[kTrThreads], cr[kTrThreads], cz[kTrThreads];  // token coordinates (CLS and padding 0)
     float par[kLEnd];                              // this block's fp32 parameters
+    __half rb[kTrHeads * kRbStride];               // this block's relative bias per head and class
     uint64_t bar_w, bar_mma;
     uint32_t tmem;
     int err;
@@ -75,21 +79,54 @@ __device__ __forceinline__ void put_row_f16(TrunkSmem* s, int t, const float* x,
     for (int c = 0; c < n / 8; c++) put_chunk8(s, c, t, x + 8 * c);
 }
 
+// packed fp32 pair arithmetic (sm_100 f32x2: one instruction for two lanes of work)
+__device__ __forceinline__ uint64_t f2_bits(float2 a) { return *reinterpret_cast<uint64_t*>(&a); }
+__device__ __forceinline__ float2 f2_val(uint64_t a) { return *reinterpret_cast<float2*>(&a); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(r);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(r);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(r);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return f2_val(r);
+}
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 pair(const float* x, int i) { return make_float2(x[i], x[i + 1]); }
+__device__ __forceinline__ void put2(float* x, int i, float2 v) {
+    x[i] = v.x;
+    x[i + 1] = v.y;
+}
+
 // LayerNorm of a 64-vector (eps 1e-5, biased variance), gamma/beta from smem
+// (8-byte aligned); sums over even and odd elements, then combined
 __device__ __forceinline__ void layer_norm64(const float* x, const float* g, const float* b, float* y) {
-    float m = 0.f;
+    float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 64; i++) m += x[i];
-    m *= (1.0f / 64.0f);
-    float var = 0.f;
+    for (int i = 0; i < 64; i += 2) s2 = add2(s2, pair(x, i));
+    const float m = (s2.x + s2.y) * (1.0f / 64.0f);
+    const float2 m2 = make_float2(m, m);
+    float2 v2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 64; i++) {
-        const float d = x[i] - m;
-        var += d * d;
+    for (int i = 0; i < 64; i += 2) {
+        const float2 d = sub2(pair(x, i), m2);
+        v2 = fma2(d, d, v2);
     }
-    const float r = rsqrtf(var * (1.0f / 64.0f) + 1e-5f);
+    const float r = rsqrtf((v2.x + v2.y) * (1.0f / 64.0f) + 1e-5f);
+    const float2 r2 = make_float2(r, r);
 #pragma unroll
-    for (int i = 0; i < 64; i++) y[i] = (x[i] - m) * r * g[i] + b[i];
+    for (int i = 0; i < 64; i += 2) put2(y, i, fma2(mul2(sub2(pair(x, i), m2), r2), ld2(g + i), ld2(b + i)));
 }
 
 // one GEMM round: operands visible to the tensor core, issue, commit, wait
@@ -150,6 +187,48 @@ __device__ __forceinline__ void mma_k16(float* d, uint32_t a0, uint32_t a1, uint
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// This block's relative bias of every (dq, dr, dz) class and head: the
+// three embedding rows summed in fp32 and rounded to fp16, as the reference
+// adds bias.to(scores.dtype) to its fp16 autocast scores
+// (fnn_transformer_net.py RelativeSelfAttention.forward); head h's table is
+// rb[h * kRbStride ...], class index ((dq * 17) + dr) * 5 + dz.
+__device__ __forceinline__ void build_rel_bias(TrunkSmem* s) {
+    for (int c = threadIdx.x; c < kRbStride; c += kTrThreads) {
+        float v[kTrHeads];
+        if (c < kRbClasses) {
+            const int dq = c / 85, rem = c - 85 * dq, dr = rem / 5, dz = rem - 5 * dr;
+            const float4* q4 = reinterpret_cast<const float4*>(s->par + kLDq + 8 * dq);
+            const float4* r4 = reinterpret_cast<const float4*>(s->par + kLDr + 8 * dr);
+            const float4* z4 = reinterpret_cast<const float4*>(s->par + kLDz + 8 * dz);
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const float4 a = q4[k], b = r4[k], z = z4[k];
+                v[4 * k + 0] = (a.x + b.x) + z.x;
+                v[4 * k + 1] = (a.y + b.y) + z.y;
+                v[4 * k + 2] = (a.z + b.z) + z.z;
+                v[4 * k + 3] = (a.w + b.w) + z.w;
+            }
+        } else {
+#pragma unroll
+            for (int h = 0; h < kTrHeads; h++) v[h] = -65504.0f;
+        }
+#pragma unroll
+        for (int h = 0; h < kTrHeads; h++) s->rb[h * kRbStride + c] = __float2half_rn(v[h]);
+    }
+}
+
+__device__ __forceinline__ float lds_f16(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return __half2float(__ushort_as_half(v));
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Attention of one position (this warp's 32 rows): per head, S = Q K^T on
 // fp16 warp MMAs with fp32 accumulation (head width 8 = one k8 step; fp16
 // keeps the softmax weights to 11 significant bits), scale + relative bias + key mask,
@@ -160,7 +239,10 @@ __device__ __forceinline__ void mma_k16(float* d, uint32_t a0, uint32_t a1, uint
 __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t kmask) {
     const int g = l >> 2, c = l & 3, base = w * 32, u = w >> 2, tb = (w & 3) * 32;
     const float scale = 0.35355339059327373f;  // 8 ** -0.5
-    // relative-offset table indices of this thread's 32 (row, key) pairs
+    const float kLog2e = 1.4426950408889634f;
+    // shared-memory address of each of this thread's 32 (row, key) pairs'
+    // bias class in head 0's table (a masked key: the masked entry)
+    const uint32_t rb0 = static_cast<uint32_t>(__cvta_generic_to_shared(s->rb));
     uint32_t rel[2][2][4][2];
 #pragma unroll
     for (int mt = 0; mt < 2; mt++)
@@ -176,12 +258,23 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                     const int dq = min(max(s->cq[j] - qi, -8), 8) + 8;
                     const int dr = min(max(s->cr[j] - ri, -8), 8) + 8;
                     const int dz = min(max(s->cz[j] - zi, -2), 2) + 2;
-                    rel[mt][hh][nt][e] = (uint32_t)(kLDq + dq * 8) | ((uint32_t)(kLDr + dr * 8) << 10) |
-                                         ((uint32_t)(kLDz + dz * 8) << 20);
+                    const int cls = ((kmask >> (8 * nt + 2 * c + e)) & 1u) ? (dq * 17 + dr) * 5 + dz : kRbClasses;
+                    rel[mt][hh][nt][e] = rb0 + 2u * (uint32_t)cls;
                 }
         }
 #pragma unroll 1
     for (int h = 0; h < kTrHeads; h++) {
+        const uint32_t hoff = 2u * (uint32_t)(h * kRbStride);
+        // this head's bias of the thread's pairs (issued before the MMAs)
+        float bias[2][2][4][2];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) bias[mt][hh][nt][e] = lds_f16(rel[mt][hh][nt][e] + hoff);
         // S = Q_h K_h^T
         float sc[2][4][4];
 #pragma unroll
@@ -195,7 +288,7 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                 mma_k8(sc[mt][nt], a0, a1, b0);
             }
         }
-        // scale, bias, mask; row max / sum over the quad
+        // scale + bias (a masked key's bias is fp16 lowest); row max / sum over the quad
         float rinv[2][2];
 #pragma unroll
         for (int mt = 0; mt < 2; mt++)
@@ -203,30 +296,27 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
             for (int hh = 0; hh < 2; hh++) {
                 float mx = -3.0e38f;
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const uint32_t r = rel[mt][hh][nt][e];
-                        const float b = s->par[(r & 1023u) + h] + s->par[((r >> 10) & 1023u) + h] +
-                                        s->par[(r >> 20) + h];
-                        float& v = sc[mt][nt][2 * hh + e];
-                        v = v * scale + b;
-                        if ((kmask >> (8 * nt + 2 * c + e)) & 1u) mx = fmaxf(mx, v);
-                    }
+                for (int nt = 0; nt < 4; nt++) {
+                    const float2 v = fma2(pair(sc[mt][nt], 2 * hh), make_float2(scale, scale),
+                                          make_float2(bias[mt][hh][nt][0], bias[mt][hh][nt][1]));
+                    put2(sc[mt][nt], 2 * hh, v);
+                    mx = fmaxf(mx, fmaxf(v.x, v.y));
+                }
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                float sum = 0.0f;
+                const float mxl = -mx * kLog2e;
+                float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        float& v = sc[mt][nt][2 * hh + e];
-                        v = ((kmask >> (8 * nt + 2 * c + e)) & 1u) ? __expf(v - mx) : 0.0f;
-                        sum += v;
-                    }
+                for (int nt = 0; nt < 4; nt++) {
+                    const float2 z = fma2(pair(sc[mt][nt], 2 * hh), make_float2(kLog2e, kLog2e), make_float2(mxl, mxl));
+                    const float2 p = make_float2(ex2_approx(z.x), ex2_approx(z.y));
+                    put2(sc[mt][nt], 2 * hh, p);
+                    sum2 = add2(sum2, p);
+                }
+                float sum = sum2.x + sum2.y;
                 sum += __shfl_xor_sync(0xffffffffu, sum, 1);
                 sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                rinv[mt][hh] = sum > 0.0f ? 1.0f / sum : 0.0f;  // no valid key: idle warp
+                rinv[mt][hh] = sum > 0.0f ? 1.0f / sum : 0.0f;
             }
         // O = P V_h (k = 32 keys in two k16 steps), normalised, into the A slab of head h
         const __half* vt = s->vt[w] + (8 * h + g) * kTrVtStride + 2 * c;
@@ -337,6 +427,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             __syncthreads();
             for (int i = t; i < kLEnd; i += kTrThreads) s->par[i] = __ldg(par + kParLayer0 + layer * kLEnd + i);
             __syncthreads();
+            build_rel_bias(s);  // read by attention_warp, after the QKV GEMM's barriers
             // ---- attention
             float y[kTrH];
             layer_norm64(x, s->par + kLLn1G, s->par + kLLn1B, y);
@@ -368,7 +459,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
                 for (int c = 0; c < 2; c++) {
                     tmem_ld32(lane_taddr(s, 32 * c), d);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) d[i] += s->par[kLBqkv + 32 * c + i];
+                    for (int i = 0; i < 32; i += 2) put2(d, i, add2(pair(d, i), ld2(s->par + kLBqkv + 32 * c + i)));
 #pragma unroll
                     for (int hh = 0; hh < 4; hh++) put_chunk8(s, 4 * c + hh, t, d + 8 * hh);
                 }
@@ -378,7 +469,8 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         const int j = 32 * c + i;
-                        const float v0 = d[i] + s->par[kLBqkv + j], v1 = d[i + 1] + s->par[kLBqkv + j + 1];
+                        const float2 v = add2(pair(d, i), ld2(s->par + kLBqkv + j));
+                        const float v0 = v.x, v1 = v.y;
                         if (j < 128) {
                             __half* row = s->k + t * kTrQkStride + (j - 64);
                             *reinterpret_cast<__half2*>(row) = __floats2half2_rn(v0, v1);
@@ -404,7 +496,8 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
                 for (int c = 0; c < 2; c++) {
                     tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) x[32 * c + i] += d[i] + s->par[kLBo + 32 * c + i];
+                    for (int i = 0; i < 32; i += 2)
+                        put2(x, 32 * c + i, add2(pair(x, 32 * c + i), add2(pair(d, i), ld2(s->par + kLBo + 32 * c + i))));
                 }
             }
             // ---- MLP
@@ -422,7 +515,11 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
                 for (int c = 0; c < 3; c++) {
                     tmem_ld32(lane_taddr(s, 32 * c), d);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) d[i] = gelu_exact(d[i] + s->par[kLB1 + 32 * c + i]);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 v = add2(pair(d, i), ld2(s->par + kLB1 + 32 * c + i));
+                        d[i] = gelu_exact(v.x);
+                        d[i + 1] = gelu_exact(v.y);
+                    }
 #pragma unroll
                     for (int u = 0; u < 4; u++) put_chunk8(s, 4 * c + u, t, d + 8 * u);
                 }
@@ -446,19 +543,16 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
                 for (int c = 0; c < 2; c++) {
                     tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) x[32 * c + i] = (x[32 * c + i] + d[i] + s->par[kLB2 + 32 * c + i]) * keep;
+                    for (int i = 0; i < 32; i += 2)
+                        put2(x, 32 * c + i, mul2(add2(add2(pair(x, 32 * c + i), pair(d, i)), ld2(s->par + kLB2 + 32 * c + i)),
+                                                 make_float2(keep, keep)));
                 }
             }
         }
         if (failed) break;
         if (live && l == 0) {
-            float g[64], bb[64], y[64];
-#pragma unroll
-            for (int i = 0; i < 64; i++) {
-                g[i] = __ldg(par + kParFnG + i);
-                bb[i] = __ldg(par + kParFnB + i);
-            }
-            layer_norm64(x, g, bb, y);
+            float y[64];
+            layer_norm64(x, par + kParFnG, par + kParFnB, y);
             float4* o4 = reinterpret_cast<float4*>(out + b * kTrH);
 #pragma unroll
             for (int i = 0; i < 16; i++) o4[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
