@@ -110,20 +110,34 @@ __device__ __forceinline__ void put2(float* x, int i, float2 v) {
 }
 
 // LayerNorm of a 64-vector (eps 1e-5, biased variance), gamma/beta from smem
-// (8-byte aligned); sums over even and odd elements, then combined
+// (8-byte aligned); the sums run as four independent pair accumulators
+// (short dependency chains), then combined
 __device__ __forceinline__ void layer_norm64(const float* x, const float* g, const float* b, float* y) {
-    float2 s2 = make_float2(0.f, 0.f);
+    float2 s2[4];
 #pragma unroll
-    for (int i = 0; i < 64; i += 2) s2 = add2(s2, pair(x, i));
-    const float m = (s2.x + s2.y) * (1.0f / 64.0f);
+    for (int k = 0; k < 4; k++) s2[k] = pair(x, 2 * k);
+#pragma unroll
+    for (int i = 8; i < 64; i += 8)
+#pragma unroll
+        for (int k = 0; k < 4; k++) s2[k] = add2(s2[k], pair(x, i + 2 * k));
+    const float2 sa = add2(add2(s2[0], s2[1]), add2(s2[2], s2[3]));
+    const float m = (sa.x + sa.y) * (1.0f / 64.0f);
     const float2 m2 = make_float2(m, m);
-    float2 v2 = make_float2(0.f, 0.f);
+    float2 v2[4];
 #pragma unroll
-    for (int i = 0; i < 64; i += 2) {
-        const float2 d = sub2(pair(x, i), m2);
-        v2 = fma2(d, d, v2);
+    for (int k = 0; k < 4; k++) {
+        const float2 d = sub2(pair(x, 2 * k), m2);
+        v2[k] = mul2(d, d);
     }
-    const float r = rsqrtf((v2.x + v2.y) * (1.0f / 64.0f) + 1e-5f);
+#pragma unroll
+    for (int i = 8; i < 64; i += 8)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float2 d = sub2(pair(x, i + 2 * k), m2);
+            v2[k] = fma2(d, d, v2[k]);
+        }
+    const float2 va = add2(add2(v2[0], v2[1]), add2(v2[2], v2[3]));
+    const float r = rsqrtf((va.x + va.y) * (1.0f / 64.0f) + 1e-5f);
     const float2 r2 = make_float2(r, r);
 #pragma unroll
     for (int i = 0; i < 64; i += 2) put2(y, i, fma2(mul2(sub2(pair(x, i), m2), r2), ld2(g + i), ld2(b + i)));
@@ -339,7 +353,31 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
     }
 }
 
-__device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// The exact (erf) GELU of two values, x * Phi(x) with Phi the standard normal
+// CDF, from Abramowitz & Stegun's erfc approximation 7.1.26 (Hastings; absolute
+// error of erf at most 1.5e-7): with z = |x| / sqrt(2) and t = 1 / (1 + p z),
+// erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), and
+// Phi(x) = 1 - erfc(z) / 2 for x >= 0, erfc(z) / 2 otherwise.  Branch free;
+// the result is rounded to fp16 for the next GEMM, far above these errors.
+__device__ __forceinline__ float2 gelu2(float2 x) {
+    const float2 t = make_float2(rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, fabsf(x.x), 1.0f)),
+                                 rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, fabsf(x.y), 1.0f)));
+    float2 p = fma2(make_float2(1.061405429f, 1.061405429f), t, make_float2(-1.453152027f, -1.453152027f));
+    p = fma2(p, t, make_float2(1.421413741f, 1.421413741f));
+    p = fma2(p, t, make_float2(-0.284496736f, -0.284496736f));
+    p = fma2(p, t, make_float2(0.254829592f, 0.254829592f));
+    p = mul2(p, mul2(t, make_float2(0.5f, 0.5f)));  // erfc(z) / 2 without the Gaussian factor
+    // exp(-z^2) = 2^(-x^2 log2(e) / 2)
+    const float2 a = mul2(mul2(x, x), make_float2(-0.72134752044448170f, -0.72134752044448170f));
+    const float2 h = mul2(p, make_float2(ex2_approx(a.x), ex2_approx(a.y)));
+    return make_float2(x.x * (x.x >= 0.0f ? 1.0f - h.x : h.x), x.y * (x.y >= 0.0f ? 1.0f - h.y : h.y));
+}
 
 // token_features [B,28,27] (first `nfeat` used), token_q/r/z [B,28], token_mask [B,28] (0/1),
 // img: fp16 weight image, par: fp32 parameters; out [B,64]: the normalised CLS row
@@ -517,8 +555,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         const float2 v = add2(pair(d, i), ld2(s->par + kLB1 + 32 * c + i));
-                        d[i] = gelu_exact(v.x);
-                        d[i + 1] = gelu_exact(v.y);
+                        put2(d, i, gelu2(v));
                     }
 #pragma unroll
                     for (int u = 0; u < 4; u++) put_chunk8(s, 4 * c + u, t, d + 8 * u);
