@@ -1891,7 +1891,7 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
     const size_t smem = sizeof(TrunkSmem);
     if (cudaFuncSetAttribute(k_hybrid_trunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return HV_ECUDA;
-    const int64_t passes = (batch + kTrWarps - 1) / kTrWarps;
+    const int64_t passes = (batch + kTrPos - 1) / kTrPos;
     const int grid = (int)(passes < d.sms ? passes : d.sms);
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;

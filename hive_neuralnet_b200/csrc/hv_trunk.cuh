@@ -3,19 +3,23 @@
 // RelativeTransformerBlock / HybridRelativeTransformerTrunk), hidden 64,
 // 8 heads of 8, GELU MLP 96, 4 pre-LayerNorm blocks, on sm_100a.
 //
-// One CTA of 8 warps owns two tiles of 4 positions = 2 x 128 rows (a
-// position is 32 rows: CLS, its 28 piece tokens, 3 padding rows), one row per
-// thread, the residual stream in registers; each tile has its own 256 TMEM
-// columns, and one issuing thread drives both tiles' MMAs per GEMM.  The five linear layers of a block (token
-// projection once, then QKV, attention output, MLP in and out) are fp16
-// tcgen05.mma GEMMs with M = 128 and fp32 accumulators in TMEM, issued by one
-// thread (fp16 operands as the reference's autocast, fp32 accumulation).
-// The per-head 32 x 32 attention of a position (head width 8, below the
-// tcgen05 K step and M tile) runs on warp-level fp16 MMAs inside the warp
-// that owns the position; the queries live in the A-operand slabs of the
-// output projection, which the heads overwrite one by one.  Block weights
-// stream from global memory (L2-resident) into shared memory with a bulk
-// copy issued as soon as the previous block's last GEMM has completed.
+// One CTA of 16 warps owns two tiles of 4 positions = 2 x 128 rows (a
+// position is 32 rows: CLS, its 28 piece tokens, 3 padding rows).  Two
+// threads share a row, each holding half of its 64-wide residual stream in
+// registers (warps u*8 + h*4 + q: tile u, half h, position q of the tile);
+// the halves exchange their LayerNorm statistics through shared memory.
+// Each tile has its own 256 TMEM columns, and one issuing thread drives both
+// tiles' MMAs per GEMM.  The five linear layers of a block (token projection
+// once, then QKV, attention output, MLP in and out) are fp16 tcgen05.mma
+// GEMMs with M = 128 and fp32 accumulators in TMEM (fp16 operands as the
+// reference's autocast, fp32 accumulation); each half reads its own columns
+// back.  The per-head 32 x 32 attention of a position (head width 8, below
+// the tcgen05 K step and M tile) runs on warp-level fp16 MMAs: the warp of
+// half h takes heads 4h..4h+3, whose queries, keys and values its own lanes
+// wrote; the queries live in the A-operand slabs of the output projection,
+// which the heads overwrite one by one.  Block weights stream from global
+// memory (L2-resident) into shared memory with a bulk copy issued as soon as
+// the previous block's last GEMM has completed.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -26,7 +30,8 @@
 namespace hv {
 
 constexpr int kTrH = 64, kTrHeads = 8, kTrFfn = 96, kTrLayers = 4;
-constexpr int kTrWarps = 8, kTrThreads = kTrWarps * 32, kTrTiles = 2;  // 8 positions per CTA pass
+constexpr int kTrWarps = 16, kTrThreads = kTrWarps * 32, kTrTiles = 2;
+constexpr int kTrPos = 8, kTrRows = kTrPos * 32;  // 8 positions (256 rows) per CTA pass
 constexpr int kTrKin = 32;   // token features, zero-padded to two MMA K steps
 constexpr int kTrQkStride = 72;  // fp16 row stride of Q / K (conflict-free fragment loads)
 constexpr int kTrVtStride = 40;  // fp16 row stride of the transposed V of one position
@@ -49,15 +54,17 @@ struct __align__(16) TrunkSmem {
     __half w[kImgLayer];                           // this block's weights
     __half tp[kImgTp];                             // token projection weights
     __half a[kTrTiles][kTrFfn / 8][128][8];        // A operand per tile (K <= 96); queries during attention
-    __half k[kTrThreads * kTrQkStride];            // keys, row-major (bias added)
-    __half vt[kTrWarps][kTrH * kTrVtStride];       // values, transposed per position [dim][key]
-    int32_t cq[kTrThreads], cr[kTrThreads], cz[kTrThreads];  // token coordinates (CLS and padding 0)
+    __half k[kTrRows * kTrQkStride];               // keys, row-major (bias added)
+    __half vt[kTrPos][kTrH * kTrVtStride];         // values, transposed per position [dim][key]
+    int32_t cq[kTrRows], cr[kTrRows], cz[kTrRows];  // token coordinates (CLS and padding 0)
     float par[kLEnd];                              // this block's fp32 parameters
     __half rb[kTrHeads * kRbStride];               // this block's relative bias per head and class
+    float2 lnx[2][kTrRows];                        // LayerNorm statistics (mean, M2) of each row's halves
     uint64_t bar_w, bar_mma;
     uint32_t tmem;
     int err;
 };
+static_assert(sizeof(TrunkSmem) <= 232448, "trunk shared memory above the 227 KB opt-in limit");
 
 // 8 values of this thread's row -> slab c of its tile's A operand (one 16-byte store)
 __device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int t, const float* x) {
@@ -73,10 +80,10 @@ __device__ __forceinline__ void put_chunk8(TrunkSmem* s, int c, int t, const flo
     *reinterpret_cast<uint4*>(&s->a[t >> 7][c][t & 127][0]) = u;
 }
 
-// write this thread's row (n values) into its tile's A operand in slab layout
-__device__ __forceinline__ void put_row_f16(TrunkSmem* s, int t, const float* x, int n) {
+// n values of this thread's row into its tile's A operand, slabs c0 .. c0 + n / 8 - 1
+__device__ __forceinline__ void put_chunks(TrunkSmem* s, int c0, int t, const float* x, int n) {
 #pragma unroll
-    for (int c = 0; c < n / 8; c++) put_chunk8(s, c, t, x + 8 * c);
+    for (int c = 0; c < n / 8; c++) put_chunk8(s, c0 + c, t, x + 8 * c);
 }
 
 // packed fp32 pair arithmetic (sm_100 f32x2: one instruction for two lanes of work)
@@ -109,51 +116,85 @@ __device__ __forceinline__ void put2(float* x, int i, float2 v) {
     x[i + 1] = v.y;
 }
 
-// LayerNorm of a 64-vector (eps 1e-5, biased variance), gamma/beta from smem
-// (8-byte aligned); the sums run as four independent pair accumulators
-// (short dependency chains), then combined
-__device__ __forceinline__ void layer_norm64(const float* x, const float* g, const float* b, float* y) {
+__device__ __forceinline__ void bar_pair(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
+// LayerNorm (eps 1e-5, biased variance) of a 64-wide row held as two 32-wide
+// halves by two threads (same lane of warps w and w ^ 4).  Each half's mean
+// and sum of squared deviations go through lnx; the pair meets at named
+// barrier `bar` and combines them as m = (m0 + m1) / 2,
+// M2 = M2_0 + M2_1 + 16 (m0 - m1)^2 (the pairwise update of Chan, Golub and
+// LeVeque), so both halves compute identical statistics.  g, b: this half's
+// gamma / beta (8-byte aligned); sums as four independent pair accumulators.
+__device__ __forceinline__ void layer_norm_half(TrunkSmem* s, int row, int hf, int bar, const float* x,
+                                                const float* g, const float* b, float* y) {
     float2 s2[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) s2[k] = pair(x, 2 * k);
 #pragma unroll
-    for (int i = 8; i < 64; i += 8)
+    for (int i = 8; i < 32; i += 8)
 #pragma unroll
         for (int k = 0; k < 4; k++) s2[k] = add2(s2[k], pair(x, i + 2 * k));
     const float2 sa = add2(add2(s2[0], s2[1]), add2(s2[2], s2[3]));
-    const float m = (sa.x + sa.y) * (1.0f / 64.0f);
-    const float2 m2 = make_float2(m, m);
+    const float mh = (sa.x + sa.y) * (1.0f / 32.0f);
+    const float2 mh2 = make_float2(mh, mh);
     float2 v2[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-        const float2 d = sub2(pair(x, 2 * k), m2);
+        const float2 d = sub2(pair(x, 2 * k), mh2);
         v2[k] = mul2(d, d);
     }
 #pragma unroll
-    for (int i = 8; i < 64; i += 8)
+    for (int i = 8; i < 32; i += 8)
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const float2 d = sub2(pair(x, i + 2 * k), m2);
+            const float2 d = sub2(pair(x, i + 2 * k), mh2);
             v2[k] = fma2(d, d, v2[k]);
         }
     const float2 va = add2(add2(v2[0], v2[1]), add2(v2[2], v2[3]));
-    const float r = rsqrtf((va.x + va.y) * (1.0f / 64.0f) + 1e-5f);
-    const float2 r2 = make_float2(r, r);
+    const float m2h = va.x + va.y;
+    s->lnx[hf][row] = make_float2(mh, m2h);
+    bar_pair(bar);
+    const float2 o = s->lnx[hf ^ 1][row];
+    const float m = 0.5f * (mh + o.x), dm = mh - o.x;
+    const float r = rsqrtf((m2h + o.y + 16.0f * dm * dm) * (1.0f / 64.0f) + 1e-5f);
+    const float2 m2 = make_float2(m, m), r2 = make_float2(r, r);
 #pragma unroll
-    for (int i = 0; i < 64; i += 2) put2(y, i, fma2(mul2(sub2(pair(x, i), m2), r2), ld2(g + i), ld2(b + i)));
+    for (int i = 0; i < 32; i += 2) put2(y, i, fma2(mul2(sub2(pair(x, i), m2), r2), ld2(g + i), ld2(b + i)));
+}
+
+// D[128 x n] = A[128 x k] * B[row0 .. row0 + n) of a B matrix with ntot rows,
+// both in the slab layout of gemm_m128
+__device__ __forceinline__ void gemm_m128_rows(uint32_t d_tmem, const void* a, const void* b, int ntot, int row0,
+                                               int n, int k) {
+    const uint32_t id = idesc_f16_m128(n);
+    const char* pa = static_cast<const char*>(a);
+    const char* pb = static_cast<const char*>(b) + row0 * 16;
+    for (int st = 0; st < k / 16; st++)
+        mma_f16(d_tmem, sdesc(pa + st * 2 * 128 * 16, 128 * 16, 128), sdesc(pb + st * 2 * ntot * 16, ntot * 16, 128),
+                id, st > 0 ? 1u : 0u);
 }
 
 // one GEMM round: operands visible to the tensor core, issue, commit, wait
-// (uniform result: false if any thread's wait gave up)
+// (uniform result: false if any thread's wait gave up).  split: the n output
+// columns go out as two halves of n / 2, at d_col and d_col + 64, so that
+// each thread half reads 32-column-aligned TMEM blocks.
 __device__ __forceinline__ bool trunk_gemm(TrunkSmem* s, uint32_t d_col, const void* b, int n, int k,
-                                           uint32_t& mphase) {
+                                           uint32_t& mphase, bool split = false) {
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
     if (threadIdx.x == 0) {
         tc_fence_after();
 #pragma unroll
-        for (int u = 0; u < kTrTiles; u++) gemm_m128(s->tmem + 256 * u + d_col, &s->a[u][0][0][0], b, n, k);
+        for (int u = 0; u < kTrTiles; u++) {
+            const uint32_t d = s->tmem + 256 * u + d_col;
+            if (split) {
+                gemm_m128_rows(d, &s->a[u][0][0][0], b, n, 0, n / 2, k);
+                gemm_m128_rows(d + 64, &s->a[u][0][0][0], b, n, n / 2, n / 2, k);
+            } else {
+                gemm_m128(d, &s->a[u][0][0][0], b, n, k);
+            }
+        }
         mma_commit(&s->bar_mma);
     }
     const bool ok = mbar_wait(&s->bar_mma, mphase);
@@ -162,10 +203,10 @@ __device__ __forceinline__ bool trunk_gemm(TrunkSmem* s, uint32_t d_col, const v
     return __syncthreads_and(ok) != 0;
 }
 
-// TMEM address of this thread's row: warp w reads lanes 32 (w % 4) of tile w / 4's columns
+// TMEM address of this thread's row: warp w reads lanes 32 (w % 4) of tile w / 8's columns
 __device__ __forceinline__ uint32_t lane_taddr(const TrunkSmem* s, int col) {
     const int w = threadIdx.x >> 5;
-    return s->tmem + ((uint32_t)((w & 3) * 32) << 16) + (uint32_t)(256 * (w >> 2) + col);
+    return s->tmem + ((uint32_t)((w & 3) * 32) << 16) + (uint32_t)(256 * (w >> 3) + col);
 }
 
 __device__ __forceinline__ void prefetch_block(TrunkSmem* s, const __half* img, int layer) {
@@ -243,29 +284,36 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// Attention of one position (this warp's 32 rows): per head, S = Q K^T on
+// Attention of one position (this warp's 32 rows, from per-row index base)
+// for heads h0 .. h0 + 3: per head, S = Q K^T on
 // fp16 warp MMAs with fp32 accumulation (head width 8 = one k8 step; fp16
 // keeps the softmax weights to 11 significant bits), scale + relative bias + key mask,
 // row softmax on the accumulator fragments (quad shuffles), O = P V with the
 // score fragments reused as the A operand; O goes straight into the A
 // operand slab of the output projection.  Fragment coordinates: g = lane/4
 // selects rows g and g+8 of a 16-row tile, c = lane%4 selects columns 2c, 2c+1.
-__device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t kmask) {
-    const int g = l >> 2, c = l & 3, base = w * 32, u = w >> 2, tb = (w & 3) * 32;
+// MT 16-row query tiles and NT 8-key blocks are computed: the rows and keys
+// past the last valid token are dead (masked as keys, and their residual is
+// zeroed after each block), so their scores are not formed; their slab rows
+// keep the (finite) queries.
+template <int MT, int NT>
+__device__ __forceinline__ void attention_heads(TrunkSmem* s, int base, int h0, int l, uint32_t kmask) {
+    constexpr int KB = (NT + 1) / 2;
+    const int g = l >> 2, c = l & 3, u = base >> 7, tb = base & 127;
     const float scale = 0.35355339059327373f;  // 8 ** -0.5
     const float kLog2e = 1.4426950408889634f;
     // shared-memory address of each of this thread's 32 (row, key) pairs'
     // bias class in head 0's table (a masked key: the masked entry)
     const uint32_t rb0 = static_cast<uint32_t>(__cvta_generic_to_shared(s->rb));
-    uint32_t rel[2][2][4][2];
+    uint32_t rel[MT][2][NT][2];
 #pragma unroll
-    for (int mt = 0; mt < 2; mt++)
+    for (int mt = 0; mt < MT; mt++)
 #pragma unroll
         for (int hh = 0; hh < 2; hh++) {
             const int i = base + 16 * mt + g + 8 * hh;
             const int qi = s->cq[i], ri = s->cr[i], zi = s->cz[i];
 #pragma unroll
-            for (int nt = 0; nt < 4; nt++)
+            for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int j = base + 8 * nt + 2 * c + e;
@@ -277,40 +325,40 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                 }
         }
 #pragma unroll 1
-    for (int h = 0; h < kTrHeads; h++) {
+    for (int h = h0; h < h0 + kTrHeads / 2; h++) {
         const uint32_t hoff = 2u * (uint32_t)(h * kRbStride);
         // this head's bias of the thread's pairs (issued before the MMAs)
-        float bias[2][2][4][2];
+        float bias[MT][2][NT][2];
 #pragma unroll
-        for (int mt = 0; mt < 2; mt++)
+        for (int mt = 0; mt < MT; mt++)
 #pragma unroll
             for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++)
+                for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                     for (int e = 0; e < 2; e++) bias[mt][hh][nt][e] = lds_f16(rel[mt][hh][nt][e] + hoff);
         // S = Q_h K_h^T
-        float sc[2][4][4];
+        float sc[MT][NT][4];
 #pragma unroll
-        for (int mt = 0; mt < 2; mt++) {
+        for (int mt = 0; mt < MT; mt++) {
             const __half* qa = &s->a[u][h][tb + 16 * mt + g][2 * c];
             const uint32_t a0 = ld_b32(qa), a1 = ld_b32(qa + 8 * 8);
 #pragma unroll
-            for (int nt = 0; nt < 4; nt++) {
+            for (int nt = 0; nt < NT; nt++) {
                 const uint32_t b0 = ld_b32(s->k + (base + 8 * nt + g) * kTrQkStride + 8 * h + 2 * c);
                 sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.0f;
                 mma_k8(sc[mt][nt], a0, a1, b0);
             }
         }
         // scale + bias (a masked key's bias is fp16 lowest); row max / sum over the quad
-        float rinv[2][2];
+        float rinv[MT][2];
 #pragma unroll
-        for (int mt = 0; mt < 2; mt++)
+        for (int mt = 0; mt < MT; mt++)
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
                 float mx = -3.0e38f;
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++) {
+                for (int nt = 0; nt < NT; nt++) {
                     const float2 v = fma2(pair(sc[mt][nt], 2 * hh), make_float2(scale, scale),
                                           make_float2(bias[mt][hh][nt][0], bias[mt][hh][nt][1]));
                     put2(sc[mt][nt], 2 * hh, v);
@@ -321,7 +369,7 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                 const float mxl = -mx * kLog2e;
                 float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++) {
+                for (int nt = 0; nt < NT; nt++) {
                     const float2 z = fma2(pair(sc[mt][nt], 2 * hh), make_float2(kLog2e, kLog2e), make_float2(mxl, mxl));
                     const float2 p = make_float2(ex2_approx(z.x), ex2_approx(z.y));
                     put2(sc[mt][nt], 2 * hh, p);
@@ -332,17 +380,18 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                 sum += __shfl_xor_sync(0xffffffffu, sum, 2);
                 rinv[mt][hh] = sum > 0.0f ? 1.0f / sum : 0.0f;
             }
-        // O = P V_h (k = 32 keys in two k16 steps), normalised, into the A slab of head h
-        const __half* vt = s->vt[w] + (8 * h + g) * kTrVtStride + 2 * c;
+        // O = P V_h (the keys in k16 steps), normalised, into the A slab of head h
+        const __half* vt = s->vt[base >> 5] + (8 * h + g) * kTrVtStride + 2 * c;
 #pragma unroll
-        for (int mt = 0; mt < 2; mt++) {
+        for (int mt = 0; mt < MT; mt++) {
             float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int kb = 0; kb < 2; kb++) {
+            for (int kb = 0; kb < KB; kb++) {
                 const uint32_t a0 = pack_f16(sc[mt][2 * kb][0], sc[mt][2 * kb][1]);
                 const uint32_t a1 = pack_f16(sc[mt][2 * kb][2], sc[mt][2 * kb][3]);
-                const uint32_t a2 = pack_f16(sc[mt][2 * kb + 1][0], sc[mt][2 * kb + 1][1]);
-                const uint32_t a3 = pack_f16(sc[mt][2 * kb + 1][2], sc[mt][2 * kb + 1][3]);
+                // (a key block past NT: zero weights)
+                const uint32_t a2 = 2 * kb + 1 < NT ? pack_f16(sc[mt][(2 * kb + 1) % NT][0], sc[mt][(2 * kb + 1) % NT][1]) : 0u;
+                const uint32_t a3 = 2 * kb + 1 < NT ? pack_f16(sc[mt][(2 * kb + 1) % NT][2], sc[mt][(2 * kb + 1) % NT][3]) : 0u;
                 mma_k16(o, a0, a1, a2, a3, ld_b32(vt + 16 * kb), ld_b32(vt + 16 * kb + 8));
             }
             const int r0 = tb + 16 * mt + g;
@@ -351,6 +400,16 @@ __device__ __noinline__ void attention_warp(TrunkSmem* s, int w, int l, uint32_t
                 pack_f16(o[2] * rinv[mt][1], o[3] * rinv[mt][1]);
         }
     }
+}
+
+// the position's attention: rows and keys up to the last valid one
+__device__ __noinline__ void attention_warp(TrunkSmem* s, int base, int h0, int l, uint32_t kmask) {
+    if (kmask < (1u << 16))
+        attention_heads<1, 2>(s, base, h0, l, kmask);
+    else if (kmask < (1u << 24))
+        attention_heads<2, 3>(s, base, h0, l, kmask);
+    else
+        attention_heads<2, 4>(s, base, h0, l, kmask);
 }
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -379,6 +438,19 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
     return make_float2(x.x * (x.x >= 0.0f ? 1.0f - h.x : h.x), x.y * (x.y >= 0.0f ? 1.0f - h.y : h.y));
 }
 
+// The token features of a pass's 8 positions (b0 ..) into shared memory,
+// [8][28][27] floats, by asynchronous 4-byte copies (no alignment asked of
+// the caller's array); positions past the batch are left alone (not read).
+__device__ __forceinline__ void stage_tokens(float* dst, const float* __restrict__ tf, int64_t b0, int64_t batch) {
+    constexpr int kPer = 28 * 27;
+    const int64_t nb = batch - b0 < kTrPos ? batch - b0 : kTrPos;
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    for (int i = threadIdx.x; i < nb * kPer; i += kTrThreads)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d + 4u * (uint32_t)i), "l"(tf + b0 * kPer + i)
+                     : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // token_features [B,28,27] (first `nfeat` used), token_q/r/z [B,28], token_mask [B,28] (0/1),
 // img: fp16 weight image, par: fp32 parameters; out [B,64]: the normalised CLS row
 __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __restrict__ tf, const int32_t* __restrict__ tq,
@@ -390,7 +462,13 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
     extern __shared__ __align__(16) uint8_t smem_raw[];
     TrunkSmem* s = reinterpret_cast<TrunkSmem*>(smem_raw);
     const int t = threadIdx.x, w = t >> 5, l = t & 31;
-    const int64_t npass = (batch + kTrWarps - 1) / kTrWarps;  // 8 positions per pass
+    // warp w = u * 8 + hf * 4 + q: tile u, half hf of every row, position q of the tile
+    const int u = w >> 3, hf = (w >> 2) & 1, q = w & 3;
+    const int base = 128 * u + 32 * q;  // per-row index of the position's row 0
+    const int row = base + l;           // this thread's row (0 .. 255)
+    const int lnbar = 1 + 4 * u + q;    // named barrier of the row pair's two warps
+    const int hc = 32 * hf;             // first hidden column of this half
+    const int64_t npass = (batch + kTrPos - 1) / kTrPos;  // 8 positions per pass
 
     if (t == 0) {
         mbar_init(&s->bar_w, 1);
@@ -420,25 +498,38 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
         prefetch_block(s, img, 0);
         wpend = true;
     }
+    // token features of each pass staged in the key buffer (free outside the attention)
+    float* stf = reinterpret_cast<float*>(s->k);
+    static_assert(sizeof(TrunkSmem::k) >= kTrPos * 28 * 27 * sizeof(float), "token staging");
+    if (blockIdx.x < npass) stage_tokens(stf, tf, (int64_t)blockIdx.x * kTrPos, batch);
 
     for (int64_t pass = blockIdx.x; pass < npass && !failed; pass += gridDim.x) {
-        const int64_t b = pass * kTrWarps + w;
+        const int64_t b = pass * kTrPos + (base >> 5);
         const bool live = b < batch;
         // ---- inputs of this row: token features (rows 1..28), CLS (row 0), padding (29..31)
         const int tok = l - 1;
         const bool is_tok = live && tok >= 0 && tok < 28;
         const bool valid = (live && l == 0) || (is_tok && tm[b * 28 + tok] != 0);
-        s->cq[t] = is_tok ? tq[b * 28 + tok] : 0;
-        s->cr[t] = is_tok ? tr[b * 28 + tok] : 0;
-        s->cz[t] = is_tok ? tz[b * 28 + tok] : 0;
-        const uint32_t kmask = __ballot_sync(0xffffffffu, valid);
-        {
-            float f[kTrKin];
-#pragma unroll
-            for (int i = 0; i < kTrKin; i++) f[i] = (is_tok && i < nfeat) ? tf[(b * 28 + tok) * 27 + i] : 0.0f;
-            put_row_f16(s, t, f, kTrKin);
+        if (hf == 0) {
+            s->cq[row] = is_tok ? tq[b * 28 + tok] : 0;
+            s->cr[row] = is_tok ? tr[b * 28 + tok] : 0;
+            s->cz[row] = is_tok ? tz[b * 28 + tok] : 0;
         }
-        float x[kTrH];
+        const uint32_t kmask = __ballot_sync(0xffffffffu, valid);
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // every thread's staged token features
+        {
+            // this half's 16 of the 32 (zero-padded) input columns
+            float f[kTrKin / 2];
+            const float* src = stf + ((base >> 5) * 28 + tok) * 27;
+#pragma unroll
+            for (int i = 0; i < kTrKin / 2; i++) {
+                const int j = kTrKin / 2 * hf + i;
+                f[i] = (is_tok && j < nfeat) ? src[j] : 0.0f;
+            }
+            put_chunks(s, 2 * hf, row, f, kTrKin / 2);
+        }
+        float x[kTrH / 2];  // this half of the row's residual stream
         mpend = true;
         if (!trunk_gemm(s, 192, s->tp, kTrH, kTrKin, mphase)) {
             failed = true;
@@ -447,29 +538,25 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
         mpend = false;
         {
             float d[32];
+            tmem_ld32(lane_taddr(s, 192 + hc), d);
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int j = 32 * c + i;
-                    // CLS row: the learned token; pieces: projection times mask; padding: 0
-                    x[j] = (l == 0) ? __ldg(par + kParCls + j)
-                                    : ((is_tok && valid) ? d[i] + __ldg(par + kParTpB + j) : 0.0f);
-                }
+            for (int i = 0; i < 32; i++) {
+                const int j = hc + i;
+                // CLS row: the learned token; pieces: projection times mask; padding: 0
+                x[i] = (l == 0) ? __ldg(par + kParCls + j) : ((is_tok && valid) ? d[i] + __ldg(par + kParTpB + j) : 0.0f);
             }
         }
 
         for (int layer = 0; layer < kTrLayers; layer++) {
-            // this block's fp32 parameters
+            // this block's fp32 parameters and relative-bias table
             __syncthreads();
             for (int i = t; i < kLEnd; i += kTrThreads) s->par[i] = __ldg(par + kParLayer0 + layer * kLEnd + i);
             __syncthreads();
             build_rel_bias(s);  // read by attention_warp, after the QKV GEMM's barriers
             // ---- attention
-            float y[kTrH];
-            layer_norm64(x, s->par + kLLn1G, s->par + kLLn1B, y);
-            put_row_f16(s, t, y, kTrH);
+            float y[kTrH / 2];
+            layer_norm_half(s, row, hf, lnbar, x, s->par + kLLn1G + hc, s->par + kLLn1B + hc, y);
+            put_chunks(s, 4 * hf, row, y, kTrH / 2);
             bool okw = true;
             if (t == 0) {
                 okw = mbar_wait(&s->bar_w, wphase);
@@ -490,76 +577,72 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             }
             mpend = false;
             {
-                // queries into the A slabs (one per head), keys row-major, values
-                // transposed per position; fp16, biases added
+                // this half's heads 4 hf .. 4 hf + 3: queries into their A slabs,
+                // keys row-major, values transposed per position; fp16, biases added
                 float d[32];
+                tmem_ld32(lane_taddr(s, hc), d);
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    tmem_ld32(lane_taddr(s, 32 * c), d);
+                for (int i = 0; i < 32; i += 2) put2(d, i, add2(pair(d, i), ld2(s->par + kLBqkv + hc + i)));
+                put_chunks(s, 4 * hf, row, d, 32);
+                tmem_ld32(lane_taddr(s, 64 + hc), d);
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) put2(d, i, add2(pair(d, i), ld2(s->par + kLBqkv + 32 * c + i)));
-#pragma unroll
-                    for (int hh = 0; hh < 4; hh++) put_chunk8(s, 4 * c + hh, t, d + 8 * hh);
+                for (int i = 0; i < 32; i += 2) {
+                    const float2 v = add2(pair(d, i), ld2(s->par + kLBqkv + 64 + hc + i));
+                    *reinterpret_cast<__half2*>(s->k + row * kTrQkStride + hc + i) = __floats2half2_rn(v.x, v.y);
                 }
+                tmem_ld32(lane_taddr(s, 128 + hc), d);
+                __half* vt = s->vt[base >> 5] + hc * kTrVtStride + l;
 #pragma unroll
-                for (int c = 2; c < 6; c++) {
-                    tmem_ld32(lane_taddr(s, 32 * c), d);
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const int j = 32 * c + i;
-                        const float2 v = add2(pair(d, i), ld2(s->par + kLBqkv + j));
-                        const float v0 = v.x, v1 = v.y;
-                        if (j < 128) {
-                            __half* row = s->k + t * kTrQkStride + (j - 64);
-                            *reinterpret_cast<__half2*>(row) = __floats2half2_rn(v0, v1);
-                        } else {
-                            __half* vt = s->vt[w] + (j - 128) * kTrVtStride + l;
-                            vt[0] = __float2half_rn(v0);
-                            vt[kTrVtStride] = __float2half_rn(v1);
-                        }
-                    }
+                for (int i = 0; i < 32; i += 2) {
+                    const float2 v = add2(pair(d, i), ld2(s->par + kLBqkv + 128 + hc + i));
+                    vt[i * kTrVtStride] = __float2half_rn(v.x);
+                    vt[(i + 1) * kTrVtStride] = __float2half_rn(v.y);
                 }
             }
+            // the residual waits in TMEM (columns hc .. hc + 31 of the row's lane,
+            // free until the next block's QKV GEMM) while the attention runs
+            tmem_st32(lane_taddr(s, hc), x);
             __syncwarp();
-            attention_warp(s, w, l, kmask);
+            attention_warp(s, base, 4 * hf, l, kmask);
             mpend = true;
             if (!trunk_gemm(s, 192, W + kImgQkv, kTrH, kTrH, mphase)) {
                 failed = true;
                 break;
             }
             mpend = false;
+            // every warp's attention is done with the key buffer: stage the
+            // token features of this CTA's next pass there
+            if (layer == kTrLayers - 1 && pass + gridDim.x < npass)
+                stage_tokens(stf, tf, (pass + gridDim.x) * kTrPos, batch);
             {
                 float d[32];
+                tmem_ld32(lane_taddr(s, hc), x);
+                tmem_ld32(lane_taddr(s, 192 + hc), d);
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2)
-                        put2(x, 32 * c + i, add2(pair(x, 32 * c + i), add2(pair(d, i), ld2(s->par + kLBo + 32 * c + i))));
-                }
+                for (int i = 0; i < 32; i += 2)
+                    put2(x, i, add2(pair(x, i), add2(pair(d, i), ld2(s->par + kLBo + hc + i))));
             }
             // ---- MLP
-            layer_norm64(x, s->par + kLLn2G, s->par + kLLn2B, y);
-            put_row_f16(s, t, y, kTrH);
+            layer_norm_half(s, row, hf, lnbar, x, s->par + kLLn2G + hc, s->par + kLLn2B + hc, y);
+            put_chunks(s, 4 * hf, row, y, kTrH / 2);
             mpend = true;
-            if (!trunk_gemm(s, 0, W + kImgQkv + kImgO, kTrFfn, kTrH, mphase)) {
+            // output columns 0..47 and 64..111: this half's 48 at 64 hf
+            if (!trunk_gemm(s, 0, W + kImgQkv + kImgO, kTrFfn, kTrH, mphase, true)) {
                 failed = true;
                 break;
             }
             mpend = false;
             {
                 float d[32];
+                tmem_ld32(lane_taddr(s, 64 * hf), d);
 #pragma unroll
-                for (int c = 0; c < 3; c++) {
-                    tmem_ld32(lane_taddr(s, 32 * c), d);
+                for (int i = 0; i < 32; i += 2) put2(d, i, gelu2(add2(pair(d, i), ld2(s->par + kLB1 + 48 * hf + i))));
+                put_chunks(s, 6 * hf, row, d, 32);
+                tmem_ld16(lane_taddr(s, 64 * hf + 32), d);
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const float2 v = add2(pair(d, i), ld2(s->par + kLB1 + 32 * c + i));
-                        put2(d, i, gelu2(v));
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) put_chunk8(s, 4 * c + u, t, d + 8 * u);
-                }
+                for (int i = 0; i < 16; i += 2)
+                    put2(d, i, gelu2(add2(pair(d, i), ld2(s->par + kLB1 + 48 * hf + 32 + i))));
+                put_chunks(s, 6 * hf + 4, row, d, 16);
             }
             mpend = true;
             if (!trunk_gemm(s, 192, W + kImgQkv + kImgO + kImgW1, kTrH, kTrFfn, mphase)) {
@@ -576,23 +659,24 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             {
                 float d[32];
                 const float keep = (l == 0) ? 1.0f : (valid ? 1.0f : 0.0f);
+                tmem_ld32(lane_taddr(s, 192 + hc), d);
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    tmem_ld32(lane_taddr(s, 192 + 32 * c), d);
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2)
-                        put2(x, 32 * c + i, mul2(add2(add2(pair(x, 32 * c + i), pair(d, i)), ld2(s->par + kLB2 + 32 * c + i)),
-                                                 make_float2(keep, keep)));
-                }
+                for (int i = 0; i < 32; i += 2)
+                    put2(x, i, mul2(add2(add2(pair(x, i), pair(d, i)), ld2(s->par + kLB2 + hc + i)),
+                                    make_float2(keep, keep)));
             }
         }
         if (failed) break;
-        if (live && l == 0) {
-            float y[64];
-            layer_norm64(x, par + kParFnG, par + kParFnB, y);
-            float4* o4 = reinterpret_cast<float4*>(out + b * kTrH);
+        // the final LayerNorm of every row pair (the pair's barrier needs
+        // both warps); the CLS row of a live position is the output
+        {
+            float y[kTrH / 2];
+            layer_norm_half(s, row, hf, lnbar, x, par + kParFnG + hc, par + kParFnB + hc, y);
+            if (live && l == 0) {
+                float4* o4 = reinterpret_cast<float4*>(out + b * kTrH + hc);
 #pragma unroll
-            for (int i = 0; i < 16; i++) o4[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+                for (int i = 0; i < 8; i++) o4[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+            }
         }
     }
 
@@ -605,6 +689,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
         }
         if (mpend) mbar_drain(&s->bar_mma, mphase ^ 1u);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no staged copy outlives the CTA
     tc_fence_before();
     __syncthreads();
     if (w == 0) {
