@@ -1172,6 +1172,13 @@ __global__ void __launch_bounds__(kThreads) k_mcts_select(TreeDev t, SelectArgs 
         select_game(t, a, g);
 }
 
+// root-slot mode: one warp per (game, candidate)
+__global__ void __launch_bounds__(kThreads) k_mcts_select_slots(TreeDev t, SelectArgs a) {
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock, n = (int64_t)a.B * a.C;
+    for (int64_t i = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); i < n; i += nwarps)
+        select_game_slot(t, a, (int)(i / a.C), (int)(i % a.C));
+}
+
 __global__ void __launch_bounds__(kThreads) k_mcts_expand(TreeDev t, ExpandArgs a) {
     const int nwarps = gridDim.x * kWarpsPerBlock;
     for (int g = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); g < a.B; g += nwarps)
@@ -2224,7 +2231,10 @@ int hv_mcts_select(const hv_tree* tree, int mode, const float* child_init_q, con
     SelectArgs a{mode, child_init_q, game_active, root_nodes, alive_mask, root_slots, num_candidates,
                  max_root_children, c_puct, B, total, deterministic_non_root, non_root_sigma,
                  q_penalty, leaf, move_paths, path_len, vl_paths, vl_len};
-    k_mcts_select<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+    if (mode == 2 && num_candidates <= 32)  // candidates' subtrees are disjoint: a warp each
+        k_mcts_select_slots<<<game_grid(B * num_candidates), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+    else
+        k_mcts_select<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
     return launch_status();
 }
 

@@ -152,9 +152,10 @@ __device__ __forceinline__ void sel_step(const TreeDev& t, const SelectArgs& a, 
     }
 }
 
-__device__ __noinline__ void select_game(const TreeDev& t, const SelectArgs& a, int g) {
+// one simulation s of game g (the warp's lanes score children in parallel)
+__device__ __forceinline__ void select_sim(const TreeDev& t, const SelectArgs& a, int g, int s) {
     const int l = lane_id();
-    for (int s = g; s < a.total; s += a.B) {
+    {
         int node = -1, plen = 0, vlen = 0;
         bool ok = a.active[g] != 0;
         const int root = a.roots[g];
@@ -217,6 +218,31 @@ __device__ __noinline__ void select_game(const TreeDev& t, const SelectArgs& a, 
         }
         __syncwarp();
     }
+}
+
+// the simulations of game g in order (s = g, g + B, ...)
+__device__ __noinline__ void select_game(const TreeDev& t, const SelectArgs& a, int g) {
+    for (int s = g; s < a.total; s += a.B) select_sim(t, a, g, s);
+}
+
+// Root-slot mode: the simulations of candidate j of game g (s = g + k B with
+// k = j, j + C, j + 2C, ...), in order.  Each descends below a distinct root
+// child, so the virtual losses and statistics it reads and writes belong to
+// that child's subtree alone: candidates of one game can run in separate
+// warps and every simulation sees the tree it sees in the sequential order
+// (the reference's).  A game whose candidate table repeats a slot runs all of
+// its simulations in order in the warp of candidate 0.  C <= 32.
+__device__ __noinline__ void select_game_slot(const TreeDev& t, const SelectArgs& a, int g, int j) {
+    const int l = lane_id();
+    const int sl = l < a.C ? a.slots[(int64_t)g * a.C + l] : -1;
+    const bool v = l < a.C && sl >= 0;
+    const uint32_t same = __match_any_sync(kFull, v ? sl : -1 - l);  // unset / unused lanes: keys of their own
+    if (__any_sync(kFull, v && __popc(same) > 1)) {
+        if (j == 0) select_game(t, a, g);
+        return;
+    }
+    const int per_game = a.total / a.B;
+    for (int k = j; k < per_game; k += a.C) select_sim(t, a, g, g + k * a.B);
 }
 
 // terminal value from the leaf player's perspective (mcts_tree.cuh:182-188)
