@@ -66,6 +66,8 @@ _SIGNATURES = {
     "hv_mcts_replay": ([_vp, _vp, _vp, _vp, _vp, _int, _int, _vp], _int),
     "hv_mcts_expand": ([_tp, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f,
                         _int, _int, _vp], _int),
+    "hv_mcts_expand_slots": ([_tp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _f,
+                              _int, _int, _vp], _int),
     "hv_mcts_backprop": ([_tp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp], _int),
     "hv_mcts_root_noise": ([_tp, _vp, _vp, _int, _f, _f, _int, _vp], _int),
     "hv_mcts_extract_policy": ([_tp, _vp, _vp, _vp, _f, _int, _f, _int, _vp], _int),

@@ -1179,6 +1179,13 @@ __global__ void __launch_bounds__(kThreads) k_mcts_select_slots(TreeDev t, Selec
         select_game_slot(t, a, (int)(i / a.C), (int)(i % a.C));
 }
 
+// root-slot mode, dense expansion + backup: one block of C warps per game
+__global__ void __launch_bounds__(1024) k_mcts_expand_slots(TreeDev t, ExpandArgs a, const int32_t* roots,
+                                                            const int32_t* slots, int C) {
+    extern __shared__ __align__(16) int32_t xs_sm[];
+    expand_game_slots(t, a, roots, slots, C, blockIdx.x, xs_sm);
+}
+
 __global__ void __launch_bounds__(kThreads) k_mcts_expand(TreeDev t, ExpandArgs a) {
     const int nwarps = gridDim.x * kWarpsPerBlock;
     for (int g = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); g < a.B; g += nwarps)
@@ -2266,6 +2273,30 @@ int hv_mcts_expand(const hv_tree* tree, int dense, int backprop, float* child_in
     ExpandArgs a{dense, backprop, child_init_q, child_q, leaf, leaf_states, legal_moves, num_legal,
                  priors, results, values, vl_paths, vl_len, was_expanded, q_penalty, B, total};
     k_mcts_expand<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+    return launch_status();
+}
+
+int hv_mcts_expand_slots(const hv_tree* tree, float* child_init_q, const float* child_q, const int32_t* leaf,
+                         const uint8_t* leaf_states, const uint8_t* legal_moves, const int32_t* num_legal,
+                         const float* priors, const int32_t* results, const float* values,
+                         const int32_t* vl_paths, const int32_t* vl_len, const int32_t* root_nodes,
+                         const int32_t* root_slots, int num_candidates, float q_penalty, int B, int total,
+                         void* stream) {
+    if (!tree_ok(tree) || B < 0 || total < 0 || num_candidates < 1) return HV_EINVAL;
+    if (total == 0 || B == 0) return HV_OK;
+    if (!leaf || !leaf_states || !legal_moves || !num_legal || !priors || !results || !child_init_q ||
+        !child_q || !values || !vl_paths || !vl_len || !root_nodes || !root_slots)
+        return HV_EINVAL;
+    ExpandArgs a{1, 1, child_init_q, child_q, leaf, leaf_states, legal_moves, num_legal, priors, results,
+                 values, vl_paths, vl_len, nullptr, q_penalty, B, total};
+    const int64_t per = total / B;
+    if (num_candidates > 32 || total % ((int64_t)B * num_candidates) != 0 || per > 1024) {
+        // outside the parallel form's shape: the per-game kernel, same results
+        k_mcts_expand<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+        return launch_status();
+    }
+    k_mcts_expand_slots<<<B, 32 * num_candidates, 6 * sizeof(int32_t) * per, (cudaStream_t)stream>>>(
+        tree_dev(tree), a, root_nodes, root_slots, num_candidates);
     return launch_status();
 }
 

@@ -408,6 +408,173 @@ __device__ __noinline__ void expand_game(const TreeDev& t, const ExpandArgs& a, 
     }
 }
 
+// The dense expansion + backup of one game whose simulations came from the
+// root-slot select (candidate (s / B) % C of each simulation s), one block of
+// C warps per game, with the results of expand_game:
+//  1. node allocation in simulation order (warp 0): a simulation expands iff
+//     its leaf is unexpanded, not terminal, has moves and fits, and no earlier
+//     simulation of the game expanded the same leaf -- a leaf lies below one
+//     candidate, so only that candidate's earlier simulations can share it;
+//  2. warp j runs candidate j's simulations in order: expansion at the
+//     allocated base, virtual-loss removal and the backup up to the root
+//     (every node below the root belongs to the candidate's subtree);
+//  3. warp 0 adds the root-level updates (root and any ancestors) of every
+//     simulation in simulation order, as the sequential backup does.
+// A candidate table that repeats a slot takes expand_game instead.  Shared
+// memory: 6 words per simulation of the game.
+__device__ void expand_game_slots(const TreeDev& t, const ExpandArgs& a, const int32_t* roots,
+                                  const int32_t* slots, int C, int g, int32_t* sm) {
+    const int l = lane_id(), j = threadIdx.x >> 5;
+    const int per = a.total / a.B;
+    int32_t *leafv = sm, *nl = sm + per, *base = sm + 2 * per, *steps = sm + 3 * per, *stopn = sm + 4 * per;
+    float* vroot = reinterpret_cast<float*>(sm + 5 * per);
+    __shared__ int dup;
+    if (j == 0) {
+        const int sl = l < C ? slots[(int64_t)g * C + l] : -1;
+        const bool v = l < C && sl >= 0;
+        const uint32_t same = __match_any_sync(kFull, v ? sl : -1 - l);
+        const bool d = __any_sync(kFull, v && __popc(same) > 1);
+        if (l == 0) dup = d;
+    }
+    __syncthreads();
+    if (dup) {
+        if (j == 0) expand_game(t, a, g);
+        return;
+    }
+    // ---- 1. allocation
+    if (j == 0) {
+        for (int k = l; k < per; k += 32) {
+            const int s = g + k * a.B, leafn = a.leaf[s];
+            int n = 0;
+            if (leafn >= 0 && a.results[s] == 0 && t.fc[tix(t, g, leafn)] == -1) n = a.num_legal[s];
+            leafv[k] = leafn;
+            nl[k] = n;  // > 0: a candidate for expansion
+        }
+        __syncwarp();
+        if (l == 0) {
+            int cur = t.cnt[g];
+            for (int k = 0; k < per; k++) {
+                int b = -1;
+                const int n = nl[k];
+                if (n > 0) {
+                    bool seen = false;
+                    for (int q = k - C; q >= 0 && !seen; q -= C) seen = base[q] >= 0 && leafv[q] == leafv[k];
+                    if (!seen && cur + n <= t.max_nodes) {
+                        b = cur;
+                        cur += n;
+                    }
+                }
+                base[k] = b;
+            }
+            t.cnt[g] = cur;
+        }
+    }
+    __syncthreads();
+    // ---- 2. candidate j's simulations
+    const int root = roots[g];
+    const uint32_t lt = lanemask_lt();
+    for (int k = j; k < per; k += C) {
+        const int s = g + k * a.B, leafn = leafv[k];
+        if (leafn < 0) {
+            if (l == 0) steps[k] = -1;
+            continue;
+        }
+        const int64_t li = tix(t, g, leafn);
+        const uint8_t* lst = a.leaf_states + (int64_t)s * kStateBytes;
+        int expanded = 0;
+        if (a.results[s] != 0) {
+            if (l == 0) {
+                t.it[li] = 1;
+                t.tval[li] = result_value(a.results[s], lst[kOffTurn] | (lst[kOffTurn + 1] << 8));
+            }
+        } else if (base[k] >= 0) {
+            const int n = nl[k], b0 = base[k];
+            int cq, cr;
+            warp_centroid(lst, cq, cr);
+            const uint8_t* mv = a.legal + (int64_t)s * kMaxMoves * kMoveBytes;
+            for (int m = l; m < n; m += 32) {
+                const int64_t ci = tix(t, g, b0 + m);
+                t.vc[ci] = 0;
+                t.tv[ci] = 0.0f;
+                t.pr[ci] = a.priors[(int64_t)s * kMaxMoves + m];
+                t.pa[ci] = leafn;
+                t.ai[ci] = move_action(mv + m * 6, cq, cr);
+                t.fc[ci] = -1;
+                t.nc[ci] = 0;
+                t.it[ci] = 0;
+                t.tval[ci] = 0.0f;
+                a.init_q[ci] = a.child_q[(int64_t)s * kMaxMoves + m];
+#pragma unroll
+                for (int q = 0; q < 6; q++) t.mb[ci * 6 + q] = mv[m * 6 + q];
+            }
+            __syncwarp();
+            if (l == 0) {
+                t.nc[li] = n;
+                t.fc[li] = b0;
+            }
+            expanded = 1;
+        }
+        __syncwarp();
+        (void)lt;
+        if (l == 0) {
+            float v = t.it[li] ? t.tval[li] : (expanded ? a.values[s] : 0.0f);
+            const int vl = a.vll[s];
+            for (int q = 0; q < vl; q++) {
+                const int64_t ni = tix(t, g, a.vlp[(int64_t)s * kTreeDepth + q]);
+                if (a.qpen > 0.0f) {
+                    t.vq[ni] = __fadd_rn(t.vq[ni], -a.qpen);
+                } else {
+                    t.vc[ni] -= 1;
+                    t.tv[ni] = __fadd_rn(t.tv[ni], 1.0f);
+                }
+            }
+            int node = leafn, q = 0;
+            for (; q < kTreeDepth + 1 && node >= 0 && node != root; q++) {
+                const int64_t ni = tix(t, g, node);
+                t.vc[ni] += 1;
+                t.tv[ni] = __fadd_rn(t.tv[ni], v);
+                v = -v;
+                node = t.pa[ni];
+            }
+            steps[k] = q;
+            stopn[k] = node;
+            vroot[k] = v;
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    // ---- 3. root-level updates in simulation order (one node cached in registers)
+    if (threadIdx.x == 0) {
+        int cn = -1, cvc = 0;
+        float ctv = 0.0f;
+        for (int k = 0; k < per; k++) {
+            int q = steps[k], node = stopn[k];
+            if (q < 0) continue;
+            float v = vroot[k];
+            for (; q < kTreeDepth + 1 && node >= 0; q++) {
+                const int64_t ni = tix(t, g, node);
+                if (node != cn) {
+                    if (cn >= 0) {
+                        t.vc[tix(t, g, cn)] = cvc;
+                        t.tv[tix(t, g, cn)] = ctv;
+                    }
+                    cn = node;
+                    cvc = t.vc[ni];
+                    ctv = t.tv[ni];
+                }
+                cvc += 1;
+                ctv = __fadd_rn(ctv, v);
+                v = -v;
+                node = t.pa[ni];
+            }
+        }
+        if (cn >= 0) {
+            t.vc[tix(t, g, cn)] = cvc;
+            t.tv[tix(t, g, cn)] = ctv;
+        }
+    }
+}
+
 // legacy backup given was_expanded (mcts_tree.cuh:555-605)
 __device__ __noinline__ void backprop_game(const TreeDev& t, const int32_t* leaf, const float* values,
                                            const int32_t* vlp, const int32_t* vll, const int8_t* was,

@@ -545,6 +545,39 @@ class HiveGPUExtension:
                      num_legal, priors_per_legal, results, nn_values, vl_paths, vl_lengths, B, total, max_nodes,
                      q_penalty, False)
 
+    def mcts_expand_and_backprop_dense_priors_slots_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt,
+                                                          child_init_q, child_q_values, leaf_indices, leaf_states,
+                                                          legal_moves, num_legal, priors_per_legal, results,
+                                                          nn_values, vl_paths, vl_lengths, root_nodes, root_slots,
+                                                          num_candidates, B, total, max_nodes, q_penalty=0.0):
+        """mcts_expand_and_backprop_dense_priors_batch for the simulations of
+        mcts_select_with_root_slots_batch (same root_nodes / root_slots): the
+        same tree, the candidates' subtrees updated in parallel
+        (hv_mcts_expand_slots)."""
+        import ctypes
+        tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
+        dev = vc.device
+        ts = self._tree(tree, max_nodes, B)
+        leaf_indices = _need(leaf_indices, "leaf_indices", torch.int32, total)
+        leaf_states = _need(leaf_states, "leaf_states", torch.uint8, total, (SIZEOF_HIVE_STATE,))
+        legal_moves = _need(legal_moves, "legal_moves", torch.uint8, total, (MAX_LEGAL_MOVES, SIZEOF_GPU_MOVE))
+        num_legal = _need(num_legal, "num_legal", torch.int32, total)
+        priors = _need(priors_per_legal, "priors", torch.float32, total, (MAX_LEGAL_MOVES,))
+        results = _need(results, "results", torch.int32, total)
+        child_q = _need(child_q_values, "child_q_values", torch.float32, total, (MAX_LEGAL_MOVES,))
+        child_init_q = _need(child_init_q, "child_init_q", torch.float32, B)
+        values = _need(nn_values.reshape(-1), "nn_values", torch.float32, total)
+        vl_paths = _need(vl_paths, "vl_paths", torch.int32, total)
+        vl_lengths = _need(vl_lengths, "vl_lengths", torch.int32, total)
+        root_nodes = _need(root_nodes, "root_nodes", torch.int32, B)
+        root_slots = _need(root_slots.to(torch.int32), "root_slots", torch.int32, B)
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.hv_mcts_expand_slots(
+                ctypes.byref(ts), _ptr(child_init_q), _ptr(child_q), _ptr(leaf_indices), _ptr(leaf_states),
+                _ptr(legal_moves), _ptr(num_legal), _ptr(priors), _ptr(results), _ptr(values), _ptr(vl_paths),
+                _ptr(vl_lengths), _ptr(root_nodes), _ptr(root_slots), int(num_candidates), float(q_penalty), B,
+                total, _stream(dev)), "mcts_expand_slots")
+
     def mcts_backprop_batch(self, vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt, leaf_indices, nn_values,
                             vl_paths, vl_lengths, was_expanded, B, total, max_nodes):
         import ctypes

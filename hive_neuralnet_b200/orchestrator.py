@@ -440,9 +440,9 @@ class FNNMCTSOrchestrator(_SearchBase):
                 self.trace.append(dict(kind="wave", root_slots=root_slots.clone(), W=aw, leaf=leaf.clone(),
                                        priors=pri.clone(),
                                        values=vals.clone(), child_q=cq.clone()))
-            self.ext.mcts_expand_and_backprop_dense_priors_batch(
+            self.ext.mcts_expand_and_backprop_dense_priors_slots_batch(
                 *self._tree_args(tree), tree["child_init_q"], cq, leaf, leaf_states, legal, nl, pri, results, vals,
-                vlp, vll, B, total, self._max_nodes, q_pen)
+                vlp, vll, tree["root_node"], root_slots, C, B, total, self._max_nodes, q_pen)
 
     def self_play_batch(self, start_states: torch.Tensor | None = None) -> list[list[FNNTrainingExample]]:
         """fnn_mcts_orchestrator.py:561-875"""

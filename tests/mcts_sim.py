@@ -25,7 +25,8 @@ class OracleBackend:
     def replay(self, root_states, paths, plen, leaf, B):
         return O.mcts_replay(self.name, root_states, paths, plen, leaf, B)
 
-    def expand_dense(self, tree, *args, **kw):
+    def expand_dense(self, tree, *args, slots=None, **kw):
+        # (the oracle's sequential expansion serves the root-slot waves too)
         return O.mcts_expand_dense(self.name, tree, *args, **kw)
 
 
@@ -39,7 +40,8 @@ def _priors(rng, nl):
 
 
 def run_waves(backend, states: np.ndarray, waves: int, W: int, mode: int, seed: int, C: int = 4,
-              max_nodes: int = 4096, det: bool = False, q_penalty: float = 0.0, c_puct: float = 1.25):
+              max_nodes: int = 4096, det: bool = False, q_penalty: float = 0.0, c_puct: float = 1.25,
+              repeat_slots: bool = False):
     orc = O.oracle()
     B = states.shape[0]
     rng = np.random.default_rng(seed)
@@ -63,6 +65,8 @@ def run_waves(backend, states: np.ndarray, waves: int, W: int, mode: int, seed: 
             slots = np.stack([rng.permutation(256)[:C] for _ in range(B)]).astype(np.int32)
             slots = np.where(slots < nl[:, None], slots, -1).astype(np.int32)
             slots[:, 0] = np.where(nl > 0, rng.integers(0, np.maximum(nl, 1)), -1)
+            if repeat_slots:  # every other game lists its first candidate twice
+                slots[::2, 1] = slots[::2, 0]
             kw.update(root_slots=slots, num_candidates=C, max_root_children=256)
         leaf, paths, plen, vlp, vll = backend.select(tree, **kw)
         ls = backend.replay(states, paths, plen, leaf, B)
@@ -72,6 +76,7 @@ def run_waves(backend, states: np.ndarray, waves: int, W: int, mode: int, seed: 
         cq = np.where(lvalid, rng.uniform(-1, 1, (len(leaf), 256)), 0).astype(np.float32)
         vals = rng.uniform(-1, 1, len(leaf)).astype(np.float32)
         backend.expand_dense(tree, cq, leaf, ls, lmv, lnl, _priors(rng, lnl), lres, vals, vlp, vll,
-                             q_penalty=q_penalty if det and W > 1 else 0.0, with_backprop=True)
+                             q_penalty=q_penalty if det and W > 1 else 0.0, with_backprop=True,
+                             slots=(roots, kw["root_slots"], C) if mode == 2 else None)
         log.append((leaf.copy(), plen.copy(), vll.copy()))
     return tree, log

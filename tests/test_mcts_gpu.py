@@ -2,7 +2,10 @@
 against the sequential oracle: after several select / replay / expand+backup
 waves the whole tree (visit counts, value sums as raw float bits, priors,
 parents, moves, actions, children, terminal flags, node counts, child Q)
-must be bit-identical, for every select mode and wave width."""
+must be bit-identical, for every select mode and wave width.  Root-slot
+waves (mode 2) run the candidate-parallel select and expansion; their random
+candidate tables repeat a slot in some games, which takes the per-game
+order, so both forms are compared with the oracle."""
 import numpy as np
 import pytest
 import torch
@@ -61,13 +64,19 @@ class GpuBackend:
         return out.cpu().numpy()
 
     def expand_dense(self, tree, child_q, leaf, leaf_states, legal, num_legal, priors, results, values=None,
-                     vl_paths=None, vl_len=None, q_penalty=0.0, with_backprop=True):
+                     vl_paths=None, vl_len=None, q_penalty=0.0, with_backprop=True, slots=None):
         ts, ciq = self._up(tree)
         B, M, total = tree.B, tree.max_nodes, len(leaf)
         args = (self._t(child_q), self._t(leaf), self._t(leaf_states), self._t(legal), self._t(num_legal),
                 self._t(priors), self._t(results))
         was = None
-        if with_backprop:
+        if with_backprop and slots is not None:
+            # root-slot waves: the candidate-parallel expansion (hv_mcts_expand_slots)
+            roots, root_slots, C = slots
+            self.ext.mcts_expand_and_backprop_dense_priors_slots_batch(
+                *ts, ciq, *args, self._t(values), self._t(vl_paths), self._t(vl_len), self._t(roots),
+                self._t(root_slots), C, B, total, M, q_penalty)
+        elif with_backprop:
             self.ext.mcts_expand_and_backprop_dense_priors_batch(*ts, ciq, *args, self._t(values), self._t(vl_paths),
                                                                  self._t(vl_len), B, total, M, q_penalty)
         else:
@@ -88,6 +97,19 @@ def test_tree_waves_bit_exact(mode, W):
     st = _states(300 + 7 * mode + W)
     a, la = run_waves(OracleBackend("orc"), st, waves=8, W=W, mode=mode, seed=11)
     b, lb = run_waves(GpuBackend(), st, waves=8, W=W, mode=mode, seed=11)
+    for (x1, y1, z1), (x2, y2, z2) in zip(la, lb):
+        assert np.array_equal(x1, x2) and np.array_equal(y1, y2) and np.array_equal(z1, z2)
+    assert a.equal(b) == []
+    assert a.visit_count[:, 0].sum() > 0
+
+
+@pytest.mark.parametrize("W", [1, 4])
+def test_root_slot_waves_with_repeated_slots_bit_exact(W):
+    # games whose candidate table lists a slot twice share a subtree between
+    # two candidates: select and expansion keep the per-game order there
+    st = _states(900 + W)
+    a, la = run_waves(OracleBackend("orc"), st, waves=8, W=W, mode=2, seed=13, repeat_slots=True)
+    b, lb = run_waves(GpuBackend(), st, waves=8, W=W, mode=2, seed=13, repeat_slots=True)
     for (x1, y1, z1), (x2, y2, z2) in zip(la, lb):
         assert np.array_equal(x1, x2) and np.array_equal(y1, y2) and np.array_equal(z1, z2)
     assert a.equal(b) == []
