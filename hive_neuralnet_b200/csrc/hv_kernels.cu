@@ -1172,6 +1172,13 @@ __global__ void __launch_bounds__(kThreads) k_mcts_select(TreeDev t, SelectArgs 
         select_game(t, a, g);
 }
 
+// plain / root-mask modes: one block per game (root steps, then the descents)
+__global__ void __launch_bounds__(kTreeThreads) k_mcts_select_tree(TreeDev t, SelectArgs a) {
+    extern __shared__ __align__(16) int32_t sel_sm[];
+    const int per = a.total / a.B;
+    select_game_tree(t, a, blockIdx.x, sel_sm, sel_sm + per);
+}
+
 // root-slot mode: one warp per (game, candidate)
 __global__ void __launch_bounds__(kThreads) k_mcts_select_slots(TreeDev t, SelectArgs a) {
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock, n = (int64_t)a.B * a.C;
@@ -1179,11 +1186,12 @@ __global__ void __launch_bounds__(kThreads) k_mcts_select_slots(TreeDev t, Selec
         select_game_slot(t, a, (int)(i / a.C), (int)(i % a.C));
 }
 
-// root-slot mode, dense expansion + backup: one block of C warps per game
+// dense expansion + backup in simulation groups: one block per game (C warps
+// for root slots, kTreeThreads otherwise)
 __global__ void __launch_bounds__(1024) k_mcts_expand_slots(TreeDev t, ExpandArgs a, const int32_t* roots,
                                                             const int32_t* slots, int C) {
     extern __shared__ __align__(16) int32_t xs_sm[];
-    expand_game_slots(t, a, roots, slots, C, blockIdx.x, xs_sm);
+    expand_game_groups(t, a, roots, slots, C, blockIdx.x, xs_sm);
 }
 
 __global__ void __launch_bounds__(kThreads) k_mcts_expand(TreeDev t, ExpandArgs a) {
@@ -2240,6 +2248,9 @@ int hv_mcts_select(const hv_tree* tree, int mode, const float* child_init_q, con
                  q_penalty, leaf, move_paths, path_len, vl_paths, vl_len};
     if (mode == 2 && num_candidates <= 32)  // candidates' subtrees are disjoint: a warp each
         k_mcts_select_slots<<<game_grid(B * num_candidates), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
+    else if (mode != 2 && total / B <= 4096)  // root steps in order, then the root children's subtrees in parallel
+        k_mcts_select_tree<<<B, kTreeThreads, 2 * sizeof(int32_t) * (total / B), (cudaStream_t)stream>>>(
+            tree_dev(tree), a);
     else
         k_mcts_select<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
     return launch_status();
@@ -2282,21 +2293,23 @@ int hv_mcts_expand_slots(const hv_tree* tree, float* child_init_q, const float* 
                          const int32_t* vl_paths, const int32_t* vl_len, const int32_t* root_nodes,
                          const int32_t* root_slots, int num_candidates, float q_penalty, int B, int total,
                          void* stream) {
-    if (!tree_ok(tree) || B < 0 || total < 0 || num_candidates < 1) return HV_EINVAL;
+    if (!tree_ok(tree) || B < 0 || total < 0 || (root_slots && num_candidates < 1)) return HV_EINVAL;
     if (total == 0 || B == 0) return HV_OK;
     if (!leaf || !leaf_states || !legal_moves || !num_legal || !priors || !results || !child_init_q ||
-        !child_q || !values || !vl_paths || !vl_len || !root_nodes || !root_slots)
+        !child_q || !values || !vl_paths || !vl_len || !root_nodes)
         return HV_EINVAL;
     ExpandArgs a{1, 1, child_init_q, child_q, leaf, leaf_states, legal_moves, num_legal, priors, results,
                  values, vl_paths, vl_len, nullptr, q_penalty, B, total};
     const int64_t per = total / B;
-    if (num_candidates > 32 || total % ((int64_t)B * num_candidates) != 0 || per > 1024) {
+    const bool shape_ok = root_slots ? (num_candidates <= 32 && total % ((int64_t)B * num_candidates) == 0)
+                                     : total % B == 0;
+    if (!shape_ok || per > 1024) {
         // outside the parallel form's shape: the per-game kernel, same results
         k_mcts_expand<<<game_grid(B), kThreads, 0, (cudaStream_t)stream>>>(tree_dev(tree), a);
         return launch_status();
     }
-    k_mcts_expand_slots<<<B, 32 * num_candidates, 6 * sizeof(int32_t) * per, (cudaStream_t)stream>>>(
-        tree_dev(tree), a, root_nodes, root_slots, num_candidates);
+    k_mcts_expand_slots<<<B, root_slots ? 32 * num_candidates : kTreeThreads, 7 * sizeof(int32_t) * per,
+                          (cudaStream_t)stream>>>(tree_dev(tree), a, root_nodes, root_slots, num_candidates);
     return launch_status();
 }
 

@@ -19,6 +19,7 @@
 namespace hv {
 
 constexpr int kTreeDepth = 128;
+constexpr int kTreeThreads = 256;  // block of the per-game tree kernels (8 warps)
 
 struct TreeDev {
     int32_t* vc;
@@ -152,71 +153,147 @@ __device__ __forceinline__ void sel_step(const TreeDev& t, const SelectArgs& a, 
     }
 }
 
+// One selection step at `node`: the chosen child, or -1 where the walk
+// stops (an unexpanded or terminal node, no candidate).  pv_at < 0: the
+// node's visit count from the tree, else that count (the parent visits the
+// scores use).  det_step: the step used the completed-Q rule.
+__device__ __forceinline__ int select_child(const TreeDev& t, const SelectArgs& a, int g, int node, int root,
+                                            int pv_at, bool& det_step) {
+    const int l = lane_id();
+    const int64_t ni = tix(t, g, node);
+    const int fc = t.fc[ni], nc = t.nc[ni];
+    det_step = false;
+    if (fc < 0 || t.it[ni] || nc == 0 || nc <= 0 || nc > 1024) return -1;
+    const bool at_root = a.mode != 2 && node == root;
+    const bool use_det = a.det && a.mode != 0 && !at_root;
+    det_step = use_det;
+    int best;
+    if (use_det) {
+        best = 0;
+        if (l == 0) best = completed_q_child(t, g, fc, nc, a.sigma, a.init_q);
+        best = __shfl_sync(kFull, best, 0);
+    } else {
+        const int pv = pv_at >= 0 ? pv_at : t.vc[ni];
+        int lim = nc;
+        if (fc + lim > t.max_nodes) lim = t.max_nodes - fc;  // reference breaks there
+        float bs = 0.0f;
+        int bi = -1;
+        for (int c = l; c < lim; c += 32) {
+            if (a.mode == 1 && at_root &&
+                (c >= a.max_root_children || !a.alive[(int64_t)g * a.max_root_children + c]))
+                continue;
+            float sc = puct(t, g, pv, fc + c, a.c_puct);
+            if (!(sc > -1e30f)) continue;  // strict > from -1e30: NaN never wins
+            if (bi < 0 || sc > bs) {
+                bs = sc;
+                bi = c;
+            }
+        }
+        warp_argmax(bs, bi);
+        best = bi >= 0 ? fc + bi : (a.mode == 0 ? fc : -1);
+    }
+    return best;
+}
+
+// the walk of simulation s below `node` (steps it0 .., path entries so far)
+__device__ __forceinline__ void select_descend(const TreeDev& t, const SelectArgs& a, int g, int s, int node,
+                                               int root, int it0, int plen, int vlen, int pv_first) {
+    const int l = lane_id();
+    for (int it = it0; it < kTreeDepth; it++) {
+        bool det_step;
+        const int best = select_child(t, a, g, node, root, it == it0 ? pv_first : -1, det_step);
+        if (best < 0) break;
+        node = best;
+        if (l == 0) sel_step(t, a, g, s, node, true, det_step, plen, vlen);
+        __syncwarp();
+    }
+    if (l == 0) {
+        a.leaf[s] = node;
+        a.plen[s] = plen;
+        a.vll[s] = vlen;
+    }
+    __syncwarp();
+}
+
 // one simulation s of game g (the warp's lanes score children in parallel)
 __device__ __forceinline__ void select_sim(const TreeDev& t, const SelectArgs& a, int g, int s) {
     const int l = lane_id();
-    {
-        int node = -1, plen = 0, vlen = 0;
-        bool ok = a.active[g] != 0;
-        const int root = a.roots[g];
-        int iter0 = 0;
-        if (ok) node = root;
-        if (ok && a.mode == 2) {
-            int slot = a.slots[(int64_t)g * a.C + (s / a.B) % a.C];
-            int64_t ri = tix(t, g, root);
-            int fc = t.fc[ri], nc = t.nc[ri];
-            ok = slot >= 0 && slot < a.max_root_children && fc >= 0 && !t.it[ri] && nc > 0 && slot < nc &&
-                 fc + slot >= 0 && fc + slot < t.max_nodes;
-            if (ok) {
-                node = fc + slot;
-                if (l == 0) sel_step(t, a, g, s, node, !a.det, false, plen, vlen);
-                iter0 = 1;
-            }
+    int node = -1, plen = 0, vlen = 0;
+    bool ok = a.active[g] != 0;
+    const int root = a.roots[g];
+    int iter0 = 0;
+    if (ok) node = root;
+    if (ok && a.mode == 2) {
+        int slot = a.slots[(int64_t)g * a.C + (s / a.B) % a.C];
+        int64_t ri = tix(t, g, root);
+        int fc = t.fc[ri], nc = t.nc[ri];
+        ok = slot >= 0 && slot < a.max_root_children && fc >= 0 && !t.it[ri] && nc > 0 && slot < nc &&
+             fc + slot >= 0 && fc + slot < t.max_nodes;
+        if (ok) {
+            node = fc + slot;
+            if (l == 0) sel_step(t, a, g, s, node, !a.det, false, plen, vlen);
+            iter0 = 1;
         }
-        if (!ok) node = -1;
-        __syncwarp();
-        for (int it = iter0; ok && it < kTreeDepth; it++) {
-            int64_t ni = tix(t, g, node);
-            int fc = t.fc[ni], nc = t.nc[ni];
-            if (fc < 0 || t.it[ni] || nc == 0 || nc <= 0 || nc > 1024) break;
-            const bool at_root = a.mode != 2 && node == root;
-            const bool use_det = a.det && a.mode != 0 && !at_root;
-            int best;
-            if (use_det) {
-                best = 0;
-                if (l == 0) best = completed_q_child(t, g, fc, nc, a.sigma, a.init_q);
-                best = __shfl_sync(kFull, best, 0);
-            } else {
-                const int pv = t.vc[ni];
-                int lim = nc;
-                if (fc + lim > t.max_nodes) lim = t.max_nodes - fc;  // reference breaks there
-                float bs = 0.0f;
-                int bi = -1;
-                for (int c = l; c < lim; c += 32) {
-                    if (a.mode == 1 && at_root &&
-                        (c >= a.max_root_children || !a.alive[(int64_t)g * a.max_root_children + c]))
-                        continue;
-                    float sc = puct(t, g, pv, fc + c, a.c_puct);
-                    if (!(sc > -1e30f)) continue;  // strict > from -1e30: NaN never wins
-                    if (bi < 0 || sc > bs) {
-                        bs = sc;
-                        bi = c;
-                    }
-                }
-                warp_argmax(bs, bi);
-                best = bi >= 0 ? fc + bi : (a.mode == 0 ? fc : -1);
-            }
-            if (best < 0) break;
-            node = best;
-            if (l == 0) sel_step(t, a, g, s, node, true, use_det, plen, vlen);
-            __syncwarp();
-        }
+    }
+    __syncwarp();
+    if (!ok) {
         if (l == 0) {
-            a.leaf[s] = node;
+            a.leaf[s] = -1;
             a.plen[s] = plen;
             a.vll[s] = vlen;
         }
         __syncwarp();
+        return;
+    }
+    plen = __shfl_sync(kFull, plen, 0);
+    vlen = __shfl_sync(kFull, vlen, 0);
+    select_descend(t, a, g, s, node, root, iter0, plen, vlen, -1);
+}
+
+// Plain and root-mask selects (modes 0, 1), one block per game: warp 0 takes
+// every simulation's root step in simulation order (each scoring the root's
+// children with the earlier simulations' virtual losses on them) and records
+// the chosen child and that child's visit count after the simulation's own
+// virtual loss -- the parent visits its first step below the child sees in
+// the sequential order; then each simulation descends below its root child,
+// the simulations of one child in order in one warp (warp = child mod the
+// block's warps).  Below the root, simulations of different children read
+// and write disjoint subtrees, so every one sees the tree of the sequential
+// order.  rc / pvc: shared, two words per simulation of the game.
+__device__ void select_game_tree(const TreeDev& t, const SelectArgs& a, int g, int32_t* rc, int32_t* pvc) {
+    const int l = lane_id(), w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int per = a.total / a.B;
+    const int root = a.roots[g];
+    const bool active = a.active[g] != 0;
+    if (w == 0) {
+        for (int k = 0; k < per; k++) {
+            const int s = g + k * a.B;
+            int c = -1;
+            if (active) {
+                bool det_step;
+                c = select_child(t, a, g, root, root, -1, det_step);
+                if (c >= 0 && l == 0) {
+                    int plen = 0, vlen = 0;
+                    sel_step(t, a, g, s, c, true, det_step, plen, vlen);
+                    pvc[k] = t.vc[tix(t, g, c)];
+                }
+            }
+            if (l == 0) {
+                rc[k] = c;
+                if (c < 0) {
+                    a.leaf[s] = active ? root : -1;
+                    a.plen[s] = 0;
+                    a.vll[s] = 0;
+                }
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    for (int k = 0; k < per; k++) {
+        const int c = rc[k];
+        if (c < 0 || c % nw != w) continue;
+        select_descend(t, a, g, g + k * a.B, c, root, 1, 1, 1, pvc[k]);
     }
 }
 
@@ -408,33 +485,42 @@ __device__ __noinline__ void expand_game(const TreeDev& t, const ExpandArgs& a, 
     }
 }
 
-// The dense expansion + backup of one game whose simulations came from the
-// root-slot select (candidate (s / B) % C of each simulation s), one block of
-// C warps per game, with the results of expand_game:
+// The dense expansion + backup of one game, one block per game, with the
+// results of expand_game, for simulations whose walks below the root fall
+// into disjoint groups: slots != NULL -- the root-slot select, group of
+// simulation s = its candidate (s / B) % C, one warp each (C warps); slots
+// == NULL -- the plain / root-mask selects, group = the root child at the
+// head of the simulation's virtual-loss path, warp = child mod the block's
+// warps (simulations that stop at the root itself go to warp 0).
 //  1. node allocation in simulation order (warp 0): a simulation expands iff
 //     its leaf is unexpanded, not terminal, has moves and fits, and no earlier
-//     simulation of the game expanded the same leaf -- a leaf lies below one
-//     candidate, so only that candidate's earlier simulations can share it;
-//  2. warp j runs candidate j's simulations in order: expansion at the
+//     simulation of the game expanded the same leaf (a leaf lies in one group,
+//     so with candidates only the same candidate's earlier simulations are
+//     checked);
+//  2. each warp runs its groups' simulations in order: expansion at the
 //     allocated base, virtual-loss removal and the backup up to the root
-//     (every node below the root belongs to the candidate's subtree);
-//  3. warp 0 adds the root-level updates (root and any ancestors) of every
+//     (every node below the root belongs to one group's subtree);
+//  3. thread 0 adds the root-level updates (root and any ancestors) of every
 //     simulation in simulation order, as the sequential backup does.
 // A candidate table that repeats a slot takes expand_game instead.  Shared
-// memory: 6 words per simulation of the game.
-__device__ void expand_game_slots(const TreeDev& t, const ExpandArgs& a, const int32_t* roots,
-                                  const int32_t* slots, int C, int g, int32_t* sm) {
-    const int l = lane_id(), j = threadIdx.x >> 5;
+// memory: 7 words per simulation of the game.
+__device__ void expand_game_groups(const TreeDev& t, const ExpandArgs& a, const int32_t* roots,
+                                   const int32_t* slots, int C, int g, int32_t* sm) {
+    const int l = lane_id(), j = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int per = a.total / a.B;
     int32_t *leafv = sm, *nl = sm + per, *base = sm + 2 * per, *steps = sm + 3 * per, *stopn = sm + 4 * per;
     float* vroot = reinterpret_cast<float*>(sm + 5 * per);
+    int32_t* grp = sm + 6 * per;  // warp of each simulation (-1: no walk)
+    const int root = roots[g];
     __shared__ int dup;
-    if (j == 0) {
+    if (j == 0 && slots) {
         const int sl = l < C ? slots[(int64_t)g * C + l] : -1;
         const bool v = l < C && sl >= 0;
         const uint32_t same = __match_any_sync(kFull, v ? sl : -1 - l);
         const bool d = __any_sync(kFull, v && __popc(same) > 1);
         if (l == 0) dup = d;
+    } else if (threadIdx.x == 0) {
+        dup = 0;
     }
     __syncthreads();
     if (dup) {
@@ -449,6 +535,12 @@ __device__ void expand_game_slots(const TreeDev& t, const ExpandArgs& a, const i
             if (leafn >= 0 && a.results[s] == 0 && t.fc[tix(t, g, leafn)] == -1) n = a.num_legal[s];
             leafv[k] = leafn;
             nl[k] = n;  // > 0: a candidate for expansion
+            int w = -1;
+            if (leafn >= 0) {
+                if (slots) w = k % C;
+                else w = a.vll[s] > 0 ? a.vlp[(int64_t)s * kTreeDepth] % nw : 0;
+            }
+            grp[k] = w;
         }
         __syncwarp();
         if (l == 0) {
@@ -458,7 +550,9 @@ __device__ void expand_game_slots(const TreeDev& t, const ExpandArgs& a, const i
                 const int n = nl[k];
                 if (n > 0) {
                     bool seen = false;
-                    for (int q = k - C; q >= 0 && !seen; q -= C) seen = base[q] >= 0 && leafv[q] == leafv[k];
+                    const int stride = slots ? C : 1;
+                    for (int q = k - stride; q >= 0 && !seen; q -= stride)
+                        seen = base[q] >= 0 && leafv[q] == leafv[k];
                     if (!seen && cur + n <= t.max_nodes) {
                         b = cur;
                         cur += n;
@@ -470,15 +564,13 @@ __device__ void expand_game_slots(const TreeDev& t, const ExpandArgs& a, const i
         }
     }
     __syncthreads();
-    // ---- 2. candidate j's simulations
-    const int root = roots[g];
-    const uint32_t lt = lanemask_lt();
-    for (int k = j; k < per; k += C) {
-        const int s = g + k * a.B, leafn = leafv[k];
-        if (leafn < 0) {
-            if (l == 0) steps[k] = -1;
+    // ---- 2. each warp's groups, in simulation order
+    for (int k = 0; k < per; k++) {
+        if (grp[k] != j) {
+            if (grp[k] < 0 && j == 0 && l == 0) steps[k] = -1;
             continue;
         }
+        const int s = g + k * a.B, leafn = leafv[k];
         const int64_t li = tix(t, g, leafn);
         const uint8_t* lst = a.leaf_states + (int64_t)s * kStateBytes;
         int expanded = 0;
@@ -515,7 +607,6 @@ __device__ void expand_game_slots(const TreeDev& t, const ExpandArgs& a, const i
             expanded = 1;
         }
         __syncwarp();
-        (void)lt;
         if (l == 0) {
             float v = t.it[li] ? t.tval[li] : (expanded ? a.values[s] : 0.0f);
             const int vl = a.vll[s];

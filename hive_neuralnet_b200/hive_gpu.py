@@ -551,9 +551,11 @@ class HiveGPUExtension:
                                                           nn_values, vl_paths, vl_lengths, root_nodes, root_slots,
                                                           num_candidates, B, total, max_nodes, q_penalty=0.0):
         """mcts_expand_and_backprop_dense_priors_batch for the simulations of
-        mcts_select_with_root_slots_batch (same root_nodes / root_slots): the
-        same tree, the candidates' subtrees updated in parallel
-        (hv_mcts_expand_slots)."""
+        one select with the same root_nodes: mcts_select_with_root_slots_batch
+        (its root_slots and num_candidates) or, with root_slots None,
+        mcts_select_batch / mcts_select_with_root_mask_batch.  The same tree;
+        the subtrees below different candidates / root children are updated
+        in parallel (hv_mcts_expand_slots)."""
         import ctypes
         tree = (vc, tv, pr, pa, vq, mb, ai, fc, nc, it, tv2, cnt)
         dev = vc.device
@@ -570,7 +572,8 @@ class HiveGPUExtension:
         vl_paths = _need(vl_paths, "vl_paths", torch.int32, total)
         vl_lengths = _need(vl_lengths, "vl_lengths", torch.int32, total)
         root_nodes = _need(root_nodes, "root_nodes", torch.int32, B)
-        root_slots = _need(root_slots.to(torch.int32), "root_slots", torch.int32, B)
+        if root_slots is not None:
+            root_slots = _need(root_slots.to(torch.int32), "root_slots", torch.int32, B)
         with torch.cuda.device(dev):
             _lib.check(self._lib.hv_mcts_expand_slots(
                 ctypes.byref(ts), _ptr(child_init_q), _ptr(child_q), _ptr(leaf_indices), _ptr(leaf_states),

@@ -298,9 +298,9 @@ class _SearchBase:
             if self.trace is not None:
                 self.trace.append(dict(kind="wave", W=aw, leaf=leaf.clone(), priors=pri.clone(),
                                        values=vals.clone(), child_q=cq.clone()))
-            self.ext.mcts_expand_and_backprop_dense_priors_batch(
+            self.ext.mcts_expand_and_backprop_dense_priors_slots_batch(
                 *self._tree_args(tree), tree["child_init_q"], cq, leaf, ls, legal, nl, pri, results, vals, vlp, vll,
-                B, total, self._max_nodes, q_pen)
+                tree["root_node"], None, 1, B, total, self._max_nodes, q_pen)
 
     def _find_immediate_wins(self, states, legal_moves, num_legal, total, *, row_mask=None, slot_mask=None):
         """First winning legal slot per game or -1 (fnn_mcts_orchestrator.py:446-493)."""

@@ -204,17 +204,21 @@ int hv_mcts_expand(const hv_tree* tree, int dense, int backprop, float* child_in
                    const int32_t* vl_len, int8_t* was_expanded, float q_penalty, int B, int total,
                    void* stream);
 
-/* hv_mcts_expand with dense = 1 and backprop = 1 for the simulations of a
- * root-slot select (hv_mcts_select mode 2: total = W * num_candidates * B,
- * simulation s below candidate (s / B) % num_candidates of game s % B; the
- * same root_nodes and root_slots).  The tree it leaves is the one
- * hv_mcts_expand leaves: node allocation in simulation order, root-level
- * backups in simulation order; the candidates' subtrees, which no two
- * candidates share, are updated in parallel.  A game whose candidate table
- * repeats a slot, or a shape outside num_candidates <= 32 and
- * total / B <= 1024, runs hv_mcts_expand's kernel.  No reference
- * counterpart as a separate call: the reference's Gumbel wave calls
- * mcts_expand_and_backprop_dense_priors_batch (bindings.cpp:200-219). */
+/* hv_mcts_expand with dense = 1 and backprop = 1, for the simulations of
+ * one hv_mcts_select call with the same root_nodes:
+ *   root_slots != NULL: a root-slot select (mode 2, the same root_slots;
+ *     total = W * num_candidates * B, simulation s below candidate
+ *     (s / B) % num_candidates of game s % B);
+ *   root_slots == NULL: a plain or root-mask select (modes 0, 1: each
+ *     simulation's virtual-loss path starts at its root child).
+ * The tree it leaves is the one hv_mcts_expand leaves: node allocation in
+ * simulation order, root-level backups in simulation order; the subtrees
+ * below different candidates / root children, which no two groups share,
+ * are updated in parallel.  A game whose candidate table repeats a slot, or
+ * a shape outside num_candidates <= 32 and total / B <= 1024, runs
+ * hv_mcts_expand's kernel.  No reference counterpart as a separate call:
+ * the reference's waves call mcts_expand_and_backprop_dense_priors_batch
+ * (bindings.cpp:200-219). */
 int hv_mcts_expand_slots(const hv_tree* tree, float* child_init_q, const float* child_q, const int32_t* leaf,
                          const uint8_t* leaf_states, const uint8_t* legal_moves, const int32_t* num_legal,
                          const float* priors, const int32_t* results, const float* values,

@@ -41,7 +41,7 @@ def _priors(rng, nl):
 
 def run_waves(backend, states: np.ndarray, waves: int, W: int, mode: int, seed: int, C: int = 4,
               max_nodes: int = 4096, det: bool = False, q_penalty: float = 0.0, c_puct: float = 1.25,
-              repeat_slots: bool = False):
+              repeat_slots: bool = False, grouped: bool = True):
     orc = O.oracle()
     B = states.shape[0]
     rng = np.random.default_rng(seed)
@@ -77,6 +77,6 @@ def run_waves(backend, states: np.ndarray, waves: int, W: int, mode: int, seed: 
         vals = rng.uniform(-1, 1, len(leaf)).astype(np.float32)
         backend.expand_dense(tree, cq, leaf, ls, lmv, lnl, _priors(rng, lnl), lres, vals, vlp, vll,
                              q_penalty=q_penalty if det and W > 1 else 0.0, with_backprop=True,
-                             slots=(roots, kw["root_slots"], C) if mode == 2 else None)
+                             slots=(roots, kw["root_slots"] if mode == 2 else None, C) if grouped else None)
         log.append((leaf.copy(), plen.copy(), vll.copy()))
     return tree, log

@@ -2,10 +2,12 @@
 against the sequential oracle: after several select / replay / expand+backup
 waves the whole tree (visit counts, value sums as raw float bits, priors,
 parents, moves, actions, children, terminal flags, node counts, child Q)
-must be bit-identical, for every select mode and wave width.  Root-slot
-waves (mode 2) run the candidate-parallel select and expansion; their random
-candidate tables repeat a slot in some games, which takes the per-game
-order, so both forms are compared with the oracle."""
+must be bit-identical, for every select mode and wave width.  The waves run
+the parallel select and expansion forms (one warp per root candidate in
+root-slot waves, the root steps first and then the root children's
+subtrees in parallel in plain and root-mask waves); root-slot tables that
+repeat a slot take the per-game order, so both forms are compared with the
+oracle."""
 import numpy as np
 import pytest
 import torch
@@ -71,11 +73,11 @@ class GpuBackend:
                 self._t(priors), self._t(results))
         was = None
         if with_backprop and slots is not None:
-            # root-slot waves: the candidate-parallel expansion (hv_mcts_expand_slots)
+            # the grouped expansion (hv_mcts_expand_slots): by candidate, or by root child
             roots, root_slots, C = slots
             self.ext.mcts_expand_and_backprop_dense_priors_slots_batch(
                 *ts, ciq, *args, self._t(values), self._t(vl_paths), self._t(vl_len), self._t(roots),
-                self._t(root_slots), C, B, total, M, q_penalty)
+                None if root_slots is None else self._t(root_slots), C, B, total, M, q_penalty)
         elif with_backprop:
             self.ext.mcts_expand_and_backprop_dense_priors_batch(*ts, ciq, *args, self._t(values), self._t(vl_paths),
                                                                  self._t(vl_len), B, total, M, q_penalty)
@@ -92,11 +94,14 @@ def _states(seed, n=32):
                            orc.generate_positions(seed + 1, 0, n - n // 2, 90, 7)])
 
 
+@pytest.mark.parametrize("grouped", [True, False])
 @pytest.mark.parametrize("mode,W", [(0, 1), (0, 4), (1, 1), (1, 4), (2, 1), (2, 4), (2, 16)])
-def test_tree_waves_bit_exact(mode, W):
+def test_tree_waves_bit_exact(mode, W, grouped):
+    # grouped: the waves' expansion + backup through hv_mcts_expand_slots,
+    # else through the per-game hv_mcts_expand
     st = _states(300 + 7 * mode + W)
     a, la = run_waves(OracleBackend("orc"), st, waves=8, W=W, mode=mode, seed=11)
-    b, lb = run_waves(GpuBackend(), st, waves=8, W=W, mode=mode, seed=11)
+    b, lb = run_waves(GpuBackend(), st, waves=8, W=W, mode=mode, seed=11, grouped=grouped)
     for (x1, y1, z1), (x2, y2, z2) in zip(la, lb):
         assert np.array_equal(x1, x2) and np.array_equal(y1, y2) and np.array_equal(z1, z2)
     assert a.equal(b) == []
