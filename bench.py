@@ -281,6 +281,12 @@ class Ranks:
             import torch.distributed as dist
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=self.dev)
             self.dist = dist
+            # the communicator's setup on its first collective, done here and
+            # not in the barrier that opens the first timed region (after a
+            # first collective the next step ran late by several ms)
+            self.barrier()
+            self.gather(0.0)
+            torch.cuda.synchronize(self.dev)
 
     def barrier(self):
         if self.dist is not None:
@@ -309,22 +315,27 @@ class Ranks:
             self.dist.destroy_process_group()
 
 
-def timed_region(ranks: Ranks, fn, steps: int) -> tuple[float, list[float]]:
+def timed_region(ranks: Ranks, fn, steps: int, step_times: list | None = None) -> tuple[float, list[float]]:
     """CUDA-event time (ms) of `steps` calls of fn on the current stream,
     bracketed by a barrier and a synchronize on both sides: (max over ranks,
-    every rank's time)."""
+    every rank's time).  step_times: filled with this rank's time of each
+    step (an event after every step; the region's time is unchanged)."""
     import torch
     stream = torch.cuda.current_stream(ranks.dev)
     ranks.barrier()
     torch.cuda.synchronize(ranks.dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1 if step_times is not None else 2)]
+    ev[0].record(stream)
+    for i in range(steps):
         fn()
-    e1.record(stream)
+        if step_times is not None:
+            ev[i + 1].record(stream)
+    ev[-1].record(stream)
     torch.cuda.synchronize(ranks.dev)
     ranks.barrier()
-    per_rank = ranks.gather(e0.elapsed_time(e1))
+    if step_times is not None:
+        step_times[:] = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    per_rank = ranks.gather(ev[0].elapsed_time(ev[-1]))
     return max(per_rank), per_rank
 
 
@@ -353,8 +364,10 @@ def bench_movegen(args, ranks: Ranks) -> dict:
     time.sleep(0.3)
     for _ in range(args.warmup):
         step()
-    ms_max, per_rank_ms = timed_region(ranks, step, args.steps)
+    own_steps: list = []
+    ms_max, per_rank_ms = timed_region(ranks, step, args.steps, own_steps)
     value = world * P * args.steps / (ms_max / 1e3)
+    rank_steps = ranks.gather_obj(own_steps)
     # ---- the same steps over a region of >= --long-s seconds (every rank the same count) ----
     long_steps = max(args.steps, int(math.ceil(1000.0 * args.long_s / (ms_max / args.steps))))
     long_max, long_per_rank = timed_region(ranks, step, long_steps) if args.long_s > 0 else (None, None)
@@ -499,6 +512,8 @@ def bench_movegen(args, ranks: Ranks) -> dict:
         "cpu_baseline": cpu,
         "clocks": clocks,
         "per_rank": {"ms_per_step": [t / args.steps for t in per_rank_ms],
+                     "first_step_ms": [st[0] for st in rank_steps],
+                     "median_step_ms": [sorted(st)[len(st) // 2] for st in rank_steps],
                      "clocks": [{"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons"),
                                  "samples": c.get("samples")} for c in rank_clocks]},
         "long_run": {"steps": long_steps, "ms_per_step": long_max / long_steps,
