@@ -92,6 +92,8 @@ _SIGNATURES = {
     "hv_generate_legal_moves_and_hybrid_root_features": ([_vp, _i64] + [_vp] * 12, _int),
     "hv_hybrid_trunk_sizes": ([_vp, _vp], _int),
     "hv_hybrid_trunk": ([_vp, _vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _vp], _int),
+    "hv_hybrid_trunk_packed_workspace_bytes": ([_i64, _vp], _int),
+    "hv_hybrid_trunk_packed": ([_vp, _vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _vp, C.c_size_t, _vp], _int),
     "hv_hybrid_head_weights_size": ([_int, _int, _int], _int),
     "hv_hybrid_eval_leaves": ([_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _int, _int, _int, _vp, _int, _vp, _vp,
                                _vp, _vp, _vp], _int),

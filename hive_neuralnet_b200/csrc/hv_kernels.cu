@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
     HybSmem* x = hyb_slot();
     const FnnOffsets fo = fnn_offsets(fd);
     const HybOffsets ho = hyb_offsets(hd);
-    const int E = hd.E, A = hd.A, V = hd.V;
+    const int E = hd.E, A = hd.A;
     const int l = lane_id();
     const int o0 = l, o1 = l + 32;
     const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
@@ -1896,15 +1896,11 @@ int hv_hybrid_trunk_sizes(int* image_elems, int* param_floats) {
     return HV_OK;
 }
 
-int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const int32_t* token_r,
-                    const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
-                    const uint16_t* weight_image, const float* params, float* graph_summary, void* stream) {
-    if (batch < 0) return HV_EINVAL;
-    if (batch == 0) return HV_OK;
-    if (!token_features || !token_q || !token_r || !token_z || !token_mask || !weight_image || !params ||
-        !graph_summary || !aligned16(weight_image) || !aligned16(graph_summary))
-        return HV_EINVAL;
-    if (node_feat_dim < 1 || node_feat_dim > 27) return HV_EINVAL;
+// the trunk over slots (slots NULL: one position per slot)
+static int launch_trunk(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                        const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                        const uint16_t* weight_image, const float* params, float* graph_summary,
+                        const int2* slots, const int* slot_cnt, void* stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HV_ECUDA;
     DeviceInfo& d = g_dev[dev];
@@ -1918,9 +1914,68 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error) != cudaSuccess) return HV_ECUDA;
     k_hybrid_trunk<<<grid, kTrThreads, smem, (cudaStream_t)stream>>>(
-        token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim,
+        token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim, slots, slot_cnt,
         reinterpret_cast<const __half*>(weight_image), params, graph_summary, err);
     return launch_status();
+}
+
+static bool trunk_args_ok(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                          const int32_t* token_z, const uint8_t* token_mask, int node_feat_dim,
+                          const uint16_t* weight_image, const float* params, const float* graph_summary) {
+    return token_features && token_q && token_r && token_z && token_mask && weight_image && params &&
+           graph_summary && aligned16(weight_image) && aligned16(graph_summary) && node_feat_dim >= 1 &&
+           node_feat_dim <= 27;
+}
+
+int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                    const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                    const uint16_t* weight_image, const float* params, float* graph_summary, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!trunk_args_ok(token_features, token_q, token_r, token_z, token_mask, node_feat_dim, weight_image, params,
+                       graph_summary))
+        return HV_EINVAL;
+    return launch_trunk(token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim, weight_image,
+                        params, graph_summary, nullptr, nullptr, stream);
+}
+
+int hv_hybrid_trunk_packed_workspace_bytes(int64_t batch, size_t* bytes) {
+    if (batch < 0 || !bytes) return HV_EINVAL;
+    *bytes = 16 + 8 * (size_t)batch;
+    return HV_OK;
+}
+
+// the slot table, then the trunk over it (workspace: two counters, then the table)
+static int trunk_packed(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                        const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                        const uint16_t* weight_image, const float* params, float* graph_summary, void* ws,
+                        void* stream) {
+    cudaStream_t s = (cudaStream_t)stream;
+    int* cnt = static_cast<int*>(ws);
+    int2* slots = reinterpret_cast<int2*>(static_cast<uint8_t*>(ws) + 16);
+    if (cudaMemsetAsync(cnt, 0, 16, s) != cudaSuccess ||
+        cudaMemsetAsync(slots, 0xFF, 8 * (size_t)batch, s) != cudaSuccess)
+        return HV_ECUDA;
+    k_trunk_classify<<<(unsigned)((batch + 255) / 256), 256, 0, s>>>(token_mask, batch, slots, cnt);
+    const int rc = launch_status();
+    if (rc) return rc;
+    return launch_trunk(token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim, weight_image,
+                        params, graph_summary, slots, cnt, stream);
+}
+
+int hv_hybrid_trunk_packed(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                           const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                           const uint16_t* weight_image, const float* params, float* graph_summary, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    if (batch < 0) return HV_EINVAL;
+    if (batch == 0) return HV_OK;
+    if (!trunk_args_ok(token_features, token_q, token_r, token_z, token_mask, node_feat_dim, weight_image, params,
+                       graph_summary) ||
+        !workspace || (reinterpret_cast<uintptr_t>(workspace) & 15) || workspace_bytes < 16 + 8 * (size_t)batch ||
+        batch > INT32_MAX)
+        return HV_EINVAL;
+    return trunk_packed(token_features, token_q, token_r, token_z, token_mask, batch, node_feat_dim, weight_image,
+                        params, graph_summary, workspace, stream);
 }
 
 // workspace of hv_hybrid_evaluate: per position tokens, coordinates, mask,
@@ -2087,7 +2142,7 @@ static size_t row_workspace_layout(int64_t count, int64_t rows, bool hybrid, boo
 int hv_leaf_rows_workspace_bytes(int64_t count, int64_t rows, int hybrid, size_t* bytes) {
     if (count < 0 || rows < 0 || !bytes) return HV_EINVAL;
     *bytes = row_workspace_layout(count, rows, hybrid != 0, true, nullptr, nullptr);
-    if (hybrid) *bytes += hybrid_workspace_layout(count, nullptr, nullptr);
+    if (hybrid) *bytes += hybrid_workspace_layout(count, nullptr, nullptr) + align256(16 + 8 * (size_t)count);
     return HV_OK;
 }
 
@@ -2126,19 +2181,24 @@ int hv_hybrid_evaluate_rows(const uint8_t* states, const uint8_t* legal_moves, c
         (reinterpret_cast<uintptr_t>(workspace) & 255))
         return HV_EINVAL;
     if (hidden < 1 || hidden > kFnnMaxDim || embed < 1 || embed > kFnnMaxDim || action_hidden < 1 ||
-        action_hidden > kFnnMaxDim || value_hidden < 1 || value_hidden > kHybMaxValue)
+        action_hidden > kFnnMaxDim || value_hidden < 1 || value_hidden > kHybMaxValue || count > INT32_MAX ||
+        !trunk_image || !trunk_params || !aligned16(trunk_image) || node_feat_dim < 1 || node_feat_dim > 27)
         return HV_EINVAL;
+    // tokens and summary, then the row arrays, then the trunk's slot table
     const size_t tok_bytes = hybrid_workspace_layout(count, nullptr, nullptr);
-    if (workspace_bytes < tok_bytes + row_workspace_layout(count, rows, true, logits == nullptr, nullptr, nullptr))
-        return HV_EINVAL;
+    const size_t slot_at =
+        tok_bytes + row_workspace_layout(count, rows, true, logits == nullptr, nullptr, nullptr);
+    if (workspace_bytes < slot_at + 16 + 8 * (size_t)count) return HV_EINVAL;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
     HybridWorkspace hw;
-    hybrid_workspace_layout(count, static_cast<uint8_t*>(workspace), &hw);
+    hybrid_workspace_layout(count, ws, &hw);
     RowWorkspace w;
-    row_workspace_layout(count, rows, true, logits == nullptr, static_cast<uint8_t*>(workspace) + tok_bytes, &w);
+    row_workspace_layout(count, rows, true, logits == nullptr, ws + tok_bytes, &w);
     int rc = hv_hybrid_encode(states, count, hw.tf, hw.tq, hw.tr, hw.tz, hw.tm, hw.gf, hw.ntok, stream);
     if (rc) return rc;
-    rc = hv_hybrid_trunk(hw.tf, hw.tq, hw.tr, hw.tz, hw.tm, count, node_feat_dim, trunk_image, trunk_params, hw.graph,
-                         stream);
+    // early-game leaves have few tokens: the packed trunk pairs them two to a slot
+    rc = trunk_packed(hw.tf, hw.tq, hw.tr, hw.tz, hw.tm, count, node_feat_dim, trunk_image, trunk_params, hw.graph,
+                      ws + slot_at, stream);
     if (rc) return rc;
     return run_row_pipeline<true>(states, legal_moves, num_legal, root_features, hw.graph, hw.gf, count, rows,
                                   fnn_weights, FnnDims{hidden, embed, action_hidden}, head_weights,

@@ -381,7 +381,7 @@ __device__ __forceinline__ void attention_heads(TrunkSmem* s, int base, int h0, 
                 rinv[mt][hh] = sum > 0.0f ? 1.0f / sum : 0.0f;
             }
         // O = P V_h (the keys in k16 steps), normalised, into the A slab of head h
-        const __half* vt = s->vt[base >> 5] + (8 * h + g) * kTrVtStride + 2 * c;
+        const __half* vt = s->vt[base >> 5] + (8 * h + g) * kTrVtStride + 2 * c + (base & 31);
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
             float o[4] = {0.f, 0.f, 0.f, 0.f};
@@ -438,17 +438,69 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
     return make_float2(x.x * (x.x >= 0.0f ? 1.0f - h.x : h.x), x.y * (x.y >= 0.0f ? 1.0f - h.y : h.y));
 }
 
-// The token features of a pass's 8 positions (b0 ..) into shared memory,
-// [8][28][27] floats, by asynchronous 4-byte copies (no alignment asked of
-// the caller's array); positions past the batch are left alone (not read).
-__device__ __forceinline__ void stage_tokens(float* dst, const float* __restrict__ tf, int64_t b0, int64_t batch) {
-    constexpr int kPer = 28 * 27;
-    const int64_t nb = batch - b0 < kTrPos ? batch - b0 : kTrPos;
+// A slot is 32 rows of a tile: one position (CLS, 28 tokens, 3 padding
+// rows), or, packed, two positions whose valid tokens all lie in their first
+// 15 token slots (16 rows each: CLS and 15 tokens).  Packed, slot si is table
+// entry si for si < nbig (one position: (p, -1)) and entry
+// batch - npair + (si - nbig) after them (a pair (p, q), or (p, -1) for a
+// lone one); unpacked, slot si is position si.
+constexpr int kSlotTok = 30;  // staged token rows per slot (28, or 15 + 15)
+struct SlotMap {
+    const int2* table;  // NULL: unpacked
+    int64_t nbig, npair, batch;
+    __device__ __forceinline__ int64_t count() const { return table ? nbig + npair : batch; }
+    __device__ __forceinline__ int2 at(int64_t si) const {
+        if (!table) return make_int2((int)si, -1);
+        return table[si < nbig ? si : batch - npair + (si - nbig)];
+    }
+};
+
+// The token features of a pass's 8 slots (slot s0 ..) into shared memory,
+// [8][30][27] floats, by asynchronous 4-byte copies (no alignment asked of
+// the caller's array); slots past the table are left alone (not read).
+__device__ __forceinline__ void stage_tokens(float* dst, const float* __restrict__ tf, const SlotMap& sm,
+                                             int64_t s0) {
+    constexpr int kPer = 28 * 27, kSlot = kSlotTok * 27;
+    const int64_t nslots = sm.count();
     const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-    for (int i = threadIdx.x; i < nb * kPer; i += kTrThreads)
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d + 4u * (uint32_t)i), "l"(tf + b0 * kPer + i)
-                     : "memory");
+    for (int i = threadIdx.x; i < kTrPos * kSlot; i += kTrThreads) {
+        const int k = i / kSlot, r = i - k * kSlot;
+        if (s0 + k >= nslots) break;  // (k grows with i)
+        const int2 sp = sm.at(s0 + k);
+        int64_t src = -1;
+        if (sp.y < 0) {
+            if (r < kPer) src = (int64_t)sp.x * kPer + r;
+        } else {
+            const int h = r >= 15 * 27, rr = r - h * 15 * 27;
+            src = (int64_t)(h ? sp.y : sp.x) * kPer + rr;
+        }
+        if (src >= 0)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d + 4u * (uint32_t)i), "l"(tf + src)
+                         : "memory");
+    }
     asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// The slot table, a thread per position: a position with no valid token
+// past its first 15 is "small" and takes half of a pair entry (filled from
+// the table's end), the others take single entries from its start; cnt =
+// (singles, smalls) and the entries' second halves start at -1 (the host
+// clears both).  The order of the entries depends on the atomics' order; a
+// position's result does not depend on its slot (rows are independent in
+// every GEMM and LayerNorm, and a position attends within its own rows).
+__global__ void k_trunk_classify(const uint8_t* __restrict__ tm, int64_t batch, int2* __restrict__ table,
+                                 int* __restrict__ cnt) {
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= batch) return;
+    bool any = false;
+#pragma unroll
+    for (int k = 15; k < 28; k++) any |= tm[p * 28 + k] != 0;
+    if (any) {
+        table[atomicAdd(&cnt[0], 1)] = make_int2((int)p, -1);
+    } else {
+        const int k = atomicAdd(&cnt[1], 1);
+        reinterpret_cast<int*>(table + (batch - 1 - k / 2))[k & 1] = (int)p;
+    }
 }
 
 // token_features [B,28,27] (first `nfeat` used), token_q/r/z [B,28], token_mask [B,28] (0/1),
@@ -456,6 +508,8 @@ __device__ __forceinline__ void stage_tokens(float* dst, const float* __restrict
 __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __restrict__ tf, const int32_t* __restrict__ tq,
                                                          const int32_t* __restrict__ tr, const int32_t* __restrict__ tz,
                                                          const uint8_t* __restrict__ tm, int64_t batch, int nfeat,
+                                                         const int2* __restrict__ slots,
+                                                         const int* __restrict__ slot_cnt,
                                                          const __half* __restrict__ img,
                                                          const float* __restrict__ par, float* __restrict__ out,
                                                          uint32_t* err_word) {
@@ -468,7 +522,15 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
     const int row = base + l;           // this thread's row (0 .. 255)
     const int lnbar = 1 + 4 * u + q;    // named barrier of the row pair's two warps
     const int hc = 32 * hf;             // first hidden column of this half
-    const int64_t npass = (batch + kTrPos - 1) / kTrPos;  // 8 positions per pass
+    // the slots (slots NULL: one position each); packed only when at least a
+    // quarter of the batch is small (pairs then save an eighth of the slots)
+    SlotMap sm{nullptr, 0, 0, batch};
+    if (slots) {
+        const int nsmall = slot_cnt[1];
+        if (4 * (int64_t)nsmall >= batch) sm = SlotMap{slots, slot_cnt[0], (nsmall + 1) / 2, batch};
+    }
+    const int64_t nslots = sm.count();
+    const int64_t npass = (nslots + kTrPos - 1) / kTrPos;  // 8 slots per pass
 
     if (t == 0) {
         mbar_init(&s->bar_w, 1);
@@ -500,16 +562,21 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
     }
     // token features of each pass staged in the key buffer (free outside the attention)
     float* stf = reinterpret_cast<float*>(s->k);
-    static_assert(sizeof(TrunkSmem::k) >= kTrPos * 28 * 27 * sizeof(float), "token staging");
-    if (blockIdx.x < npass) stage_tokens(stf, tf, (int64_t)blockIdx.x * kTrPos, batch);
+    static_assert(sizeof(TrunkSmem::k) >= kTrPos * kSlotTok * 27 * sizeof(float), "token staging");
+    if (blockIdx.x < npass) stage_tokens(stf, tf, sm, (int64_t)blockIdx.x * kTrPos);
 
     for (int64_t pass = blockIdx.x; pass < npass && !failed; pass += gridDim.x) {
-        const int64_t b = pass * kTrPos + (base >> 5);
-        const bool live = b < batch;
-        // ---- inputs of this row: token features (rows 1..28), CLS (row 0), padding (29..31)
-        const int tok = l - 1;
-        const bool is_tok = live && tok >= 0 && tok < 28;
-        const bool valid = (live && l == 0) || (is_tok && tm[b * 28 + tok] != 0);
+        const int64_t si = pass * kTrPos + (base >> 5);
+        const int2 sp = si < nslots ? sm.at(si) : make_int2(-1, -1);
+        const bool paired = sp.y >= 0;         // two 16-row positions in this slot
+        const int half = paired ? l >> 4 : 0;  // which of them this row belongs to
+        const int64_t b = half ? sp.y : sp.x;
+        const bool live = b >= 0;
+        // ---- inputs of this row: token features (rows 1..), CLS (row 0 of the position), padding
+        const int tok = (paired ? (l & 15) : l) - 1;
+        const bool cls = live && tok < 0;
+        const bool is_tok = live && tok >= 0 && tok < (paired ? 15 : 28);
+        const bool valid = cls || (is_tok && tm[b * 28 + tok] != 0);
         if (hf == 0) {
             s->cq[row] = is_tok ? tq[b * 28 + tok] : 0;
             s->cr[row] = is_tok ? tr[b * 28 + tok] : 0;
@@ -521,7 +588,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
         {
             // this half's 16 of the 32 (zero-padded) input columns
             float f[kTrKin / 2];
-            const float* src = stf + ((base >> 5) * 28 + tok) * 27;
+            const float* src = stf + ((base >> 5) * kSlotTok + half * 15 + tok) * 27;
 #pragma unroll
             for (int i = 0; i < kTrKin / 2; i++) {
                 const int j = kTrKin / 2 * hf + i;
@@ -543,7 +610,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             for (int i = 0; i < 32; i++) {
                 const int j = hc + i;
                 // CLS row: the learned token; pieces: projection times mask; padding: 0
-                x[i] = (l == 0) ? __ldg(par + kParCls + j) : ((is_tok && valid) ? d[i] + __ldg(par + kParTpB + j) : 0.0f);
+                x[i] = cls ? __ldg(par + kParCls + j) : ((is_tok && valid) ? d[i] + __ldg(par + kParTpB + j) : 0.0f);
             }
         }
 
@@ -603,7 +670,12 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             // free until the next block's QKV GEMM) while the attention runs
             tmem_st32(lane_taddr(s, hc), x);
             __syncwarp();
-            attention_warp(s, base, 4 * hf, l, kmask);
+            if (paired) {  // each position of the slot attends within its own 16 rows
+                attention_warp(s, base, 4 * hf, l, kmask & 0xffffu);
+                attention_warp(s, base + 16, 4 * hf, l, kmask >> 16);
+            } else {
+                attention_warp(s, base, 4 * hf, l, kmask);
+            }
             mpend = true;
             if (!trunk_gemm(s, 192, W + kImgQkv, kTrH, kTrH, mphase)) {
                 failed = true;
@@ -613,7 +685,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             // every warp's attention is done with the key buffer: stage the
             // token features of this CTA's next pass there
             if (layer == kTrLayers - 1 && pass + gridDim.x < npass)
-                stage_tokens(stf, tf, (pass + gridDim.x) * kTrPos, batch);
+                stage_tokens(stf, tf, sm, (pass + gridDim.x) * kTrPos);
             {
                 float d[32];
                 tmem_ld32(lane_taddr(s, hc), x);
@@ -658,7 +730,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
             }
             {
                 float d[32];
-                const float keep = (l == 0) ? 1.0f : (valid ? 1.0f : 0.0f);
+                const float keep = valid ? 1.0f : 0.0f;
                 tmem_ld32(lane_taddr(s, 192 + hc), d);
 #pragma unroll
                 for (int i = 0; i < 32; i += 2)
@@ -672,7 +744,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) k_hybrid_trunk(const float* __r
         {
             float y[kTrH / 2];
             layer_norm_half(s, row, hf, lnbar, x, par + kParFnG + hc, par + kParFnB + hc, y);
-            if (live && l == 0) {
+            if (cls) {
                 float4* o4 = reinterpret_cast<float4*>(out + b * kTrH + hc);
 #pragma unroll
                 for (int i = 0; i < 8; i++) o4[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);

@@ -304,7 +304,10 @@ class HybridTrunk:
             raise ValueError(f"packed ({self.image.numel()}, {self.params.numel()}), kernel expects "
                              f"({ie.value}, {pf.value})")
 
-    def __call__(self, pb: HybridPieceTensorBatch) -> torch.Tensor:
+    def __call__(self, pb: HybridPieceTensorBatch, packed: bool = False) -> torch.Tensor:
+        """packed: positions with at most 15 token slots in use share the
+        kernel's 32-row slots in pairs (hv_hybrid_trunk_packed); the same output."""
+        import ctypes
         tf = pb.token_features
         B = tf.shape[0]
         out = torch.empty((B, TRUNK_HIDDEN), dtype=torch.float32, device=tf.device)
@@ -314,11 +317,21 @@ class HybridTrunk:
             raise ValueError("token_features: expected float32 [B, 28, 27] (the encoder's full rows)")
         tq, tr, tz = (t.to(torch.int32).contiguous() for t in (pb.token_q, pb.token_r, pb.token_z))
         tm = pb.token_mask.to(torch.uint8).contiguous()
+        tf = tf.contiguous()
+        stream = torch.cuda.current_stream(tf.device).cuda_stream
+        args = (tf.data_ptr(), tq.data_ptr(), tr.data_ptr(), tz.data_ptr(), tm.data_ptr(), B,
+                self.net.config.node_feat_dim, self.image.data_ptr(), self.params.data_ptr(), out.data_ptr())
         with torch.cuda.device(tf.device):
-            _lib.check(self.lib.hv_hybrid_trunk(
-                tf.contiguous().data_ptr(), tq.data_ptr(), tr.data_ptr(), tz.data_ptr(), tm.data_ptr(), B,
-                self.net.config.node_feat_dim, self.image.data_ptr(), self.params.data_ptr(), out.data_ptr(),
-                torch.cuda.current_stream(tf.device).cuda_stream), "hybrid_trunk")
+            if packed:
+                need = ctypes.c_size_t(0)
+                _lib.check(self.lib.hv_hybrid_trunk_packed_workspace_bytes(B, ctypes.addressof(need)), "trunk ws")
+                ws = getattr(self, "_slot_ws", None)
+                if ws is None or ws.device != tf.device or ws.numel() < need.value:
+                    ws = self._slot_ws = torch.empty((int(need.value),), dtype=torch.uint8, device=tf.device)
+                _lib.check(self.lib.hv_hybrid_trunk_packed(*args, ws.data_ptr(), ws.numel(), stream),
+                           "hybrid_trunk_packed")
+            else:
+                _lib.check(self.lib.hv_hybrid_trunk(*args, stream), "hybrid_trunk")
         return out
 
 

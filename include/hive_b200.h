@@ -297,6 +297,22 @@ int hv_hybrid_trunk(const float* token_features, const int32_t* token_q, const i
                     const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
                     const uint16_t* weight_image, const float* params, float* graph_summary, void* stream);
 
+/* hv_hybrid_trunk with the positions packed: two positions whose valid
+ * tokens all lie in their first 15 token slots share one 32-row slot of the
+ * kernel's tiles (16 rows each), so a batch of early-game positions takes
+ * fewer rows; when fewer than a quarter of the batch qualify, one position
+ * per slot as in hv_hybrid_trunk.  The same graph_summary bit for bit (rows
+ * are independent in every GEMM and LayerNorm, and a position attends
+ * within its own rows).
+ * workspace: 16-byte aligned, at least
+ * hv_hybrid_trunk_packed_workspace_bytes(batch) bytes (the slot table,
+ * built on the device); batch <= 2^31 - 1.  No reference counterpart. */
+int hv_hybrid_trunk_packed_workspace_bytes(int64_t batch, size_t* bytes);
+int hv_hybrid_trunk_packed(const float* token_features, const int32_t* token_q, const int32_t* token_r,
+                           const int32_t* token_z, const uint8_t* token_mask, int64_t batch, int node_feat_dim,
+                           const uint16_t* weight_image, const float* params, float* graph_summary, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Hybrid leaf evaluation: HybridMCTSOrchestrator._eval_states
  * (hive_fnn_transformer/fnn_transformer_mcts_orchestrator.py:42-169) given
  * the trunk's graph_summary [count, 64] and the encoder's global_features
@@ -356,7 +372,8 @@ int hv_hybrid_evaluate_noalloc(const uint8_t* states, const uint8_t* legal_moves
  * successors of all `count` leaves are compacted into `rows` rows
  * (rows = sum over leaves of min(max(num_legal, 0), 256)), their features
  * written to the workspace, the network run as a tiled fp32 GEMM pipeline
- * over rows, the per-leaf parts and the softmax by warp-per-leaf kernels.
+ * over rows, the per-leaf parts and the softmax by warp-per-leaf kernels
+ * (the hybrid trunk runs packed, as hv_hybrid_trunk_packed).
  * Same outputs as hv_fnn_eval_leaves / hv_hybrid_evaluate (fp32, a
  * different summation order).  workspace: 256-byte aligned, at least
  * hv_leaf_rows_workspace_bytes(count, rows, hybrid) bytes; with logits ==

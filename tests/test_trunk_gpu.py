@@ -63,3 +63,29 @@ def test_trunk_matches_reference_module_outputs():
     assert np.array_equal(pb.token_features.cpu().numpy(), g["token_features"])
     got = HybridTrunk(net)(pb).cpu().numpy()
     np.testing.assert_allclose(got, g["default/graph_summary"], atol=TOL, rtol=TOL)
+
+
+@pytest.mark.parametrize("n", [1, 3, 37, 601])
+def test_packed_trunk_equals_unpacked(n):
+    # positions with at most 15 token slots in use share a 32-row slot in
+    # pairs: the output is the one-position-per-slot output bit for bit,
+    # for batches with an odd number of small positions and ragged passes
+    from hive_neuralnet_b200.hive_gpu import load_extension
+    from hive_neuralnet_b200.hybrid import HiveHybridGNN, HybridTrunk
+    ext = load_extension()
+    torch.manual_seed(5)
+    net = HiveHybridGNN().eval()
+    with torch.no_grad():
+        net.graph_trunk.cls_token.normal_(0, 0.5)
+    orc = O.oracle()
+    st = np.concatenate([orc.generate_positions(81, 0, n, 12, 0), orc.generate_positions(82, 0, n, 150, 7)])
+    rng = np.random.default_rng(n)
+    st = st[rng.permutation(len(st))][:max(n, 2)]
+    pb = _batch(ext, st)
+    small = int((pb.token_mask[:, 15:].sum(1) == 0).sum().item())
+    trunk = HybridTrunk(net)
+    a = trunk(pb, packed=True)
+    b = trunk(pb, packed=False)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32)), f"{small} small of {len(st)}"
+    assert ext.device_error_word(clear=True) == 0
