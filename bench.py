@@ -395,7 +395,17 @@ def bench_movegen(args, ranks: Ranks) -> dict:
     e2e_value = world * P * e2e_steps / (e2e_ms / 1e3)
     h2d = staged_upload_bytes(states)
     n_tall = int((states[:, 2645:2645 + 529].amax(1) >= 3).sum().item())
-    d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
+    # bytes that crossed the link: with the pinned buffers each row's first
+    # HOST_MOVE_PREFIX moves (pitched copy) and, for longer lists, the moves
+    # past them in 16-byte stores; the rest of each row is cleared on the host
+    from hive_neuralnet_b200.hive_gpu import HOST_MOVE_PREFIX
+    nl64 = h_nl.to(torch.int64).clamp(0, MAX_MOVES)
+    tail = torch.where(nl64 > HOST_MOVE_PREFIX, (nl64 * MOVE_BYTES + 15) // 16 * 16 - HOST_MOVE_PREFIX * MOVE_BYTES,
+                       torch.zeros_like(nl64))
+    d2h = P * (HOST_MOVE_PREFIX * MOVE_BYTES + 4 + FEAT * 4) + int(tail.sum())
+    # the host results equal the device-resident step's (same positions)
+    host_equal = (torch.equal(h_nl, out[1].cpu()) and torch.equal(h_moves, out[0].cpu())
+                  and torch.equal(h_feat.view(torch.int32), out[2].cpu().view(torch.int32)))
 
     # ---- the host link the e2e leg runs against: plain pinned copies of the
     # step's state bytes, each direction alone, CUDA events on this stream
@@ -506,7 +516,10 @@ def bench_movegen(args, ranks: Ranks) -> dict:
                 "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
                         f"staged upload (hv_stage_host_states: stack levels over occupied rows; "
                         f"{n_tall} states with a 3-high stack), "
-                        f"{args.e2e_chunk}-position chunks over 3 streams",
+                        f"{args.e2e_chunk}-position chunks over 3 streams; moves: the first "
+                        f"{HOST_MOVE_PREFIX} of each row by a pitched copy, longer lists' rest stored into "
+                        f"the mapped rows, the row tails cleared by the calling thread (hv_download_moves)",
+                "host_results_equal_device": host_equal,
                 "link": link},
         "roofline": roofline,
         "cpu_baseline": cpu,

@@ -80,6 +80,7 @@ _SIGNATURES = {
     "hv_generate_legal_moves_and_fnn_features": ([_vp, _i64, _vp, _vp, _vp, _vp], _int),
     "hv_extract_fnn_features": ([_vp, _vp, _vp, _i64, _vp, _vp], _int),
     "hv_stage_host_states": ([_vp, _i64, _vp, _vp], _int),
+    "hv_download_moves": ([_vp, _vp, _i64, _vp, _int, _vp], _int),
     "hv_generate_legal_moves_linked": ([_vp, _i64, _vp, _vp, _vp, _vp], _int),
     "hv_fnn_features_linked": ([_vp, _vp, _vp, _i64, _vp, _vp], _int),
     "hv_fnn_successor_features": ([_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp], _int),

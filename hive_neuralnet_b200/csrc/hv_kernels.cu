@@ -1695,6 +1695,25 @@ __global__ void __launch_bounds__(kThreads) k_stage_levels(const uint8_t* __rest
     }
 }
 
+// The moves of a chunk past its first `prefix` (a multiple of 8) of each
+// position, written into mapped host memory: warp per position, 16-byte
+// stores over bytes 6*prefix up to 6*n rounded up to 16 (the device rows are
+// zero past n, so the rounding writes zeros over the host's zeroed tail).
+__global__ void __launch_bounds__(kThreads) k_download_tail(const uint8_t* __restrict__ dev,
+                                                            const int32_t* __restrict__ num_legal, int64_t count,
+                                                            uint8_t* __restrict__ host, int prefix) {
+    const int l = lane_id();
+    const int64_t nwarps = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); p < count; p += nwarps) {
+        const int n = min(max(num_legal[p], 0), kMaxMoves);
+        if (n <= prefix) continue;
+        const int w0 = (prefix * kMoveBytes) >> 4, w1 = (n * kMoveBytes + 15) >> 4;
+        const uint4* src = reinterpret_cast<const uint4*>(dev + p * (kMaxMoves * kMoveBytes));
+        uint4* dst = reinterpret_cast<uint4*>(host + p * (kMaxMoves * kMoveBytes));
+        for (int i = w0 + l; i < w1; i += 32) dst[i] = src[i];
+    }
+}
+
 }  // namespace hv
 
 using namespace hv;
@@ -1816,6 +1835,36 @@ int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev
     int rc = grid_for(k_stage_levels, count, 0, &grid);
     if (rc) return rc;
     k_stage_levels<<<grid, kThreads, 0, s>>>(static_cast<const uint8_t*>(mapped), count, dev_states);
+    return launch_status();
+}
+
+int hv_download_moves(const uint8_t* dev_moves, const int32_t* dev_num_legal, int64_t count, uint8_t* host_moves,
+                      int prefix, void* stream) {
+    if (count < 0 || prefix < 0 || prefix > kMaxMoves || (prefix & 7)) return HV_EINVAL;
+    if (count == 0) return HV_OK;
+    if (!dev_moves || !dev_num_legal || !host_moves) return HV_EINVAL;
+    cudaStream_t s = (cudaStream_t)stream;
+    constexpr size_t kRow = (size_t)kMaxMoves * kMoveBytes;
+    cudaPointerAttributes attr;
+    uint8_t* mapped = nullptr;
+    if (prefix < kMaxMoves && aligned16(dev_moves) && aligned16(host_moves)) {
+        if (cudaPointerGetAttributes(&attr, host_moves) == cudaSuccess && attr.type == cudaMemoryTypeHost)
+            mapped = static_cast<uint8_t*>(attr.devicePointer);
+        else
+            cudaGetLastError();  // a pageable pointer is not an error here
+    }
+    if (!mapped) {
+        if (cudaMemcpyAsync(host_moves, dev_moves, (size_t)count * kRow, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+            return HV_ECUDA;
+        return HV_OK;
+    }
+    if (prefix > 0 && cudaMemcpy2DAsync(host_moves, kRow, dev_moves, kRow, (size_t)prefix * kMoveBytes, (size_t)count,
+                                         cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return HV_ECUDA;
+    int grid = 0;
+    int rc = grid_for(k_download_tail, count, 0, &grid);
+    if (rc) return rc;
+    k_download_tail<<<grid, kThreads, 0, s>>>(dev_moves, dev_num_legal, count, mapped, prefix);
     return launch_status();
 }
 

@@ -27,6 +27,10 @@ MAX_STACK = 5
 SIZEOF_HIVE_STATE = 3424
 # device staging slots (and streams) of the chunked host-buffer pipeline
 HOST_PIPELINE_STAGES = 3
+# moves per position that the host-buffer pipeline sends over the host link
+# as one pitched copy; the rest of each 256-move row is cleared on the host
+# and the moves past this prefix are stored into the mapped host rows
+HOST_MOVE_PREFIX = 64
 SIZEOF_GPU_MOVE = 6
 OFF_TURN = 3412
 OFF_QUEEN_PLACED = 3414
@@ -140,7 +144,8 @@ class HiveGPUExtension:
 
     def generate_legal_moves_and_fnn_features_host(self, states: torch.Tensor, batch_size: int,
                                                    out: tuple | None = None, chunk: int = 16384,
-                                                   device: torch.device | None = None):
+                                                   device: torch.device | None = None,
+                                                   move_prefix: int = HOST_MOVE_PREFIX):
         """Host-buffer form of :meth:`generate_legal_moves_and_fnn_features_batch`.
 
         ``states`` is a CPU uint8 ``[>=batch_size, 3424]`` tensor (pinned for
@@ -149,8 +154,14 @@ class HiveGPUExtension:
         caller's ``out`` triple.  The batch is cut into chunks that cycle
         through three streams and three device staging slots, so the
         host-to-device copy of one chunk, the kernel of the next and the
-        device-to-host copy of a third overlap.  Returns after queuing; the
-        caller's current stream is ordered after every chunk, so
+        device-to-host copy of a third overlap.  With pinned ``moves``, only
+        the first ``move_prefix`` moves of each row cross the host link in
+        one pitched copy, plus the moves of longer lists past it (stored
+        into the mapped rows by a kernel); the calling thread clears the rest
+        of each row in host memory meanwhile, so the zero padding (about
+        half of the bytes returned) never crosses the link
+        (``hv_download_moves``).  Returns after queuing; the caller's current
+        stream is ordered after every chunk, so
         ``torch.cuda.current_stream().synchronize()`` makes the outputs valid.
         """
         if not isinstance(states, torch.Tensor) or states.is_cuda or states.dtype != torch.uint8:
@@ -161,6 +172,8 @@ class HiveGPUExtension:
             raise ValueError("states: expected a contiguous tensor")
         if chunk <= 0:
             raise ValueError("chunk must be positive")
+        if not 0 <= move_prefix <= MAX_LEGAL_MOVES or move_prefix % 8:
+            raise ValueError("move_prefix: a multiple of 8 in 0..256")
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         if out is None:
             pin = states.is_pinned()
@@ -175,6 +188,9 @@ class HiveGPUExtension:
                     or not t.is_contiguous():
                 raise ValueError(f"out {nm}: expected a contiguous CPU {dt} tensor [>= {batch_size}, {tail}]")
         chunk = min(chunk, max(batch_size, 1))
+        # rows cleared on the host take the prefix download (hv_download_moves
+        # falls back to one full copy for pageable memory or a misaligned row)
+        split = move_prefix < MAX_LEGAL_MOVES and h_moves.is_pinned() and h_moves.data_ptr() % 16 == 0
         slots, streams = self._staging(dev, chunk)
         cur = torch.cuda.current_stream(dev)
         ready = cur.record_event()
@@ -194,7 +210,16 @@ class HiveGPUExtension:
                     _lib.check(self._lib.hv_generate_legal_moves_and_fnn_features(
                         _ptr(d_st), n, _ptr(d_mv), _ptr(d_nl), _ptr(d_ft), s.cuda_stream),
                         "generate_legal_moves_and_fnn_features_host")
-                    h_moves[lo:lo + n].copy_(d_mv[:n], non_blocking=True)
+                    if split:
+                        # the row tails, on this thread while the device works;
+                        # cleared before the download that may store into them
+                        h_moves[lo:lo + n, move_prefix:].zero_()
+                        _lib.check(self._lib.hv_download_moves(_ptr(d_mv), _ptr(d_nl), n,
+                                                               h_moves.data_ptr() + lo * MAX_LEGAL_MOVES *
+                                                               SIZEOF_GPU_MOVE, move_prefix, s.cuda_stream),
+                                   "generate_legal_moves_and_fnn_features_host")
+                    else:
+                        h_moves[lo:lo + n].copy_(d_mv[:n], non_blocking=True)
                     h_nl[lo:lo + n].copy_(d_nl[:n], non_blocking=True)
                     h_feat[lo:lo + n].copy_(d_ft[:n], non_blocking=True)
             for s in streams:

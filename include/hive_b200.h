@@ -110,6 +110,20 @@ int hv_fnn_features_linked(const uint8_t* states, const uint8_t* moves, const in
  * reaches it. */
 int hv_stage_host_states(const uint8_t* host_states, int64_t count, uint8_t* dev_states, void* stream);
 
+/* The download half of the host-buffer movegen pipeline: a chunk's move
+ * rows [count, 256, 6] from the device into pinned host memory, sending
+ * over the host link only the first `prefix` moves of every row (one
+ * pitched copy) and, for positions with more legal moves, the moves past
+ * the prefix (a kernel that stores into the mapped host rows).  Bytes
+ * 6*prefix .. 1535 of every host row must already be zero (the caller
+ * clears them on the host, before this call; the device rows are zero past
+ * num_legal).  prefix: 0 .. 256, a multiple of 8.  Pageable host memory,
+ * prefix 256, or either pointer off a 16-byte boundary: one full copy, no
+ * precondition.  Asynchronous on `stream`.  No reference counterpart (the
+ * reference returns device tensors). */
+int hv_download_moves(const uint8_t* dev_moves, const int32_t* dev_num_legal, int64_t count, uint8_t* host_moves,
+                      int prefix, void* stream);
+
 /* extract_fnn_features_batch(states, legal_moves, num_legal, batch_size)
  * replaces bindings.cpp:330-333 / game_logic.cu:1409-1431. */
 int hv_extract_fnn_features(const uint8_t* states, const uint8_t* moves, const int32_t* num_legal,

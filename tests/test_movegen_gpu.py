@@ -183,6 +183,42 @@ def test_host_buffer_pipeline_matches_device_call(ext, orc):
         assert np.array_equal(_bits(fh.numpy()), _bits(fg))
 
 
+@pytest.mark.parametrize("prefix", [0, 8, 96, 248, 256])
+def test_host_pipeline_prefix_download_into_poisoned_buffers(ext, orc, prefix):
+    """Pinned output buffers full of 0xAB: the prefix download (hv_download_moves)
+    plus the host-cleared row tails give the device call's bytes, for any prefix
+    (lists shorter and longer than it, a ragged last chunk); a pageable moves
+    buffer takes the full copy."""
+    st = orc.generate_positions(5150 + prefix, 0, 3000, 200, 7)
+    mg, ng, fg = (x.cpu().numpy() for x in ext.generate_legal_moves_and_fnn_features_batch(_cuda(st), 3000))
+    if prefix in (8, 96):
+        assert (ng > prefix).any() and (ng < prefix).any()
+    host = torch.from_numpy(st).pin_memory()
+    for pinned in (True, False):
+        out = (torch.full((3000, 256, 6), 0xAB, dtype=torch.uint8, pin_memory=pinned),
+               torch.full((3000,), -7, dtype=torch.int32, pin_memory=pinned),
+               torch.full((3000, 122), float("nan"), dtype=torch.float32, pin_memory=pinned))
+        mh, nh, fh = ext.generate_legal_moves_and_fnn_features_host(host, 3000, out=out, chunk=1024,
+                                                                    move_prefix=prefix)
+        torch.cuda.current_stream().synchronize()
+        assert np.array_equal(mh.numpy(), mg)
+        assert np.array_equal(nh.numpy(), ng)
+        assert np.array_equal(_bits(fh.numpy()), _bits(fg))
+
+
+def test_download_moves_rejects_bad_prefix(ext):
+    lib = ext._lib
+    d = torch.zeros((4, 256, 6), dtype=torch.uint8, device="cuda")
+    n = torch.zeros((4,), dtype=torch.int32, device="cuda")
+    h = torch.zeros((4, 256, 6), dtype=torch.uint8).pin_memory()
+    s = torch.cuda.current_stream().cuda_stream
+    for bad in (-8, 12, 264):
+        assert lib.hv_download_moves(d.data_ptr(), n.data_ptr(), 4, h.data_ptr(), bad, s) != 0
+    assert lib.hv_download_moves(d.data_ptr(), n.data_ptr(), -1, h.data_ptr(), 96, s) != 0
+    assert lib.hv_download_moves(d.data_ptr(), n.data_ptr(), 4, h.data_ptr(), 96, s) == 0
+    torch.cuda.current_stream().synchronize()
+
+
 @pytest.mark.parametrize("mask,max_ply", [(0, 60), (7, 120), (7, 200)])
 def test_hybrid_transformer_inputs_bit_exact(ext, orc, mask, max_ply):
     """Piece tokens, global and move features (state_encoder.cuh:372-550) against the oracle,
