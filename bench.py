@@ -931,7 +931,7 @@ def main() -> None:
     ap.add_argument("--hybrid-warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline legs")
-    ap.add_argument("--e2e-chunk", type=int, default=16384, help="positions per pipelined chunk of the e2e leg")
+    ap.add_argument("--e2e-chunk", type=int, default=32768, help="positions per pipelined chunk of the e2e leg")
     ap.add_argument("--long-s", type=float, default=2.0,
                     help="seconds of the config-2 steps' second, long timed region (0: none; profiling runs)")
     ap.add_argument("--positions", type=int, default=POSITIONS,

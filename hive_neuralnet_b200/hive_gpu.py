@@ -143,7 +143,7 @@ class HiveGPUExtension:
         return moves, num_legal, feats
 
     def generate_legal_moves_and_fnn_features_host(self, states: torch.Tensor, batch_size: int,
-                                                   out: tuple | None = None, chunk: int = 16384,
+                                                   out: tuple | None = None, chunk: int = 32768,
                                                    device: torch.device | None = None,
                                                    move_prefix: int = HOST_MOVE_PREFIX):
         """Host-buffer form of :meth:`generate_legal_moves_and_fnn_features_batch`.
