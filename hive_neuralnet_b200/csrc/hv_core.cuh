@@ -265,19 +265,28 @@ __device__ __forceinline__ uint32_t load_row(const uint8_t* st, int off, int lan
 // Articulation flag of the piece lane: every lane removes its vertex and
 // floods the rest (the lane loops run for the longest flood).
 __device__ __forceinline__ bool articulation_flood(WarpSmem* w, const Setup& S) {
-    Pos P{w};
     const int l = lane_id();
-    // adjacency in piece-index space
+    // adjacency in piece-index space, from the occupancy words and piece
+    // prefixes of the three rows around the cell (neighbours E (r, q+1),
+    // NE (r-1, q+1), NW (r-1, q), W (r, q-1), SW (r+1, q-1), SE (r+1, q);
+    // padding bits are zero, row 23 is empty)
     uint32_t adj = 0;
     if (S.my_cell >= 0) {
-#pragma unroll 1
-        for (int d = 0; d < 6; d++) {
-            int nb = nbr(S.my_cell, d);
-            if (nb >= 0 && rowbit(w->occ, nb)) {
-                int j = P.pidx(nb);
+        const int r = S.my_cell >> 5, q = S.my_cell & 31;
+        const uint32_t ou = r ? w->occ[r - 1] : 0u, om = w->occ[r], od = w->occ[r + 1];
+        const int pu = r ? w->pref[r - 1] : 0, pm = w->pref[r], pd = w->pref[r + 1];
+        auto take = [&](uint32_t row, int pre, int col) {
+            if (col >= 0 && ((row >> col) & 1u)) {
+                const int j = pre + __popc(row & ((1u << col) - 1u));
                 if (j < S.n) adj |= 1u << j;
             }
-        }
+        };
+        take(ou, pu, q);
+        take(ou, pu, q + 1);
+        take(om, pm, q - 1);
+        take(om, pm, q + 1);
+        take(od, pd, q - 1);
+        take(od, pd, q);
     }
     w->adj[l] = adj;
     __syncwarp();

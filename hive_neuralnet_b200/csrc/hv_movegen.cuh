@@ -705,9 +705,13 @@ __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* ou
     bool adjq0 = false, adjq1 = false;
     if (cell >= 0 && pt >= 1 && pt <= 8) {
         atomicAdd(&w->acc[A_CNT + tc], 1);
-        int occn = 0;
-#pragma unroll 1
-        for (int d = 0; d < 6; d++) occn += P.height(nbr(cell, d)) > 0;
+        // occupied neighbours from the occupancy row words (a cell is
+        // occupied iff its height is nonzero; padding bits are zero): row r-1
+        // columns q, q+1; row r columns q-1, q+1; row r+1 columns q-1, q
+        const int rr = cell >> 5, qq = cell & 31;
+        const uint32_t up = rr ? w->occ[rr - 1] : 0u, mid = w->occ[rr], dn = w->occ[rr + 1];
+        const int occn =
+            __popc(((up >> qq) & 3u) | ((((mid << 1) >> qq) & 5u) << 2) | ((((dn << 1) >> qq) & 3u) << 5));
         if (occn == 0) atomicAdd(&w->acc[A_SINGLE + col], 1);
         int oq = col ? q0 : q1;
         if (oq >= 0) {
