@@ -454,11 +454,17 @@ __device__ __forceinline__ void placement_list(WarpSmem* w) {
 }
 
 // placeable piece-type mask of the side to move (move_gen.cuh:1161-1174)
+static_assert(kOffHands % 4 == 0, "the hand counts are read as 32-bit words");
 __device__ __forceinline__ uint32_t placeable_types(const Pos& P, int color, bool forced) {
-    uint32_t m = 0;
-#pragma unroll 1
-    for (int t = 0; t < 8; t++)
-        if (P.hand(color, t) > 0) m |= 1u << t;
+    // the eight hand counts as two words: bit 7 of a byte is set iff the byte
+    // is nonzero, then bits 7, 15, 23, 31 move to 0..3 by one multiply (the
+    // partial products land on distinct bits)
+    const uint32_t* hw = reinterpret_cast<const uint32_t*>(P.w->st + kOffHands + color * 8);
+    auto nz4 = [](uint32_t x) {
+        x = (((x & 0x7f7f7f7fu) + 0x7f7f7f7fu) | x) & 0x80808080u;
+        return (((x >> 7) * 0x00204081u) >> 21) & 15u;
+    };
+    const uint32_t m = nz4(hw[0]) | (nz4(hw[1]) << 4);
     return forced ? (m & 1u) : m;
 }
 
