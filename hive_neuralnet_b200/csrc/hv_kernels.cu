@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
                 store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes), n);
                 if (lane_id() == 0) nl_out[p] = n;
             }
-            if (FEATS) features(w, n, feats_out + p * kFeat);
+            if (FEATS) features_full(w, n, feats_out + p * kFeat);
         } else {
             n = nl_in[p];
             n = n < 0 ? 0 : (n > kMaxMoves ? kMaxMoves : n);
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
                 setup_position<false, true, true>(w, reinterpret_cast<const uint32_t*>(feats_out)[p * kFeat]);
             else
                 setup_position<false, true>(w);
-            features(w, n, feats_out + p * kFeat);
+            features_full(w, n, feats_out + p * kFeat);
         }
         __syncwarp();
         p = q;
@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_fnn_eval(
         } else {
             stage_state_moves(w, st_g, mv_g);
             Setup S = setup_position(w);
-            features(w, n, f->xs[0]);
+            features_full(w, n, f->xs[0]);
         }
         float val[kFnnChunk], lg[kFnnChunk];
         fnn_encode_chunk(wts, dims, off, f, 1, val);
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_hybrid_eval(
         } else {
             stage_state_moves(w, st_g, mv_g);
             Setup S = setup_position(w);
-            features(w, n, f->xs[0]);
+            features_full(w, n, f->xs[0]);
         }
         float val[kFnnChunk], lg[kFnnChunk];
         const float root_value = hybrid_root(f, p, graph, glob, fw, fd, hw, hd);
@@ -744,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_leaf_root(
             int n = (int)clamp_rows(num_legal[p]);
             stage_state_moves(w, states + p * kStateBytes, legal_moves + p * (kMaxMoves * kMoveBytes));
             Setup S = setup_position(w);
-            features(w, n, f->xs[0]);
+            features_full(w, n, f->xs[0]);
         }
         float v;
         if (HYB) {
@@ -926,7 +926,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_hybrid(const uint8_
             n = gen_legal(w, &g_error);
             store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes), n);
             if (l == 0) nl_out[p] = n;
-            features(w, n, feats_out + p * kFeat);
+            features_full(w, n, feats_out + p * kFeat);
             if (TOKENS) {
                 // reads only the staged state and S, which features() leaves intact
                 int t = hybrid_tokens(w, o.tf + p * kTokens * kTokFeat, o.tq + p * kTokens,

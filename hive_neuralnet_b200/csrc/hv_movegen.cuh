@@ -690,6 +690,12 @@ __device__ __forceinline__ int top_c(const WarpSmem* w, int c) {
     return h ? w->st[(h - 1) * kCells + c] : 0;
 }
 
+// RUNS: the list is a full legal list, whose moves come in runs (the moves
+// of one piece, the types placed on one cell): the source-cell and
+// placement sets are then set once per run instead of by every lane of it
+// (atomics of one instruction to one word serialise).  A compact list has
+// one entry per (type, owner) and per placement cell: no runs to skip.
+template <bool RUNS = false>
 __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* out) {
     const Setup S = reload_setup(w);
     Pos P{w};
@@ -765,17 +771,47 @@ __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* ou
         }
     }
     // source cells per (type, owner) and placement cells from the list
+    if (RUNS) {
 #pragma unroll 1
-    for (int m = l; m < nmoves; m += 32) {
-        int tp = w->mv[3 * m], from = w->mv[3 * m + 1], to = w->mv[3 * m + 2];
-        int type = tp & 255, mpt = tp >> 8;
-        if (type == 1) {
-            if (mpt >= 1 && mpt <= 8 && from < kCells) {
-                int owner = w->st[kOffHeight + from] > 0 ? ((top_c(w, from) >> 4) & 1) : cur;
-                atomicOr(&w->bm[((mpt - 1) * 2 + owner) * 17 + (from >> 5)], 1u << (from & 31));
+        for (int base = 0; base < nmoves; base += 32) {
+            const int m = base + l;
+            // the bit a move sets: (piece type, source cell) for a movement,
+            // the cell for a placement; in a run of equal keys only the
+            // first lane sets it (the owner is that of the cell's top piece)
+            int key = -1;
+            if (m < nmoves) {
+                const int tp = w->mv[3 * m], from = w->mv[3 * m + 1], to = w->mv[3 * m + 2];
+                const int type = tp & 255, mpt = tp >> 8;
+                if (type == 1) {
+                    if (mpt >= 1 && mpt <= 8 && from < kCells) key = (mpt << 10) | from;
+                } else if (type == 0 && to < kCells) {
+                    key = (1 << 14) | to;
+                }
             }
-        } else if (type == 0 && to < kCells) {
-            atomicOr(&w->pl[to >> 5], 1u << (to & 31));
+            const int prev = __shfl_up_sync(kFull, key, 1);
+            if (key >= 0 && (l == 0 || prev != key)) {
+                const int c = key & 1023;
+                if (key >> 14) {
+                    atomicOr(&w->pl[c >> 5], 1u << (c & 31));
+                } else {
+                    const int owner = w->st[kOffHeight + c] > 0 ? ((top_c(w, c) >> 4) & 1) : cur;
+                    atomicOr(&w->bm[(((key >> 10) - 1) * 2 + owner) * 17 + (c >> 5)], 1u << (c & 31));
+                }
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int m = l; m < nmoves; m += 32) {
+            int tp = w->mv[3 * m], from = w->mv[3 * m + 1], to = w->mv[3 * m + 2];
+            int type = tp & 255, mpt = tp >> 8;
+            if (type == 1) {
+                if (mpt >= 1 && mpt <= 8 && from < kCells) {
+                    int owner = w->st[kOffHeight + from] > 0 ? ((top_c(w, from) >> 4) & 1) : cur;
+                    atomicOr(&w->bm[((mpt - 1) * 2 + owner) * 17 + (from >> 5)], 1u << (from & 31));
+                }
+            } else if (type == 0 && to < kCells) {
+                atomicOr(&w->pl[to >> 5], 1u << (to & 31));
+            }
         }
     }
     __syncwarp();
@@ -844,5 +880,9 @@ __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* ou
 // out-of-line forms for the kernels that are not bound by their calls
 __device__ __noinline__ int gen_compact(WarpSmem* w, uint32_t* err) { return gen_compact_body(w, err); }
 __device__ __noinline__ void features(WarpSmem* w, int nmoves, float* out) { features_body(w, nmoves, out); }
+// the features of a position from its full legal list
+__device__ __noinline__ void features_full(WarpSmem* w, int nmoves, float* out) {
+    features_body<true>(w, nmoves, out);
+}
 
 }  // namespace hv
