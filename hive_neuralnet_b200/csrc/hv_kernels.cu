@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, HV_MIN_BLOCKS) k_root(const uint8_t*
                 const uint32_t apm = __ballot_sync(kFull, S.my_ap);
                 if (lane_id() == 0) reinterpret_cast<uint32_t*>(feats_out)[p * kFeat] = apm;
             }
-            n = gen_legal(w, &g_error);
+            n = gen_legal(w, S, &g_error);
             if (WRITE_MOVES) {
                 store_moves(w, moves_out + p * (kMaxMoves * kMoveBytes), n);
                 if (lane_id() == 0) nl_out[p] = n;

@@ -474,9 +474,9 @@ __device__ __forceinline__ uint32_t placeable_types(const Pos& P, int color, boo
 // Inlined into its kernels, with placement_cells and gen_mosquito: the calls'
 // saved registers went through local memory once per position (generator
 // 1.81 -> 1.52 ms per 262,144 positions); the walks stay out of line (their
-// code is shared by every piece, and inlining them spilled).
-__device__ __forceinline__ int gen_legal(WarpSmem* w, uint32_t* err) {
-    const Setup S = reload_setup(w);
+// code is shared by every piece, and inlining them spilled).  S: the Setup
+// that setup_position returned for the staged position.
+__device__ __forceinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* err) {
     Pos P{w};
     int l = lane_id();
     if (P.result() != 0) return 0;
@@ -566,6 +566,9 @@ __device__ __forceinline__ int gen_legal(WarpSmem* w, uint32_t* err) {
     __syncwarp();
     return count;
 }
+
+// the same from the Setup of the staged position, re-read from the warp slot
+__device__ __forceinline__ int gen_legal(WarpSmem* w, uint32_t* err) { return gen_legal(w, reload_setup(w), err); }
 
 // ---------------------------------------------------------------------------
 // compact list for successor features (move_gen.cuh:1362-1563)
@@ -762,13 +765,29 @@ __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* ou
     uint32_t cap0 = __ballot_sync(kFull, capable && col == 0);
     uint32_t cap1 = __ballot_sync(kFull, capable && col == 1);
     if (capable && __popc((col ? cap1 : cap0) & lanemask_lt()) < 8) {
-#pragma unroll 1
-        for (int d = 0; d < 6; d++) {
-            int nb = nbr(cell, d);
-            if (nb < 0 || P.height(nb) == 0 || stun == nb) continue;
-            int nc = (P.top(nb) >> 4) & 1;
-            atomicAdd(&w->acc[nc == col ? A_TOWN + col : A_TOPP + nc], 1);
+        // occupied neighbours and those topped by the side to move, from the
+        // row words (bits: row r-1 q, q+1 -> 0, 1; row r q-1, q+1 -> 2, 4;
+        // row r+1 q-1, q -> 5, 6), the stunned cell taken out; a cell's top
+        // piece belongs to the side to move or to the other side
+        const int rr = cell >> 5, qq = cell & 31;
+        auto nb7 = [&](const uint32_t* rows) {
+            const uint32_t up = rr ? rows[rr - 1] : 0u, mid = rows[rr], dn = rows[rr + 1];
+            return ((up >> qq) & 3u) | ((((mid << 1) >> qq) & 5u) << 2) | ((((dn << 1) >> qq) & 3u) << 5);
+        };
+        uint32_t occm = nb7(w->occ), ownm = nb7(w->own);
+        if (stun >= 0) {
+            const int dr = (stun >> 5) - rr + 1, dc = (stun & 31) - qq + 1;
+            if ((unsigned)dr < 3u && (unsigned)dc < 3u) {
+                // bit of (dr, dc) in row-major 3 x 3 order; 7 (outside the code) for none
+                const uint32_t bit = (uint32_t)((0x765472107ull >> (4 * (dr * 3 + dc))) & 15ull);
+                occm &= ~(1u << bit);
+                ownm &= ~(1u << bit);
+            }
         }
+        const int n_occ = __popc(occm), n_own = __popc(ownm);
+        const int same = col == cur ? n_own : n_occ - n_own;
+        if (same) atomicAdd(&w->acc[A_TOWN + col], same);
+        if (n_occ - same) atomicAdd(&w->acc[A_TOPP + (col ^ 1)], n_occ - same);
     }
     // source cells per (type, owner) and placement cells from the list
     if (RUNS) {
