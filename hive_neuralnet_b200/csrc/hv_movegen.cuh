@@ -376,6 +376,20 @@ __device__ __forceinline__ int piece_moves(WarpSmem* w, uint32_t occ_row, int ce
     return walk(w, cell, mode, w->dst, c, first_only);
 }
 
+// Is the cell of a piece in `lanes` (piece-list indices) a neighbour of
+// cell?  Neighbours differ by +-1, +-31 or +-32 on the padded grid, and no
+// other pair of cells does (a row's padding columns hold no piece).
+__device__ __forceinline__ bool next_to_any(const WarpSmem* w, uint32_t lanes, int cell) {
+#pragma unroll 1
+    while (lanes) {
+        const int j = __ffs(lanes) - 1;
+        lanes &= lanes - 1;
+        const int dp = (int)w->pcell[j] - cell, a = dp < 0 ? -dp : dp;
+        if (a == 1 || a == 31 || a == 32) return true;
+    }
+    return false;
+}
+
 // Is any neighbour topped by a pillbug (move_gen.cuh:1326-1336)?
 __device__ __forceinline__ bool next_to_pillbug(WarpSmem* w, int cell) {
     Pos P{w};
@@ -533,8 +547,10 @@ __device__ __forceinline__ int gen_legal(WarpSmem* w, const Setup& S, uint32_t* 
         // (the piece lane's fields read again: nothing held across the calls)
         const Setup T = reload_setup(w);
         const int mt = T.my_top & 15;
+        // cells topped by a pillbug, of either side (move_gen.cuh:1326-1336)
+        const uint32_t pbt = __ballot_sync(kFull, T.my_cell >= 0 && mt == 8);
         const bool thr = T.my_cell >= 0 && rowbit(w->own, T.my_cell) &&
-                         (mt == 8 || (mt == 6 && T.my_h == 1 && next_to_pillbug(w, T.my_cell)));
+                         (mt == 8 || (mt == 6 && T.my_h == 1 && next_to_any(w, pbt, T.my_cell)));
         uint32_t throwers = __ballot_sync(kFull, thr);
 #pragma unroll 1
         while (throwers) {
@@ -639,8 +655,10 @@ __device__ __forceinline__ int gen_compact_body(WarpSmem* w, uint32_t* err) {
     }
     const Setup T = reload_setup(w);
     const int mt = T.my_top & 15;
+    // cells topped by a pillbug, of either side (move_gen.cuh:1326-1336)
+    const uint32_t pbt = __ballot_sync(kFull, T.my_cell >= 0 && mt == 8);
     const bool thr = T.my_cell >= 0 && rowbit(w->own, T.my_cell) &&
-                     (mt == 8 || (mt == 6 && T.my_h == 1 && next_to_pillbug(w, T.my_cell)));
+                     (mt == 8 || (mt == 6 && T.my_h == 1 && next_to_any(w, pbt, T.my_cell)));
     uint32_t throwers = __ballot_sync(kFull, thr);
 #pragma unroll 1
     while (throwers && count < kMaxMoves) {
@@ -718,6 +736,8 @@ __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* ou
     const int pt = top & 15, col = (top >> 4) & 1, tc = (pt - 1) * 2 + col;
     bool capable = false;
     bool adjq0 = false, adjq1 = false;
+    // the pieces whose cell is topped by a pillbug that is not stunned
+    const uint32_t pbm = __ballot_sync(kFull, cell >= 0 && pt == 8 && stun != cell);
     if (cell >= 0 && pt >= 1 && pt <= 8) {
         atomicAdd(&w->acc[A_CNT + tc], 1);
         // occupied neighbours from the occupancy row words (a cell is
@@ -747,17 +767,7 @@ __device__ __forceinline__ void features_body(WarpSmem* w, int nmoves, float* ou
             }
         }
         capable = stun != cell && pt == 8;
-        if (!capable && stun != cell && pt == 6 && h == 1) {
-#pragma unroll 1
-            for (int d = 0; d < 6; d++) {
-                int nb = nbr(cell, d);
-                if (nb < 0 || P.height(nb) == 0 || stun == nb) continue;
-                if ((P.top(nb) & 15) == 8) {
-                    capable = true;
-                    break;
-                }
-            }
-        }
+        if (!capable && stun != cell && pt == 6 && h == 1) capable = next_to_any(w, pbm, cell);
         if (capable) w->acc[A_CAP + col] = 1;
     }
     uint32_t s0 = __ballot_sync(kFull, adjq0), s1 = __ballot_sync(kFull, adjq1);
