@@ -53,6 +53,36 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     assert lib.hv_apply_moves(None, None, 0, None) == 0  # empty batch is a no-op
 
 
+def test_download_and_packed_trunk_arguments_without_gpu(lib):
+    v = ctypes.c_void_p(256)
+    # the row prefix is a multiple of 8 moves in 0..256; counts are not negative
+    for bad in (-8, 12, 264):
+        assert lib.hv_download_moves(v, v, 4, v, bad, None) == 1
+    assert lib.hv_download_moves(v, v, -1, v, 64, None) == 1
+    assert lib.hv_download_moves(None, v, 4, v, 64, None) == 1
+    assert lib.hv_download_moves(None, None, 0, None, 64, None) == 0  # empty chunk: nothing to do
+    # the packed trunk's slot table: two counters and one entry per position
+    need = ctypes.c_size_t(0)
+    assert lib.hv_hybrid_trunk_packed_workspace_bytes(1000, ctypes.addressof(need)) == 0
+    assert need.value == 16 + 8 * 1000
+    assert lib.hv_hybrid_trunk_packed_workspace_bytes(-1, ctypes.addressof(need)) == 1
+    # workspace missing, off a 16-byte boundary or too small
+    args = [v] * 5 + [1000, 27, v, v, v]
+    assert lib.hv_hybrid_trunk_packed(*args, None, 16 + 8 * 1000, None) == 1
+    assert lib.hv_hybrid_trunk_packed(*args, ctypes.c_void_p(264), 16 + 8 * 1000, None) == 1
+    assert lib.hv_hybrid_trunk_packed(*args, v, 8 * 1000, None) == 1
+
+
+def test_host_pipeline_rejects_bad_prefix_without_gpu():
+    import torch
+    from hive_neuralnet_b200.hive_gpu import load_extension
+    ext = load_extension()
+    st = torch.zeros((4, 3424), dtype=torch.uint8)
+    for bad in (-8, 12, 264):
+        with pytest.raises(ValueError):
+            ext.generate_legal_moves_and_fnn_features_host(st, 4, move_prefix=bad)
+
+
 def test_loader_fails_loudly_without_library(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "_lib", None)
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "missing.so"))
