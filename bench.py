@@ -278,6 +278,12 @@ class Ranks:
         if self.world > 1:
             import datetime
 
+            # torchrun gives each rank one CPU thread; the host-buffer
+            # pipeline clears its row tails on torch's threads, so each rank
+            # takes its share of the host's cores
+            local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(self.world)))
+            torch.set_num_threads(max(1, host_cores() // max(1, local_world)))
+
             import torch.distributed as dist
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=self.dev)
             self.dist = dist
@@ -395,14 +401,23 @@ def bench_movegen(args, ranks: Ranks) -> dict:
     e2e_value = world * P * e2e_steps / (e2e_ms / 1e3)
     h2d = staged_upload_bytes(states)
     n_tall = int((states[:, 2645:2645 + 529].amax(1) >= 3).sum().item())
-    # bytes that crossed the link: with the pinned buffers each row's first
-    # HOST_MOVE_PREFIX moves (pitched copy) and, for longer lists, the moves
-    # past them in 16-byte stores; the rest of each row is cleared on the host
-    from hive_neuralnet_b200.hive_gpu import HOST_MOVE_PREFIX
-    nl64 = h_nl.to(torch.int64).clamp(0, MAX_MOVES)
-    tail = torch.where(nl64 > HOST_MOVE_PREFIX, (nl64 * MOVE_BYTES + 15) // 16 * 16 - HOST_MOVE_PREFIX * MOVE_BYTES,
-                       torch.zeros_like(nl64))
-    d2h = P * (HOST_MOVE_PREFIX * MOVE_BYTES + 4 + FEAT * 4) + int(tail.sum())
+    # bytes that crossed the link: with the pinned buffers (and enough host
+    # threads to clear the row tails) each row's first HOST_MOVE_PREFIX moves
+    # (pitched copy) and, for longer lists, the moves past them in 16-byte
+    # stores; the rest of each row is cleared on the host.  Else whole rows.
+    from hive_neuralnet_b200.hive_gpu import HOST_CLEAR_MIN_THREADS, HOST_MOVE_PREFIX
+    split = torch.get_num_threads() >= HOST_CLEAR_MIN_THREADS
+    if split:
+        nl64 = h_nl.to(torch.int64).clamp(0, MAX_MOVES)
+        tail = torch.where(nl64 > HOST_MOVE_PREFIX,
+                           (nl64 * MOVE_BYTES + 15) // 16 * 16 - HOST_MOVE_PREFIX * MOVE_BYTES, torch.zeros_like(nl64))
+        d2h = P * (HOST_MOVE_PREFIX * MOVE_BYTES + 4 + FEAT * 4) + int(tail.sum())
+        moves_path = (f"moves: the first {HOST_MOVE_PREFIX} of each row by a pitched copy, longer lists' rest "
+                      f"stored into the mapped rows, the row tails cleared on {torch.get_num_threads()} host "
+                      f"threads (hv_download_moves)")
+    else:
+        d2h = P * (MAX_MOVES * MOVE_BYTES + 4 + FEAT * 4)
+        moves_path = f"moves: whole rows ({torch.get_num_threads()} host threads per rank: too few to clear tails)"
     # the host results equal the device-resident step's (same positions)
     host_equal = (torch.equal(h_nl, out[1].cpu()) and torch.equal(h_moves, out[0].cpu())
                   and torch.equal(h_feat.view(torch.int32), out[2].cpu().view(torch.int32)))
@@ -516,9 +531,7 @@ def bench_movegen(args, ranks: Ranks) -> dict:
                 "path": f"generate_legal_moves_and_fnn_features_host, pinned host buffers, "
                         f"staged upload (hv_stage_host_states: stack levels over occupied rows; "
                         f"{n_tall} states with a 3-high stack), "
-                        f"{args.e2e_chunk}-position chunks over 3 streams; moves: the first "
-                        f"{HOST_MOVE_PREFIX} of each row by a pitched copy, longer lists' rest stored into "
-                        f"the mapped rows, the row tails cleared by the calling thread (hv_download_moves)",
+                        f"{args.e2e_chunk}-position chunks over 3 streams; {moves_path}",
                 "host_results_equal_device": host_equal,
                 "link": link},
         "roofline": roofline,

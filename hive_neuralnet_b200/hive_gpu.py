@@ -31,6 +31,10 @@ HOST_PIPELINE_STAGES = 3
 # as one pitched copy; the rest of each 256-move row is cleared on the host
 # and the moves past this prefix are stored into the mapped host rows
 HOST_MOVE_PREFIX = 64
+# the row tails are cleared by torch's CPU threads; with fewer threads than
+# this the clearing (about 300 MB per 262,144 positions) is slower than
+# sending the tails over the link, and the whole rows are copied instead
+HOST_CLEAR_MIN_THREADS = 8
 SIZEOF_GPU_MOVE = 6
 OFF_TURN = 3412
 OFF_QUEEN_PLACED = 3414
@@ -160,7 +164,8 @@ class HiveGPUExtension:
         into the mapped rows by a kernel); the calling thread clears the rest
         of each row in host memory meanwhile, so the zero padding (about
         half of the bytes returned) never crosses the link
-        (``hv_download_moves``).  Returns after queuing; the caller's current
+        (``hv_download_moves``; with fewer than ``HOST_CLEAR_MIN_THREADS``
+        torch threads the whole rows are copied).  Returns after queuing; the caller's current
         stream is ordered after every chunk, so
         ``torch.cuda.current_stream().synchronize()`` makes the outputs valid.
         """
@@ -190,7 +195,8 @@ class HiveGPUExtension:
         chunk = min(chunk, max(batch_size, 1))
         # rows cleared on the host take the prefix download (hv_download_moves
         # falls back to one full copy for pageable memory or a misaligned row)
-        split = move_prefix < MAX_LEGAL_MOVES and h_moves.is_pinned() and h_moves.data_ptr() % 16 == 0
+        split = (move_prefix < MAX_LEGAL_MOVES and h_moves.is_pinned() and h_moves.data_ptr() % 16 == 0
+                 and torch.get_num_threads() >= HOST_CLEAR_MIN_THREADS)
         slots, streams = self._staging(dev, chunk)
         cur = torch.cuda.current_stream(dev)
         ready = cur.record_event()
