@@ -278,12 +278,6 @@ class Ranks:
         if self.world > 1:
             import datetime
 
-            # torchrun gives each rank one CPU thread; the host-buffer
-            # pipeline clears its row tails on torch's threads, so each rank
-            # takes its share of the host's cores
-            local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(self.world)))
-            torch.set_num_threads(max(1, host_cores() // max(1, local_world)))
-
             import torch.distributed as dist
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=self.dev)
             self.dist = dist
